@@ -1,0 +1,339 @@
+"""Benchmark of the B200 selective-scan hot path.
+
+Default workload: the fused selective scan forward + backward, fp32, with D skip,
+SiLU(z) gate and softplus(delta + delta_bias): b=8, L=2048, D=512, N=16 (one block of a
+d_model=256, expand=2 Sift model).  One step = one forward (with state checkpoints)
+plus one backward over one batch of seeded synthetic inputs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (torchrun, one rank per GPU) each rank runs its own batch (weak scaling:
+batch rows are independent channels of the scan, no collective on the data path).
+Metric: algorithmic GB/s (each input read once, each output written once; 375.4 MB
+per step at b=8) summed over ranks, timed on the device with CUDA events, max over
+ranks.  Prints one JSON line on rank 0.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "selective-scan fwd+bwd GB/s & % HBM peak; Sift LM train tokens/s at 1/2/4/8 B200"
+CFG = dict(b=8, L=2048, D=512, N=16)
+FALLBACK_HBM_GBS = 6650.0
+
+
+def alg_bytes(b, L, D, N, es=4):
+    """Algorithmic bytes of one fwd+bwd: fwd reads u, delta, z, B, C and writes out;
+    bwd reads u, delta, z, dout, B, C and writes du, ddelta, dz, dB, dC.
+    (Parameters A, D, delta_bias and their grads are O(D*N) and not counted.)"""
+    bld, bln = b * L * D * es, b * L * N * es
+    fwd = 3 * bld + 2 * bln + bld
+    bwd = 4 * bld + 2 * bln + 3 * bld + 2 * bln
+    return fwd, bwd
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic():
+    """dram bytes per launch of the backward kernel from the committed ncu summary."""
+    p = os.path.join(ROOT, "profiles", "scan_bwd_kernel_c1.md")
+    try:
+        with open(p) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(float(line.split(":")[1]))
+    except Exception:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = float(parts[1])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x, world, device):
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ----------------------------------------------------------------- our arm
+def run_ours(args, world, rank, local):
+    from swiftx_b200 import _lib
+    from swiftx_b200.selective_scan import scan_backward, scan_forward
+    from swiftx_b200.workloads import config_inputs
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    b, L, D, N = CFG["b"], CFG["L"], CFG["D"], CFG["N"]
+    inp = config_inputs(b, L, D, N, seed=rank, device=dev)
+    args_f = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+
+    def step(rec=None):
+        if rec is not None:
+            rec[0].record()
+        _, ck, _ = scan_forward(*args_f, checkpoints=True)
+        if rec is not None:
+            rec[1].record()
+        scan_backward(*args_f, None, ck, inp["dout"])
+        if rec is not None:
+            rec[2].record()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    recs = [[ev(), ev(), ev()] for _ in range(args.steps)]
+    sampler = ClockSampler(local) if local == 0 else None
+    if sampler:
+        sampler.__enter__()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0, t1 = ev(), ev()
+    t0.record()
+    for k in range(args.steps):
+        step(recs[k])
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    if sampler:
+        sampler.__exit__()
+    ms = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(ms, world, dev)
+    fwd_ms = statistics.mean(r[0].elapsed_time(r[1]) for r in recs)
+    bwd_ms = statistics.mean(r[1].elapsed_time(r[2]) for r in recs)
+
+    fwd_b, bwd_b = alg_bytes(b, L, D, N)
+    step_bytes = fwd_b + bwd_b
+    value = step_bytes * world / (ms * 1e-3) / 1e9
+
+    # end to end through the public API with host buffers (pinned), copies inside the region
+    e2e = run_e2e(args, inp, dev, world)
+
+    peak, peak_kind = measured_peak()
+    dom_ms, dom_bytes, dom_name = (bwd_ms, bwd_b, "scan_bwd_kernel") if bwd_ms >= fwd_ms else \
+        (fwd_ms, fwd_b, "scan_fwd_kernel")
+    achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
+    res = {
+        "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded; BASELINE config-1 value distributions)",
+        "config": {"workload": "selective_scan fwd+bwd, fp32, D-skip + SiLU(z) gate + softplus(delta+bias)",
+                   "batch": b, "seqlen": L, "d_inner": D, "d_state": N, "per_gpu_batch": b,
+                   "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
+                   "l2": "inputs larger than L2 (working set ~440 MB/step > 126 MB)",
+                   "alg_bytes_per_step": step_bytes},
+        "fwd_ms": round(fwd_ms, 4), "bwd_ms": round(bwd_ms, 4),
+        "frac_of_hbm_step": round(value / world / peak, 4),
+        "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
+                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "traffic": profiled_traffic(), "alg_bytes_per_launch": dom_bytes},
+        "gpu_launches": 3 * args.steps,
+        "e2e": e2e,
+    }
+    if sampler:
+        res["clocks"] = sampler.summary()
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        res["cpu_baseline"] = cpu_baseline(args, sample_b=1, reps=2)
+    return res
+
+
+def run_e2e(args, inp, dev, world):
+    from swiftx_b200.selective_scan import scan_backward, scan_forward
+    host = {k: (v.cpu().pin_memory() if v is not None else None) for k, v in inp.items()}
+    keys_in = ["u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias"]
+    h2d = sum(host[k].numel() * host[k].element_size() for k in keys_in)
+
+    def step():
+        d = {k: host[k].to(dev, non_blocking=True) for k in keys_in}
+        out, ck, _ = scan_forward(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"],
+                                  d["delta_bias"], True, checkpoints=True)
+        g = scan_backward(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"],
+                          d["delta_bias"], True, None, ck, d["dout"])
+        res = [out] + [v for v in g.values() if v is not None]
+        outs = [r.to("cpu", non_blocking=True) for r in res]
+        return outs, sum(r.numel() * r.element_size() for r in res)
+
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    d2h = 0
+    for _ in range(args.steps):
+        _, d2h = step()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world, dev)
+    b, L, D, N = CFG["b"], CFG["L"], CFG["D"], CFG["N"]
+    fwd_b, bwd_b = alg_bytes(b, L, D, N)
+    return {"value": round((fwd_b + bwd_b) * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "swiftx_b200.selective_scan.scan_forward/scan_backward (C ABI) from pinned host buffers"}
+
+
+# ----------------------------------------------------------------- CPU oracle (reference arm / baseline)
+def cpu_baseline(args, sample_b=1, reps=1):
+    """The oracle port of the reference's scan (float64 C, OpenMP over all host threads)
+    on a bounded sample of the workload: `sample_b` of the 8 batch rows, full L and D."""
+    import numpy as np
+
+    import oracle
+    from swiftx_b200.workloads import config_inputs
+
+    b, L, D, N = sample_b, CFG["L"], CFG["D"], CFG["N"]
+    inp = config_inputs(b, L, D, N, seed=0)
+    a = {k: (v.double().numpy() if v is not None else None) for k, v in inp.items()}
+    oracle.set_num_threads(os.cpu_count() or 1)
+    times = []
+    for _ in range(reps):
+        t = time.perf_counter()
+        oracle.scan_fwd(a["u"], a["delta"], a["A"], a["B"], a["C"], D=a["D"], z=a["z"],
+                        delta_bias=a["delta_bias"], delta_softplus=True)
+        oracle.scan_bwd(a["u"], a["delta"], a["A"], a["B"], a["C"], a["dout"], D=a["D"], z=a["z"],
+                        delta_bias=a["delta_bias"], delta_softplus=True)
+        times.append(time.perf_counter() - t)
+    fwd_b, bwd_b = alg_bytes(b, L, D, N)
+    best = min(times)
+    _ = np
+    return {"value": round((fwd_b + bwd_b) / best / 1e9, 4), "unit": "GB/s", "cores": oracle.num_threads(),
+            "kind": "port", "seconds_per_sample": round(best, 3),
+            "sample": f"b={b} of 8 rows, L={L}, D={D}, N={N}, fwd+bwd, best of {reps}"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    reps = 1
+    times = []
+    for _ in range(args.warmup):
+        cpu_baseline(args, sample_b=1, reps=1)
+    for _ in range(args.steps):
+        times.append(cpu_baseline(args, sample_b=1, reps=reps))
+    best = max(times, key=lambda r: r["value"])
+    v = statistics.mean(r["value"] for r in times)
+    return {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
+            "config": {"workload": "selective_scan fwd+bwd, D-skip + SiLU(z) gate + softplus(delta+bias)",
+                       "batch": CFG["b"], "seqlen": CFG["L"], "d_inner": CFG["D"], "d_state": CFG["N"]},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": best["cores"], "kind": "port",
+                             "sample": best["sample"]},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        res = run_reference(args, world, rank)
+    else:
+        res = run_ours(args, world, rank, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    if world > 1 and args.impl == "ours":
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

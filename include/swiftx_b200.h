@@ -1,0 +1,107 @@
+/*
+ * swiftx_b200 -- C ABI of the B200 selective-scan hot path.
+ *
+ * Plain C: device pointers, element strides and sizes; no framework types.
+ * Every entry point returns an int status (SWX_OK on success) and launches its
+ * kernels on the given cudaStream_t (passed as void*; NULL = legacy default
+ * stream).  Nothing here allocates device memory: outputs, checkpoints and
+ * workspaces are provided by the caller (the Python host layer allocates them
+ * with torch on the current stream).  The library holds no global state and
+ * takes no locks; concurrent calls on different streams are independent.
+ *
+ * Shapes follow the reference API (models/selective_scan.py:36-43):
+ *   u, delta, z, out, dout, du, ddelta, dz : (b, L, D)   innermost stride 1
+ *   B, C, dB, dC                           : (b, L, N)   innermost stride 1
+ *   A, dA : (D, N) dense;  Dskip, delta_bias, dD, ddelta_bias : (D,)
+ *   h0, h_last, dh0 : (b, D, N) dense fp32
+ * Strides are in elements.  N <= 16.
+ */
+#ifndef SWIFTX_B200_H
+#define SWIFTX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SWX_ABI_VERSION 1
+
+/* status codes */
+#define SWX_OK 0
+#define SWX_ERR_INVALID_ARG 1   /* bad shape, size, stride or missing pointer */
+#define SWX_ERR_UNSUPPORTED 2   /* dtype / layout this build does not handle */
+#define SWX_ERR_CUDA 3          /* a CUDA launch or runtime call failed */
+#define SWX_ERR_TIMEOUT 4       /* a bounded device-side wait gave up */
+
+/* element types */
+#define SWX_DTYPE_F32 0
+#define SWX_DTYPE_BF16 1
+
+/* Arguments of the scan entry points (forward and backward share one struct). */
+typedef struct swx_scan_args {
+    int64_t batch, seqlen, dim, dstate;
+    int32_t in_dtype;        /* u, delta, z, B, C, dout and the (b,L,*) gradients */
+    int32_t out_dtype;       /* out */
+    int32_t delta_softplus;  /* delta_eff = softplus(delta + delta_bias) when nonzero */
+    int32_t reserved;
+    /* inputs */
+    const void* u;     int64_t u_sb, u_sl;
+    const void* delta; int64_t delta_sb, delta_sl;
+    const void* z;     int64_t z_sb, z_sl;      /* optional SiLU gate */
+    const void* B;     int64_t B_sb, B_sl;
+    const void* C;     int64_t C_sb, C_sl;
+    const float* A;            /* (D, N) */
+    const float* Dskip;        /* optional */
+    const float* delta_bias;   /* optional */
+    const float* h0;           /* optional initial state */
+    /* forward outputs */
+    void* out;                 /* (b, L, D) dense */
+    float* h_last;             /* optional final state */
+    float* checkpoints;        /* optional in forward (required for backward):
+                                  swx_scan_checkpoint_floats() fp32 values */
+    /* backward inputs / outputs */
+    const void* dout;  int64_t dout_sb, dout_sl;
+    void* du; void* ddelta; void* dz;   /* (b, L, D) dense, in_dtype; dz only with z */
+    void* dB; void* dC;                 /* (b, L, N) dense, in_dtype */
+    float* dA;                          /* (D, N) */
+    float* dD;                          /* optional (with Dskip) */
+    float* ddelta_bias;                 /* optional (with delta_bias) */
+    float* dh0;                         /* optional (with h0) */
+    void* workspace; int64_t workspace_bytes;  /* >= swx_scan_bwd_workspace_bytes() */
+} swx_scan_args;
+
+int swx_abi_version(void);
+const char* swx_status_string(int status);
+/* sizeof(swx_scan_args), so a binding can check its mirror of the struct. */
+int64_t swx_scan_args_size(void);
+
+/* Number of fp32 values of the forward's state checkpoints (one (D, 16) slab per
+ * 16 time steps per batch row). */
+int64_t swx_scan_checkpoint_floats(int64_t batch, int64_t seqlen, int64_t dim);
+/* Bytes of scratch the backward needs for its deterministic cross-CTA reductions. */
+int64_t swx_scan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim);
+
+/* Forward selective scan:
+ *   delta_eff = softplus(delta + delta_bias) | delta + delta_bias | delta
+ *   h_t = exp(delta_eff_t * A) * h_{t-1} + delta_eff_t * u_t * B_t     (h_{-1} = h0 or 0)
+ *   y_t = <C_t, h_t> + Dskip * u_t ;  out_t = y_t * silu(z_t)  (or y_t without z)
+ * Replaces selective_scan_fast / selective_scan_ref forward
+ * (models/selective_scan.py:34-60, :112-125, :246-265) and TritonScanFn.forward
+ * (models/triton_scan.py:118-135); the gate and softplus fold in the block glue of
+ * models/sift_block.py:108,134. */
+int swx_scan_fwd(const swx_scan_args* args, void* stream);
+
+/* Backward of swx_scan_fwd; needs the checkpoints the forward wrote with the same
+ * inputs.  Replaces _SelectiveScanFn.backward / _FusedScanFn.backward
+ * (models/selective_scan.py:127-167, :209-243) and TritonScanFn.backward
+ * (models/triton_scan.py:137-155).  Reductions (dA, dB, dC, dD, ddelta_bias) are
+ * deterministic: fixed-order sums, no float atomics. */
+int swx_scan_bwd(const swx_scan_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWIFTX_B200_H */

@@ -1,0 +1,93 @@
+"""ctypes binding of the C ABI declared in include/swiftx_b200.h.
+
+The shared library is built in-tree (swiftx_b200/libswiftx_b200.so).  Loading
+fails loudly if it is missing: there is no CPU or eager fallback behind it.
+"""
+import ctypes
+import os
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libswiftx_b200.so")
+
+SWX_OK = 0
+SWX_ERR_INVALID_ARG = 1
+SWX_ERR_UNSUPPORTED = 2
+SWX_ERR_CUDA = 3
+SWX_ERR_TIMEOUT = 4
+
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
+
+i64 = ctypes.c_int64
+i32 = ctypes.c_int32
+vp = ctypes.c_void_p
+
+
+class ScanArgs(ctypes.Structure):
+    """Mirror of ``swx_scan_args``."""
+    _fields_ = [
+        ("batch", i64), ("seqlen", i64), ("dim", i64), ("dstate", i64),
+        ("in_dtype", i32), ("out_dtype", i32), ("delta_softplus", i32), ("reserved", i32),
+        ("u", vp), ("u_sb", i64), ("u_sl", i64),
+        ("delta", vp), ("delta_sb", i64), ("delta_sl", i64),
+        ("z", vp), ("z_sb", i64), ("z_sl", i64),
+        ("B", vp), ("B_sb", i64), ("B_sl", i64),
+        ("C", vp), ("C_sb", i64), ("C_sl", i64),
+        ("A", vp), ("Dskip", vp), ("delta_bias", vp), ("h0", vp),
+        ("out", vp), ("h_last", vp), ("checkpoints", vp),
+        ("dout", vp), ("dout_sb", i64), ("dout_sl", i64),
+        ("du", vp), ("ddelta", vp), ("dz", vp), ("dB", vp), ("dC", vp),
+        ("dA", vp), ("dD", vp), ("ddelta_bias", vp), ("dh0", vp),
+        ("workspace", vp), ("workspace_bytes", i64),
+    ]
+
+
+_lib = None
+
+
+def load():
+    """Load the kernel library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"swiftx_b200 kernel library not found at {LIB_PATH}; build it with "
+            "`python -m swiftx_b200.build` (nvcc, sm_100a)")
+    lib = ctypes.CDLL(LIB_PATH)
+    lib.swx_abi_version.restype = ctypes.c_int
+    lib.swx_status_string.restype = ctypes.c_char_p
+    lib.swx_status_string.argtypes = [ctypes.c_int]
+    lib.swx_scan_args_size.restype = i64
+    if lib.swx_scan_args_size() != ctypes.sizeof(ScanArgs):
+        raise RuntimeError("swx_scan_args layout mismatch between the library and its binding")
+    lib.swx_scan_checkpoint_floats.restype = i64
+    lib.swx_scan_checkpoint_floats.argtypes = [i64, i64, i64]
+    lib.swx_scan_bwd_workspace_bytes.restype = i64
+    lib.swx_scan_bwd_workspace_bytes.argtypes = [i64, i64, i64]
+    for name in ("swx_scan_fwd", "swx_scan_bwd"):
+        fn = getattr(lib, name)
+        fn.restype = ctypes.c_int
+        fn.argtypes = [ctypes.POINTER(ScanArgs), vp]
+    _lib = lib
+    return lib
+
+
+def check(status, what):
+    """Turn a nonzero status into an exception, in the reference's RuntimeError style
+    (models/triton_scan.py:160-161); argument errors become ValueError."""
+    if status == SWX_OK:
+        return
+    msg = load().swx_status_string(status).decode()
+    if status in (SWX_ERR_INVALID_ARG, SWX_ERR_UNSUPPORTED):
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg} (status {status})")
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)

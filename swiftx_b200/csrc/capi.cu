@@ -1,0 +1,139 @@
+// extern "C" entry points: argument checks, parameter packing, launches.
+#include <algorithm>
+#include <cstdint>
+
+#include "common.cuh"
+#include "scan_params.cuh"
+
+namespace swx {
+cudaError_t launch_scan_fwd(const ScanDev& p, int in_dtype, int out_dtype, bool has_z, cudaStream_t st);
+cudaError_t launch_scan_bwd(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st);
+}  // namespace swx
+
+namespace {
+
+int elem_size(int dt) { return dt == SWX_DTYPE_F32 ? 4 : (dt == SWX_DTYPE_BF16 ? 2 : 0); }
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 16-byte cp.async is legal for every row start of a (b, L, W) tile.
+bool vec_ok(const void* p, int64_t sb, int64_t sl, int es) {
+    return p && aligned16(p) && ((sb * es) % 16 == 0) && ((sl * es) % 16 == 0);
+}
+
+constexpr int64_t kAlign = 256;
+int64_t round_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+
+struct WsLayout {
+    int64_t bc, a, d, bias, total;
+};
+
+WsLayout ws_layout(int64_t b, int64_t L, int64_t D) {
+    const int64_t nblk = (D + 31) / 32;
+    WsLayout w;
+    w.bc = 0;
+    w.a = w.bc + round_up(nblk * b * L * 2 * swx::NS * 4);
+    w.d = w.a + round_up(b * D * swx::NS * 4);
+    w.bias = w.d + round_up(b * D * 4);
+    w.total = w.bias + round_up(b * D * 4);
+    return w;
+}
+
+int check_common(const swx_scan_args* a) {
+    if (!a) return SWX_ERR_INVALID_ARG;
+    if (a->batch < 0 || a->seqlen < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
+    if (a->dstate < 1 || a->dstate > swx::NS) return SWX_ERR_UNSUPPORTED;
+    if (a->batch > INT32_MAX || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
+    if (elem_size(a->in_dtype) == 0) return SWX_ERR_UNSUPPORTED;
+    if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
+    if (!a->u || !a->delta || !a->B || !a->C || !a->A) return SWX_ERR_INVALID_ARG;
+    return SWX_OK;
+}
+
+swx::ScanDev pack(const swx_scan_args* a) {
+    swx::ScanDev p{};
+    const int es = elem_size(a->in_dtype);
+    p.b = (int)a->batch; p.L = (int)a->seqlen; p.D = (int)a->dim; p.N = (int)a->dstate;
+    p.nck = (int)((a->seqlen + swx::TCK - 1) / swx::TCK);
+    p.softplus = a->delta_softplus ? 1 : 0;
+    p.u = a->u; p.u_sb = a->u_sb; p.u_sl = a->u_sl;
+    p.dl = a->delta; p.dl_sb = a->delta_sb; p.dl_sl = a->delta_sl;
+    p.z = a->z; p.z_sb = a->z_sb; p.z_sl = a->z_sl;
+    p.B = a->B; p.B_sb = a->B_sb; p.B_sl = a->B_sl;
+    p.C = a->C; p.C_sb = a->C_sb; p.C_sl = a->C_sl;
+    p.A = a->A; p.Dskip = a->Dskip; p.dbias = a->delta_bias; p.h0 = a->h0;
+    p.vec_u = vec_ok(a->u, a->u_sb, a->u_sl, es);
+    p.vec_dl = vec_ok(a->delta, a->delta_sb, a->delta_sl, es);
+    p.vec_z = vec_ok(a->z, a->z_sb, a->z_sl, es);
+    p.vec_B = vec_ok(a->B, a->B_sb, a->B_sl, es);
+    p.vec_C = vec_ok(a->C, a->C_sb, a->C_sl, es);
+    p.vec_dout = vec_ok(a->dout, a->dout_sb, a->dout_sl, es);
+    p.out = a->out; p.h_last = a->h_last; p.ck = a->checkpoints;
+    p.dout = a->dout; p.dout_sb = a->dout_sb; p.dout_sl = a->dout_sl;
+    p.du = a->du; p.ddl = a->ddelta; p.dz = a->dz; p.dB = a->dB; p.dC = a->dC;
+    p.dA = a->dA; p.dD = a->dD; p.ddbias = a->ddelta_bias; p.dh0 = a->dh0;
+    p.nblk = (int)((a->dim + 31) / 32);
+    return p;
+}
+
+int from_cuda(cudaError_t e) { return e == cudaSuccess ? SWX_OK : SWX_ERR_CUDA; }
+
+}  // namespace
+
+extern "C" {
+
+int swx_abi_version(void) { return SWX_ABI_VERSION; }
+
+int64_t swx_scan_args_size(void) { return (int64_t)sizeof(swx_scan_args); }
+
+const char* swx_status_string(int status) {
+    switch (status) {
+        case SWX_OK: return "ok";
+        case SWX_ERR_INVALID_ARG: return "invalid argument (shape, stride, size or missing pointer)";
+        case SWX_ERR_UNSUPPORTED: return "unsupported dtype or layout";
+        case SWX_ERR_CUDA: return "CUDA launch or runtime error";
+        case SWX_ERR_TIMEOUT: return "a bounded device-side wait timed out";
+        default: return "unknown status";
+    }
+}
+
+int64_t swx_scan_checkpoint_floats(int64_t batch, int64_t seqlen, int64_t dim) {
+    return batch * ((seqlen + swx::TCK - 1) / swx::TCK) * dim * swx::NS;
+}
+
+int64_t swx_scan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim) {
+    return ws_layout(batch, seqlen, dim).total;
+}
+
+int swx_scan_fwd(const swx_scan_args* a, void* stream) {
+    int s = check_common(a);
+    if (s != SWX_OK) return s;
+    if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
+    if (elem_size(a->out_dtype) == 0) return SWX_ERR_UNSUPPORTED;
+    if (!a->out) return SWX_ERR_INVALID_ARG;
+    if (a->checkpoints && !aligned16(a->checkpoints)) return SWX_ERR_INVALID_ARG;
+    swx::ScanDev p = pack(a);
+    return from_cuda(swx::launch_scan_fwd(p, a->in_dtype, a->out_dtype, a->z != nullptr,
+                                          static_cast<cudaStream_t>(stream)));
+}
+
+int swx_scan_bwd(const swx_scan_args* a, void* stream) {
+    int s = check_common(a);
+    if (s != SWX_OK) return s;
+    if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
+    if (!a->dout || !a->du || !a->ddelta || !a->dB || !a->dC || !a->dA || !a->checkpoints)
+        return SWX_ERR_INVALID_ARG;
+    if (a->z && !a->dz) return SWX_ERR_INVALID_ARG;
+    if (!aligned16(a->checkpoints) || !a->workspace || !aligned16(a->workspace)) return SWX_ERR_INVALID_ARG;
+    const WsLayout w = ws_layout(a->batch, a->seqlen, a->dim);
+    if (a->workspace_bytes < w.total) return SWX_ERR_INVALID_ARG;
+    swx::ScanDev p = pack(a);
+    char* ws = static_cast<char*>(a->workspace);
+    p.ws_bc = reinterpret_cast<float*>(ws + w.bc);
+    p.ws_a = reinterpret_cast<float*>(ws + w.a);
+    p.ws_d = reinterpret_cast<float*>(ws + w.d);
+    p.ws_bias = reinterpret_cast<float*>(ws + w.bias);
+    return from_cuda(swx::launch_scan_bwd(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
+}
+
+}  // extern "C"

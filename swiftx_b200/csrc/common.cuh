@@ -1,0 +1,108 @@
+// Shared device helpers for the sm_100a selective-scan kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "swiftx_b200.h"
+
+namespace swx {
+
+constexpr int NS = 16;        // padded state count (N <= 16)
+constexpr int TCK = 16;       // checkpoint interval of the forward / chunk of the backward
+constexpr float LOG2E = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- element types
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+    static __device__ __forceinline__ float to_f(float v) { return v; }
+    static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Elem<__nv_bfloat16> {
+    static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+    static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// ---------------------------------------------------------------- math
+// 2^x on the MUFU unit (PTX ex2.approx, flush-to-zero).
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float lg2(float x) {
+    float y;
+    asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// softplus with torch's threshold (beta=1, threshold=20).  For e = exp(x) < 1/8,
+// log1p(e) is its alternating Taylor series to e^8 (relative truncation error
+// below e^8/9 / e < 6e-8), because lg2.approx has an absolute error near 1 that
+// would be a large relative error of a small result; otherwise log2(1+e)*ln2.
+__device__ __forceinline__ float softplus_f(float x) {
+    float e = ex2(x * LOG2E);
+    float p = -0.125f;
+    p = fmaf(p, e, 0.14285715f);
+    p = fmaf(p, e, -0.16666667f);
+    p = fmaf(p, e, 0.2f);
+    p = fmaf(p, e, -0.25f);
+    p = fmaf(p, e, 0.33333334f);
+    p = fmaf(p, e, -0.5f);
+    p = fmaf(p, e, 1.f);
+    float series = p * e;
+    float logv = lg2(1.f + e) * 0.69314718055994531f;
+    float r = e < 0.125f ? series : logv;
+    return x > 20.f ? x : r;
+}
+__device__ __forceinline__ float sigmoid_f(float x) { return rcp(1.f + ex2(-x * LOG2E)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
+
+// ---------------------------------------------------------------- async copies
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+// 16-byte cp.async; bytes < 16 zero-fills the tail (bytes = 0 zero-fills all 16).
+__device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc, int bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n"
+                 :: "r"(smem_u32(sdst)), "l"(gsrc), "r"(bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N)); }
+
+// Copy a [rows x W] tile (row r at g + r*row_stride, columns [0, w_valid)) into
+// dense shared memory s[rows][W], zero-filling invalid rows and columns.
+// vec: every row start is 16-byte aligned, so 16-byte cp.async is used;
+// otherwise scalar loads (for odd shapes and strides).
+template <typename T, int W>
+__device__ __forceinline__ void stage_tile(T* s, const T* g, int64_t row_stride, int rows,
+                                           int rows_valid, int w_valid, bool vec, int tid,
+                                           int nthreads) {
+    if (vec) {
+        constexpr int EPS = 16 / sizeof(T);          // elements per 16-byte segment
+        constexpr int SEGS = W / EPS;
+        for (int i = tid; i < rows * SEGS; i += nthreads) {
+            int r = i / SEGS, sg = i % SEGS;
+            int c0 = sg * EPS;
+            int valid = (r < rows_valid) ? min(EPS, max(0, w_valid - c0)) : 0;
+            const T* src = valid > 0 ? g + (int64_t)r * row_stride + c0 : g;
+            cp_async16(s + r * W + c0, src, valid * (int)sizeof(T));
+        }
+    } else {
+        for (int i = tid; i < rows * W; i += nthreads) {
+            int r = i / W, c = i % W;
+            T v = T(0.f);
+            if (r < rows_valid && c < w_valid) v = g[(int64_t)r * row_stride + c];
+            s[i] = v;
+        }
+    }
+}
+
+}  // namespace swx

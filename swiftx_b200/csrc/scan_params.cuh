@@ -1,0 +1,39 @@
+// Device-side parameter block shared by the scan kernels and their launchers.
+#pragma once
+
+#include <stdint.h>
+
+namespace swx {
+
+struct ScanDev {
+    int b, L, D, N;
+    int nck;                 // number of 16-step checkpoint slabs = ceil(L / 16)
+    int softplus;
+    // inputs (element strides; channel / state stride is 1)
+    const void* u;  int64_t u_sb, u_sl;
+    const void* dl; int64_t dl_sb, dl_sl;
+    const void* z;  int64_t z_sb, z_sl;
+    const void* B;  int64_t B_sb, B_sl;
+    const void* C;  int64_t C_sb, C_sl;
+    const float* A;
+    const float* Dskip;
+    const float* dbias;
+    const float* h0;
+    // 16-byte cp.async is legal for these tiles
+    bool vec_u, vec_dl, vec_z, vec_B, vec_C, vec_dout;
+    // forward outputs
+    void* out;
+    float* h_last;
+    float* ck;               // (b, nck, D, 16)
+    // backward
+    const void* dout; int64_t dout_sb, dout_sl;
+    void* du; void* ddl; void* dz; void* dB; void* dC;
+    float* dA; float* dD; float* ddbias; float* dh0;
+    float* ws_bc;            // (nblk, b, L, 2, 16) per-CTA dB/dC partials
+    float* ws_a;             // (b, D, 16)
+    float* ws_d;             // (b, D)
+    float* ws_bias;          // (b, D)
+    int nblk;                // CTAs along D
+};
+
+}  // namespace swx

@@ -1,0 +1,189 @@
+"""Selective scan on B200: the reference's Python entry points over the CUDA kernels.
+
+Mirrors models/selective_scan.py of the reference:
+
+* ``selective_scan_fast(u, delta, A, B, C, D=None, mode="auto", chunk=16)``
+  (models/selective_scan.py:246-265) -- every mode runs the sm_100a kernel;
+* ``selective_scan_ref(u, delta, A, B, C, D=None)`` (:34-60) -- same kernel;
+* ``selective_scan_fn(...)`` -- the extended entry point with the SiLU(z) gate and
+  softplus(delta + delta_bias) folded in (the block glue of models/sift_block.py:108,134).
+
+Shapes: u, delta, z (b, L, D); A (D, N); B, C (b, L, N); D, delta_bias (D,).
+Autograd follows the reference's custom Functions: the forward saves only its inputs
+plus state checkpoints every 16 steps, the backward recomputes
+(models/selective_scan.py:124, models/triton_scan.py:133), and gradients come back
+in the input dtype with dA / dD in fp32 (models/triton_scan.py:153-155).
+
+There is no CPU path: CPU tensors raise.  The kernel library must be built.
+"""
+import torch
+
+from . import _lib
+
+_FLOAT_IN = (torch.float32, torch.bfloat16)
+
+
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("swiftx_b200 selective scan runs on CUDA tensors only "
+                               "(no CPU path); move the inputs to the GPU")
+
+
+def _rows(t):
+    """(b, L, W) tensor with unit innermost stride (copies only if that is not so)."""
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _in_dtype(*ts):
+    dt = ts[0].dtype
+    return dt if dt in _FLOAT_IN else torch.float32
+
+
+def _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, softplus, in_dt):
+    b, L, Dm = u.shape
+    a.batch, a.seqlen, a.dim, a.dstate = b, L, Dm, A.shape[1]
+    a.in_dtype = _lib.DTYPE_CODES[in_dt]
+    a.delta_softplus = 1 if softplus else 0
+    a.u, a.u_sb, a.u_sl = u.data_ptr(), u.stride(0), u.stride(1)
+    a.delta, a.delta_sb, a.delta_sl = delta.data_ptr(), delta.stride(0), delta.stride(1)
+    if z is not None:
+        a.z, a.z_sb, a.z_sl = z.data_ptr(), z.stride(0), z.stride(1)
+    a.B, a.B_sb, a.B_sl = B.data_ptr(), B.stride(0), B.stride(1)
+    a.C, a.C_sb, a.C_sl = C.data_ptr(), C.stride(0), C.stride(1)
+    a.A = A.data_ptr()
+    a.Dskip = D.data_ptr() if D is not None else None
+    a.delta_bias = delta_bias.data_ptr() if delta_bias is not None else None
+    a.h0 = h0.data_ptr() if h0 is not None else None
+
+
+def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
+    _require_cuda(u, delta, A, B, C, D, z, delta_bias, h0)
+    in_dt = _in_dtype(u)
+    cast = lambda t: None if t is None else _rows(t.to(in_dt))  # noqa: E731
+    u, delta, B, C, z = cast(u), cast(delta), cast(B), cast(C), cast(z)
+    f32 = lambda t: None if t is None else t.detach().float().contiguous()  # noqa: E731
+    A, D, delta_bias, h0 = f32(A), f32(D), f32(delta_bias), f32(h0)
+    if u.dim() != 3 or delta.shape != u.shape or B.dim() != 3 or C.shape != B.shape:
+        raise ValueError("expected u, delta (b, L, D) and B, C (b, L, N)")
+    b, L, Dm = u.shape
+    N = A.shape[1]
+    if A.shape != (Dm, N) or B.shape != (b, L, N) or (z is not None and z.shape != u.shape):
+        raise ValueError(f"shape mismatch: u {tuple(u.shape)}, A {tuple(A.shape)}, B {tuple(B.shape)}")
+    if N > 16:
+        raise ValueError(f"d_state {N} > 16 is not supported")
+    return u, delta, A, B, C, D, z, delta_bias, h0, in_dt
+
+
+def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                 h0=None, out_dtype=None, checkpoints=False, return_last_state=False):
+    """One kernel launch of the forward scan (no autograd).
+
+    Returns (out, checkpoints or None, last_state or None)."""
+    lib = _lib.load()
+    u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
+    b, L, Dm = u.shape
+    N = A.shape[1]
+    out_dt = out_dtype or in_dt
+    out = torch.empty((b, L, Dm), device=u.device, dtype=out_dt)
+    ck = (torch.empty(lib.swx_scan_checkpoint_floats(b, L, Dm), device=u.device, dtype=torch.float32)
+          if checkpoints else None)
+    hl = torch.empty((b, Dm, N), device=u.device, dtype=torch.float32) if return_last_state else None
+    a = _lib.ScanArgs()
+    _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt)
+    a.out_dtype = _lib.DTYPE_CODES[out_dt]
+    a.out = out.data_ptr()
+    a.h_last = hl.data_ptr() if hl is not None else None
+    a.checkpoints = ck.data_ptr() if ck is not None else None
+    _lib.check(lib.swx_scan_fwd(a, _lib.stream_ptr(u.device)), "swx_scan_fwd")
+    return out, ck, hl
+
+
+def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, dout):
+    """One call of the backward kernels (no autograd).  Returns a dict of gradients."""
+    lib = _lib.load()
+    u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
+    b, L, Dm = u.shape
+    N = A.shape[1]
+    dout = _rows(dout.to(in_dt))
+    dev = u.device
+    e = lambda *s, dt=in_dt: torch.empty(s, device=dev, dtype=dt)  # noqa: E731
+    g = {"du": e(b, L, Dm), "ddelta": e(b, L, Dm), "dB": e(b, L, N), "dC": e(b, L, N),
+         "dA": e(Dm, N, dt=torch.float32)}
+    g["dz"] = e(b, L, Dm) if z is not None else None
+    g["dD"] = e(Dm, dt=torch.float32) if D is not None else None
+    g["ddelta_bias"] = e(Dm, dt=torch.float32) if delta_bias is not None else None
+    g["dh0"] = e(b, Dm, N, dt=torch.float32) if h0 is not None else None
+    wsb = lib.swx_scan_bwd_workspace_bytes(b, L, Dm)
+    ws = torch.empty(max(wsb, 1), device=dev, dtype=torch.uint8)
+    a = _lib.ScanArgs()
+    _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt)
+    a.out_dtype = a.in_dtype
+    a.checkpoints = ck.data_ptr()
+    a.dout, a.dout_sb, a.dout_sl = dout.data_ptr(), dout.stride(0), dout.stride(1)
+    for k in ("du", "ddelta", "dz", "dB", "dC", "dA", "dD", "ddelta_bias", "dh0"):
+        setattr(a, k, g[k].data_ptr() if g[k] is not None else None)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
+    _lib.check(lib.swx_scan_bwd(a, _lib.stream_ptr(dev)), "swx_scan_bwd")
+    return g
+
+
+class SelectiveScanFn(torch.autograd.Function):
+    """Custom autograd Function over the fused kernels (same save/recompute trade as
+    _FusedScanFn / TritonScanFn in the reference)."""
+
+    @staticmethod
+    def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, out_dtype,
+                return_last_state):
+        need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9))
+        out, ck, hl = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0,
+                                   out_dtype, checkpoints=need_grad,
+                                   return_last_state=return_last_state)
+        ctx.delta_softplus = delta_softplus
+        ctx.dtypes = [t.dtype if t is not None else None for t in (u, delta, A, B, C, D, z, delta_bias, h0)]
+        if need_grad:
+            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, h0, ck)
+        if return_last_state:
+            ctx.mark_non_differentiable(hl)
+            return out, hl
+        return out
+
+    @staticmethod
+    def backward(ctx, dout, *unused):
+        u, delta, A, B, C, D, z, delta_bias, h0, ck = ctx.saved_tensors
+        g = scan_backward(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, h0, ck, dout)
+        dts = ctx.dtypes
+        cast = lambda t, dt: None if t is None or dt is None else t.to(dt)  # noqa: E731
+        return (cast(g["du"], dts[0]), cast(g["ddelta"], dts[1]), cast(g["dA"], dts[2]),
+                cast(g["dB"], dts[3]), cast(g["dC"], dts[4]), cast(g["dD"], dts[5]),
+                cast(g["dz"], dts[6]), cast(g["ddelta_bias"], dts[7]), None,
+                cast(g["dh0"], dts[8]), None, None)
+
+
+def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
+                      h0=None, out_dtype=None, return_last_state=False):
+    """Fused selective scan with optional SiLU(z) gate and softplus(delta + delta_bias).
+
+    out = (scan(u, delta_eff, A, B, C) + D*u) * silu(z),  delta_eff = softplus(delta + delta_bias).
+    Returns out (and the final state (b, D, N) when return_last_state)."""
+    return SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, bool(delta_softplus), h0,
+                                 out_dtype, bool(return_last_state))
+
+
+_MODES = ("auto", "parallel", "sequential", "fused", "triton")
+
+
+def selective_scan_fast(u, delta, A, B, C, D=None, mode="auto", chunk=16):
+    """Drop-in for the reference dispatcher (models/selective_scan.py:246-265).
+
+    Every mode computes the same function; on B200 they all run the fused sm_100a
+    kernel (the checkpoint interval is fixed at 16 steps, so ``chunk`` has no effect)."""
+    if mode not in _MODES:
+        raise ValueError(f"unknown mode {mode!r}; expected one of {_MODES}")
+    return selective_scan_fn(u, delta, A, B, C, D)
+
+
+def selective_scan_ref(u, delta, A, B, C, D=None):
+    """Reference-named entry (models/selective_scan.py:34): the exact sequential
+    recurrence, computed by the same CUDA kernel."""
+    return selective_scan_fn(u, delta, A, B, C, D)

@@ -1,0 +1,225 @@
+"""Parity of the sm_100a selective-scan kernels with the CPU oracle (float64).
+
+Every case calls the kernels through the C ABI (swiftx_b200/_lib -> libswiftx_b200.so)
+and compares with oracle.scan_fwd / oracle.scan_bwd on the same seeded inputs.
+
+Tolerances: fp32 outputs rtol 1e-4 / atol 1e-5 (the reference's fast-vs-ref pin,
+tests/test_selective_scan.py:74).  Gradients that are sums over many terms (dA, dD,
+d delta_bias over b*L terms; dB, dC over D channels) are compared with atol scaled
+by the magnitude of what was summed (sum of |terms|, computed by the oracle on
+|inputs|) times 1e-5, the fp32 re-association error of such sums.  bf16 inputs with
+fp32 state: rtol 2e-2 against the oracle run on the same bf16-rounded values.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from swiftx_b200 import selective_scan_fast, selective_scan_fn, selective_scan_ref
+from swiftx_b200.selective_scan import scan_backward, scan_forward
+from swiftx_b200.triton_scan import selective_scan_triton
+from swiftx_b200.workloads import config_inputs, reference_test_inputs
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def np64(t):
+    return None if t is None else t.detach().float().cpu().double().numpy()
+
+
+def assert_close(got, want, rtol, atol, name=""):
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    err = np.abs(got - want)
+    bad = err > atol + rtol * np.abs(want)
+    if bad.any():
+        i = np.unravel_index(np.argmax(err - rtol * np.abs(want)), err.shape)
+        raise AssertionError(f"{name}: {bad.sum()}/{bad.size} out of tolerance; worst at {i}: "
+                             f"got {got[i]:.8g} want {want[i]:.8g} (max abs err {err.max():.3g})")
+
+
+def oracle_case(inp, gate=True, softplus=True, with_D=True, h0=None):
+    kw = dict(D=np64(inp["D"]) if with_D else None, z=np64(inp["z"]) if gate else None,
+              delta_bias=np64(inp["delta_bias"]) if softplus else None, delta_softplus=softplus,
+              h0=np64(h0))
+    args = [np64(inp[k]) for k in ("u", "delta", "A", "B", "C")]
+    out, hl = oracle.scan_fwd(*args, return_last_state=True, **kw)
+    grads = oracle.scan_bwd(*args, np64(inp["dout"]), **kw)
+    # magnitude scale of each reduction: the same sums over |terms|
+    absargs = [np.abs(a) for a in args]
+    absargs[2] = -absargs[2]                       # keep A negative (a decay)
+    kwa = dict(kw)
+    for k in ("D", "z"):
+        if kwa[k] is not None:
+            kwa[k] = np.abs(kwa[k])
+    scale = oracle.scan_bwd(*absargs, np.abs(np64(inp["dout"])), **kwa)
+    return out, hl, grads, scale
+
+
+def check_grads(g, want, scale, rtol=1e-4, atol=1e-5):
+    for k, v in want.items():
+        if k in ("dA", "dD", "ddelta_bias", "dB", "dC"):
+            tol = atol + 1e-5 * np.abs(scale[k])
+        else:
+            tol = atol
+        assert_close(np64(g[k]), v, rtol, tol, k)
+
+
+# ----------------------------------------------------------------- golden fixtures
+def test_golden_hand_tiny(golden):
+    g = golden("hand_tiny")
+    t = {k: torch.tensor(v, device=DEV, dtype=torch.float32) for k, v in g.items()}
+    y = selective_scan_ref(t["u"], t["delta"], t["A"], t["B"], t["C"])
+    assert_close(np64(y).ravel(), [2.0, 5.0, 8.5], 0, 1e-6, "y")
+
+
+@pytest.mark.parametrize("L", [1, 7, 64])
+def test_golden_forward(golden, L):
+    g = golden(f"fwd_L{L}")
+    t = {k: torch.tensor(v, device=DEV, dtype=torch.float32) for k, v in g.items()}
+    for mode in ("auto", "parallel", "sequential", "fused", "triton"):
+        y = selective_scan_fast(t["u"], t["delta"], t["A"], t["B"], t["C"], t["D"], mode=mode)
+        assert_close(np64(y), g["y"], 1e-4, 1e-5, f"y[{mode}]")
+
+
+@pytest.mark.parametrize("name", ["tail_2x37x40x16", "tail_1x20x8x5"])
+def test_golden_tail_shapes_fwd_bwd(golden, name):
+    g = golden(name)
+    keys = ["u", "delta", "A", "B", "C"] + (["D"] if "D" in g else [])
+    ins = [torch.tensor(g[k], device=DEV, dtype=torch.float32, requires_grad=True) for k in keys]
+    y = selective_scan_triton(*ins, chunk=8)
+    assert_close(np64(y), g["y"], 1e-4, 1e-4, "y")
+    grads = torch.autograd.grad(y, ins, torch.tensor(g["gy"], device=DEV))
+    for k, gr in zip(["du", "ddelta", "dA", "dB", "dC", "dD"], grads):
+        # the reference's own Triton pin uses 2e-3 for grads (tests/test_triton_scan.py:30)
+        assert_close(np64(gr), g[k], 1e-4, 1e-4, k)
+
+
+def test_golden_gated_softplus(golden):
+    g = golden("gated")
+    keys = ["u", "delta_raw", "A", "B", "C", "D", "z", "delta_bias"]
+    t = {k: torch.tensor(g[k], device=DEV, dtype=torch.float32, requires_grad=True) for k in keys}
+    out = selective_scan_fn(t["u"], t["delta_raw"], t["A"], t["B"], t["C"], t["D"], z=t["z"],
+                            delta_bias=t["delta_bias"], delta_softplus=True)
+    assert_close(np64(out), g["out"], 1e-4, 1e-5, "out")
+    grads = torch.autograd.grad(out, [t[k] for k in keys], torch.tensor(g["gout"], device=DEV))
+    names = ["du", "ddelta", "dA", "dB", "dC", "dD", "dz", "ddelta_bias"]
+    for k, gr in zip(names, grads):
+        assert_close(np64(gr), g[k], 1e-4, 1e-4, k)
+
+
+def test_golden_config0(golden):
+    g = golden("config0")
+    t = {k: torch.tensor(v, device=DEV, dtype=torch.float32) for k, v in g.items()}
+    y = selective_scan_fn(t["u"], t["delta_raw"], t["A"], t["B"], t["C"], t["D"],
+                          delta_bias=t["delta_bias"], delta_softplus=True)
+    assert_close(np64(y), g["y"], 1e-4, 1e-5, "y")
+
+
+# ----------------------------------------------------------------- oracle parity
+CASES = [
+    # b, L, D, N, gate, softplus, with_D
+    (2, 256, 128, 16, True, True, True),
+    (1, 100, 40, 16, True, True, True),       # L not a multiple of 16/64, D not of 32
+    (3, 33, 64, 5, False, False, True),       # N < 16, no gate, plain delta
+    (2, 17, 24, 16, True, False, False),      # no D skip
+    (1, 1, 32, 16, True, True, True),         # single step
+    (2, 300, 96, 8, False, True, True),
+]
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_fwd_bwd_vs_oracle(case):
+    b, L, D, N, gate, sp, wD = case
+    inp = config_inputs(b, L, D, N, seed=b * 1000 + L, gate=gate, device=DEV)
+    if not sp:   # plain delta: pass the positive softplus(delta_raw + bias) as the block does
+        inp["delta"] = torch.nn.functional.softplus(inp["delta"] + inp["delta_bias"])
+    out_o, hl_o, gr_o, scale = oracle_case(inp, gate, sp, wD)
+    out, ck, hl = scan_forward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"],
+                               inp["D"] if wD else None, inp["z"] if gate else None,
+                               inp["delta_bias"] if sp else None, sp, checkpoints=True,
+                               return_last_state=True)
+    assert_close(np64(out), out_o, 1e-4, 1e-5, "out")
+    assert_close(np64(hl), hl_o, 1e-4, 1e-5, "h_last")
+    g = scan_backward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"] if wD else None,
+                      inp["z"] if gate else None, inp["delta_bias"] if sp else None, sp, None, ck,
+                      inp["dout"])
+    check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
+
+
+def test_initial_state_and_grad():
+    b, L, D, N = 2, 50, 32, 16
+    inp = config_inputs(b, L, D, N, seed=11, device=DEV)
+    h0 = torch.randn(b, D, N, generator=torch.Generator().manual_seed(12)).to(DEV) * 0.3
+    out_o, hl_o, gr_o, scale = oracle_case(inp, True, True, True, h0=h0)
+    args = {k: inp[k].clone().requires_grad_() for k in ("u", "delta", "A", "B", "C", "D", "z", "delta_bias")}
+    h0r = h0.clone().requires_grad_()
+    out, hl = selective_scan_fn(args["u"], args["delta"], args["A"], args["B"], args["C"], args["D"],
+                                z=args["z"], delta_bias=args["delta_bias"], delta_softplus=True,
+                                h0=h0r, return_last_state=True)
+    assert_close(np64(out), out_o, 1e-4, 1e-5, "out")
+    assert_close(np64(hl), hl_o, 1e-4, 1e-5, "h_last")
+    out.backward(inp["dout"])
+    assert h0r.grad is not None and torch.isfinite(h0r.grad).all()
+    oh = oracle.scan_bwd(*[np64(inp[k]) for k in ("u", "delta", "A", "B", "C")], np64(inp["dout"]),
+                         D=np64(inp["D"]), z=np64(inp["z"]), delta_bias=np64(inp["delta_bias"]),
+                         delta_softplus=True, h0=np64(h0))
+    assert_close(np64(h0r.grad), oh["dh0"], 1e-4, 1e-5, "dh0")
+
+
+def test_strided_inputs_match_contiguous():
+    """x and z as the two halves of one (b, L, 2D) in_proj output (models/sift_block.py:115)."""
+    b, L, D, N = 2, 70, 64, 16
+    inp = config_inputs(b, L, D, N, seed=3, device=DEV)
+    xz = torch.cat([inp["u"], inp["z"]], dim=-1)
+    u_v, z_v = xz.chunk(2, dim=-1)
+    assert u_v.stride(1) == 2 * D
+    a = selective_scan_fn(u_v, inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], z=z_v,
+                          delta_bias=inp["delta_bias"], delta_softplus=True)
+    c = selective_scan_fn(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], z=inp["z"],
+                          delta_bias=inp["delta_bias"], delta_softplus=True)
+    assert torch.equal(a, c)
+
+
+def test_deterministic_backward():
+    b, L, D, N = 2, 128, 96, 16
+    inp = config_inputs(b, L, D, N, seed=4, device=DEV)
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+    _, ck, _ = scan_forward(*args, checkpoints=True)
+    g1 = scan_backward(*args, None, ck, inp["dout"])
+    g2 = scan_backward(*args, None, ck, inp["dout"])
+    for k in g1:
+        if g1[k] is not None:
+            assert torch.equal(g1[k], g2[k]), k
+
+
+def test_bf16_inputs_fp32_state():
+    b, L, D, N = 2, 200, 64, 16
+    inp = config_inputs(b, L, D, N, seed=9, device=DEV, dtype=torch.bfloat16)
+    out, _, _ = scan_forward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
+                             inp["delta_bias"], True, out_dtype=torch.float32)
+    assert out.dtype == torch.float32
+    want = oracle.scan_fwd(*[np64(inp[k]) for k in ("u", "delta", "A", "B", "C")], D=np64(inp["D"]),
+                           z=np64(inp["z"]), delta_bias=np64(inp["delta_bias"]), delta_softplus=True)
+    assert_close(np64(out), want, 2e-2, 1e-3, "out")
+
+
+def test_cpu_tensors_raise():
+    u, delta, A, B, C, Ds = reference_test_inputs(2, 6, 3, 4)
+    with pytest.raises(RuntimeError):
+        selective_scan_fast(u, delta, A, B, C, Ds)
+
+
+def test_config1_full_size_vs_oracle():
+    """The benchmark configuration itself (b=8, L=2048, D=512, N=16, gated, softplus)."""
+    inp = config_inputs(8, 2048, 512, 16, seed=0, device=DEV)
+    oracle.set_num_threads(max(1, oracle.num_threads()))
+    out_o, hl_o, gr_o, scale = oracle_case(inp)
+    out, ck, _ = scan_forward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
+                              inp["delta_bias"], True, checkpoints=True)
+    assert_close(np64(out), out_o, 1e-4, 1e-5, "out")
+    g = scan_backward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
+                      inp["delta_bias"], True, None, ck, inp["dout"])
+    check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
