@@ -64,6 +64,24 @@ __device__ __forceinline__ float softplus_f(float x) {
 __device__ __forceinline__ float sigmoid_f(float x) { return rcp(1.f + ex2(-x * LOG2E)); }
 __device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
 
+// ---------------------------------------------------------------- packed fp32 (sm_100 f32x2)
+__device__ __forceinline__ float2 f2(float a, float b) { return make_float2(a, b); }
+__device__ __forceinline__ float2 bc2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 ex2x2(float2 x) { return make_float2(ex2(x.x), ex2(x.y)); }
+
+// ---------------------------------------------------------------- named barriers
+// Producer/consumer hand-off between warp groups: the producer arrives (no wait),
+// the consumer syncs; `n` counts all participating threads of both groups.
+__device__ __forceinline__ void bar_sync(int id, int n) {
+    asm volatile("bar.sync %0, %1;\n" :: "r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void bar_arrive(int id, int n) {
+    asm volatile("bar.arrive %0, %1;\n" :: "r"(id), "r"(n) : "memory");
+}
+
 // ---------------------------------------------------------------- async copies
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -1,55 +1,88 @@
 // Selective scan forward / backward kernels for sm_100a.
 //
-// Work decomposition (both directions): one CTA owns 32 channels of one batch
-// row for the whole sequence; each thread owns one channel and 4 of its 16
-// states, so the N=16 state of a channel lives in the fp32 registers of 4
-// adjacent lanes and a warp covers 8 channels.  Time is walked sequentially
-// (a state chain is a first-order recurrence); the channel-shared B_t / C_t and
-// the per-channel u, delta, z, dout tiles are staged in shared memory by
-// double-buffered 16-byte cp.async, one chunk ahead of the math.
+// Work decomposition (both directions): one CTA owns 32 channels of one batch row
+// for the whole sequence.  A state chain h[d, n] is a first-order recurrence in
+// time, so time is walked sequentially and the parallelism is b * D * N chains.
+// The CTA is warp-specialised:
 //
-// Per staged chunk the CTA runs three phases separated by __syncthreads:
-//   A  per (t, channel) scalars, computed once per channel instead of once per
-//      state: delta_eff = softplus(delta + bias), delta_eff*u, the gate.
-//   B  the recurrence: a = 2^(delta_eff * A*log2e) on the MUFU unit, h = a*h + delta_eff*u*B.
-//   C  per (t, channel) epilogue: sum of the 4 lanes' partial readouts, D-skip,
-//      SiLU(z) gate, coalesced store.
+//   * 4 recurrence warps: thread (channel, state group) owns 4 of the 16 states of
+//     one channel in fp32 registers (4 adjacent lanes hold a channel, a warp covers
+//     8 channels).  Per step: a = 2^(delta_eff * A*log2e) on the MUFU unit, then
+//     h = a*h + delta_eff*u*B with packed f32x2 FMAs.  They read only pre-computed
+//     per-(t, channel) scalars and the channel-shared B_t / C_t from shared memory.
+//   * 4 helper warps: stage raw tiles of u, delta, z, dout, B, C with 16-byte
+//     cp.async into a 4-slot ring (two tiles ahead), compute the per-(t, channel)
+//     scalars once per channel (softplus(delta + bias), delta*u, the gate terms),
+//     and run the epilogues (readout / gradient reductions, coalesced stores).
 //
-// Backward: chunks of 16 steps are walked last to first.  Each chunk restarts
-// from the state checkpoint the forward stored, recomputes the 16 states and
-// decays into registers (one exp per element), then runs the reverse
-// recurrence g_t = a_{t+1} g_{t+1} + dy_t C_t (models/selective_scan.py:146-148,
-// :225-238).  Channel reductions (dB, dC) and state reductions (du, ddelta)
-// go through shared memory in fixed order; cross-CTA and cross-batch sums are
-// written as partials and summed by a second kernel in fixed order, so every
-// gradient is bit-reproducible (no float atomics, unlike
-// models/triton_scan.py:101-102,108-109).
+// The two groups hand tiles over through double-buffered shared memory guarded by
+// named barriers (producer bar.arrive, consumer bar.sync), so the recurrence never
+// waits for the per-channel work of the neighbouring tiles.
+//
+// Backward: 16-step chunks are walked last to first.  Each chunk restarts from the
+// state checkpoint the forward stored, recomputes the 16 states and decays into
+// registers (one exp per element), then runs the reverse recurrence
+// g_t = a_{t+1} g_{t+1} + dy_t C_t (models/selective_scan.py:146-148, :225-238).
+// State sums (du, ddelta, pre-gate y) and channel sums (dB, dC) are reduced through
+// shared memory in fixed order; cross-CTA and cross-batch sums are written as
+// partials and summed by a second kernel in fixed order, so every gradient is
+// bit-reproducible (no float atomics, unlike models/triton_scan.py:101-102,108-109).
 #include "common.cuh"
 #include "scan_params.cuh"
 
 namespace swx {
 
-constexpr int SCH = 32;   // channels per CTA
-constexpr int SNT = 128;  // threads per CTA
-constexpr int FTS = 64;   // staged steps per forward chunk (multiple of TCK)
+constexpr int SCH = 32;               // channels per CTA
+constexpr int NSCAN = 128;            // recurrence threads
+constexpr int NAUX = 128;             // helper threads
+constexpr int NTH = NSCAN + NAUX;
+constexpr int FT = 32;                // forward tile (steps)
+constexpr int HT = TCK / 2;           // backward half tile (steps)
+constexpr int RING = 4;               // raw staging slots
+
+enum : int { BAR_AUX = 1, BAR_D0 = 2, BAR_X0 = 4, BAR_E0 = 6 };
 
 // =============================================================== forward
 template <typename Tin>
 struct FwdSmem {
-    Tin u[2][FTS][SCH];
-    Tin dl[2][FTS][SCH];
-    Tin z[2][FTS][SCH];
-    Tin B[2][FTS][NS];
-    Tin C[2][FTS][NS];
-    float dlt[FTS][SCH];        // delta_eff
-    float dlu[FTS][SCH];        // delta_eff * u
-    float Bf[FTS][NS];
-    float Cf[FTS][NS];
-    float yp[FTS][SCH][4];      // partial readouts of the 4 state groups
+    Tin u[RING][FT][SCH];
+    Tin dl[RING][FT][SCH];
+    Tin z[RING][FT][SCH];
+    Tin B[RING][FT][NS];
+    Tin C[RING][FT][NS];
+    float2 dd[2][FT][SCH];        // (delta_eff, delta_eff * u)
+    float Bf[2][FT][NS];
+    float Cf[2][FT][NS];
+    float yp[2][FT][SCH][4];      // partial readouts of the 4 state groups
 };
 
+template <bool FULL>
+__device__ __forceinline__ void fwd_tile(const float2 (*dd)[SCH], const float (*Bf)[NS],
+                                         const float (*Cf)[NS], float (*yp)[SCH][4], int nt, int ch,
+                                         int j, float2 A01, float2 A23, float2& h01, float2& h23,
+                                         float* ckp, int64_t ck_stride) {
+#pragma unroll
+    for (int t = 0; t < FT; ++t) {
+        if (FULL || t < nt) {
+            if ((t % TCK) == 0 && ckp)
+                *reinterpret_cast<float4*>(ckp + (t / TCK) * ck_stride) = make_float4(h01.x, h01.y, h23.x, h23.y);
+            const float2 d = dd[t][ch];
+            const float4 b = *reinterpret_cast<const float4*>(&Bf[t][4 * j]);
+            const float4 c = *reinterpret_cast<const float4*>(&Cf[t][4 * j]);
+            const float2 dt = bc2(d.x), du = bc2(d.y);
+            const float2 a01 = ex2x2(mul2(dt, A01));
+            const float2 a23 = ex2x2(mul2(dt, A23));
+            h01 = fma2(a01, h01, mul2(du, f2(b.x, b.y)));
+            h23 = fma2(a23, h23, mul2(du, f2(b.z, b.w)));
+            float2 y = mul2(h01, f2(c.x, c.y));
+            y = fma2(h23, f2(c.z, c.w), y);
+            yp[t][ch][j] = y.x + y.y;
+        }
+    }
+}
+
 template <typename Tin, typename Tout, bool HAS_Z>
-__global__ void __launch_bounds__(SNT, 1) scan_fwd_kernel(const ScanDev p) {
+__global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem<Tin>& S = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
 
@@ -57,131 +90,188 @@ __global__ void __launch_bounds__(SNT, 1) scan_fwd_kernel(const ScanDev p) {
     const int bi = blockIdx.y;
     const int d0 = blockIdx.x * SCH;
     const int nd = min(SCH, p.D - d0);
-    // recurrence role
-    const int ch = tid >> 2, j = tid & 3;
-    const int d = d0 + ch;
-    const bool dvalid = ch < nd;
-    // per-(t, channel) role
-    const int ech = tid & (SCH - 1);
-    const bool evalid = ech < nd;
-    const float eD = (p.Dskip && evalid) ? p.Dskip[d0 + ech] : 0.f;
-    const float ebias = (p.dbias && evalid) ? p.dbias[d0 + ech] : 0.f;
+    const int nchunk = (p.L + FT - 1) / FT;
 
-    float A2[4], h[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int n = 4 * j + i;
-        const bool ok = dvalid && n < p.N;
-        A2[i] = ok ? p.A[(int64_t)d * p.N + n] * LOG2E : 0.f;
-        h[i] = (ok && p.h0) ? p.h0[((int64_t)bi * p.D + d) * p.N + n] : 0.f;
-    }
-
-    const Tin* gu = static_cast<const Tin*>(p.u) + bi * p.u_sb + d0;
-    const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + d0;
-    const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + d0 : nullptr;
-    const Tin* gB = static_cast<const Tin*>(p.B) + bi * p.B_sb;
-    const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
-    Tout* gout = static_cast<Tout*>(p.out) + (int64_t)bi * p.L * p.D + d0;
-
-    const int nchunks = (p.L + FTS - 1) / FTS;
-    auto issue = [&](int c) {
-        const int t0 = c * FTS, rv = min(FTS, p.L - t0), buf = c & 1;
-        stage_tile<Tin, SCH>(&S.u[buf][0][0], gu + t0 * p.u_sl, p.u_sl, FTS, rv, nd, p.vec_u, tid, SNT);
-        stage_tile<Tin, SCH>(&S.dl[buf][0][0], gdl + t0 * p.dl_sl, p.dl_sl, FTS, rv, nd, p.vec_dl, tid, SNT);
-        if (HAS_Z)
-            stage_tile<Tin, SCH>(&S.z[buf][0][0], gz + t0 * p.z_sl, p.z_sl, FTS, rv, nd, p.vec_z, tid, SNT);
-        stage_tile<Tin, NS>(&S.B[buf][0][0], gB + t0 * p.B_sl, p.B_sl, FTS, rv, p.N, p.vec_B, tid, SNT);
-        stage_tile<Tin, NS>(&S.C[buf][0][0], gC + t0 * p.C_sl, p.C_sl, FTS, rv, p.N, p.vec_C, tid, SNT);
-        cp_async_commit();
-    };
-
-    issue(0);
-    for (int c = 0; c < nchunks; ++c) {
-        if (c + 1 < nchunks) issue(c + 1); else cp_async_commit();
-        cp_async_wait<1>();
-        __syncthreads();
-        const int buf = c & 1, t0 = c * FTS, nt = min(FTS, p.L - t0);
-
-        // ---- phase A: per (t, channel) scalars
-        for (int i = tid; i < FTS * SCH; i += SNT) {
-            const int t = i / SCH, cc = i % SCH;
-            const float raw = Elem<Tin>::to_f(S.dl[buf][t][cc]) + ebias;
-            const float dte = p.softplus ? softplus_f(raw) : raw;
-            S.dlt[t][cc] = dte;
-            S.dlu[t][cc] = dte * Elem<Tin>::to_f(S.u[buf][t][cc]);
-        }
-        for (int i = tid; i < FTS * NS; i += SNT) {
-            (&S.Bf[0][0])[i] = Elem<Tin>::to_f((&S.B[buf][0][0])[i]);
-            (&S.Cf[0][0])[i] = Elem<Tin>::to_f((&S.C[buf][0][0])[i]);
-        }
-        __syncthreads();
-
-        // ---- phase B: recurrence
-        float* ckp = (p.ck && dvalid) ? p.ck + (((int64_t)bi * p.nck + t0 / TCK) * p.D + d) * NS + 4 * j
-                                      : nullptr;
-        for (int t = 0; t < nt; ++t) {
-            if ((t & (TCK - 1)) == 0 && ckp) {
-                *reinterpret_cast<float4*>(ckp) = make_float4(h[0], h[1], h[2], h[3]);
-                ckp += (int64_t)p.D * NS;
-            }
-            const float dte = S.dlt[t][ch], dtu = S.dlu[t][ch];
-            const float4 b4 = *reinterpret_cast<const float4*>(&S.Bf[t][4 * j]);
-            const float4 c4 = *reinterpret_cast<const float4*>(&S.Cf[t][4 * j]);
-            h[0] = fmaf(ex2(dte * A2[0]), h[0], dtu * b4.x);
-            h[1] = fmaf(ex2(dte * A2[1]), h[1], dtu * b4.y);
-            h[2] = fmaf(ex2(dte * A2[2]), h[2], dtu * b4.z);
-            h[3] = fmaf(ex2(dte * A2[3]), h[3], dtu * b4.w);
-            float y = h[0] * c4.x;
-            y = fmaf(h[1], c4.y, y);
-            y = fmaf(h[2], c4.z, y);
-            y = fmaf(h[3], c4.w, y);
-            S.yp[t][ch][j] = y;
-        }
-        __syncthreads();
-
-        // ---- phase C: readout reduction, D-skip, gate, store
-        if (evalid) {
-            for (int t = tid / SCH; t < nt; t += SNT / SCH) {
-                const float4 q = *reinterpret_cast<const float4*>(&S.yp[t][ech][0]);
-                float y = (q.x + q.y) + (q.z + q.w);
-                y = fmaf(eD, Elem<Tin>::to_f(S.u[buf][t][ech]), y);
-                if (HAS_Z) y *= silu_f(Elem<Tin>::to_f(S.z[buf][t][ech]));
-                gout[(int64_t)(t0 + t) * p.D + ech] = Elem<Tout>::from_f(y);
-            }
-        }
-        __syncthreads();
-    }
-
-    if (p.h_last && dvalid) {
+    if (tid < NSCAN) {
+        // ------------------------------------------------ recurrence warps
+        const int ch = tid >> 2, j = tid & 3;
+        const int d = d0 + ch;
+        const bool dvalid = ch < nd;
+        float av[4], hv[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int n = 4 * j + i;
-            if (n < p.N) p.h_last[((int64_t)bi * p.D + d) * p.N + n] = h[i];
+            const bool ok = dvalid && n < p.N;
+            av[i] = ok ? p.A[(int64_t)d * p.N + n] * LOG2E : 0.f;
+            hv[i] = (ok && p.h0) ? p.h0[((int64_t)bi * p.D + d) * p.N + n] : 0.f;
         }
+        const float2 A01 = f2(av[0], av[1]), A23 = f2(av[2], av[3]);
+        float2 h01 = f2(hv[0], hv[1]), h23 = f2(hv[2], hv[3]);
+        const int64_t ck_stride = (int64_t)p.D * NS;
+        for (int c = 0; c < nchunk; ++c) {
+            const int s = c & 1, t0 = c * FT, nt = min(FT, p.L - t0);
+            bar_sync(BAR_D0 + s, NTH);
+            float* ckp = (p.ck && dvalid)
+                             ? p.ck + (((int64_t)bi * p.nck + t0 / TCK) * p.D + d) * NS + 4 * j
+                             : nullptr;
+            if (nt == FT)
+                fwd_tile<true>(S.dd[s], S.Bf[s], S.Cf[s], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
+            else
+                fwd_tile<false>(S.dd[s], S.Bf[s], S.Cf[s], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
+            bar_arrive(BAR_X0 + s, NTH);
+        }
+        if (p.h_last && dvalid) {
+            hv[0] = h01.x; hv[1] = h01.y; hv[2] = h23.x; hv[3] = h23.y;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int n = 4 * j + i;
+                if (n < p.N) p.h_last[((int64_t)bi * p.D + d) * p.N + n] = hv[i];
+            }
+        }
+    } else {
+        // ------------------------------------------------ helper warps
+        const int at = tid - NSCAN;
+        const int ech = at & (SCH - 1);
+        const bool evalid = ech < nd;
+        const float eD = (p.Dskip && evalid) ? p.Dskip[d0 + ech] : 0.f;
+        const float ebias = (p.dbias && evalid) ? p.dbias[d0 + ech] : 0.f;
+        const Tin* gu = static_cast<const Tin*>(p.u) + bi * p.u_sb + d0;
+        const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + d0;
+        const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + d0 : nullptr;
+        const Tin* gB = static_cast<const Tin*>(p.B) + bi * p.B_sb;
+        const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
+        Tout* gout = static_cast<Tout*>(p.out) + (int64_t)bi * p.L * p.D + d0;
+
+        auto issue = [&](int c) {
+            if (c < nchunk) {
+                const int t0 = c * FT, rv = min(FT, p.L - t0), r = c % RING;
+                stage_tile<Tin, SCH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, FT, rv, nd, p.vec_u, at, NAUX);
+                stage_tile<Tin, SCH>(&S.dl[r][0][0], gdl + t0 * p.dl_sl, p.dl_sl, FT, rv, nd, p.vec_dl, at, NAUX);
+                if (HAS_Z)
+                    stage_tile<Tin, SCH>(&S.z[r][0][0], gz + t0 * p.z_sl, p.z_sl, FT, rv, nd, p.vec_z, at, NAUX);
+                stage_tile<Tin, NS>(&S.B[r][0][0], gB + t0 * p.B_sl, p.B_sl, FT, rv, p.N, p.vec_B, at, NAUX);
+                stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, FT, rv, p.N, p.vec_C, at, NAUX);
+            }
+            cp_async_commit();
+        };
+        auto derive = [&](int c) {
+            const int r = c % RING, s = c & 1;
+#pragma unroll 4
+            for (int i = at; i < FT * SCH; i += NAUX) {
+                const int t = i / SCH;
+                const float raw = Elem<Tin>::to_f(S.dl[r][t][ech]) + ebias;
+                const float dte = p.softplus ? softplus_f(raw) : raw;
+                S.dd[s][t][ech] = f2(dte, dte * Elem<Tin>::to_f(S.u[r][t][ech]));
+            }
+#pragma unroll 4
+            for (int i = at; i < FT * NS; i += NAUX) {
+                (&S.Bf[s][0][0])[i] = Elem<Tin>::to_f((&S.B[r][0][0])[i]);
+                (&S.Cf[s][0][0])[i] = Elem<Tin>::to_f((&S.C[r][0][0])[i]);
+            }
+        };
+        auto epilogue = [&](int c) {
+            const int r = c % RING, s = c & 1, t0 = c * FT, nt = min(FT, p.L - t0);
+            if (!evalid) return;
+#pragma unroll 4
+            for (int t = at / SCH; t < nt; t += NAUX / SCH) {
+                const float4 q = *reinterpret_cast<const float4*>(&S.yp[s][t][ech][0]);
+                float y = (q.x + q.y) + (q.z + q.w);
+                y = fmaf(eD, Elem<Tin>::to_f(S.u[r][t][ech]), y);
+                if (HAS_Z) y *= silu_f(Elem<Tin>::to_f(S.z[r][t][ech]));
+                gout[(int64_t)(t0 + t) * p.D + ech] = Elem<Tout>::from_f(y);
+            }
+        };
+
+        issue(0);
+        issue(1);
+        issue(2);
+        cp_async_wait<2>();
+        bar_sync(BAR_AUX, NAUX);
+        derive(0);
+        bar_arrive(BAR_D0, NTH);
+        for (int c = 0; c < nchunk; ++c) {
+            if (c >= 1) {
+                bar_sync(BAR_X0 + ((c - 1) & 1), NTH);
+                epilogue(c - 1);
+            }
+            if (c + 1 < nchunk) {
+                cp_async_wait<1>();
+                bar_sync(BAR_AUX, NAUX);
+                derive(c + 1);
+                bar_arrive(BAR_D0 + ((c + 1) & 1), NTH);
+            }
+            bar_sync(BAR_AUX, NAUX);      // raw slot (c-1) % RING no longer read
+            issue(c + 3);
+        }
+        bar_sync(BAR_X0 + ((nchunk - 1) & 1), NTH);
+        epilogue(nchunk - 1);
+        cp_async_wait<0>();
     }
 }
 
 // =============================================================== backward
 template <typename Tin>
 struct BwdSmem {
-    Tin u[2][TCK][SCH];
-    Tin dl[2][TCK][SCH];
-    Tin z[2][TCK][SCH];
-    Tin dout[2][TCK][SCH];
-    Tin B[2][TCK][NS];
-    Tin C[2][TCK][NS];
-    float dlt[TCK][SCH];
-    float dlu[TCK][SCH];
-    float dy[TCK][SCH];
-    float Bf[TCK][NS];
-    float Cf[TCK][NS];
-    float nred[3][TCK][SCH][4];      // sum_n g*B, sum_n g*a*h_prev*A, sum_n h*C  (per state group)
-    float bc[2][TCK][SCH][NS];       // dB, dC contributions per channel
-    float red[2][SNT];               // per-thread dD / dbias accumulators
+    Tin u[RING][TCK][SCH];
+    Tin dl[RING][TCK][SCH];
+    Tin z[RING][TCK][SCH];
+    Tin dout[RING][TCK][SCH];
+    Tin B[RING][TCK][NS];
+    Tin C[RING][TCK][NS];
+    float4 dd[2][TCK][SCH];            // (delta_eff, delta_eff * u, dy, u)
+    float2 ee[2][TCK][SCH];            // (d delta_eff / d delta_raw, dout * silu'(z))
+    float Bf[2][TCK][NS];
+    float Cf[2][TCK][NS];
+    float bc[2][HT][SCH][2 * NS];      // per-channel dB | dC contributions of a half tile
+    float4 nred[2][HT][SCH][4];        // per state group: (sum g*B, sum g*a*h_prev*A, sum h*C, -)
+    float red[2][NAUX];
 };
 
+// One half tile (8 steps, processed last to first) of the reverse recurrence.
+template <bool FULL>
+__device__ __forceinline__ void bwd_half(const float4 (*dd)[SCH], const float (*Bf)[NS],
+                                         const float (*Cf)[NS], float (*bc)[SCH][2 * NS],
+                                         float4 (*nred)[SCH][4], int tlo, int nt, int ch, int j,
+                                         const float2 (&a01)[TCK], const float2 (&a23)[TCK],
+                                         const float2 (&hs01)[TCK], const float2 (&hs23)[TCK],
+                                         const float (&yv)[TCK], float2 hck01, float2 hck23,
+                                         float2 An01, float2 An23, float2& g01, float2& g23,
+                                         float2& an01, float2& an23, float2& dA01, float2& dA23) {
+#pragma unroll
+    for (int tt = HT - 1; tt >= 0; --tt) {
+        const int t = tlo + tt;
+        if (FULL || t < nt) {
+            const float4 d = dd[t][ch];
+            const float4 b = *reinterpret_cast<const float4*>(&Bf[t][4 * j]);
+            const float4 c = *reinterpret_cast<const float4*>(&Cf[t][4 * j]);
+            const float2 dy = bc2(d.z);
+            g01 = fma2(an01, g01, mul2(dy, f2(c.x, c.y)));
+            g23 = fma2(an23, g23, mul2(dy, f2(c.z, c.w)));
+            const float2 du = bc2(d.y);
+            const float2 db01 = mul2(g01, du), db23 = mul2(g23, du);
+            const float2 dc01 = mul2(dy, hs01[t]), dc23 = mul2(dy, hs23[t]);
+            *reinterpret_cast<float4*>(&bc[tt][ch][4 * j]) = make_float4(db01.x, db01.y, db23.x, db23.y);
+            *reinterpret_cast<float4*>(&bc[tt][ch][NS + 4 * j]) = make_float4(dc01.x, dc01.y, dc23.x, dc23.y);
+            float2 sg = mul2(g01, f2(b.x, b.y));
+            sg = fma2(g23, f2(b.z, b.w), sg);
+            const float2 hp01 = (t > 0) ? hs01[t > 0 ? t - 1 : 0] : hck01;
+            const float2 hp23 = (t > 0) ? hs23[t > 0 ? t - 1 : 0] : hck23;
+            const float2 w01 = mul2(mul2(g01, a01[t]), hp01);
+            const float2 w23 = mul2(mul2(g23, a23[t]), hp23);
+            const float2 dte = bc2(d.x);
+            dA01 = fma2(w01, dte, dA01);
+            dA23 = fma2(w23, dte, dA23);
+            float2 sd = mul2(w01, An01);
+            sd = fma2(w23, An23, sd);
+            nred[tt][ch][j] = make_float4(sg.x + sg.y, sd.x + sd.y, yv[t], 0.f);
+            an01 = a01[t];
+            an23 = a23[t];
+        }
+    }
+}
+
 template <typename Tin, bool HAS_Z>
-__global__ void __launch_bounds__(SNT, 1) scan_bwd_kernel(const ScanDev p) {
+__global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     BwdSmem<Tin>& S = *reinterpret_cast<BwdSmem<Tin>*>(smem_raw);
 
@@ -189,207 +279,235 @@ __global__ void __launch_bounds__(SNT, 1) scan_bwd_kernel(const ScanDev p) {
     const int bi = blockIdx.y;
     const int d0 = blockIdx.x * SCH;
     const int nd = min(SCH, p.D - d0);
-    const int ch = tid >> 2, j = tid & 3;
-    const int d = d0 + ch;
-    const bool dvalid = ch < nd;
-    const int ech = tid & (SCH - 1);
-    const bool evalid = ech < nd;
-    const float eD = (p.Dskip && evalid) ? p.Dskip[d0 + ech] : 0.f;
-    const float ebias = (p.dbias && evalid) ? p.dbias[d0 + ech] : 0.f;
+    const int nck = p.nck;
 
-    float A2[4], An[4];
+    if (tid < NSCAN) {
+        // ------------------------------------------------ recurrence warps
+        const int ch = tid >> 2, j = tid & 3;
+        const int d = d0 + ch;
+        const bool dvalid = ch < nd;
+        float av[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int n = 4 * j + i;
-        An[i] = (dvalid && n < p.N) ? p.A[(int64_t)d * p.N + n] : 0.f;
-        A2[i] = An[i] * LOG2E;
-    }
-
-    const Tin* gu = static_cast<const Tin*>(p.u) + bi * p.u_sb + d0;
-    const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + d0;
-    const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + d0 : nullptr;
-    const Tin* gdo = static_cast<const Tin*>(p.dout) + bi * p.dout_sb + d0;
-    const Tin* gB = static_cast<const Tin*>(p.B) + bi * p.B_sb;
-    const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
-    const int64_t orow = (int64_t)bi * p.L * p.D + d0;      // dense (b, L, D) outputs
-    Tin* gdu = static_cast<Tin*>(p.du) + orow;
-    Tin* gddl = static_cast<Tin*>(p.ddl) + orow;
-    Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + orow : nullptr;
-    float* wbc = p.ws_bc + ((int64_t)blockIdx.x * p.b + bi) * p.L * 2 * NS;
-
-    auto issue = [&](int c) {
-        const int t0 = c * TCK, rv = min(TCK, p.L - t0), buf = c & 1;
-        stage_tile<Tin, SCH>(&S.u[buf][0][0], gu + t0 * p.u_sl, p.u_sl, TCK, rv, nd, p.vec_u, tid, SNT);
-        stage_tile<Tin, SCH>(&S.dl[buf][0][0], gdl + t0 * p.dl_sl, p.dl_sl, TCK, rv, nd, p.vec_dl, tid, SNT);
-        if (HAS_Z)
-            stage_tile<Tin, SCH>(&S.z[buf][0][0], gz + t0 * p.z_sl, p.z_sl, TCK, rv, nd, p.vec_z, tid, SNT);
-        stage_tile<Tin, SCH>(&S.dout[buf][0][0], gdo + t0 * p.dout_sl, p.dout_sl, TCK, rv, nd, p.vec_dout, tid, SNT);
-        stage_tile<Tin, NS>(&S.B[buf][0][0], gB + t0 * p.B_sl, p.B_sl, TCK, rv, p.N, p.vec_B, tid, SNT);
-        stage_tile<Tin, NS>(&S.C[buf][0][0], gC + t0 * p.C_sl, p.C_sl, TCK, rv, p.N, p.vec_C, tid, SNT);
-        cp_async_commit();
-    };
-
-    float g[4] = {0.f, 0.f, 0.f, 0.f};      // dL/dh_t carried backwards in time
-    float an[4] = {0.f, 0.f, 0.f, 0.f};     // a_{t+1}; zero after the last step
-    float dAacc[4] = {0.f, 0.f, 0.f, 0.f};
-    float accD = 0.f, accB = 0.f;
-
-    issue(p.nck - 1);
-    for (int c = p.nck - 1; c >= 0; --c) {
-        if (c > 0) issue(c - 1); else cp_async_commit();
-        cp_async_wait<1>();
-        __syncthreads();
-        const int buf = c & 1, t0 = c * TCK, nt = min(TCK, p.L - t0);
-
-        // ---- phase A
-        for (int i = tid; i < TCK * SCH; i += SNT) {
-            const int t = i / SCH, cc = i % SCH;
-            const float raw = Elem<Tin>::to_f(S.dl[buf][t][cc]) + ebias;
-            const float dte = p.softplus ? softplus_f(raw) : raw;
-            S.dlt[t][cc] = dte;
-            S.dlu[t][cc] = dte * Elem<Tin>::to_f(S.u[buf][t][cc]);
-            float dyv = Elem<Tin>::to_f(S.dout[buf][t][cc]);
-            if (HAS_Z) dyv *= silu_f(Elem<Tin>::to_f(S.z[buf][t][cc]));
-            S.dy[t][cc] = dyv;
+        for (int i = 0; i < 4; ++i) {
+            const int n = 4 * j + i;
+            av[i] = (dvalid && n < p.N) ? p.A[(int64_t)d * p.N + n] : 0.f;
         }
-        for (int i = tid; i < TCK * NS; i += SNT) {
-            (&S.Bf[0][0])[i] = Elem<Tin>::to_f((&S.B[buf][0][0])[i]);
-            (&S.Cf[0][0])[i] = Elem<Tin>::to_f((&S.C[buf][0][0])[i]);
-        }
-        __syncthreads();
+        const float2 An01 = f2(av[0], av[1]), An23 = f2(av[2], av[3]);
+        const float2 A01 = mul2(An01, bc2(LOG2E)), A23 = mul2(An23, bc2(LOG2E));
+        float2 g01 = f2(0.f, 0.f), g23 = g01, an01 = g01, an23 = g01, dA01 = g01, dA23 = g01;
 
-        // ---- phase B1: recompute the chunk's decays and states from its checkpoint
-        float hck[4] = {0.f, 0.f, 0.f, 0.f};
-        if (dvalid) {
-            const float4 v = *reinterpret_cast<const float4*>(
-                p.ck + (((int64_t)bi * p.nck + c) * p.D + d) * NS + 4 * j);
-            hck[0] = v.x; hck[1] = v.y; hck[2] = v.z; hck[3] = v.w;
-        }
-        float a[TCK][4], hs[TCK][4];
-        {
-            float h0 = hck[0], h1 = hck[1], h2 = hck[2], h3 = hck[3];
+        for (int k = 0; k < nck; ++k) {
+            const int c = nck - 1 - k, s = k & 1, t0 = c * TCK, nt = min(TCK, p.L - t0);
+            bar_sync(BAR_D0 + s, NTH);
+            float2 hck01 = f2(0.f, 0.f), hck23 = hck01;
+            if (dvalid) {
+                const float4 v = *reinterpret_cast<const float4*>(
+                    p.ck + (((int64_t)bi * nck + c) * p.D + d) * NS + 4 * j);
+                hck01 = f2(v.x, v.y);
+                hck23 = f2(v.z, v.w);
+            }
+            // recompute decays and states of the chunk
+            float2 a01[TCK], a23[TCK], hs01[TCK], hs23[TCK];
+            float yv[TCK];
+            {
+                float2 h01 = hck01, h23 = hck23;
 #pragma unroll
-            for (int t = 0; t < TCK; ++t) {
-                if (t < nt) {
-                    const float dte = S.dlt[t][ch], dtu = S.dlu[t][ch];
-                    const float4 b4 = *reinterpret_cast<const float4*>(&S.Bf[t][4 * j]);
-                    a[t][0] = ex2(dte * A2[0]);
-                    a[t][1] = ex2(dte * A2[1]);
-                    a[t][2] = ex2(dte * A2[2]);
-                    a[t][3] = ex2(dte * A2[3]);
-                    h0 = fmaf(a[t][0], h0, dtu * b4.x);
-                    h1 = fmaf(a[t][1], h1, dtu * b4.y);
-                    h2 = fmaf(a[t][2], h2, dtu * b4.z);
-                    h3 = fmaf(a[t][3], h3, dtu * b4.w);
-                    hs[t][0] = h0; hs[t][1] = h1; hs[t][2] = h2; hs[t][3] = h3;
-                    if (HAS_Z) {
-                        const float4 c4 = *reinterpret_cast<const float4*>(&S.Cf[t][4 * j]);
-                        float y = h0 * c4.x;
-                        y = fmaf(h1, c4.y, y);
-                        y = fmaf(h2, c4.z, y);
-                        y = fmaf(h3, c4.w, y);
-                        S.nred[2][t][ch][j] = y;
+                for (int t = 0; t < TCK; ++t) {
+                    if (t < nt) {
+                        const float4 dv = S.dd[s][t][ch];
+                        const float4 b = *reinterpret_cast<const float4*>(&S.Bf[s][t][4 * j]);
+                        const float2 dt = bc2(dv.x), du = bc2(dv.y);
+                        a01[t] = ex2x2(mul2(dt, A01));
+                        a23[t] = ex2x2(mul2(dt, A23));
+                        h01 = fma2(a01[t], h01, mul2(du, f2(b.x, b.y)));
+                        h23 = fma2(a23[t], h23, mul2(du, f2(b.z, b.w)));
+                        hs01[t] = h01;
+                        hs23[t] = h23;
+                        if (HAS_Z) {
+                            const float4 cc = *reinterpret_cast<const float4*>(&S.Cf[s][t][4 * j]);
+                            float2 y = mul2(h01, f2(cc.x, cc.y));
+                            y = fma2(h23, f2(cc.z, cc.w), y);
+                            yv[t] = y.x + y.y;
+                        } else {
+                            yv[t] = 0.f;
+                        }
+                    } else {
+                        a01[t] = a23[t] = hs01[t] = hs23[t] = f2(0.f, 0.f);
+                        yv[t] = 0.f;
                     }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) { a[t][i] = 0.f; hs[t][i] = 0.f; }
                 }
             }
-        }
-
-        // ---- phase B2: reverse recurrence through the chunk
+            // reverse recurrence: upper half (steps 8..15) into slot 0, lower half into slot 1
 #pragma unroll
-        for (int t = TCK - 1; t >= 0; --t) {
-            if (t < nt) {
-                const float dte = S.dlt[t][ch], dtu = S.dlu[t][ch], dyv = S.dy[t][ch];
-                const float4 b4 = *reinterpret_cast<const float4*>(&S.Bf[t][4 * j]);
-                const float4 c4 = *reinterpret_cast<const float4*>(&S.Cf[t][4 * j]);
-                const float bb[4] = {b4.x, b4.y, b4.z, b4.w};
-                const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
-                float sgb = 0.f, sda = 0.f;
-                float gB4[4], gC4[4];
+            for (int hh = 0; hh < 2; ++hh) {
+                const int tlo = hh == 0 ? HT : 0;
+                bar_sync(BAR_E0 + hh, NTH);
+                if (nt == TCK)
+                    bwd_half<true>(S.dd[s], S.Bf[s], S.Cf[s], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
+                                   hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
+                else
+                    bwd_half<false>(S.dd[s], S.Bf[s], S.Cf[s], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
+                                    hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
+                bar_arrive(BAR_X0 + hh, NTH);
+            }
+        }
+        if (dvalid) {
+            *reinterpret_cast<float4*>(p.ws_a + ((int64_t)bi * p.D + d) * NS + 4 * j) =
+                make_float4(dA01.x, dA01.y, dA23.x, dA23.y);
+            if (p.dh0) {
+                const float hv[4] = {an01.x * g01.x, an01.y * g01.y, an23.x * g23.x, an23.y * g23.y};
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
-                    g[i] = fmaf(an[i], g[i], dyv * cv[i]);
-                    gC4[i] = dyv * hs[t][i];
-                    gB4[i] = g[i] * dtu;
-                    sgb = fmaf(g[i], bb[i], sgb);
-                    const float hp = (t > 0) ? hs[t > 0 ? t - 1 : 0][i] : hck[i];
-                    const float w = g[i] * a[t][i] * hp;
-                    dAacc[i] = fmaf(w, dte, dAacc[i]);
-                    sda = fmaf(w, An[i], sda);
-                    an[i] = a[t][i];
+                    const int n = 4 * j + i;
+                    if (n < p.N) p.dh0[((int64_t)bi * p.D + d) * p.N + n] = hv[i];
                 }
-                *reinterpret_cast<float4*>(&S.bc[0][t][ch][4 * j]) = make_float4(gB4[0], gB4[1], gB4[2], gB4[3]);
-                *reinterpret_cast<float4*>(&S.bc[1][t][ch][4 * j]) = make_float4(gC4[0], gC4[1], gC4[2], gC4[3]);
-                S.nred[0][t][ch][j] = sgb;
-                S.nred[1][t][ch][j] = sda;
             }
         }
-        __syncthreads();
+    } else {
+        // ------------------------------------------------ helper warps
+        const int at = tid - NSCAN;
+        const int ech = at & (SCH - 1);
+        const bool evalid = ech < nd;
+        const float eD = (p.Dskip && evalid) ? p.Dskip[d0 + ech] : 0.f;
+        const float ebias = (p.dbias && evalid) ? p.dbias[d0 + ech] : 0.f;
+        const Tin* gu = static_cast<const Tin*>(p.u) + bi * p.u_sb + d0;
+        const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + d0;
+        const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + d0 : nullptr;
+        const Tin* gdo = static_cast<const Tin*>(p.dout) + bi * p.dout_sb + d0;
+        const Tin* gB = static_cast<const Tin*>(p.B) + bi * p.B_sb;
+        const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
+        const int64_t orow = (int64_t)bi * p.L * p.D + d0;
+        Tin* gdu = static_cast<Tin*>(p.du) + orow;
+        Tin* gddl = static_cast<Tin*>(p.ddl) + orow;
+        Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + orow : nullptr;
+        float* wbc = p.ws_bc + ((int64_t)blockIdx.x * p.b + bi) * p.L * 2 * NS;
+        float accD = 0.f, accB = 0.f;
 
-        // ---- phase C: per (t, channel) gradients
-        if (evalid) {
-            for (int t = tid / SCH; t < nt; t += SNT / SCH) {
-                const float4 q0 = *reinterpret_cast<const float4*>(&S.nred[0][t][ech][0]);
-                const float4 q1 = *reinterpret_cast<const float4*>(&S.nred[1][t][ech][0]);
-                const float sgb = (q0.x + q0.y) + (q0.z + q0.w);
-                const float sda = (q1.x + q1.y) + (q1.z + q1.w);
-                const float uv = Elem<Tin>::to_f(S.u[buf][t][ech]);
-                const float dte = S.dlt[t][ech], dyv = S.dy[t][ech];
-                const float du = fmaf(dte, sgb, eD * dyv);
-                const float ddte = fmaf(uv, sgb, sda);
-                const float raw = Elem<Tin>::to_f(S.dl[buf][t][ech]) + ebias;
-                const float draw = p.softplus ? (raw > 20.f ? ddte : ddte * sigmoid_f(raw)) : ddte;
-                const int64_t o = (int64_t)(t0 + t) * p.D + ech;
-                gdu[o] = Elem<Tin>::from_f(du);
-                gddl[o] = Elem<Tin>::from_f(draw);
+        auto issue = [&](int k) {
+            if (k < nck) {
+                const int c = nck - 1 - k, t0 = c * TCK, rv = min(TCK, p.L - t0), r = k % RING;
+                stage_tile<Tin, SCH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, TCK, rv, nd, p.vec_u, at, NAUX);
+                stage_tile<Tin, SCH>(&S.dl[r][0][0], gdl + t0 * p.dl_sl, p.dl_sl, TCK, rv, nd, p.vec_dl, at, NAUX);
+                if (HAS_Z)
+                    stage_tile<Tin, SCH>(&S.z[r][0][0], gz + t0 * p.z_sl, p.z_sl, TCK, rv, nd, p.vec_z, at, NAUX);
+                stage_tile<Tin, SCH>(&S.dout[r][0][0], gdo + t0 * p.dout_sl, p.dout_sl, TCK, rv, nd, p.vec_dout, at, NAUX);
+                stage_tile<Tin, NS>(&S.B[r][0][0], gB + t0 * p.B_sl, p.B_sl, TCK, rv, p.N, p.vec_B, at, NAUX);
+                stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, TCK, rv, p.N, p.vec_C, at, NAUX);
+            }
+            cp_async_commit();
+        };
+        auto derive = [&](int k) {
+            const int r = k % RING, s = k & 1;
+#pragma unroll
+            for (int i = at; i < TCK * SCH; i += NAUX) {
+                const int t = i / SCH;
+                const float raw = Elem<Tin>::to_f(S.dl[r][t][ech]) + ebias;
+                const float uv = Elem<Tin>::to_f(S.u[r][t][ech]);
+                float dte = raw, dsp = 1.f;
+                if (p.softplus) {
+                    dte = softplus_f(raw);
+                    dsp = raw > 20.f ? 1.f : sigmoid_f(raw);
+                }
+                const float dov = Elem<Tin>::to_f(S.dout[r][t][ech]);
+                float dy = dov, q = 0.f;
                 if (HAS_Z) {
-                    const float4 q2 = *reinterpret_cast<const float4*>(&S.nred[2][t][ech][0]);
-                    const float y = fmaf(eD, uv, (q2.x + q2.y) + (q2.z + q2.w));
-                    const float zv = Elem<Tin>::to_f(S.z[buf][t][ech]);
+                    const float zv = Elem<Tin>::to_f(S.z[r][t][ech]);
                     const float sg = sigmoid_f(zv);
-                    const float dsilu = sg * fmaf(zv, 1.f - sg, 1.f);
-                    gdz[o] = Elem<Tin>::from_f(Elem<Tin>::to_f(S.dout[buf][t][ech]) * y * dsilu);
+                    dy = dov * zv * sg;
+                    q = dov * sg * fmaf(zv, 1.f - sg, 1.f);
                 }
-                accD = fmaf(dyv, uv, accD);
-                accB += draw;
+                S.dd[s][t][ech] = make_float4(dte, dte * uv, dy, uv);
+                S.ee[s][t][ech] = f2(dsp, q);
             }
-        }
-        // CTA partial of dB / dC for this chunk: fixed-order sum over the 32 channels
-        for (int i = tid; i < 2 * TCK * NS; i += SNT) {
-            const int kind = i / (TCK * NS), t = (i / NS) % TCK, n = i % NS;
-            if (t < nt) {
-                float s = 0.f;
-#pragma unroll 8
-                for (int cc = 0; cc < SCH; ++cc) s += S.bc[kind][t][cc][n];
-                wbc[((int64_t)(t0 + t) * 2 + kind) * NS + n] = s;
+#pragma unroll
+            for (int i = at; i < TCK * NS; i += NAUX) {
+                (&S.Bf[s][0][0])[i] = Elem<Tin>::to_f((&S.B[r][0][0])[i]);
+                (&S.Cf[s][0][0])[i] = Elem<Tin>::to_f((&S.C[r][0][0])[i]);
             }
-        }
-        __syncthreads();
-    }
+        };
+        auto epilogue = [&](int k, int hh) {
+            const int c = nck - 1 - k, s = k & 1, t0 = c * TCK, nt = min(TCK, p.L - t0);
+            const int tlo = hh == 0 ? HT : 0;
+            if (evalid) {
+#pragma unroll
+                for (int m = 0; m < HT * SCH / NAUX; ++m) {
+                    const int tt = at / SCH + m * (NAUX / SCH);
+                    const int t = tlo + tt;
+                    if (t < nt) {
+                        const float4 n0 = S.nred[hh][tt][ech][0], n1 = S.nred[hh][tt][ech][1];
+                        const float4 n2 = S.nred[hh][tt][ech][2], n3 = S.nred[hh][tt][ech][3];
+                        const float sgb = (n0.x + n1.x) + (n2.x + n3.x);
+                        const float sda = (n0.y + n1.y) + (n2.y + n3.y);
+                        const float4 dv = S.dd[s][t][ech];
+                        const float2 e = S.ee[s][t][ech];
+                        const float du = fmaf(dv.x, sgb, eD * dv.z);
+                        const float draw = fmaf(dv.w, sgb, sda) * e.x;
+                        const int64_t o = (int64_t)(t0 + t) * p.D + ech;
+                        gdu[o] = Elem<Tin>::from_f(du);
+                        gddl[o] = Elem<Tin>::from_f(draw);
+                        if (HAS_Z) {
+                            const float y = fmaf(eD, dv.w, (n0.z + n1.z) + (n2.z + n3.z));
+                            gdz[o] = Elem<Tin>::from_f(e.y * y);
+                        }
+                        accD = fmaf(dv.z, dv.w, accD);
+                        accB += draw;
+                    }
+                }
+            }
+            // CTA partial of dB | dC: fixed-order sum over the 32 channels
+            {
+                const int o2 = at & 15, tt = at >> 4, t = tlo + tt;
+                if (t < nt) {
+                    float2 s0 = f2(0.f, 0.f), s1 = s0, s2 = s0, s3 = s0;
+#pragma unroll
+                    for (int cc = 0; cc < SCH; cc += 4) {
+                        s0 = add2(s0, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 0][2 * o2]));
+                        s1 = add2(s1, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 1][2 * o2]));
+                        s2 = add2(s2, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 2][2 * o2]));
+                        s3 = add2(s3, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 3][2 * o2]));
+                    }
+                    *reinterpret_cast<float2*>(wbc + (int64_t)(t0 + t) * 2 * NS + 2 * o2) =
+                        add2(add2(s0, s1), add2(s2, s3));
+                }
+            }
+        };
 
-    // per-(b, d, n) and per-(b, d) partials; summed over b by the finalize kernel
-    if (dvalid) {
-        *reinterpret_cast<float4*>(p.ws_a + ((int64_t)bi * p.D + d) * NS + 4 * j) =
-            make_float4(dAacc[0], dAacc[1], dAacc[2], dAacc[3]);
-        if (p.dh0) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int n = 4 * j + i;
-                if (n < p.N) p.dh0[((int64_t)bi * p.D + d) * p.N + n] = an[i] * g[i];
+        issue(0);
+        issue(1);
+        issue(2);
+        cp_async_wait<2>();
+        bar_sync(BAR_AUX, NAUX);
+        derive(0);
+        bar_arrive(BAR_D0, NTH);
+        bar_arrive(BAR_E0, NTH);          // both half-tile slots start empty
+        bar_arrive(BAR_E0 + 1, NTH);
+        for (int k = 0; k < nck; ++k) {
+            if (k + 1 < nck) {
+                cp_async_wait<1>();
+                bar_sync(BAR_AUX, NAUX);
+                derive(k + 1);
+                bar_arrive(BAR_D0 + ((k + 1) & 1), NTH);
             }
-        }
-    }
-    S.red[0][tid] = accD;
-    S.red[1][tid] = accB;
-    __syncthreads();
-    if (tid < SCH && tid < nd) {
-        float sD = 0.f, sB = 0.f;
 #pragma unroll
-        for (int k = 0; k < SNT / SCH; ++k) { sD += S.red[0][tid + k * SCH]; sB += S.red[1][tid + k * SCH]; }
-        p.ws_d[(int64_t)bi * p.D + d0 + tid] = sD;
-        p.ws_bias[(int64_t)bi * p.D + d0 + tid] = sB;
+            for (int hh = 0; hh < 2; ++hh) {
+                bar_sync(BAR_X0 + hh, NTH);
+                epilogue(k, hh);
+                if (k + 1 < nck) bar_arrive(BAR_E0 + hh, NTH);
+            }
+            bar_sync(BAR_AUX, NAUX);      // raw slot (k-1) % RING no longer read
+            issue(k + 3);
+        }
+        cp_async_wait<0>();
+        S.red[0][at] = accD;
+        S.red[1][at] = accB;
+        bar_sync(BAR_AUX, NAUX);
+        if (at < SCH && at < nd) {
+            float sD = 0.f, sB = 0.f;
+#pragma unroll
+            for (int m = 0; m < NAUX / SCH; ++m) { sD += S.red[0][at + m * SCH]; sB += S.red[1][at + m * SCH]; }
+            p.ws_d[(int64_t)bi * p.D + d0 + at] = sD;
+            p.ws_bias[(int64_t)bi * p.D + d0 + at] = sB;
+        }
     }
 }
 
@@ -439,7 +557,7 @@ static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
-    k<<<grid, SNT, smem, st>>>(p);
+    k<<<grid, NTH, smem, st>>>(p);
     return cudaGetLastError();
 }
 
@@ -450,7 +568,7 @@ static cudaError_t launch_bwd_t(const ScanDev& p, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
-    k<<<grid, SNT, smem, st>>>(p);
+    k<<<grid, NTH, smem, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const int64_t total = 2LL * p.b * p.L * p.N + (int64_t)p.D * p.N + p.D;
