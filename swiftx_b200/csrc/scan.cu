@@ -42,6 +42,14 @@ constexpr int RING = 4;               // raw staging slots
 
 enum : int { BAR_AUX = 1, BAR_D0 = 2, BAR_X0 = 4, BAR_E0 = 6 };
 
+// Four consecutive staged elements as fp32 (one 16-byte load for fp32, 8-byte for bf16).
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
+    const uint2 v = *reinterpret_cast<const uint2*>(p);
+    return make_float4(__uint_as_float(v.x << 16), __uint_as_float(v.x & 0xffff0000u),
+                       __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
+}
+
 // =============================================================== forward
 template <typename Tin>
 struct FwdSmem {
@@ -51,32 +59,40 @@ struct FwdSmem {
     Tin B[RING][FT][NS];
     Tin C[RING][FT][NS];
     float2 dd[2][FT][SCH];        // (delta_eff, delta_eff * u)
-    float Bf[2][FT][NS];
-    float Cf[2][FT][NS];
     float yp[2][FT][SCH][4];      // partial readouts of the 4 state groups
 };
 
-template <bool FULL>
-__device__ __forceinline__ void fwd_tile(const float2 (*dd)[SCH], const float (*Bf)[NS],
-                                         const float (*Cf)[NS], float (*yp)[SCH][4], int nt, int ch,
-                                         int j, float2 A01, float2 A23, float2& h01, float2& h23,
-                                         float* ckp, int64_t ck_stride) {
+template <bool FULL, typename Tin>
+__device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], const Tin (*__restrict__ Bs)[NS],
+                                         const Tin (*__restrict__ Cs)[NS], float (*__restrict__ yp)[SCH][4],
+                                         int nt, int ch, int j, float2 A01, float2 A23, float2& h01, float2& h23,
+                                         float* __restrict__ ckp, int64_t ck_stride) {
 #pragma unroll
-    for (int t = 0; t < FT; ++t) {
-        if (FULL || t < nt) {
-            if ((t % TCK) == 0 && ckp)
-                *reinterpret_cast<float4*>(ckp + (t / TCK) * ck_stride) = make_float4(h01.x, h01.y, h23.x, h23.y);
-            const float2 d = dd[t][ch];
-            const float4 b = *reinterpret_cast<const float4*>(&Bf[t][4 * j]);
-            const float4 c = *reinterpret_cast<const float4*>(&Cf[t][4 * j]);
-            const float2 dt = bc2(d.x), du = bc2(d.y);
-            const float2 a01 = ex2x2(mul2(dt, A01));
-            const float2 a23 = ex2x2(mul2(dt, A23));
-            h01 = fma2(a01, h01, mul2(du, f2(b.x, b.y)));
-            h23 = fma2(a23, h23, mul2(du, f2(b.z, b.w)));
-            float2 y = mul2(h01, f2(c.x, c.y));
-            y = fma2(h23, f2(c.z, c.w), y);
-            yp[t][ch][j] = y.x + y.y;
+    for (int g = 0; g < FT / 8; ++g) {
+        float yv[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int t = 8 * g + q;
+            if (FULL || t < nt) {
+                if ((t % TCK) == 0 && ckp)
+                    *reinterpret_cast<float4*>(ckp + (t / TCK) * ck_stride) = make_float4(h01.x, h01.y, h23.x, h23.y);
+                const float2 d = dd[t][ch];
+                const float4 b = ld4(&Bs[t][4 * j]);
+                const float4 c = ld4(&Cs[t][4 * j]);
+                const float2 dt = bc2(d.x), du = bc2(d.y);
+                const float2 a01 = ex2x2(mul2(dt, A01));
+                const float2 a23 = ex2x2(mul2(dt, A23));
+                h01 = fma2(a01, h01, mul2(du, f2(b.x, b.y)));
+                h23 = fma2(a23, h23, mul2(du, f2(b.z, b.w)));
+                float2 y = mul2(h01, f2(c.x, c.y));
+                y = fma2(h23, f2(c.z, c.w), y);
+                yv[q] = y.x + y.y;
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const int t = 8 * g + q;
+            if (FULL || t < nt) yp[t][ch][j] = yv[q];
         }
     }
 }
@@ -114,10 +130,11 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
             float* ckp = (p.ck && dvalid)
                              ? p.ck + (((int64_t)bi * p.nck + t0 / TCK) * p.D + d) * NS + 4 * j
                              : nullptr;
+            const int r = c % RING;
             if (nt == FT)
-                fwd_tile<true>(S.dd[s], S.Bf[s], S.Cf[s], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
+                fwd_tile<true>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
             else
-                fwd_tile<false>(S.dd[s], S.Bf[s], S.Cf[s], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
+                fwd_tile<false>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
             bar_arrive(BAR_X0 + s, NTH);
         }
         if (p.h_last && dvalid) {
@@ -162,11 +179,6 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
                 const float raw = Elem<Tin>::to_f(S.dl[r][t][ech]) + ebias;
                 const float dte = p.softplus ? softplus_f(raw) : raw;
                 S.dd[s][t][ech] = f2(dte, dte * Elem<Tin>::to_f(S.u[r][t][ech]));
-            }
-#pragma unroll 4
-            for (int i = at; i < FT * NS; i += NAUX) {
-                (&S.Bf[s][0][0])[i] = Elem<Tin>::to_f((&S.B[r][0][0])[i]);
-                (&S.Cf[s][0][0])[i] = Elem<Tin>::to_f((&S.C[r][0][0])[i]);
             }
         };
         auto epilogue = [&](int c) {
@@ -218,40 +230,43 @@ struct BwdSmem {
     Tin dout[RING][TCK][SCH];
     Tin B[RING][TCK][NS];
     Tin C[RING][TCK][NS];
-    float4 dd[2][TCK][SCH];            // (delta_eff, delta_eff * u, dy, u)
-    float2 ee[2][TCK][SCH];            // (d delta_eff / d delta_raw, dout * silu'(z))
-    float Bf[2][TCK][NS];
-    float Cf[2][TCK][NS];
-    float bc[2][HT][SCH][2 * NS];      // per-channel dB | dC contributions of a half tile
+    float2 dd[2][TCK][SCH];            // (delta_eff, delta_eff * u)
+    float dy[2][TCK][SCH];             // dy = dout * silu(z) (or dout)
+    float4 ee[2][TCK][SCH];            // (u, d delta_eff / d delta_raw, dout * silu'(z), dy)
+    float bc[2][HT][SCH][2 * NS];      // per-channel dB | dC contributions of a half tile; the two
+                                       // 16-wide halves swap on odd channels (bank-conflict-free stores)
     float4 nred[2][HT][SCH][4];        // per state group: (sum g*B, sum g*a*h_prev*A, sum h*C, -)
     float red[2][NAUX];
 };
 
 // One half tile (8 steps, processed last to first) of the reverse recurrence.
-template <bool FULL>
-__device__ __forceinline__ void bwd_half(const float4 (*dd)[SCH], const float (*Bf)[NS],
-                                         const float (*Cf)[NS], float (*bc)[SCH][2 * NS],
-                                         float4 (*nred)[SCH][4], int tlo, int nt, int ch, int j,
+template <bool FULL, typename Tin>
+__device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], const float (*__restrict__ dyv)[SCH],
+                                         const Tin (*__restrict__ Bs)[NS], const Tin (*__restrict__ Cs)[NS],
+                                         float (*__restrict__ bc)[SCH][2 * NS], float4 (*__restrict__ nred)[SCH][4],
+                                         int tlo, int nt, int ch, int j,
                                          const float2 (&a01)[TCK], const float2 (&a23)[TCK],
                                          const float2 (&hs01)[TCK], const float2 (&hs23)[TCK],
                                          const float (&yv)[TCK], float2 hck01, float2 hck23,
                                          float2 An01, float2 An23, float2& g01, float2& g23,
                                          float2& an01, float2& an23, float2& dA01, float2& dA23) {
+    const int colB = (ch & 1) * NS + 4 * j;           // swizzled dB / dC columns
+    const int colC = ((ch & 1) ^ 1) * NS + 4 * j;
 #pragma unroll
     for (int tt = HT - 1; tt >= 0; --tt) {
         const int t = tlo + tt;
         if (FULL || t < nt) {
-            const float4 d = dd[t][ch];
-            const float4 b = *reinterpret_cast<const float4*>(&Bf[t][4 * j]);
-            const float4 c = *reinterpret_cast<const float4*>(&Cf[t][4 * j]);
-            const float2 dy = bc2(d.z);
+            const float2 d = dd[t][ch];
+            const float2 dy = bc2(dyv[t][ch]);
+            const float4 b = ld4(&Bs[t][4 * j]);
+            const float4 c = ld4(&Cs[t][4 * j]);
             g01 = fma2(an01, g01, mul2(dy, f2(c.x, c.y)));
             g23 = fma2(an23, g23, mul2(dy, f2(c.z, c.w)));
             const float2 du = bc2(d.y);
             const float2 db01 = mul2(g01, du), db23 = mul2(g23, du);
             const float2 dc01 = mul2(dy, hs01[t]), dc23 = mul2(dy, hs23[t]);
-            *reinterpret_cast<float4*>(&bc[tt][ch][4 * j]) = make_float4(db01.x, db01.y, db23.x, db23.y);
-            *reinterpret_cast<float4*>(&bc[tt][ch][NS + 4 * j]) = make_float4(dc01.x, dc01.y, dc23.x, dc23.y);
+            *reinterpret_cast<float4*>(&bc[tt][ch][colB]) = make_float4(db01.x, db01.y, db23.x, db23.y);
+            *reinterpret_cast<float4*>(&bc[tt][ch][colC]) = make_float4(dc01.x, dc01.y, dc23.x, dc23.y);
             float2 sg = mul2(g01, f2(b.x, b.y));
             sg = fma2(g23, f2(b.z, b.w), sg);
             const float2 hp01 = (t > 0) ? hs01[t > 0 ? t - 1 : 0] : hck01;
@@ -297,7 +312,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
         float2 g01 = f2(0.f, 0.f), g23 = g01, an01 = g01, an23 = g01, dA01 = g01, dA23 = g01;
 
         for (int k = 0; k < nck; ++k) {
-            const int c = nck - 1 - k, s = k & 1, t0 = c * TCK, nt = min(TCK, p.L - t0);
+            const int c = nck - 1 - k, s = k & 1, r = k % RING, t0 = c * TCK, nt = min(TCK, p.L - t0);
             bar_sync(BAR_D0 + s, NTH);
             float2 hck01 = f2(0.f, 0.f), hck23 = hck01;
             if (dvalid) {
@@ -314,8 +329,8 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
 #pragma unroll
                 for (int t = 0; t < TCK; ++t) {
                     if (t < nt) {
-                        const float4 dv = S.dd[s][t][ch];
-                        const float4 b = *reinterpret_cast<const float4*>(&S.Bf[s][t][4 * j]);
+                        const float2 dv = S.dd[s][t][ch];
+                        const float4 b = ld4(&S.B[r][t][4 * j]);
                         const float2 dt = bc2(dv.x), du = bc2(dv.y);
                         a01[t] = ex2x2(mul2(dt, A01));
                         a23[t] = ex2x2(mul2(dt, A23));
@@ -324,7 +339,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                         hs01[t] = h01;
                         hs23[t] = h23;
                         if (HAS_Z) {
-                            const float4 cc = *reinterpret_cast<const float4*>(&S.Cf[s][t][4 * j]);
+                            const float4 cc = ld4(&S.C[r][t][4 * j]);
                             float2 y = mul2(h01, f2(cc.x, cc.y));
                             y = fma2(h23, f2(cc.z, cc.w), y);
                             yv[t] = y.x + y.y;
@@ -343,10 +358,10 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                 const int tlo = hh == 0 ? HT : 0;
                 bar_sync(BAR_E0 + hh, NTH);
                 if (nt == TCK)
-                    bwd_half<true>(S.dd[s], S.Bf[s], S.Cf[s], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
+                    bwd_half<true>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
                                    hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
                 else
-                    bwd_half<false>(S.dd[s], S.Bf[s], S.Cf[s], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
+                    bwd_half<false>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
                                     hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
                 bar_arrive(BAR_X0 + hh, NTH);
             }
@@ -416,13 +431,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                     dy = dov * zv * sg;
                     q = dov * sg * fmaf(zv, 1.f - sg, 1.f);
                 }
-                S.dd[s][t][ech] = make_float4(dte, dte * uv, dy, uv);
-                S.ee[s][t][ech] = f2(dsp, q);
-            }
-#pragma unroll
-            for (int i = at; i < TCK * NS; i += NAUX) {
-                (&S.Bf[s][0][0])[i] = Elem<Tin>::to_f((&S.B[r][0][0])[i]);
-                (&S.Cf[s][0][0])[i] = Elem<Tin>::to_f((&S.C[r][0][0])[i]);
+                S.dd[s][t][ech] = f2(dte, dte * uv);
+                S.dy[s][t][ech] = dy;
+                S.ee[s][t][ech] = make_float4(uv, dsp, q, dy);
             }
         };
         auto epilogue = [&](int k, int hh) {
@@ -434,22 +445,26 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                     const int tt = at / SCH + m * (NAUX / SCH);
                     const int t = tlo + tt;
                     if (t < nt) {
-                        const float4 n0 = S.nred[hh][tt][ech][0], n1 = S.nred[hh][tt][ech][1];
-                        const float4 n2 = S.nred[hh][tt][ech][2], n3 = S.nred[hh][tt][ech][3];
+                        // rotate the state-group order per lane pair: conflict-free 16-byte loads
+                        const int rot = (ech >> 1) & 3;
+                        const float4 n0 = S.nred[hh][tt][ech][(rot + 0) & 3];
+                        const float4 n1 = S.nred[hh][tt][ech][(rot + 1) & 3];
+                        const float4 n2 = S.nred[hh][tt][ech][(rot + 2) & 3];
+                        const float4 n3 = S.nred[hh][tt][ech][(rot + 3) & 3];
                         const float sgb = (n0.x + n1.x) + (n2.x + n3.x);
                         const float sda = (n0.y + n1.y) + (n2.y + n3.y);
-                        const float4 dv = S.dd[s][t][ech];
-                        const float2 e = S.ee[s][t][ech];
-                        const float du = fmaf(dv.x, sgb, eD * dv.z);
-                        const float draw = fmaf(dv.w, sgb, sda) * e.x;
+                        const float dte = S.dd[s][t][ech].x;
+                        const float4 e = S.ee[s][t][ech];          // (u, dsoftplus, q, dy)
+                        const float du = fmaf(dte, sgb, eD * e.w);
+                        const float draw = fmaf(e.x, sgb, sda) * e.y;
                         const int64_t o = (int64_t)(t0 + t) * p.D + ech;
                         gdu[o] = Elem<Tin>::from_f(du);
                         gddl[o] = Elem<Tin>::from_f(draw);
                         if (HAS_Z) {
-                            const float y = fmaf(eD, dv.w, (n0.z + n1.z) + (n2.z + n3.z));
-                            gdz[o] = Elem<Tin>::from_f(e.y * y);
+                            const float y = fmaf(eD, e.x, (n0.z + n1.z) + (n2.z + n3.z));
+                            gdz[o] = Elem<Tin>::from_f(e.z * y);
                         }
-                        accD = fmaf(dv.z, dv.w, accD);
+                        accD = fmaf(e.w, e.x, accD);
                         accB += draw;
                     }
                 }
@@ -459,12 +474,13 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                 const int o2 = at & 15, tt = at >> 4, t = tlo + tt;
                 if (t < nt) {
                     float2 s0 = f2(0.f, 0.f), s1 = s0, s2 = s0, s3 = s0;
+                    const int col0 = 2 * o2, col1 = (2 * o2) ^ NS;   // even / odd channel columns
 #pragma unroll
                     for (int cc = 0; cc < SCH; cc += 4) {
-                        s0 = add2(s0, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 0][2 * o2]));
-                        s1 = add2(s1, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 1][2 * o2]));
-                        s2 = add2(s2, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 2][2 * o2]));
-                        s3 = add2(s3, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 3][2 * o2]));
+                        s0 = add2(s0, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 0][col0]));
+                        s1 = add2(s1, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 1][col1]));
+                        s2 = add2(s2, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 2][col0]));
+                        s3 = add2(s3, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 3][col1]));
                     }
                     *reinterpret_cast<float2*>(wbc + (int64_t)(t0 + t) * 2 * NS + 2 * o2) =
                         add2(add2(s0, s1), add2(s2, s3));
