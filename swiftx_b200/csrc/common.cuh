@@ -72,6 +72,34 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 __device__ __forceinline__ float2 ex2x2(float2 x) { return make_float2(ex2(x.x), ex2(x.y)); }
 
+__device__ __forceinline__ float2 rcp2(float2 x) { return make_float2(rcp(x.x), rcp(x.y)); }
+
+// softplus of two values (torch threshold 20) and its derivative sigmoid(x), sharing
+// e = exp(x).  For e < 1/16, log1p(e) is its alternating Taylor series through e^6
+// (relative truncation error below e^6/7 < 3e-9) because lg2.approx has an absolute
+// error near 1 that would be a large relative error of a small result; otherwise
+// log2(1 + e) * ln2.  sigmoid(x) = e / (1 + e).
+__device__ __forceinline__ void softplus2(float2 x, float2& sp, float2& dsp) {
+    const float2 e = ex2x2(mul2(x, bc2(LOG2E)));
+    float2 p = bc2(-0.16666667f);
+    p = fma2(p, e, bc2(0.2f));
+    p = fma2(p, e, bc2(-0.25f));
+    p = fma2(p, e, bc2(0.33333334f));
+    p = fma2(p, e, bc2(-0.5f));
+    p = fma2(p, e, bc2(1.f));
+    const float2 ser = mul2(p, e);
+    const float2 ope = add2(bc2(1.f), e);
+    const float2 lg = mul2(make_float2(lg2(ope.x), lg2(ope.y)), bc2(0.69314718055994531f));
+    const float2 sg = mul2(e, rcp2(ope));
+    sp.x = x.x > 20.f ? x.x : (e.x < 0.0625f ? ser.x : lg.x);
+    sp.y = x.y > 20.f ? x.y : (e.y < 0.0625f ? ser.y : lg.y);
+    dsp.x = x.x > 20.f ? 1.f : sg.x;
+    dsp.y = x.y > 20.f ? 1.f : sg.y;
+}
+__device__ __forceinline__ float2 sigmoid2(float2 x) {
+    return rcp2(add2(bc2(1.f), ex2x2(mul2(x, bc2(-LOG2E)))));
+}
+
 // ---------------------------------------------------------------- named barriers
 // Producer/consumer hand-off between warp groups: the producer arrives (no wait),
 // the consumer syncs; `n` counts all participating threads of both groups.

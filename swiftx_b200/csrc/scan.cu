@@ -171,26 +171,39 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
             }
             cp_async_commit();
         };
+        // per-(t, channel) work: each thread takes pairs of steps (t, t+1) of channel `ech`
+        const float2 bias2 = bc2(ebias), D2 = bc2(eD);
         auto derive = [&](int c) {
             const int r = c % RING, s = c & 1;
-#pragma unroll 4
-            for (int i = at; i < FT * SCH; i += NAUX) {
-                const int t = i / SCH;
-                const float raw = Elem<Tin>::to_f(S.dl[r][t][ech]) + ebias;
-                const float dte = p.softplus ? softplus_f(raw) : raw;
-                S.dd[s][t][ech] = f2(dte, dte * Elem<Tin>::to_f(S.u[r][t][ech]));
+#pragma unroll
+            for (int m = 0; m < FT * SCH / (2 * NAUX); ++m) {
+                const int t = 2 * (at / SCH + m * (NAUX / SCH));
+                const float2 raw = add2(f2(Elem<Tin>::to_f(S.dl[r][t][ech]), Elem<Tin>::to_f(S.dl[r][t + 1][ech])), bias2);
+                float2 dte = raw, dsp;
+                if (p.softplus) softplus2(raw, dte, dsp);
+                const float2 du = mul2(dte, f2(Elem<Tin>::to_f(S.u[r][t][ech]), Elem<Tin>::to_f(S.u[r][t + 1][ech])));
+                S.dd[s][t][ech] = f2(dte.x, du.x);
+                S.dd[s][t + 1][ech] = f2(dte.y, du.y);
             }
         };
         auto epilogue = [&](int c) {
             const int r = c % RING, s = c & 1, t0 = c * FT, nt = min(FT, p.L - t0);
-            if (!evalid) return;
-#pragma unroll 4
-            for (int t = at / SCH; t < nt; t += NAUX / SCH) {
-                const float4 q = *reinterpret_cast<const float4*>(&S.yp[s][t][ech][0]);
-                float y = (q.x + q.y) + (q.z + q.w);
-                y = fmaf(eD, Elem<Tin>::to_f(S.u[r][t][ech]), y);
-                if (HAS_Z) y *= silu_f(Elem<Tin>::to_f(S.z[r][t][ech]));
-                gout[(int64_t)(t0 + t) * p.D + ech] = Elem<Tout>::from_f(y);
+#pragma unroll
+            for (int m = 0; m < FT * SCH / (2 * NAUX); ++m) {
+                const int t = 2 * (at / SCH + m * (NAUX / SCH));
+                const float4 q0 = *reinterpret_cast<const float4*>(&S.yp[s][t][ech][0]);
+                const float4 q1 = *reinterpret_cast<const float4*>(&S.yp[s][t + 1][ech][0]);
+                float2 y = f2((q0.x + q0.y) + (q0.z + q0.w), (q1.x + q1.y) + (q1.z + q1.w));
+                y = fma2(D2, f2(Elem<Tin>::to_f(S.u[r][t][ech]), Elem<Tin>::to_f(S.u[r][t + 1][ech])), y);
+                if (HAS_Z) {
+                    const float2 zz = f2(Elem<Tin>::to_f(S.z[r][t][ech]), Elem<Tin>::to_f(S.z[r][t + 1][ech]));
+                    y = mul2(y, mul2(zz, sigmoid2(zz)));
+                }
+                if (evalid) {
+                    Tout* o = gout + (int64_t)(t0 + t) * p.D + ech;
+                    if (t < nt) o[0] = Elem<Tout>::from_f(y.x);
+                    if (t + 1 < nt) o[p.D] = Elem<Tout>::from_f(y.y);
+                }
             }
         };
 
@@ -411,29 +424,32 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
             }
             cp_async_commit();
         };
+        const float2 bias2 = bc2(ebias);
         auto derive = [&](int k) {
             const int r = k % RING, s = k & 1;
 #pragma unroll
-            for (int i = at; i < TCK * SCH; i += NAUX) {
-                const int t = i / SCH;
-                const float raw = Elem<Tin>::to_f(S.dl[r][t][ech]) + ebias;
-                const float uv = Elem<Tin>::to_f(S.u[r][t][ech]);
-                float dte = raw, dsp = 1.f;
-                if (p.softplus) {
-                    dte = softplus_f(raw);
-                    dsp = raw > 20.f ? 1.f : sigmoid_f(raw);
-                }
-                const float dov = Elem<Tin>::to_f(S.dout[r][t][ech]);
-                float dy = dov, q = 0.f;
+            for (int m = 0; m < TCK * SCH / (2 * NAUX); ++m) {
+                const int t = 2 * (at / SCH + m * (NAUX / SCH));
+                const float2 raw = add2(f2(Elem<Tin>::to_f(S.dl[r][t][ech]), Elem<Tin>::to_f(S.dl[r][t + 1][ech])), bias2);
+                const float2 uv = f2(Elem<Tin>::to_f(S.u[r][t][ech]), Elem<Tin>::to_f(S.u[r][t + 1][ech]));
+                const float2 dov = f2(Elem<Tin>::to_f(S.dout[r][t][ech]), Elem<Tin>::to_f(S.dout[r][t + 1][ech]));
+                float2 dte = raw, dsp = bc2(1.f);
+                if (p.softplus) softplus2(raw, dte, dsp);
+                float2 dy = dov, q = bc2(0.f);
                 if (HAS_Z) {
-                    const float zv = Elem<Tin>::to_f(S.z[r][t][ech]);
-                    const float sg = sigmoid_f(zv);
-                    dy = dov * zv * sg;
-                    q = dov * sg * fmaf(zv, 1.f - sg, 1.f);
+                    const float2 zv = f2(Elem<Tin>::to_f(S.z[r][t][ech]), Elem<Tin>::to_f(S.z[r][t + 1][ech]));
+                    const float2 sg = sigmoid2(zv);
+                    dy = mul2(dov, mul2(zv, sg));
+                    // d silu / dz = sg * (1 + z * (1 - sg))
+                    q = mul2(mul2(dov, sg), fma2(zv, add2(bc2(1.f), mul2(sg, bc2(-1.f))), bc2(1.f)));
                 }
-                S.dd[s][t][ech] = f2(dte, dte * uv);
-                S.dy[s][t][ech] = dy;
-                S.ee[s][t][ech] = make_float4(uv, dsp, q, dy);
+                const float2 du = mul2(dte, uv);
+                S.dd[s][t][ech] = f2(dte.x, du.x);
+                S.dd[s][t + 1][ech] = f2(dte.y, du.y);
+                S.dy[s][t][ech] = dy.x;
+                S.dy[s][t + 1][ech] = dy.y;
+                S.ee[s][t][ech] = make_float4(uv.x, dsp.x, q.x, dy.x);
+                S.ee[s][t + 1][ech] = make_float4(uv.y, dsp.y, q.y, dy.y);
             }
         };
         auto epilogue = [&](int k, int hh) {
