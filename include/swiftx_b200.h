@@ -76,6 +76,9 @@ int swx_abi_version(void);
 const char* swx_status_string(int status);
 /* sizeof(swx_scan_args), so a binding can check its mirror of the struct. */
 int64_t swx_scan_args_size(void);
+/* sizeof(swx_conv_args) and sizeof(swx_decode_args), for the same check. */
+int64_t swx_conv_args_size(void);
+int64_t swx_decode_args_size(void);
 
 /* Number of fp32 values of the forward's state checkpoints (one (D, 16) slab per
  * 16 time steps per batch row). */
@@ -99,6 +102,65 @@ int swx_scan_fwd(const swx_scan_args* args, void* stream);
  * (models/triton_scan.py:137-155).  Reductions (dA, dB, dC, dD, ddelta_bias) are
  * deterministic: fixed-order sums, no float atomics. */
 int swx_scan_bwd(const swx_scan_args* args, void* stream);
+
+/* ------------------------------------------------------------------ conv1d */
+/* Causal depthwise conv1d (+ SiLU).  x: (b, L, D) with element strides (x_sb, x_sl) and
+ * unit channel stride (e.g. the x half of the in_proj output, row stride 2D);
+ * weight (D, width) dense fp32 (= nn.Conv1d weight (D, 1, width)); bias (D,) optional;
+ * out, dout-sized gradients (b, L, D) dense, same dtype as x.  width <= 6. */
+typedef struct swx_conv_args {
+    int64_t batch, seqlen, dim, width;
+    int32_t dtype;           /* SWX_DTYPE_F32 | SWX_DTYPE_BF16 for x, out, dout, dx */
+    int32_t silu;            /* apply SiLU after the conv */
+    const void* x; int64_t x_sb, x_sl;
+    const float* weight;
+    const float* bias;
+    void* out;
+    const void* dout; int64_t dout_sb, dout_sl;
+    void* dx;
+    float* dweight;          /* (D, width) */
+    float* dbias;            /* (D,) optional */
+    void* workspace; int64_t workspace_bytes;  /* >= swx_conv1d_bwd_workspace_bytes() */
+} swx_conv_args;
+
+/* out = silu(conv(x) + bias), the conv segment of SiftBlock.forward
+ * (models/sift_block.py:62-65, 117-118: nn.Conv1d(padding=width-1) keeping the first
+ * L outputs, then F.silu). */
+int swx_conv1d_fwd(const swx_conv_args* args, void* stream);
+/* Backward of swx_conv1d_fwd (recomputes the pre-activation); dweight / dbias are
+ * fixed-order sums (deterministic). */
+int swx_conv1d_bwd(const swx_conv_args* args, void* stream);
+int64_t swx_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim, int64_t width);
+
+/* ------------------------------------------------------------------ decode step */
+#define SWX_DECODE_CONV 1   /* roll the conv window, append x, xc = silu(conv + bias) */
+#define SWX_DECODE_SSM 2    /* h = exp(delta*A)*h + delta*B*xc ; out = (<h,C> + D*xc)*silu(z) */
+
+/* One token of recurrent generation, fp32.  Row strides are in elements; the channel
+ * (and state) stride is 1.  States are updated in place. */
+typedef struct swx_decode_args {
+    int64_t batch, dim, dstate, width;
+    int32_t delta_softplus;
+    int32_t mode;                     /* SWX_DECODE_CONV, SWX_DECODE_SSM, or both */
+    const float* x; int64_t x_sb;     /* (b, D): token input (CONV) or xc (SSM only) */
+    const float* z; int64_t z_sb;     /* (b, D) optional gate */
+    const float* delta; int64_t delta_sb;  /* (b, D) delta before softplus */
+    const float* B; int64_t B_sb;     /* (b, N) */
+    const float* C; int64_t C_sb;     /* (b, N) */
+    const float* conv_weight;         /* (D, width) */
+    const float* conv_bias;           /* (D,) optional */
+    const float* A;                   /* (D, N) */
+    const float* Dskip;               /* (D,) optional */
+    const float* delta_bias;          /* (D,) optional */
+    float* conv_state;                /* (b, D, width) in/out */
+    float* ssm_state;                 /* (b, D, N) in/out */
+    float* xc_out;                    /* (b, D) optional: the post-conv activation */
+    float* out;                       /* (b, D) */
+} swx_decode_args;
+
+/* Replaces SiftBlock.step's conv-window roll, conv dot + bias + SiLU and in-place
+ * state update / readout / gate (models/sift_block.py:153-175). */
+int swx_decode_step(const swx_decode_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -43,6 +43,35 @@ class ScanArgs(ctypes.Structure):
     ]
 
 
+class ConvArgs(ctypes.Structure):
+    """Mirror of ``swx_conv_args``."""
+    _fields_ = [
+        ("batch", i64), ("seqlen", i64), ("dim", i64), ("width", i64),
+        ("dtype", i32), ("silu", i32),
+        ("x", vp), ("x_sb", i64), ("x_sl", i64),
+        ("weight", vp), ("bias", vp), ("out", vp),
+        ("dout", vp), ("dout_sb", i64), ("dout_sl", i64),
+        ("dx", vp), ("dweight", vp), ("dbias", vp),
+        ("workspace", vp), ("workspace_bytes", i64),
+    ]
+
+
+SWX_DECODE_CONV = 1
+SWX_DECODE_SSM = 2
+
+
+class DecodeArgs(ctypes.Structure):
+    """Mirror of ``swx_decode_args``."""
+    _fields_ = [
+        ("batch", i64), ("dim", i64), ("dstate", i64), ("width", i64),
+        ("delta_softplus", i32), ("mode", i32),
+        ("x", vp), ("x_sb", i64), ("z", vp), ("z_sb", i64),
+        ("delta", vp), ("delta_sb", i64), ("B", vp), ("B_sb", i64), ("C", vp), ("C_sb", i64),
+        ("conv_weight", vp), ("conv_bias", vp), ("A", vp), ("Dskip", vp), ("delta_bias", vp),
+        ("conv_state", vp), ("ssm_state", vp), ("xc_out", vp), ("out", vp),
+    ]
+
+
 _lib = None
 
 
@@ -59,17 +88,22 @@ def load():
     lib.swx_abi_version.restype = ctypes.c_int
     lib.swx_status_string.restype = ctypes.c_char_p
     lib.swx_status_string.argtypes = [ctypes.c_int]
-    lib.swx_scan_args_size.restype = i64
-    if lib.swx_scan_args_size() != ctypes.sizeof(ScanArgs):
-        raise RuntimeError("swx_scan_args layout mismatch between the library and its binding")
+    for fn, st in (("swx_scan_args_size", ScanArgs), ("swx_conv_args_size", ConvArgs),
+                   ("swx_decode_args_size", DecodeArgs)):
+        getattr(lib, fn).restype = i64
+        if getattr(lib, fn)() != ctypes.sizeof(st):
+            raise RuntimeError(f"{st.__name__} layout mismatch between the library and its binding")
     lib.swx_scan_checkpoint_floats.restype = i64
     lib.swx_scan_checkpoint_floats.argtypes = [i64, i64, i64]
     lib.swx_scan_bwd_workspace_bytes.restype = i64
     lib.swx_scan_bwd_workspace_bytes.argtypes = [i64, i64, i64]
-    for name in ("swx_scan_fwd", "swx_scan_bwd"):
+    for name, st in (("swx_scan_fwd", ScanArgs), ("swx_scan_bwd", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
+                     ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs)):
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
-        fn.argtypes = [ctypes.POINTER(ScanArgs), vp]
+        fn.argtypes = [ctypes.POINTER(st), vp]
+    lib.swx_conv1d_bwd_workspace_bytes.restype = i64
+    lib.swx_conv1d_bwd_workspace_bytes.argtypes = [i64, i64, i64, i64]
     _lib = lib
     return lib
 

@@ -85,6 +85,8 @@ extern "C" {
 int swx_abi_version(void) { return SWX_ABI_VERSION; }
 
 int64_t swx_scan_args_size(void) { return (int64_t)sizeof(swx_scan_args); }
+int64_t swx_conv_args_size(void) { return (int64_t)sizeof(swx_conv_args); }
+int64_t swx_decode_args_size(void) { return (int64_t)sizeof(swx_decode_args); }
 
 const char* swx_status_string(int status) {
     switch (status) {

@@ -1,0 +1,238 @@
+// Causal depthwise conv1d (+ SiLU) forward / backward for sm_100a.
+//
+// out[b,t,d] = silu(bias[d] + sum_{k<K} w[d,k] * x[b, t-(K-1)+k, d]),  x[s<0] = 0
+// (nn.Conv1d(D, D, K, groups=D, padding=K-1) keeping the first L outputs, then SiLU:
+// models/sift_block.py:62-65,117-118).
+//
+// The op is HBM-bound (K=4 multiply-adds per element), so the layout is chosen for
+// coalescing: a thread owns one channel and a tile of consecutive steps, a warp covers
+// 32 adjacent channels (128 contiguous bytes per step for fp32), and the K-1 step halo is
+// kept in registers as a sliding window.  x may be the strided x half of the in_proj
+// output (row stride 2D); no copy is made.
+//
+// Backward recomputes the pre-activation from x, so nothing but the inputs is saved.
+// dw and dbias are per-(batch row, step tile) partials summed in fixed order by a
+// second kernel (deterministic, no float atomics).
+#include "common.cuh"
+
+namespace swx {
+
+constexpr int CONV_MAXK = 6;
+constexpr int CONV_TT = 64;       // steps per thread
+constexpr int CONV_NT = 128;      // threads (channels) per CTA
+
+struct ConvDev {
+    int b, L, D, K, silu;
+    const void* x; int64_t x_sb, x_sl;
+    const float* w; const float* bias;
+    void* out;
+    const void* dout; int64_t do_sb, do_sl;
+    void* dx; float* dw; float* dbias;
+    float* ws;        // (b, ntiles, D, K+1) partials of dw | dbias
+    int ntiles;
+};
+
+template <typename T, int K>
+__global__ void __launch_bounds__(CONV_NT) conv_fwd_kernel(const ConvDev p) {
+    const int d = blockIdx.x * CONV_NT + threadIdx.x;
+    const int t0 = blockIdx.y * CONV_TT;
+    const int bi = blockIdx.z;
+    if (d >= p.D) return;
+    const T* x = static_cast<const T*>(p.x) + bi * p.x_sb + d;
+    T* out = static_cast<T*>(p.out) + (int64_t)bi * p.L * p.D + d;
+    float w[K], win[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) w[k] = p.w[(int64_t)d * K + k];
+    const float bias = p.bias ? p.bias[d] : 0.f;
+    // window slot k holds x[t-(K-1)+k]; prime it with the K-1 steps before the tile
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) {
+        const int s = t0 - (K - 1) + k;
+        win[k] = s >= 0 ? Elem<T>::to_f(x[(int64_t)s * p.x_sl]) : 0.f;
+    }
+    const int tend = min(t0 + CONV_TT, p.L);
+    for (int t = t0; t < tend; ++t) {
+        win[K - 1] = Elem<T>::to_f(x[(int64_t)t * p.x_sl]);
+        float acc = bias;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(w[k], win[k], acc);
+        out[(int64_t)t * p.D] = Elem<T>::from_f(p.silu ? silu_f(acc) : acc);
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) win[k] = win[k + 1];
+    }
+}
+
+template <typename T, int K>
+__global__ void __launch_bounds__(CONV_NT) conv_bwd_kernel(const ConvDev p) {
+    const int d = blockIdx.x * CONV_NT + threadIdx.x;
+    const int tile = blockIdx.y;
+    const int t0 = tile * CONV_TT;
+    const int bi = blockIdx.z;
+    if (d >= p.D) return;
+    const T* x = static_cast<const T*>(p.x) + bi * p.x_sb + d;
+    const T* dout = static_cast<const T*>(p.dout) + bi * p.do_sb + d;
+    T* dx = static_cast<T*>(p.dx) + (int64_t)bi * p.L * p.D + d;
+    float w[K];
+#pragma unroll
+    for (int k = 0; k < K; ++k) w[k] = p.w[(int64_t)d * K + k];
+    const float bias = p.bias ? p.bias[d] : 0.f;
+
+    // xw[k] = x[s-(K-1)+k] for the current step s; gq[k] = dL/dpre at step s-(K-1)+k
+    float xw[K], gq[K], dwacc[K];
+    float dbacc = 0.f;
+#pragma unroll
+    for (int k = 0; k < K; ++k) { dwacc[k] = 0.f; gq[k] = 0.f; }
+#pragma unroll
+    for (int k = 0; k < K - 1; ++k) {
+        const int s = t0 - (K - 1) + k;
+        xw[k] = s >= 0 ? Elem<T>::to_f(x[(int64_t)s * p.x_sl]) : 0.f;
+    }
+    // dx[t] = sum_k w[k] * gp(t + K-1-k): walk s over the tile plus a K-1 step halo
+    const int tend = min(t0 + CONV_TT, p.L);
+    const int send = min(tend + K - 1, p.L);
+    for (int s = t0; s < send; ++s) {
+        xw[K - 1] = Elem<T>::to_f(x[(int64_t)s * p.x_sl]);
+        float acc = bias;
+#pragma unroll
+        for (int k = 0; k < K; ++k) acc = fmaf(w[k], xw[k], acc);
+        float g = Elem<T>::to_f(dout[(int64_t)s * p.do_sl]);
+        if (p.silu) {
+            const float sg = sigmoid_f(acc);
+            g *= sg * fmaf(acc, 1.f - sg, 1.f);
+        }
+        if (s < tend) {                 // dw, dbias partials of the steps this tile owns
+            dbacc += g;
+#pragma unroll
+            for (int k = 0; k < K; ++k) dwacc[k] = fmaf(g, xw[k], dwacc[k]);
+        }
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) gq[k] = gq[k + 1];
+        gq[K - 1] = g;                  // gq holds gp(s-K+1 .. s)
+        const int t = s - (K - 1);
+        if (t >= t0) {
+            float a = 0.f;
+#pragma unroll
+            for (int k = 0; k < K; ++k) a = fmaf(w[k], gq[K - 1 - k], a);
+            dx[(int64_t)t * p.D] = Elem<T>::from_f(a);
+        }
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) xw[k] = xw[k + 1];
+    }
+    // steps whose window reaches past the end of the sequence see gp = 0 there
+    for (int t = send - (K - 1); t < tend; ++t) {
+#pragma unroll
+        for (int k = 0; k < K - 1; ++k) gq[k] = gq[k + 1];
+        gq[K - 1] = 0.f;
+        if (t >= t0) {
+            float a = 0.f;
+#pragma unroll
+            for (int k = 0; k < K; ++k) a = fmaf(w[k], gq[K - 1 - k], a);
+            dx[(int64_t)t * p.D] = Elem<T>::from_f(a);
+        }
+    }
+    float* ws = p.ws + (((int64_t)bi * p.ntiles + tile) * p.D + d) * (K + 1);
+#pragma unroll
+    for (int k = 0; k < K; ++k) ws[k] = dwacc[k];
+    ws[K] = dbacc;
+}
+
+__global__ void conv_bwd_finalize_kernel(const ConvDev p) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;      // (d, k) with k <= K
+    const int K1 = p.K + 1;
+    if (i >= p.D * K1) return;
+    const int d = i / K1, k = i % K1;
+    float s = 0.f;
+    for (int bi = 0; bi < p.b; ++bi)
+        for (int tl = 0; tl < p.ntiles; ++tl)
+            s += p.ws[(((int64_t)bi * p.ntiles + tl) * p.D + d) * K1 + k];
+    if (k < p.K) p.dw[(int64_t)d * p.K + k] = s;
+    else if (p.dbias) p.dbias[d] = s;
+}
+
+template <typename T, int K>
+static void launch_k(const ConvDev& p, dim3 grid, cudaStream_t st, bool bwd) {
+    if (bwd) conv_bwd_kernel<T, K><<<grid, CONV_NT, 0, st>>>(p);
+    else conv_fwd_kernel<T, K><<<grid, CONV_NT, 0, st>>>(p);
+}
+
+template <typename T>
+static void dispatch_k(const ConvDev& p, dim3 grid, cudaStream_t st, bool bwd) {
+    switch (p.K) {
+        case 1: launch_k<T, 1>(p, grid, st, bwd); break;
+        case 2: launch_k<T, 2>(p, grid, st, bwd); break;
+        case 3: launch_k<T, 3>(p, grid, st, bwd); break;
+        case 4: launch_k<T, 4>(p, grid, st, bwd); break;
+        case 5: launch_k<T, 5>(p, grid, st, bwd); break;
+        default: launch_k<T, 6>(p, grid, st, bwd); break;
+    }
+}
+
+}  // namespace swx
+
+// ----------------------------------------------------------------- C ABI
+namespace {
+int conv_es(int dt) { return dt == SWX_DTYPE_F32 ? 4 : (dt == SWX_DTYPE_BF16 ? 2 : 0); }
+
+int conv_check(const swx_conv_args* a) {
+    if (!a) return SWX_ERR_INVALID_ARG;
+    if (a->batch < 0 || a->seqlen < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
+    if (a->width < 1 || a->width > swx::CONV_MAXK) return SWX_ERR_UNSUPPORTED;
+    if (conv_es(a->dtype) == 0) return SWX_ERR_UNSUPPORTED;
+    if (a->batch > 65535 || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
+    if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
+    if (!a->x || !a->weight) return SWX_ERR_INVALID_ARG;
+    return SWX_OK;
+}
+
+swx::ConvDev conv_pack(const swx_conv_args* a) {
+    swx::ConvDev p{};
+    p.b = (int)a->batch; p.L = (int)a->seqlen; p.D = (int)a->dim; p.K = (int)a->width;
+    p.silu = a->silu ? 1 : 0;
+    p.x = a->x; p.x_sb = a->x_sb; p.x_sl = a->x_sl;
+    p.w = a->weight; p.bias = a->bias;
+    p.out = a->out;
+    p.dout = a->dout; p.do_sb = a->dout_sb; p.do_sl = a->dout_sl;
+    p.dx = a->dx; p.dw = a->dweight; p.dbias = a->dbias;
+    p.ntiles = (int)((a->seqlen + swx::CONV_TT - 1) / swx::CONV_TT);
+    return p;
+}
+}  // namespace
+
+extern "C" {
+
+int64_t swx_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim, int64_t width) {
+    const int64_t ntiles = (seqlen + swx::CONV_TT - 1) / swx::CONV_TT;
+    return batch * ntiles * dim * (width + 1) * 4;
+}
+
+int swx_conv1d_fwd(const swx_conv_args* a, void* stream) {
+    int s = conv_check(a);
+    if (s != SWX_OK || a->batch * a->seqlen * a->dim == 0) return s;
+    if (!a->out) return SWX_ERR_INVALID_ARG;
+    swx::ConvDev p = conv_pack(a);
+    dim3 grid((p.D + swx::CONV_NT - 1) / swx::CONV_NT, p.ntiles, p.b);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (a->dtype == SWX_DTYPE_F32) swx::dispatch_k<float>(p, grid, st, false);
+    else swx::dispatch_k<__nv_bfloat16>(p, grid, st, false);
+    return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
+}
+
+int swx_conv1d_bwd(const swx_conv_args* a, void* stream) {
+    int s = conv_check(a);
+    if (s != SWX_OK || a->batch * a->seqlen * a->dim == 0) return s;
+    if (!a->dout || !a->dx || !a->dweight || !a->workspace) return SWX_ERR_INVALID_ARG;
+    if (a->workspace_bytes < swx_conv1d_bwd_workspace_bytes(a->batch, a->seqlen, a->dim, a->width))
+        return SWX_ERR_INVALID_ARG;
+    swx::ConvDev p = conv_pack(a);
+    p.ws = static_cast<float*>(a->workspace);
+    dim3 grid((p.D + swx::CONV_NT - 1) / swx::CONV_NT, p.ntiles, p.b);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (a->dtype == SWX_DTYPE_F32) swx::dispatch_k<float>(p, grid, st, true);
+    else swx::dispatch_k<__nv_bfloat16>(p, grid, st, true);
+    if (cudaGetLastError() != cudaSuccess) return SWX_ERR_CUDA;
+    const int n = p.D * (p.K + 1);
+    swx::conv_bwd_finalize_kernel<<<(n + 255) / 256, 256, 0, st>>>(p);
+    return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
+}
+
+}  // extern "C"

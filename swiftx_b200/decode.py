@@ -1,0 +1,90 @@
+"""Recurrent decode step on B200 (SiftBlock.step, models/sift_block.py:153-175).
+
+``decode_conv_step``  -- roll the conv window, append x, xc = silu(conv + bias) (in place);
+``decode_ssm_step``   -- h = exp(delta*A)*h + delta*B*xc; out = (<h,C> + D*xc)*silu(z) (in place);
+``decode_step``       -- both in one launch when delta/B/C are already known.
+All tensors fp32 on CUDA; row strides may differ from dense (e.g. the x/z halves of
+the in_proj output), the channel / state stride must be 1.
+"""
+import torch
+
+from . import _lib
+
+
+def _row(t):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("swiftx_b200 decode runs on CUDA tensors only (no CPU path)")
+    if t.dtype != torch.float32:
+        raise ValueError("decode step expects fp32 tensors")
+    return t if t.stride(-1) == 1 else t.contiguous()
+
+
+def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, delta=None, B=None,
+          C=None, A=None, Dskip=None, delta_bias=None, ssm_state=None, delta_softplus=True,
+          want_xc=False):
+    lib = _lib.load()
+    x, z, delta, B, C = map(_row, (x, z, delta, B, C))
+    b, D = x.shape
+    a = _lib.DecodeArgs()
+    a.batch, a.dim, a.mode = b, D, mode
+    a.delta_softplus = 1 if delta_softplus else 0
+    a.x, a.x_sb = x.data_ptr(), x.stride(0)
+    keep = []
+    if mode & _lib.SWX_DECODE_CONV:
+        if not conv_state.is_contiguous() or conv_state.dtype != torch.float32:
+            raise ValueError("conv_state must be a dense fp32 (b, D, K) tensor")
+        w = conv_weight.detach().reshape(D, -1).float().contiguous()
+        keep.append(w)
+        a.width = w.shape[1]
+        a.conv_weight, a.conv_state = w.data_ptr(), conv_state.data_ptr()
+        if conv_bias is not None:
+            cb = conv_bias.detach().float().contiguous()
+            keep.append(cb)
+            a.conv_bias = cb.data_ptr()
+    xc = None
+    if want_xc or not (mode & _lib.SWX_DECODE_SSM):
+        xc = torch.empty((b, D), device=x.device, dtype=torch.float32)
+        a.xc_out = xc.data_ptr()
+    out = None
+    if mode & _lib.SWX_DECODE_SSM:
+        if not ssm_state.is_contiguous() or ssm_state.dtype != torch.float32:
+            raise ValueError("ssm_state must be a dense fp32 (b, D, N) tensor")
+        Af = A.detach().float().contiguous()
+        keep.append(Af)
+        a.dstate = Af.shape[1]
+        out = torch.empty((b, D), device=x.device, dtype=torch.float32)
+        a.delta, a.delta_sb = delta.data_ptr(), delta.stride(0)
+        a.B, a.B_sb, a.C, a.C_sb = B.data_ptr(), B.stride(0), C.data_ptr(), C.stride(0)
+        a.A, a.ssm_state, a.out = Af.data_ptr(), ssm_state.data_ptr(), out.data_ptr()
+        if z is not None:
+            a.z, a.z_sb = z.data_ptr(), z.stride(0)
+        for name, t in (("Dskip", Dskip), ("delta_bias", delta_bias)):
+            if t is not None:
+                tf = t.detach().float().contiguous()
+                keep.append(tf)
+                setattr(a, name, tf.data_ptr())
+    _lib.check(lib.swx_decode_step(a, _lib.stream_ptr(x.device)), "swx_decode_step")
+    return out, xc
+
+
+def decode_conv_step(x, conv_state, conv_weight, conv_bias=None):
+    """Returns xc (b, D); conv_state (b, D, K) is updated in place."""
+    return _call(_lib.SWX_DECODE_CONV, x, conv_state, conv_weight, conv_bias)[1]
+
+
+def decode_ssm_step(xc, delta, B, C, A, ssm_state, Dskip=None, z=None, delta_bias=None,
+                    delta_softplus=True):
+    """Returns out (b, D); ssm_state (b, D, N) is updated in place."""
+    return _call(_lib.SWX_DECODE_SSM, xc, z=z, delta=delta, B=B, C=C, A=A, Dskip=Dskip,
+                 delta_bias=delta_bias, ssm_state=ssm_state, delta_softplus=delta_softplus)[0]
+
+
+def decode_step(x, conv_state, conv_weight, conv_bias, delta, B, C, A, ssm_state, Dskip=None,
+                z=None, delta_bias=None, delta_softplus=True, return_xc=False):
+    """Fused conv-window shift + conv + SiLU + state update + readout + gate.
+    Returns out (b, D) (and xc when asked); both states are updated in place."""
+    out, xc = _call(_lib.SWX_DECODE_CONV | _lib.SWX_DECODE_SSM, x, conv_state, conv_weight, conv_bias,
+                    z, delta, B, C, A, Dskip, delta_bias, ssm_state, delta_softplus, want_xc=return_xc)
+    return (out, xc) if return_xc else out

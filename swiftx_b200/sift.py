@@ -1,0 +1,236 @@
+"""Sift (Mamba-1) block and language model on the B200 hot path.
+
+A caller-side mirror of the reference's models/sift_block.py and models/sift_model.py:
+same constructor arguments, same parameter names and shapes (so reference state_dicts
+load unchanged: in_proj, conv1d (D,1,K)+bias, x_proj, dt_proj, A_log, D, out_proj, norm,
+norm_f, embedding, tied lm_head), same forward / step / generate behaviour.  The mixer
+runs on the sm_100a kernels:
+
+  in_proj (cuBLAS) -> causal conv1d + SiLU (kernel, reads the strided x half in place)
+  -> x_proj (cuBLAS) -> dt_proj without bias (cuBLAS)
+  -> fused selective scan with softplus(delta + dt_proj.bias), D skip and the SiLU(z)
+     gate (kernel) -> out_proj (cuBLAS)
+
+and decode runs the conv-window / state-update kernels around the x_proj / dt_proj GEMVs.
+Fusing the gate is exactly the reference's y * silu(z) when no SiftX pathway mixing is
+configured (models/sift_block.py:132-142); pathway gating is not supported here.
+"""
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from .conv import causal_conv1d_fn
+from .decode import decode_conv_step, decode_ssm_step
+from .selective_scan import selective_scan_fn
+
+
+def init_A_log(d_inner, d_state):
+    """S4D-real: A_n = -(n+1) for every channel, stored as log(-A) (models/ssm.py:43-51)."""
+    A = torch.arange(1, d_state + 1, dtype=torch.float32).repeat(d_inner, 1)
+    return torch.log(A)
+
+
+def init_dt_proj(dt_proj, dt_rank, dt_min=1e-3, dt_max=1e-1, dt_init_floor=1e-4, dt_scale=1.0):
+    """softplus(bias) log-uniform in [dt_min, dt_max]; weights U(+-dt_rank^-0.5)
+    (models/ssm.py:54-71)."""
+    std = dt_rank ** -0.5 * dt_scale
+    nn.init.uniform_(dt_proj.weight, -std, std)
+    d_inner = dt_proj.out_features
+    dt = torch.exp(torch.rand(d_inner) * (math.log(dt_max) - math.log(dt_min))
+                   + math.log(dt_min)).clamp(min=dt_init_floor)
+    inv_dt = dt + torch.log(-torch.expm1(-dt))        # inverse softplus
+    with torch.no_grad():
+        dt_proj.bias.copy_(inv_dt)
+    dt_proj.bias._no_reinit = True
+
+
+class SiftBlock(nn.Module):
+    def __init__(self, d_model, d_state=16, d_conv=4, expand=2, dt_rank="auto", dt_min=1e-3,
+                 dt_max=1e-1, conv_bias=True, bias=False, scan_impl="fast", scan_mode="auto",
+                 timescales=None, pathway_gate=False):
+        super().__init__()
+        if pathway_gate:
+            raise NotImplementedError("SiftX pathway gating is not part of the B200 hot path")
+        self.d_model = d_model
+        self.d_state = d_state
+        self.d_conv = d_conv
+        self.d_inner = expand * d_model
+        self.dt_rank = math.ceil(d_model / 16) if dt_rank == "auto" else dt_rank
+        self.scan_impl = scan_impl          # every impl / mode runs the same kernel
+        self.scan_mode = scan_mode
+        self.in_proj = nn.Linear(d_model, 2 * self.d_inner, bias=bias)
+        self.conv1d = nn.Conv1d(self.d_inner, self.d_inner, kernel_size=d_conv, groups=self.d_inner,
+                                padding=d_conv - 1, bias=conv_bias)
+        self.x_proj = nn.Linear(self.d_inner, self.dt_rank + 2 * d_state, bias=False)
+        self.dt_proj = nn.Linear(self.dt_rank, self.d_inner, bias=True)
+        init_dt_proj(self.dt_proj, self.dt_rank, dt_min, dt_max)
+        self.timescales = [tuple(t) for t in timescales] if timescales else None
+        if self.timescales:
+            bounds = torch.linspace(0, self.d_inner, len(self.timescales) + 1).round().long().tolist()
+            for i, (lo, hi) in enumerate(self.timescales):
+                a, b = bounds[i], bounds[i + 1]
+                tmp = nn.Linear(self.dt_rank, b - a, bias=True)
+                init_dt_proj(tmp, self.dt_rank, lo, hi)
+                with torch.no_grad():
+                    self.dt_proj.bias[a:b] = tmp.bias
+        self.pathway = None
+        self.A_log = nn.Parameter(init_A_log(self.d_inner, d_state))
+        self.A_log._no_weight_decay = True
+        self.D = nn.Parameter(torch.ones(self.d_inner))
+        self.D._no_weight_decay = True
+        self.out_proj = nn.Linear(self.d_inner, d_model, bias=bias)
+
+    def _split(self, x):
+        x_dbl = self.x_proj(x)
+        dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
+        return F.linear(dt, self.dt_proj.weight), B, C      # dt_proj bias fused into the scan
+
+    def forward(self, hidden):
+        """hidden: (b, L, d_model) -> (b, L, d_model)"""
+        xz = self.in_proj(hidden)
+        x, z = xz.chunk(2, dim=-1)                        # strided views, row stride 2D
+        x = causal_conv1d_fn(x, self.conv1d.weight, self.conv1d.bias, "silu")
+        delta, B, C = self._split(x)
+        A = -torch.exp(self.A_log.float())
+        with torch.autocast(device_type=x.device.type, enabled=False):
+            y = selective_scan_fn(x, delta, A, B, C, self.D.float(), z=z,
+                                  delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
+        return self.out_proj(y.to(xz.dtype))
+
+    def allocate_state(self, batch, device=None, dtype=torch.float32):
+        conv_state = torch.zeros(batch, self.d_inner, self.d_conv, device=device, dtype=dtype)
+        ssm_state = torch.zeros(batch, self.d_inner, self.d_state, device=device, dtype=dtype)
+        return conv_state, ssm_state
+
+    def step(self, hidden, state):
+        """hidden: (b, d_model) one token; state (conv_state, ssm_state) updated in place."""
+        conv_state, ssm_state = state
+        xz = self.in_proj(hidden).float()
+        x, z = xz.chunk(2, dim=-1)
+        xc = decode_conv_step(x, conv_state, self.conv1d.weight, self.conv1d.bias)
+        delta, B, C = self._split(xc)
+        y = decode_ssm_step(xc, delta.float(), B.float(), C.float(), -torch.exp(self.A_log.float()),
+                            ssm_state, Dskip=self.D, z=z, delta_bias=self.dt_proj.bias)
+        return self.out_proj(y.to(self.out_proj.weight.dtype))
+
+
+class RMSNorm(nn.Module):
+    def __init__(self, d, eps=1e-5):
+        super().__init__()
+        self.eps = eps
+        self.weight = nn.Parameter(torch.ones(d))
+
+    def forward(self, x):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
+
+
+@dataclass
+class SiftConfig:
+    vocab_size: int = 65
+    d_model: int = 128
+    n_layers: int = 4
+    d_state: int = 16
+    d_conv: int = 4
+    expand: int = 2
+    dt_rank: object = "auto"
+    scan_impl: str = "fast"
+    scan_mode: str = "auto"
+    tie_embeddings: bool = True
+    timescales: object = None
+    pathway_gate: bool = False
+
+
+class ResidualBlock(nn.Module):
+    def __init__(self, cfg):
+        super().__init__()
+        self.norm = RMSNorm(cfg.d_model)
+        self.mixer = SiftBlock(cfg.d_model, d_state=cfg.d_state, d_conv=cfg.d_conv, expand=cfg.expand,
+                               dt_rank=cfg.dt_rank, scan_impl=cfg.scan_impl, scan_mode=cfg.scan_mode,
+                               timescales=cfg.timescales, pathway_gate=cfg.pathway_gate)
+
+    def forward(self, x):
+        return x + self.mixer(self.norm(x))
+
+    def step(self, x, state):
+        return x + self.mixer.step(self.norm(x), state)
+
+
+class SiftBackbone(nn.Module):
+    def __init__(self, cfg):
+        super().__init__()
+        self.layers = nn.ModuleList([ResidualBlock(cfg) for _ in range(cfg.n_layers)])
+        self.norm_f = RMSNorm(cfg.d_model)
+        self._init_weights(cfg.n_layers)
+
+    def _init_weights(self, n_layers):
+        for _, m in self.named_modules():
+            if isinstance(m, nn.Linear) and m.bias is not None and not getattr(m.bias, "_no_reinit", False):
+                nn.init.zeros_(m.bias)
+        for layer in self.layers:
+            w = layer.mixer.out_proj.weight
+            nn.init.kaiming_uniform_(w, a=math.sqrt(5))
+            with torch.no_grad():
+                w /= math.sqrt(n_layers)
+
+    def forward(self, x):
+        for layer in self.layers:
+            x = layer(x)
+        return self.norm_f(x)
+
+
+class SiftLM(nn.Module):
+    def __init__(self, cfg: SiftConfig):
+        super().__init__()
+        self.cfg = cfg
+        self.embedding = nn.Embedding(cfg.vocab_size, cfg.d_model)
+        nn.init.normal_(self.embedding.weight, std=0.02)
+        self.backbone = SiftBackbone(cfg)
+        self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)
+        if cfg.tie_embeddings:
+            self.lm_head.weight = self.embedding.weight
+
+    def forward(self, idx, targets=None):
+        logits = self.lm_head(self.backbone(self.embedding(idx)))
+        loss = None
+        if targets is not None:
+            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), targets.reshape(-1))
+        return logits, loss
+
+    def allocate_state(self, batch, device=None):
+        return [l.mixer.allocate_state(batch, device) for l in self.backbone.layers]
+
+    def step(self, token, state):
+        x = self.embedding(token)
+        for layer, s in zip(self.backbone.layers, state):
+            x = layer.step(x, s)
+        return self.lm_head(self.backbone.norm_f(x))
+
+    @torch.no_grad()
+    def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None):
+        state = self.allocate_state(idx.shape[0], idx.device)
+        logits = None
+        for t in range(idx.shape[1]):
+            logits = self.step(idx[:, t], state)
+        out = [idx]
+        for _ in range(max_new_tokens):
+            nxt = sample(logits, temperature, top_k)
+            out.append(nxt[:, None])
+            logits = self.step(nxt, state)
+        return torch.cat(out, dim=1)
+
+
+def sample(logits, temperature=1.0, top_k=None):
+    if temperature == 0:
+        return logits.argmax(-1)
+    logits = logits / temperature
+    if top_k is not None:
+        v, _ = torch.topk(logits, min(top_k, logits.size(-1)))
+        logits = logits.masked_fill(logits < v[:, [-1]], float("-inf"))
+    return torch.multinomial(F.softmax(logits.float(), -1), 1).squeeze(-1)
+
+
+def count_params(model):
+    return sum(p.numel() for p in model.parameters())

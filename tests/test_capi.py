@@ -1,0 +1,81 @@
+"""The C-ABI library loads and exports every entry point include/swiftx_b200.h declares;
+argument validation runs on the host before any CUDA call (no GPU needed)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from swiftx_b200 import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    src = open(os.path.join(ROOT, "include", "swiftx_b200.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(swx_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 10
+    for n in names:
+        assert hasattr(lib, n), f"missing export {n}"
+
+
+def test_struct_mirrors_match():
+    lib = _lib.load()
+    assert lib.swx_scan_args_size() == ctypes.sizeof(_lib.ScanArgs)
+    assert lib.swx_conv_args_size() == ctypes.sizeof(_lib.ConvArgs)
+    assert lib.swx_decode_args_size() == ctypes.sizeof(_lib.DecodeArgs)
+    assert lib.swx_abi_version() == 1
+
+
+def test_status_strings():
+    lib = _lib.load()
+    for code in range(5):
+        assert lib.swx_status_string(code)
+    assert lib.swx_status_string(0) == b"ok"
+
+
+def test_sizes_of_checkpoints_and_workspace():
+    lib = _lib.load()
+    assert lib.swx_scan_checkpoint_floats(8, 2048, 512) == 8 * 128 * 512 * 16
+    assert lib.swx_scan_checkpoint_floats(1, 17, 3) == 1 * 2 * 3 * 16
+    assert lib.swx_scan_bwd_workspace_bytes(8, 2048, 512) >= 16 * 8 * 2048 * 32 * 4
+    assert lib.swx_conv1d_bwd_workspace_bytes(2, 130, 8, 4) == 2 * 3 * 8 * 5 * 4
+
+
+def test_host_side_validation_without_gpu():
+    lib = _lib.load()
+    # NULL argument block
+    assert lib.swx_scan_fwd(None, None) == _lib.SWX_ERR_INVALID_ARG
+    a = _lib.ScanArgs()
+    a.batch, a.seqlen, a.dim, a.dstate = 1, 4, 4, 17          # N > 16
+    assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_UNSUPPORTED
+    a.dstate, a.in_dtype = 16, 7                              # unknown dtype
+    assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_UNSUPPORTED
+    a.in_dtype = 0                                            # missing pointers
+    assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_INVALID_ARG
+    assert lib.swx_scan_bwd(a, None) == _lib.SWX_ERR_INVALID_ARG
+    a.seqlen = 0                                              # empty problem: nothing to do
+    assert lib.swx_scan_fwd(a, None) == _lib.SWX_OK
+    c = _lib.ConvArgs()
+    c.batch, c.seqlen, c.dim, c.width = 1, 4, 4, 9            # width > 6
+    assert lib.swx_conv1d_fwd(c, None) == _lib.SWX_ERR_UNSUPPORTED
+    d = _lib.DecodeArgs()
+    d.batch, d.dim, d.mode = 1, 4, 0                          # no mode
+    assert lib.swx_decode_step(d, None) == _lib.SWX_ERR_INVALID_ARG
+
+
+def test_cpu_tensors_are_rejected_not_computed():
+    torch = pytest.importorskip("torch")
+    from swiftx_b200 import selective_scan_fast
+    from swiftx_b200.conv import causal_conv1d_fn
+    u = torch.randn(1, 4, 3)
+    with pytest.raises(RuntimeError):
+        selective_scan_fast(u, u.abs(), -torch.ones(3, 2), torch.randn(1, 4, 2), torch.randn(1, 4, 2))
+    with pytest.raises(RuntimeError):
+        causal_conv1d_fn(u, torch.randn(3, 1, 4))

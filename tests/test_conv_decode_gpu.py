@@ -1,0 +1,124 @@
+"""Parity of the conv1d + SiLU and decode-step kernels with the CPU oracle.
+
+Golden fixtures conv.npz / decode.npz come from the reference's own SiftBlock
+(models/sift_block.py:117-118, :153-175).  fp32 tolerance rtol 1e-4 / atol 1e-5.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from swiftx_b200.conv import causal_conv1d_fn, conv1d_backward, conv1d_forward
+from swiftx_b200.decode import decode_conv_step, decode_ssm_step, decode_step
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def t(a, dtype=torch.float32):
+    return torch.tensor(np.asarray(a), device=DEV, dtype=dtype)
+
+
+def n64(x):
+    return x.detach().double().cpu().numpy()
+
+
+def close(got, want, rtol=1e-4, atol=1e-5):
+    np.testing.assert_allclose(n64(got) if torch.is_tensor(got) else got, want, rtol=rtol, atol=atol)
+
+
+def test_conv_golden(golden):
+    g = golden("conv")
+    D = g["w"].shape[0]
+    xz = t(g["xz"])
+    x = xz[..., :D]                                 # strided view, row stride 2D
+    assert x.stride(1) == 2 * D
+    w = t(g["w"]).reshape(D, 1, -1).requires_grad_()
+    b = t(g["bias"]).requires_grad_()
+    xr = x.detach().clone().requires_grad_()
+    out = causal_conv1d_fn(xr, w, b)
+    close(out, g["out"])
+    out.backward(t(g["gout"]))
+    close(xr.grad, g["dx"])
+    close(w.grad.reshape(D, -1), g["dw"], atol=1e-4)
+    close(b.grad, g["dbias"], atol=1e-4)
+
+
+@pytest.mark.parametrize("shape", [(2, 200, 96, 4), (3, 65, 40, 4), (1, 1, 32, 4), (2, 130, 64, 3),
+                                   (2, 70, 33, 2)])
+def test_conv_vs_oracle(shape):
+    b, L, D, K = shape
+    g = torch.Generator().manual_seed(L * 7 + D)
+    xz = torch.randn(b, L, 2 * D, generator=g).to(DEV)
+    x = xz[..., :D]
+    w = (torch.randn(D, K, generator=g) * 0.5).to(DEV)
+    bias = torch.randn(D, generator=g).to(DEV)
+    dout = torch.randn(b, L, D, generator=g).to(DEV)
+    out = conv1d_forward(x, w, bias)
+    close(out, oracle.conv1d_fwd(n64(x), n64(w), n64(bias)))
+    dx, dw, db = conv1d_backward(x, w, bias, dout)
+    odx, odw, odb = oracle.conv1d_bwd(n64(x), n64(w), n64(bias), n64(dout))
+    close(dx, odx)
+    close(dw, odw, atol=1e-3)          # sums over b*L terms
+    close(db, odb, atol=1e-3)
+
+
+def test_conv_causal_impulse():
+    """Impulse response of the conv (tests/test_sift_block.py:38-45 in the reference)."""
+    D, L = 32, 10
+    x = torch.zeros(1, L, D, device=DEV)
+    x[:, 5] = 1.0
+    w = torch.randn(D, 4, generator=torch.Generator().manual_seed(0)).to(DEV)
+    out = conv1d_forward(x, w, None, silu=False)
+    assert torch.all(out[:, :5].abs() < 1e-7)
+    assert torch.all(out[:, 9:].abs() < 1e-7)
+    assert torch.allclose(out[0, 5:9].T, w.flip(1), atol=1e-6)
+
+
+def test_conv_bf16():
+    b, L, D = 2, 96, 64
+    x = torch.randn(b, L, D, generator=torch.Generator().manual_seed(1)).to(DEV, torch.bfloat16)
+    w = torch.randn(D, 4, generator=torch.Generator().manual_seed(2)).to(DEV)
+    out = conv1d_forward(x, w, None)
+    assert out.dtype == torch.bfloat16
+    close(out.float(), oracle.conv1d_fwd(n64(x.float()), n64(w), None), rtol=2e-2, atol=2e-2)
+
+
+def test_decode_golden(golden):
+    g = golden("decode")
+    cs, ss = t(g["conv_state0"]), t(g["ssm_state0"])
+    # two launches, as in the model (x_proj / dt_proj sit between them)
+    xc = decode_conv_step(t(g["x"]), cs, t(g["conv_w"]), t(g["conv_b"]))
+    y = decode_ssm_step(xc, t(g["delta_raw"]), t(g["B"]), t(g["C"]), t(g["A"]), ss, Dskip=t(g["D"]),
+                        z=t(g["z"]))
+    close(y, g["y"])
+    close(cs, g["conv_state1"], atol=0, rtol=0)
+    close(ss, g["ssm_state1"])
+    # one fused launch
+    cs2, ss2 = t(g["conv_state0"]), t(g["ssm_state0"])
+    y2 = decode_step(t(g["x"]), cs2, t(g["conv_w"]), t(g["conv_b"]), t(g["delta_raw"]), t(g["B"]),
+                     t(g["C"]), t(g["A"]), ss2, Dskip=t(g["D"]), z=t(g["z"]))
+    close(y2, g["y"])
+    close(ss2, g["ssm_state1"])
+
+
+@pytest.mark.parametrize("N", [16, 5])
+def test_decode_vs_oracle_multi_step(N):
+    b, D, K = 4, 96, 4
+    g = torch.Generator().manual_seed(N)
+    A = -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1)
+    cw, cb = torch.randn(D, K, generator=g) * 0.5, torch.randn(D, generator=g)
+    Dskip, dbias = torch.ones(D), torch.randn(D, generator=g) * 0.5 - 3
+    cs = torch.randn(b, D, K, generator=g)
+    ss = torch.randn(b, D, N, generator=g) * 0.1
+    cs_o, ss_o = cs.double().numpy(), ss.double().numpy()
+    csd, ssd = cs.to(DEV), ss.to(DEV)
+    for step in range(5):
+        x, z, dr = (torch.randn(b, D, generator=g) for _ in range(3))
+        Bm, Cm = torch.randn(b, N, generator=g), torch.randn(b, N, generator=g)
+        y = decode_step(x.to(DEV), csd, cw.to(DEV), cb.to(DEV), dr.to(DEV), Bm.to(DEV), Cm.to(DEV),
+                        A.to(DEV), ssd, Dskip=Dskip.to(DEV), z=z.to(DEV), delta_bias=dbias.to(DEV))
+        yo, cs_o, ss_o, _ = oracle.decode_step(x, z, dr, Bm, Cm, cw, cb, A, Dskip, dbias, cs_o, ss_o)
+        close(y, yo)
+        close(csd, cs_o)
+        close(ssd, ss_o)
