@@ -92,7 +92,7 @@ def test_decode_golden(golden):
     y = decode_ssm_step(xc, t(g["delta_raw"]), t(g["B"]), t(g["C"]), t(g["A"]), ss, Dskip=t(g["D"]),
                         z=t(g["z"]))
     close(y, g["y"])
-    close(cs, g["conv_state1"], atol=0, rtol=0)
+    close(cs, np.float32(g["conv_state1"]), atol=0, rtol=0)     # a shift + append: exact
     close(ss, g["ssm_state1"])
     # one fused launch
     cs2, ss2 = t(g["conv_state0"]), t(g["ssm_state0"])
