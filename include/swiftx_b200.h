@@ -6,8 +6,9 @@
  * kernels on the given cudaStream_t (passed as void*; NULL = legacy default
  * stream).  Nothing here allocates device memory: outputs, checkpoints and
  * workspaces are provided by the caller (the Python host layer allocates them
- * with torch on the current stream).  The library holds no global state and
- * takes no locks; concurrent calls on different streams are independent.
+ * with torch on the current stream).  Apart from swx_scan_bwd_static_scratch
+ * (below), the library holds no global state and takes no locks; concurrent
+ * calls on different streams are independent.
  *
  * Shapes follow the reference API (models/selective_scan.py:36-43):
  *   u, delta, z, out, dout, du, ddelta, dz : (b, L, D)   innermost stride 1
@@ -102,6 +103,27 @@ int swx_scan_fwd(const swx_scan_args* args, void* stream);
  * (models/triton_scan.py:137-155).  Reductions (dA, dB, dC, dD, ddelta_bias) are
  * deterministic: fixed-order sums, no float atomics. */
 int swx_scan_bwd(const swx_scan_args* args, void* stream);
+
+/* Capacity of the static scratch used by swx_scan_bwd_static_scratch: 8 MiB, enough
+ * for swx_scan_bwd_workspace_bytes(batch, seqlen, dim) of roughly batch*seqlen*dim up
+ * to 2M (e.g. 2 x 1024 x 1024). */
+#define SWX_STATIC_SCRATCH_BYTES (8u << 20)
+
+/* swx_scan_bwd for callers that cannot allocate device memory (a process that has
+ * reserved all of its device memory up front and forbids later cudaMalloc, or a
+ * binding that receives ready-made buffers and has no allocator of its own).  It has
+ * no counterpart in the reference.  The caller still passes every input and output
+ * (including the forward's checkpoints); args->workspace is ignored and the scratch
+ * comes from a fixed array in the library's device memory, which every GPU that loads
+ * the library holds until the process exits.  Returns SWX_ERR_INVALID_ARG (without
+ * launching) when swx_scan_bwd_workspace_bytes() exceeds SWX_STATIC_SCRATCH_BYTES.
+ * The first call on each device looks the array's address up (cudaGetSymbolAddress,
+ * with that device current); make that first call before any stream capture.  All
+ * calls on a device share the one array: calls that overlap on the GPU (other streams,
+ * other host threads) race and must be serialised by the caller.  Every scratch byte
+ * that is read is first written by the same call, so nothing needs clearing between
+ * calls.  Calls no cudaMalloc / cudaFree. */
+int swx_scan_bwd_static_scratch(const swx_scan_args* args, void* stream);
 
 /* ------------------------------------------------------------------ conv1d */
 /* Causal depthwise conv1d (+ SiLU).  x: (b, L, D) with element strides (x_sb, x_sl) and

@@ -16,6 +16,8 @@ SWX_ERR_INVALID_ARG = 1
 SWX_ERR_UNSUPPORTED = 2
 SWX_ERR_CUDA = 3
 SWX_ERR_TIMEOUT = 4
+# capacity of the static scratch of swx_scan_bwd_static_scratch (SWX_STATIC_SCRATCH_BYTES)
+SWX_STATIC_SCRATCH_BYTES = 8 << 20
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 
@@ -97,7 +99,8 @@ def load():
     lib.swx_scan_checkpoint_floats.argtypes = [i64, i64, i64]
     lib.swx_scan_bwd_workspace_bytes.restype = i64
     lib.swx_scan_bwd_workspace_bytes.argtypes = [i64, i64, i64]
-    for name, st in (("swx_scan_fwd", ScanArgs), ("swx_scan_bwd", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
+    for name, st in (("swx_scan_fwd", ScanArgs), ("swx_scan_bwd", ScanArgs),
+                     ("swx_scan_bwd_static_scratch", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
                      ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs)):
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
