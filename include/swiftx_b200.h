@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 1
+#define SWX_ABI_VERSION 2
 
 /* status codes */
 #define SWX_OK 0
@@ -58,7 +58,8 @@ typedef struct swx_scan_args {
     const float* delta_bias;   /* optional */
     const float* h0;           /* optional initial state */
     /* forward outputs */
-    void* out;                 /* (b, L, D) dense */
+    void* out;                 /* (b, L, D) dense; NULL = compute only h_last / delta_sum /
+                                  checkpoints (skips C, z, the readout and the stores) */
     float* h_last;             /* optional final state */
     float* checkpoints;        /* optional in forward (required for backward):
                                   swx_scan_checkpoint_floats() fp32 values */
@@ -71,6 +72,9 @@ typedef struct swx_scan_args {
     float* ddelta_bias;                 /* optional (with delta_bias) */
     float* dh0;                         /* optional (with h0) */
     void* workspace; int64_t workspace_bytes;  /* >= swx_scan_bwd_workspace_bytes() */
+    /* forward, optional: (b, D) fp32 sum over t of delta_eff, i.e. log of the chunk's
+       decay per state is A * delta_sum (used to chain sequence-parallel chunks) */
+    float* delta_sum;
 } swx_scan_args;
 
 int swx_abi_version(void);

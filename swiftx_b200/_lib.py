@@ -42,6 +42,7 @@ class ScanArgs(ctypes.Structure):
         ("du", vp), ("ddelta", vp), ("dz", vp), ("dB", vp), ("dC", vp),
         ("dA", vp), ("dD", vp), ("ddelta_bias", vp), ("dh0", vp),
         ("workspace", vp), ("workspace_bytes", i64),
+        ("delta_sum", vp),
     ]
 
 

@@ -68,7 +68,7 @@ swx::ScanDev pack(const swx_scan_args* a) {
     p.vec_B = vec_ok(a->B, a->B_sb, a->B_sl, es);
     p.vec_C = vec_ok(a->C, a->C_sb, a->C_sl, es);
     p.vec_dout = vec_ok(a->dout, a->dout_sb, a->dout_sl, es);
-    p.out = a->out; p.h_last = a->h_last; p.ck = a->checkpoints;
+    p.out = a->out; p.h_last = a->h_last; p.ck = a->checkpoints; p.dsum = a->delta_sum;
     p.dout = a->dout; p.dout_sb = a->dout_sb; p.dout_sl = a->dout_sl;
     p.du = a->du; p.ddl = a->ddelta; p.dz = a->dz; p.dB = a->dB; p.dC = a->dC;
     p.dA = a->dA; p.dD = a->dD; p.ddbias = a->ddelta_bias; p.dh0 = a->dh0;
@@ -112,7 +112,7 @@ int swx_scan_fwd(const swx_scan_args* a, void* stream) {
     if (s != SWX_OK) return s;
     if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
     if (elem_size(a->out_dtype) == 0) return SWX_ERR_UNSUPPORTED;
-    if (!a->out) return SWX_ERR_INVALID_ARG;
+    if (!a->out && !a->h_last && !a->delta_sum && !a->checkpoints) return SWX_OK;   // nothing requested
     if (a->checkpoints && !aligned16(a->checkpoints)) return SWX_ERR_INVALID_ARG;
     swx::ScanDev p = pack(a);
     return from_cuda(swx::launch_scan_fwd(p, a->in_dtype, a->out_dtype, a->z != nullptr,

@@ -60,9 +60,10 @@ struct FwdSmem {
     Tin C[RING][FT][NS];
     float2 dd[2][FT][SCH];        // (delta_eff, delta_eff * u)
     float yp[2][FT][SCH][4];      // partial readouts of the 4 state groups
+    float red[NAUX];              // per-thread sums of delta_eff
 };
 
-template <bool FULL, typename Tin>
+template <bool FULL, bool WR, typename Tin>
 __device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], const Tin (*__restrict__ Bs)[NS],
                                          const Tin (*__restrict__ Cs)[NS], float (*__restrict__ yp)[SCH][4],
                                          int nt, int ch, int j, float2 A01, float2 A23, float2& h01, float2& h23,
@@ -78,26 +79,32 @@ __device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], c
                     *reinterpret_cast<float4*>(ckp + (t / TCK) * ck_stride) = make_float4(h01.x, h01.y, h23.x, h23.y);
                 const float2 d = dd[t][ch];
                 const float4 b = ld4(&Bs[t][4 * j]);
-                const float4 c = ld4(&Cs[t][4 * j]);
                 const float2 dt = bc2(d.x), du = bc2(d.y);
                 const float2 a01 = ex2x2(mul2(dt, A01));
                 const float2 a23 = ex2x2(mul2(dt, A23));
                 h01 = fma2(a01, h01, mul2(du, f2(b.x, b.y)));
                 h23 = fma2(a23, h23, mul2(du, f2(b.z, b.w)));
-                float2 y = mul2(h01, f2(c.x, c.y));
-                y = fma2(h23, f2(c.z, c.w), y);
-                yv[q] = y.x + y.y;
+                if (WR) {
+                    const float4 c = ld4(&Cs[t][4 * j]);
+                    float2 y = mul2(h01, f2(c.x, c.y));
+                    y = fma2(h23, f2(c.z, c.w), y);
+                    yv[q] = y.x + y.y;
+                }
             }
         }
+        if (WR) {
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int t = 8 * g + q;
-            if (FULL || t < nt) yp[t][ch][j] = yv[q];
+            for (int q = 0; q < 8; ++q) {
+                const int t = 8 * g + q;
+                if (FULL || t < nt) yp[t][ch][j] = yv[q];
+            }
         }
     }
 }
 
-template <typename Tin, typename Tout, bool HAS_Z>
+// WR: write the output (pass 1 of the sequence-parallel scan needs only the final state
+// and the per-channel sum of delta_eff, so it skips C, z, the readout and the stores).
+template <typename Tin, typename Tout, bool HAS_Z, bool WR>
 __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem<Tin>& S = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
@@ -132,9 +139,9 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
                              : nullptr;
             const int r = c % RING;
             if (nt == FT)
-                fwd_tile<true>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
+                fwd_tile<true, WR>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
             else
-                fwd_tile<false>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
+                fwd_tile<false, WR>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
             bar_arrive(BAR_X0 + s, NTH);
         }
         if (p.h_last && dvalid) {
@@ -164,17 +171,19 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
                 const int t0 = c * FT, rv = min(FT, p.L - t0), r = c % RING;
                 stage_tile<Tin, SCH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, FT, rv, nd, p.vec_u, at, NAUX);
                 stage_tile<Tin, SCH>(&S.dl[r][0][0], gdl + t0 * p.dl_sl, p.dl_sl, FT, rv, nd, p.vec_dl, at, NAUX);
-                if (HAS_Z)
+                if (HAS_Z && WR)
                     stage_tile<Tin, SCH>(&S.z[r][0][0], gz + t0 * p.z_sl, p.z_sl, FT, rv, nd, p.vec_z, at, NAUX);
                 stage_tile<Tin, NS>(&S.B[r][0][0], gB + t0 * p.B_sl, p.B_sl, FT, rv, p.N, p.vec_B, at, NAUX);
-                stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, FT, rv, p.N, p.vec_C, at, NAUX);
+                if (WR)
+                    stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, FT, rv, p.N, p.vec_C, at, NAUX);
             }
             cp_async_commit();
         };
         // per-(t, channel) work: each thread takes pairs of steps (t, t+1) of channel `ech`
         const float2 bias2 = bc2(ebias), D2 = bc2(eD);
+        float dsum = 0.f;
         auto derive = [&](int c) {
-            const int r = c % RING, s = c & 1;
+            const int r = c % RING, s = c & 1, nt = min(FT, p.L - c * FT);
 #pragma unroll
             for (int m = 0; m < FT * SCH / (2 * NAUX); ++m) {
                 const int t = 2 * (at / SCH + m * (NAUX / SCH));
@@ -184,9 +193,12 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
                 const float2 du = mul2(dte, f2(Elem<Tin>::to_f(S.u[r][t][ech]), Elem<Tin>::to_f(S.u[r][t + 1][ech])));
                 S.dd[s][t][ech] = f2(dte.x, du.x);
                 S.dd[s][t + 1][ech] = f2(dte.y, du.y);
+                if (t < nt) dsum += dte.x;
+                if (t + 1 < nt) dsum += dte.y;
             }
         };
         auto epilogue = [&](int c) {
+            if (!WR) return;
             const int r = c % RING, s = c & 1, t0 = c * FT, nt = min(FT, p.L - t0);
 #pragma unroll
             for (int m = 0; m < FT * SCH / (2 * NAUX); ++m) {
@@ -231,6 +243,16 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
         bar_sync(BAR_X0 + ((nchunk - 1) & 1), NTH);
         epilogue(nchunk - 1);
         cp_async_wait<0>();
+        if (p.dsum) {                      // sum over the 4 thread groups of a channel
+            S.red[at] = dsum;
+            bar_sync(BAR_AUX, NAUX);
+            if (at < SCH && evalid) {
+                float sum = 0.f;
+#pragma unroll
+                for (int m = 0; m < NAUX / SCH; ++m) sum += S.red[at + m * SCH];
+                p.dsum[(int64_t)bi * p.D + d0 + at] = sum;
+            }
+        }
     }
 }
 
@@ -584,7 +606,7 @@ __global__ void scan_bwd_finalize_kernel(const ScanDev p) {
 // =============================================================== launchers
 template <typename Tin, typename Tout, bool HAS_Z>
 static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
-    auto k = scan_fwd_kernel<Tin, Tout, HAS_Z>;
+    auto k = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true> : scan_fwd_kernel<Tin, Tout, HAS_Z, false>;
     const int smem = sizeof(FwdSmem<Tin>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;

@@ -25,6 +25,7 @@ struct ScanDev {
     void* out;
     float* h_last;
     float* ck;               // (b, nck, D, 16)
+    float* dsum;             // (b, D) sum over t of delta_eff, optional
     // backward
     const void* dout; int64_t dout_sb, dout_sl;
     void* du; void* ddl; void* dz; void* dB; void* dC;

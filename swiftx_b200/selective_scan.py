@@ -76,26 +76,33 @@ def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
 
 
 def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
-                 h0=None, out_dtype=None, checkpoints=False, return_last_state=False):
+                 h0=None, out_dtype=None, checkpoints=False, return_last_state=False,
+                 return_delta_sum=False, write_out=True):
     """One kernel launch of the forward scan (no autograd).
 
-    Returns (out, checkpoints or None, last_state or None)."""
+    Returns (out, checkpoints or None, last_state or None), plus delta_sum (b, D) -- the
+    sum over t of delta_eff -- when return_delta_sum.  write_out=False skips the output
+    (out is None), for callers that only need the final state / delta_sum."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
     b, L, Dm = u.shape
     N = A.shape[1]
     out_dt = out_dtype or in_dt
-    out = torch.empty((b, L, Dm), device=u.device, dtype=out_dt)
+    out = torch.empty((b, L, Dm), device=u.device, dtype=out_dt) if write_out else None
     ck = (torch.empty(lib.swx_scan_checkpoint_floats(b, L, Dm), device=u.device, dtype=torch.float32)
           if checkpoints else None)
     hl = torch.empty((b, Dm, N), device=u.device, dtype=torch.float32) if return_last_state else None
+    ds = torch.empty((b, Dm), device=u.device, dtype=torch.float32) if return_delta_sum else None
     a = _lib.ScanArgs()
     _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt)
     a.out_dtype = _lib.DTYPE_CODES[out_dt]
-    a.out = out.data_ptr()
+    a.out = out.data_ptr() if out is not None else None
     a.h_last = hl.data_ptr() if hl is not None else None
     a.checkpoints = ck.data_ptr() if ck is not None else None
+    a.delta_sum = ds.data_ptr() if ds is not None else None
     _lib.check(lib.swx_scan_fwd(a, _lib.stream_ptr(u.device)), "swx_scan_fwd")
+    if return_delta_sum:
+        return out, ck, hl, ds
     return out, ck, hl
 
 

@@ -1,0 +1,86 @@
+"""Host logic of the sequence-parallel scan on CPU ranks (gloo, world sizes 2 and 3).
+
+Each rank runs sequence_parallel_scan on its chunk; the per-chunk kernel is replaced by
+the CPU oracle (through the `local_scan` hook), so what is tested here is the boundary
+exchange (all_gather) and the prefix combine.  The concatenated outputs must equal the
+oracle's scan of the whole sequence."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+from swiftx_b200.seqpar import combine_prefix, sequence_parallel_scan
+from swiftx_b200.workloads import config_inputs
+
+B_, L_, D_, N_ = 2, 90, 12, 16
+
+
+def oracle_local_scan(u, delta, A, B, C, D, z, delta_bias, softplus, h0, write_out, out_dtype):
+    n = lambda t: None if t is None else t.double().numpy()  # noqa: E731
+    out, h_end = oracle.scan_fwd(n(u), n(delta), n(A), n(B), n(C), n(D), z=n(z), delta_bias=n(delta_bias),
+                                 delta_softplus=softplus, h0=n(h0), return_last_state=True)
+    bias = delta_bias if delta_bias is not None else 0.0
+    dte = torch.nn.functional.softplus(delta.double() + bias) if softplus else delta.double() + bias
+    dsum = dte.sum(1)
+    if not write_out:
+        return None, torch.from_numpy(h_end), dsum
+    return torch.from_numpy(out), None, None
+
+
+def _worker(rank, world, port, bounds, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        inp = config_inputs(B_, L_, D_, N_, seed=3)
+        s, e = bounds[rank], bounds[rank + 1]
+        ch = {k: inp[k][:, s:e] for k in ("u", "delta", "z", "B", "C")}
+        out = sequence_parallel_scan(ch["u"], ch["delta"], inp["A"], ch["B"], ch["C"], inp["D"], ch["z"],
+                                     inp["delta_bias"], True, local_scan=oracle_local_scan)
+        q.put((rank, out.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.parametrize("bounds", [[0, 41, 90], [0, 30, 31, 90]])
+def test_sequence_parallel_matches_whole_sequence(bounds):
+    world = len(bounds) - 1
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, bounds, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    out = np.concatenate([got[r] for r in range(world)], axis=1)
+    inp = config_inputs(B_, L_, D_, N_, seed=3)
+    want = oracle.scan_fwd(*(inp[k] for k in ("u", "delta", "A", "B", "C")), D=inp["D"], z=inp["z"],
+                           delta_bias=inp["delta_bias"], delta_softplus=True)
+    np.testing.assert_allclose(out, want, rtol=1e-9, atol=1e-10)
+
+
+def test_combine_prefix_is_the_chained_recurrence():
+    g = torch.Generator().manual_seed(0)
+    b, D, N = 2, 3, 4
+    A = -torch.rand(D, N, generator=g, dtype=torch.float64) - 0.1
+    h_ends = [torch.randn(b, D, N, generator=g, dtype=torch.float64) for _ in range(4)]
+    dsums = [torch.rand(b, D, generator=g, dtype=torch.float64) for _ in range(4)]
+    h = torch.zeros(b, D, N, dtype=torch.float64)
+    for k in range(3):
+        h = torch.exp(A * dsums[k][..., None]) * h + h_ends[k]
+    assert torch.allclose(combine_prefix(h_ends, dsums, A, 3), h)
+    assert torch.equal(combine_prefix(h_ends, dsums, A, 0), torch.zeros(b, D, N, dtype=torch.float64))
