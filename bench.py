@@ -315,6 +315,181 @@ def run_reference(args, world, rank):
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
+
+# ----------------------------------------------------------------- other workloads
+def timed_steps(step, args, world, local, dev):
+    """Warm up, then time exactly args.steps calls of step() with CUDA events between a
+    barrier + synchronize on both sides; returns (ms per step, max over ranks; clocks)."""
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if local == 0 else None
+    if sampler:
+        sampler.__enter__()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(args.steps):
+        step()
+    t1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    if sampler:
+        sampler.__exit__()
+    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world, dev)
+    return ms, (sampler.summary() if sampler else None)
+
+
+def base_line(args, world, metric, value, unit, ms, dtype, config, scaling="weak"):
+    return {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": scaling,
+            "vs_baseline": None, "dtype": dtype, "data": "synthetic (seeded)", "config": config}
+
+
+def run_lm_train(args, world, rank, local):
+    """Sift byte-level LM training step: 8 layers, d_model 256, expand 2, d_state 16, d_conv 4,
+    vocab 256, tied embedding, batch 16 x 512 i.i.d. random bytes per GPU, AdamW lr 3e-4
+    (betas 0.9/0.95, weight decay 0.1 on matrices), grad clip 1.0, bf16 autocast as the
+    reference trainer (training/train.py:133-172); data parallel with NCCL all-reduce."""
+    from swiftx_b200.sift import SiftConfig, SiftLM
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    model = SiftLM(SiftConfig(vocab_size=256, d_model=256, n_layers=8, d_state=16, d_conv=4, expand=2)).to(dev)
+    decay = [p for p in model.parameters() if p.dim() >= 2 and not getattr(p, "_no_weight_decay", False)]
+    ids = {id(p) for p in decay}
+    no_decay = [p for p in model.parameters() if id(p) not in ids]
+    net = model
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+        net = DDP(model, device_ids=[local], gradient_as_bucket_view=True)
+    opt = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1}, {"params": no_decay, "weight_decay": 0.0}],
+                            lr=3e-4, betas=(0.9, 0.95), fused=True)
+    B, L = 16, 512
+    g = torch.Generator().manual_seed(1234 + rank)
+    host = torch.randint(0, 256, (B, L + 1), generator=g, dtype=torch.long).pin_memory()
+    tok = host.to(dev)
+
+    def train_step(t):
+        with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+            _, loss = net(t[:, :-1], t[:, 1:])
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        return loss
+
+    ms, clocks = timed_steps(lambda: train_step(tok), args, world, local, dev)
+    tokens = B * L * world
+
+    def e2e_step():
+        t = host.to(dev, non_blocking=True)
+        return train_step(t).detach().to("cpu", non_blocking=True)
+    ms_e2e, _ = timed_steps(e2e_step, args, world, local, dev)
+    res = base_line(args, world, METRIC, round(tokens / (ms * 1e-3), 1), "tokens/s", ms, "bf16",
+                    {"workload": "Sift LM train step (config 2)", "model": "SiftLM 8L d256 e2 N16 vocab256",
+                     "global_batch": B * world, "seq_len": L, "parallelism": f"dp{world}",
+                     "l2": "activations and weights per step exceed L2"})
+    res["e2e"] = {"value": round(tokens / (ms_e2e * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step":
+                  host.numel() * host.element_size(), "d2h_bytes_per_step": 4}
+    res["gpu_launches"] = 6 * 8 * args.steps      # per layer: conv fwd, scan fwd, conv bwd x2, scan bwd x2
+    res["clocks"] = clocks
+    return res
+
+
+def run_long_scan(args, world, rank, local):
+    """Long-sequence forward scan, bf16 u/delta/B/C/z, fp32 state and output, gated:
+    b=4, L=65536, D=2048, N=16, split along the sequence over the ranks (sequence
+    parallel: pass 1 boundary values, NCCL all_gather, prefix combine, pass 2)."""
+    import math
+
+    from swiftx_b200.selective_scan import scan_forward
+    from swiftx_b200.seqpar import sequence_parallel_scan
+    dev = torch.device("cuda", local)
+    b, L, D, N = 4, 65536, 2048, 16
+    Lr = L // world
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    bf = torch.bfloat16
+    u = torch.randn(b, Lr, D, generator=g, device=dev).to(bf)
+    dr = (torch.randn(b, Lr, D, generator=g, device=dev) * 0.5).to(bf)
+    z = torch.randn(b, Lr, D, generator=g, device=dev).to(bf)
+    Bm = torch.randn(b, Lr, N, generator=g, device=dev).to(bf)
+    Cm = torch.randn(b, Lr, N, generator=g, device=dev).to(bf)
+    gc = torch.Generator().manual_seed(0)
+    dt = torch.exp(torch.rand(D, generator=gc) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+    bias = (dt + torch.log(-torch.expm1(-dt))).to(dev)
+    A = -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1).to(dev)
+    Dsk = torch.ones(D, device=dev)
+
+    def step():
+        if world > 1:
+            return sequence_parallel_scan(u, dr, A, Bm, Cm, Dsk, z, bias, True, out_dtype=torch.float32)
+        return scan_forward(u, dr, A, Bm, Cm, Dsk, z, bias, True, out_dtype=torch.float32)[0]
+
+    ms, clocks = timed_steps(step, args, world, local, dev)
+    alg = (3 * b * L * D * 2 + 2 * b * L * N * 2 + b * L * D * 4)        # whole job
+    res = base_line(args, world, METRIC, round(alg / (ms * 1e-3) / 1e9, 1), "GB/s", ms, "bf16-in/f32-state",
+                    {"workload": "long-sequence scan fwd (config 3)", "batch": b, "seqlen": L, "d_inner": D,
+                     "d_state": N, "parallelism": f"sequence-parallel x{world}" if world > 1 else "single GPU",
+                     "alg_bytes": alg}, scaling="strong")
+    res["clocks"] = clocks
+    res["gpu_launches"] = (2 if world > 1 else 1) * args.steps
+    return res
+
+
+def run_decode(args, world, rank, local):
+    """Recurrent decode: batch 256 (sharded over the ranks), 24 layers, D=2048, N=16,
+    d_conv=4, fp32 state ~ N(0, 0.1); per layer one fused conv-window shift + state update
+    + C readout + gate launch; the 24-layer step is replayed as one CUDA graph."""
+    import math
+
+    from swiftx_b200.decode import decode_step
+    dev = torch.device("cuda", local)
+    btot, layers, D, N, K = 256, 24, 2048, 16, 4
+    b = btot // world
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    gc = torch.Generator().manual_seed(0)
+    lay = []
+    for _ in range(layers):
+        dt = torch.exp(torch.rand(D, generator=gc) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+        lay.append({
+            "cw": (torch.randn(D, K, generator=gc) * 0.5).to(dev), "cb": torch.randn(D, generator=gc).to(dev),
+            "A": -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1).to(dev), "Dsk": torch.ones(D, device=dev),
+            "bias": (dt + torch.log(-torch.expm1(-dt))).to(dev),
+            "cs": torch.randn(b, D, K, generator=g, device=dev), "ss": torch.randn(b, D, N, generator=g, device=dev) * 0.1,
+            "x": torch.randn(b, D, generator=g, device=dev), "z": torch.randn(b, D, generator=g, device=dev),
+            "dr": torch.randn(b, D, generator=g, device=dev) * 0.5,
+            "B": torch.randn(b, N, generator=g, device=dev), "C": torch.randn(b, N, generator=g, device=dev)})
+
+    def token_step():
+        for p in lay:
+            p["y"] = decode_step(p["x"], p["cs"], p["cw"], p["cb"], p["dr"], p["B"], p["C"], p["A"], p["ss"],
+                                 Dskip=p["Dsk"], z=p["z"], delta_bias=p["bias"])
+
+    for _ in range(3):
+        token_step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        token_step()
+    ms, clocks = timed_steps(graph.replay, args, world, local, dev)
+    per_layer = b * D * (2 * N * 4 + 2 * K * 4 + 4 * 4) + b * 2 * N * 4
+    res = base_line(args, world, METRIC, round(btot / (ms * 1e-3), 1), "tokens/s", ms, "f32",
+                    {"workload": "recurrent decode step (config 4)", "batch": btot, "layers": layers, "d_inner": D,
+                     "d_state": N, "d_conv": K, "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
+                     "cuda_graph": True}, scaling="strong")
+    res["latency_ms_per_token"] = round(ms, 4)
+    achieved = per_layer * layers / (ms * 1e-3) / 1e9
+    peak, kind = measured_peak()
+    res["roofline"] = {"bound": "hbm", "kernel": "decode_kernel", "achieved": round(achieved, 1), "peak": peak,
+                       "peak_kind": kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                       "alg_bytes_per_launch": per_layer}
+    res["clocks"] = clocks
+    res["gpu_launches"] = layers * args.steps
+    del graph
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -322,10 +497,23 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode"], default="scan",
+                    help="scan: config 1 (default, the headline); lm_train: config 2; long_scan: config 3; "
+                         "decode: config 4")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
-        res = run_reference(args, world, rank)
+        if args.workload != "scan":
+            res = {"impl": "reference", "unavailable": "the reference arm is the CPU oracle port of the scan "
+                   "(default workload); other workloads have no CPU reference run on the GPU box"} if rank == 0 else None
+        else:
+            res = run_reference(args, world, rank)
+    elif args.workload == "lm_train":
+        res = run_lm_train(args, world, rank, local)
+    elif args.workload == "long_scan":
+        res = run_long_scan(args, world, rank, local)
+    elif args.workload == "decode":
+        res = run_decode(args, world, rank, local)
     else:
         res = run_ours(args, world, rank, local)
     if rank == 0 and res is not None:
