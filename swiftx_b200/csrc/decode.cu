@@ -27,88 +27,137 @@ struct DecDev {
     float* conv_state; float* ssm_state; float* xc_out; float* out;
 };
 
-constexpr int DEC_NT = 256;
+constexpr int DEC_NT = 256;          // 64 channels x 4 state groups per CTA
+constexpr int DEC_CH = DEC_NT / 4;
+constexpr int DEC_RB = 4;            // batch rows per thread (independent chains in flight)
 
+// Thread (channel d, state group j) handles DEC_RB batch rows of that channel: all of
+// their loads are issued before any math, and the per-channel parameters (A, conv
+// weights, biases) are loaded once and reused across the rows.
 template <int K, bool HAS_Z>
 __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
-    const int64_t gid = (int64_t)blockIdx.x * DEC_NT + threadIdx.x;
-    const int j = (int)(gid & 3);
-    const int64_t total = (int64_t)p.b * p.D;
-    const int64_t bd = gid >> 2;
-    const bool valid = bd < total;
-    const int64_t bdc = valid ? bd : 0;
-    const int bi = (int)(bdc / p.D), d = (int)(bdc % p.D);
+    const int j = threadIdx.x & 3;
+    const int d = blockIdx.x * DEC_CH + (threadIdx.x >> 2);
+    const int b0 = blockIdx.y * DEC_RB;
+    const bool dvalid = d < p.D;
+    const int dc = dvalid ? d : 0;
+    const bool conv = p.mode & SWX_DECODE_CONV, ssm = p.mode & SWX_DECODE_SSM;
+    const bool full = (p.N == NS);
 
-    float xc;
-    if (p.mode & SWX_DECODE_CONV) {
-        const float xin = p.x[bi * p.x_sb + d];
-        float win[K];
-        const float* cs = p.conv_state + bdc * K;
+    float cw[K];
+    float cb = 0.f;
+    if (conv) {
 #pragma unroll
-        for (int k = 0; k < K - 1; ++k) win[k] = cs[k + 1];
-        win[K - 1] = xin;
-        float acc = p.cb ? p.cb[d] : 0.f;
+        for (int k = 0; k < K; ++k) cw[k] = p.cw[(int64_t)dc * K + k];
+        cb = p.cb ? p.cb[dc] : 0.f;
+    }
+    float4 A4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float dsk = 0.f, dbi = 0.f;
+    if (ssm) {
+        if (full) A4 = *reinterpret_cast<const float4*>(p.A + (int64_t)dc * NS + 4 * j);
+        dsk = p.Dskip ? p.Dskip[dc] : 0.f;
+        dbi = p.dbias ? p.dbias[dc] : 0.f;
+    }
+
+    // ---- loads for all rows
+    float xin[DEC_RB], zv[DEC_RB], raw[DEC_RB], win[DEC_RB][K];
+    float4 h4[DEC_RB], b4[DEC_RB], c4[DEC_RB];
+    bool valid[DEC_RB];
 #pragma unroll
-        for (int k = 0; k < K; ++k) acc = fmaf(win[k], p.cw[(int64_t)d * K + k], acc);
-        xc = silu_f(acc);
-        if (valid && j == 0) {
-            float* csw = p.conv_state + bdc * K;
+    for (int r = 0; r < DEC_RB; ++r) {
+        const int bi = b0 + r;
+        valid[r] = dvalid && bi < p.b;
+        const int bc = valid[r] ? bi : 0;
+        const int64_t bd = (int64_t)bc * p.D + dc;
+        xin[r] = p.x[bc * p.x_sb + dc];
+        if (conv) {
+            const float* cs = p.conv_state + bd * K;
+            if (K == 4) {
+                const float4 w = *reinterpret_cast<const float4*>(cs);
+                win[r][0] = w.y; win[r][1 % K] = w.z; win[r][2 % K] = w.w;
+            } else {
 #pragma unroll
-            for (int k = 0; k < K; ++k) csw[k] = win[k];
-            if (p.xc_out) p.xc_out[bdc] = xc;
+                for (int k = 0; k < K - 1; ++k) win[r][k] = cs[k + 1];
+            }
         }
-    } else {
-        xc = p.x[bi * p.x_sb + d];
-    }
-    if (!(p.mode & SWX_DECODE_SSM)) return;
-
-    const float raw = p.dl[bi * p.dl_sb + d] + (p.dbias ? p.dbias[d] : 0.f);
-    float dte = raw;
-    if (p.softplus) {
-        float2 sp, dsp;
-        softplus2(bc2(raw), sp, dsp);
-        dte = sp.x;
-    }
-    const float dxc = dte * xc;
-    float* hp = p.ssm_state + bdc * p.N;
-    float y = 0.f;
-    if (p.N == NS) {
-        const float4 h4 = *reinterpret_cast<const float4*>(hp + 4 * j);
-        const float4 a4 = *reinterpret_cast<const float4*>(p.A + (int64_t)d * NS + 4 * j);
-        const float4 b4 = *reinterpret_cast<const float4*>(p.B + bi * p.B_sb + 4 * j);
-        const float4 c4 = *reinterpret_cast<const float4*>(p.C + bi * p.C_sb + 4 * j);
-        const float2 dt = bc2(dte * LOG2E), dx = bc2(dxc);
-        float2 h01 = fma2(ex2x2(mul2(dt, f2(a4.x, a4.y))), f2(h4.x, h4.y), mul2(dx, f2(b4.x, b4.y)));
-        float2 h23 = fma2(ex2x2(mul2(dt, f2(a4.z, a4.w))), f2(h4.z, h4.w), mul2(dx, f2(b4.z, b4.w)));
-        float2 yy = mul2(h01, f2(c4.x, c4.y));
-        yy = fma2(h23, f2(c4.z, c4.w), yy);
-        y = yy.x + yy.y;
-        if (valid) *reinterpret_cast<float4*>(hp + 4 * j) = make_float4(h01.x, h01.y, h23.x, h23.y);
-    } else {
-        for (int i = 0; i < 4; ++i) {
-            const int n = 4 * j + i;
-            if (n < p.N) {
-                const float h = fmaf(ex2(dte * p.A[(int64_t)d * p.N + n] * LOG2E), hp[n], dxc * p.B[bi * p.B_sb + n]);
-                y = fmaf(h, p.C[bi * p.C_sb + n], y);
-                if (valid) hp[n] = h;
+        if (ssm) {
+            raw[r] = p.dl[bc * p.dl_sb + dc] + dbi;
+            zv[r] = HAS_Z ? p.z[bc * p.z_sb + dc] : 0.f;
+            if (full) {
+                h4[r] = *reinterpret_cast<const float4*>(p.ssm_state + bd * NS + 4 * j);
+                b4[r] = *reinterpret_cast<const float4*>(p.B + bc * p.B_sb + 4 * j);
+                c4[r] = *reinterpret_cast<const float4*>(p.C + bc * p.C_sb + 4 * j);
             }
         }
     }
-    y += __shfl_xor_sync(0xffffffffu, y, 1);
-    y += __shfl_xor_sync(0xffffffffu, y, 2);
-    if (valid && j == 0) {
-        y = fmaf(p.Dskip ? p.Dskip[d] : 0.f, xc, y);
-        if (HAS_Z) y *= silu_f(p.z[bi * p.z_sb + d]);
-        p.out[bdc] = y;
+
+    // ---- math and stores
+#pragma unroll
+    for (int r = 0; r < DEC_RB; ++r) {
+        const int bc = valid[r] ? b0 + r : 0;
+        const int64_t bd = (int64_t)bc * p.D + dc;
+        float xc = xin[r];
+        if (conv) {
+            win[r][K - 1] = xin[r];
+            float acc = cb;
+#pragma unroll
+            for (int k = 0; k < K; ++k) acc = fmaf(win[r][k], cw[k], acc);
+            xc = silu_f(acc);
+            if (valid[r] && j == 0) {
+                float* csw = p.conv_state + bd * K;
+                if (K == 4) {
+                    *reinterpret_cast<float4*>(csw) = make_float4(win[r][0], win[r][1 % K], win[r][2 % K], win[r][3 % K]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < K; ++k) csw[k] = win[r][k];
+                }
+                if (p.xc_out) p.xc_out[bd] = xc;
+            }
+        }
+        if (!ssm) continue;
+        float dte = raw[r];
+        if (p.softplus) {
+            float2 sp, dsp;
+            softplus2(bc2(raw[r]), sp, dsp);
+            dte = sp.x;
+        }
+        const float dxc = dte * xc;
+        float y = 0.f;
+        if (full) {
+            const float2 dt = bc2(dte * LOG2E), dx = bc2(dxc);
+            const float2 h01 = fma2(ex2x2(mul2(dt, f2(A4.x, A4.y))), f2(h4[r].x, h4[r].y), mul2(dx, f2(b4[r].x, b4[r].y)));
+            const float2 h23 = fma2(ex2x2(mul2(dt, f2(A4.z, A4.w))), f2(h4[r].z, h4[r].w), mul2(dx, f2(b4[r].z, b4[r].w)));
+            float2 yy = mul2(h01, f2(c4[r].x, c4[r].y));
+            yy = fma2(h23, f2(c4[r].z, c4[r].w), yy);
+            y = yy.x + yy.y;
+            if (valid[r]) *reinterpret_cast<float4*>(p.ssm_state + bd * NS + 4 * j) = make_float4(h01.x, h01.y, h23.x, h23.y);
+        } else {
+            float* hp = p.ssm_state + bd * p.N;
+            for (int i = 0; i < 4; ++i) {
+                const int n = 4 * j + i;
+                if (n < p.N) {
+                    const float h = fmaf(ex2(dte * p.A[(int64_t)dc * p.N + n] * LOG2E), hp[n],
+                                         dxc * p.B[bc * p.B_sb + n]);
+                    y = fmaf(h, p.C[bc * p.C_sb + n], y);
+                    if (valid[r]) hp[n] = h;
+                }
+            }
+        }
+        y += __shfl_xor_sync(0xffffffffu, y, 1);
+        y += __shfl_xor_sync(0xffffffffu, y, 2);
+        if (valid[r] && j == 0) {
+            y = fmaf(dsk, xc, y);
+            if (HAS_Z) y *= silu_f(zv[r]);
+            p.out[bd] = y;
+        }
     }
 }
 
 template <int K>
 static void launch_dec(const DecDev& p, cudaStream_t st) {
-    const int64_t threads = (int64_t)p.b * p.D * 4;
-    const int blocks = (int)((threads + DEC_NT - 1) / DEC_NT);
-    if (p.z) decode_kernel<K, true><<<blocks, DEC_NT, 0, st>>>(p);
-    else decode_kernel<K, false><<<blocks, DEC_NT, 0, st>>>(p);
+    dim3 grid((p.D + DEC_CH - 1) / DEC_CH, (p.b + DEC_RB - 1) / DEC_RB);
+    if (p.z) decode_kernel<K, true><<<grid, DEC_NT, 0, st>>>(p);
+    else decode_kernel<K, false><<<grid, DEC_NT, 0, st>>>(p);
 }
 
 }  // namespace swx
@@ -120,7 +169,7 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     if ((a->mode & SWX_DECODE_CONV) && (a->width < 1 || a->width > 6)) return SWX_ERR_UNSUPPORTED;
     if ((a->mode & SWX_DECODE_SSM) && (a->dstate < 1 || a->dstate > swx::NS)) return SWX_ERR_UNSUPPORTED;
     if (a->batch * a->dim == 0) return SWX_OK;
-    if (a->batch * a->dim * 4 > (int64_t)INT32_MAX * 256) return SWX_ERR_UNSUPPORTED;
+    if (a->dim > (int64_t)INT32_MAX || (a->batch + 3) / 4 > 65535) return SWX_ERR_UNSUPPORTED;
     if (!a->x) return SWX_ERR_INVALID_ARG;
     if ((a->mode & SWX_DECODE_CONV) && (!a->conv_weight || !a->conv_state)) return SWX_ERR_INVALID_ARG;
     if ((a->mode & SWX_DECODE_SSM) && (!a->delta || !a->B || !a->C || !a->A || !a->ssm_state || !a->out))
@@ -128,6 +177,8 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     if ((a->mode & SWX_DECODE_SSM) && a->dstate == swx::NS &&
         (((uintptr_t)a->ssm_state | (uintptr_t)a->A | (uintptr_t)a->B | (uintptr_t)a->C) & 15u ||
          (a->B_sb % 4) || (a->C_sb % 4)))
+        return SWX_ERR_INVALID_ARG;
+    if ((a->mode & SWX_DECODE_CONV) && a->width == 4 && ((uintptr_t)a->conv_state & 15u))
         return SWX_ERR_INVALID_ARG;
     swx::DecDev p{};
     p.b = (int)a->batch; p.D = (int)a->dim; p.N = (int)a->dstate; p.K = (int)a->width;
