@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 2
+#define SWX_ABI_VERSION 3
 
 /* status codes */
 #define SWX_OK 0
@@ -75,6 +75,10 @@ typedef struct swx_scan_args {
     /* forward, optional: (b, D) fp32 sum over t of delta_eff, i.e. log of the chunk's
        decay per state is A * delta_sum (used to chain sequence-parallel chunks) */
     float* delta_sum;
+    /* optional, with z: (b, L, D) dense fp32 pre-gate output y.  The forward writes it
+       when non-NULL; the backward then reads it for the gate gradient instead of
+       recomputing the readout (Mamba's save-vs-recompute trade for the gate). */
+    float* out_pre;
 } swx_scan_args;
 
 int swx_abi_version(void);

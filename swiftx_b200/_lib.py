@@ -43,6 +43,7 @@ class ScanArgs(ctypes.Structure):
         ("dA", vp), ("dD", vp), ("ddelta_bias", vp), ("dh0", vp),
         ("workspace", vp), ("workspace_bytes", i64),
         ("delta_sum", vp),
+        ("out_pre", vp),
     ]
 
 

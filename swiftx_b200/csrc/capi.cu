@@ -69,6 +69,8 @@ swx::ScanDev pack(const swx_scan_args* a) {
     p.vec_C = vec_ok(a->C, a->C_sb, a->C_sl, es);
     p.vec_dout = vec_ok(a->dout, a->dout_sb, a->dout_sl, es);
     p.out = a->out; p.h_last = a->h_last; p.ck = a->checkpoints; p.dsum = a->delta_sum;
+    p.ypre = a->z ? a->out_pre : nullptr;
+    p.vec_yp = vec_ok(a->out_pre, a->seqlen * a->dim, a->dim, 4);
     p.dout = a->dout; p.dout_sb = a->dout_sb; p.dout_sl = a->dout_sl;
     p.du = a->du; p.ddl = a->ddelta; p.dz = a->dz; p.dB = a->dB; p.dC = a->dC;
     p.dA = a->dA; p.dD = a->dD; p.ddbias = a->ddelta_bias; p.dh0 = a->dh0;

@@ -208,6 +208,11 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
                 float2 y = f2((q0.x + q0.y) + (q0.z + q0.w), (q1.x + q1.y) + (q1.z + q1.w));
                 y = fma2(D2, f2(Elem<Tin>::to_f(S.u[r][t][ech]), Elem<Tin>::to_f(S.u[r][t + 1][ech])), y);
                 if (HAS_Z) {
+                    if (p.ypre && evalid) {            // pre-gate output, saved for the backward
+                        float* q = p.ypre + (int64_t)bi * p.L * p.D + (int64_t)(t0 + t) * p.D + d0 + ech;
+                        if (t < nt) q[0] = y.x;
+                        if (t + 1 < nt) q[p.D] = y.y;
+                    }
                     const float2 zz = f2(Elem<Tin>::to_f(S.z[r][t][ech]), Elem<Tin>::to_f(S.z[r][t + 1][ech]));
                     y = mul2(y, mul2(zz, sigmoid2(zz)));
                 }
@@ -268,20 +273,61 @@ struct BwdSmem {
     float2 dd[2][TCK][SCH];            // (delta_eff, delta_eff * u)
     float dy[2][TCK][SCH];             // dy = dout * silu(z) (or dout)
     float4 ee[2][TCK][SCH];            // (u, d delta_eff / d delta_raw, dout * silu'(z), dy)
+    float yp[RING][TCK][SCH];          // pre-gate output saved by the forward (YPRE)
     float bc[2][HT][SCH][2 * NS];      // per-channel dB | dC contributions of a half tile; the two
                                        // 16-wide halves swap on odd channels (bank-conflict-free stores)
-    float4 nred[2][HT][SCH][4];        // per state group: (sum g*B, sum g*a*h_prev*A, sum h*C, -)
+    float2 nsd[2][HT][SCH][4];         // per state group: (sum g*B, sum g*a*h_prev*A)
+    float nyp[2][HT][SCH][4];          // per state group: sum h*C (gate without YPRE)
     float red[2][NAUX];
 };
 
-// One half tile (8 steps, processed last to first) of the reverse recurrence.
-template <bool FULL, typename Tin>
+// Recompute the 16 states of a chunk from its checkpoint (and, without a saved pre-gate
+// output, the partial readouts).  FULL chunks are branch-free so the scheduler can
+// overlap the steps' loads and exponentials with the state chain.
+template <bool FULL, bool YV, typename Tin>
+__device__ __forceinline__ void bwd_recompute(const float2 (*__restrict__ dd)[SCH], const Tin (*__restrict__ Bs)[NS],
+                                              const Tin (*__restrict__ Cs)[NS], int nt, int ch, int j,
+                                              float2 A01, float2 A23, float2 hck01, float2 hck23,
+                                              float2 (&hs01)[TCK], float2 (&hs23)[TCK], float4 (&bv)[TCK],
+                                              float (&yv)[TCK]) {
+    float2 h01 = hck01, h23 = hck23;
+#pragma unroll
+    for (int t = 0; t < TCK; ++t) {
+        if (FULL || t < nt) {
+            const float2 dv = dd[t][ch];
+            const float4 b = ld4(&Bs[t][4 * j]);
+            bv[t] = b;
+            const float2 dt = bc2(dv.x), du = bc2(dv.y);
+            h01 = fma2(ex2x2(mul2(dt, A01)), h01, mul2(du, f2(b.x, b.y)));
+            h23 = fma2(ex2x2(mul2(dt, A23)), h23, mul2(du, f2(b.z, b.w)));
+            hs01[t] = h01;
+            hs23[t] = h23;
+            if (YV) {
+                const float4 cc = ld4(&Cs[t][4 * j]);
+                float2 y = mul2(h01, f2(cc.x, cc.y));
+                y = fma2(h23, f2(cc.z, cc.w), y);
+                yv[t] = y.x + y.y;
+            } else {
+                yv[t] = 0.f;
+            }
+        } else {
+            hs01[t] = hs23[t] = f2(0.f, 0.f);
+            bv[t] = make_float4(0.f, 0.f, 0.f, 0.f);
+            yv[t] = 0.f;
+        }
+    }
+}
+
+// One half tile (8 steps, processed last to first) of the reverse recurrence.  The
+// decays are recomputed here (one exp per element; the MUFU pipe has room in the
+// backward), the states and B come from the chunk's registers.
+template <bool FULL, bool YV, typename Tin>
 __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], const float (*__restrict__ dyv)[SCH],
-                                         const Tin (*__restrict__ Bs)[NS], const Tin (*__restrict__ Cs)[NS],
-                                         float (*__restrict__ bc)[SCH][2 * NS], float4 (*__restrict__ nred)[SCH][4],
-                                         int tlo, int nt, int ch, int j,
-                                         const float2 (&a01)[TCK], const float2 (&a23)[TCK],
-                                         const float2 (&hs01)[TCK], const float2 (&hs23)[TCK],
+                                         const Tin (*__restrict__ Cs)[NS],
+                                         float (*__restrict__ bc)[SCH][2 * NS], float2 (*__restrict__ nsd)[SCH][4],
+                                         float (*__restrict__ nyp)[SCH][4],
+                                         int tlo, int nt, int ch, int j, float2 A01, float2 A23,
+                                         const float4 (&bv)[TCK], const float2 (&hs01)[TCK], const float2 (&hs23)[TCK],
                                          const float (&yv)[TCK], float2 hck01, float2 hck23,
                                          float2 An01, float2 An23, float2& g01, float2& g23,
                                          float2& an01, float2& an23, float2& dA01, float2& dA23) {
@@ -293,8 +339,10 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
         if (FULL || t < nt) {
             const float2 d = dd[t][ch];
             const float2 dy = bc2(dyv[t][ch]);
-            const float4 b = ld4(&Bs[t][4 * j]);
+            const float4 b = bv[t];
             const float4 c = ld4(&Cs[t][4 * j]);
+            const float2 dte = bc2(d.x);
+            const float2 a01 = ex2x2(mul2(dte, A01)), a23 = ex2x2(mul2(dte, A23));
             g01 = fma2(an01, g01, mul2(dy, f2(c.x, c.y)));
             g23 = fma2(an23, g23, mul2(dy, f2(c.z, c.w)));
             const float2 du = bc2(d.y);
@@ -306,22 +354,25 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
             sg = fma2(g23, f2(b.z, b.w), sg);
             const float2 hp01 = (t > 0) ? hs01[t > 0 ? t - 1 : 0] : hck01;
             const float2 hp23 = (t > 0) ? hs23[t > 0 ? t - 1 : 0] : hck23;
-            const float2 w01 = mul2(mul2(g01, a01[t]), hp01);
-            const float2 w23 = mul2(mul2(g23, a23[t]), hp23);
-            const float2 dte = bc2(d.x);
+            const float2 w01 = mul2(mul2(g01, a01), hp01);
+            const float2 w23 = mul2(mul2(g23, a23), hp23);
             dA01 = fma2(w01, dte, dA01);
             dA23 = fma2(w23, dte, dA23);
             float2 sd = mul2(w01, An01);
             sd = fma2(w23, An23, sd);
-            nred[tt][ch][j] = make_float4(sg.x + sg.y, sd.x + sd.y, yv[t], 0.f);
-            an01 = a01[t];
-            an23 = a23[t];
+            nsd[tt][ch][j] = f2(sg.x + sg.y, sd.x + sd.y);
+            if (YV) nyp[tt][ch][j] = yv[t];
+            an01 = a01;
+            an23 = a23;
         }
     }
 }
 
-template <typename Tin, bool HAS_Z>
+// YPRE: the forward saved the pre-gate output, so the gate gradient reads it instead
+// of recomputing the readout (which would need C in the recompute pass).
+template <typename Tin, bool HAS_Z, bool YPRE>
 __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
+    constexpr bool YV = HAS_Z && !YPRE;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     BwdSmem<Tin>& S = *reinterpret_cast<BwdSmem<Tin>*>(smem_raw);
 
@@ -356,48 +407,27 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                 hck01 = f2(v.x, v.y);
                 hck23 = f2(v.z, v.w);
             }
-            // recompute decays and states of the chunk
-            float2 a01[TCK], a23[TCK], hs01[TCK], hs23[TCK];
+            // recompute the chunk's states (B kept in registers for the reverse pass)
+            float2 hs01[TCK], hs23[TCK];
+            float4 bv[TCK];
             float yv[TCK];
-            {
-                float2 h01 = hck01, h23 = hck23;
-#pragma unroll
-                for (int t = 0; t < TCK; ++t) {
-                    if (t < nt) {
-                        const float2 dv = S.dd[s][t][ch];
-                        const float4 b = ld4(&S.B[r][t][4 * j]);
-                        const float2 dt = bc2(dv.x), du = bc2(dv.y);
-                        a01[t] = ex2x2(mul2(dt, A01));
-                        a23[t] = ex2x2(mul2(dt, A23));
-                        h01 = fma2(a01[t], h01, mul2(du, f2(b.x, b.y)));
-                        h23 = fma2(a23[t], h23, mul2(du, f2(b.z, b.w)));
-                        hs01[t] = h01;
-                        hs23[t] = h23;
-                        if (HAS_Z) {
-                            const float4 cc = ld4(&S.C[r][t][4 * j]);
-                            float2 y = mul2(h01, f2(cc.x, cc.y));
-                            y = fma2(h23, f2(cc.z, cc.w), y);
-                            yv[t] = y.x + y.y;
-                        } else {
-                            yv[t] = 0.f;
-                        }
-                    } else {
-                        a01[t] = a23[t] = hs01[t] = hs23[t] = f2(0.f, 0.f);
-                        yv[t] = 0.f;
-                    }
-                }
-            }
+            if (nt == TCK)
+                bwd_recompute<true, YV>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
+            else
+                bwd_recompute<false, YV>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
             // reverse recurrence: upper half (steps 8..15) into slot 0, lower half into slot 1
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
                 const int tlo = hh == 0 ? HT : 0;
                 bar_sync(BAR_E0 + hh, NTH);
                 if (nt == TCK)
-                    bwd_half<true>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
-                                   hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
+                    bwd_half<true, YV>(S.dd[s], S.dy[s], S.C[r], S.bc[hh], S.nsd[hh], S.nyp[hh], tlo, nt, ch, j,
+                                       A01, A23, bv, hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23,
+                                       dA01, dA23);
                 else
-                    bwd_half<false>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[hh], S.nred[hh], tlo, nt, ch, j, a01, a23,
-                                    hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
+                    bwd_half<false, YV>(S.dd[s], S.dy[s], S.C[r], S.bc[hh], S.nsd[hh], S.nyp[hh], tlo, nt, ch, j,
+                                        A01, A23, bv, hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23,
+                                        dA01, dA23);
                 bar_arrive(BAR_X0 + hh, NTH);
             }
         }
@@ -431,6 +461,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
         Tin* gddl = static_cast<Tin*>(p.ddl) + orow;
         Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + orow : nullptr;
         float* wbc = p.ws_bc + ((int64_t)blockIdx.x * p.b + bi) * p.L * 2 * NS;
+        const float* gyp = YPRE ? p.ypre + (int64_t)bi * p.L * p.D + d0 : nullptr;
         float accD = 0.f, accB = 0.f;
 
         auto issue = [&](int k) {
@@ -441,6 +472,8 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                 if (HAS_Z)
                     stage_tile<Tin, SCH>(&S.z[r][0][0], gz + t0 * p.z_sl, p.z_sl, TCK, rv, nd, p.vec_z, at, NAUX);
                 stage_tile<Tin, SCH>(&S.dout[r][0][0], gdo + t0 * p.dout_sl, p.dout_sl, TCK, rv, nd, p.vec_dout, at, NAUX);
+                if (YPRE)
+                    stage_tile<float, SCH>(&S.yp[r][0][0], gyp + (int64_t)t0 * p.D, p.D, TCK, rv, nd, p.vec_yp, at, NAUX);
                 stage_tile<Tin, NS>(&S.B[r][0][0], gB + t0 * p.B_sl, p.B_sl, TCK, rv, p.N, p.vec_B, at, NAUX);
                 stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, TCK, rv, p.N, p.vec_C, at, NAUX);
             }
@@ -483,12 +516,12 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                     const int tt = at / SCH + m * (NAUX / SCH);
                     const int t = tlo + tt;
                     if (t < nt) {
-                        // rotate the state-group order per lane pair: conflict-free 16-byte loads
-                        const int rot = (ech >> 1) & 3;
-                        const float4 n0 = S.nred[hh][tt][ech][(rot + 0) & 3];
-                        const float4 n1 = S.nred[hh][tt][ech][(rot + 1) & 3];
-                        const float4 n2 = S.nred[hh][tt][ech][(rot + 2) & 3];
-                        const float4 n3 = S.nred[hh][tt][ech][(rot + 3) & 3];
+                        // rotate the state-group order per lane quad: conflict-free 8-byte loads
+                        const int rot = (ech >> 2) & 3;
+                        const float2 n0 = S.nsd[hh][tt][ech][(rot + 0) & 3];
+                        const float2 n1 = S.nsd[hh][tt][ech][(rot + 1) & 3];
+                        const float2 n2 = S.nsd[hh][tt][ech][(rot + 2) & 3];
+                        const float2 n3 = S.nsd[hh][tt][ech][(rot + 3) & 3];
                         const float sgb = (n0.x + n1.x) + (n2.x + n3.x);
                         const float sda = (n0.y + n1.y) + (n2.y + n3.y);
                         const float dte = S.dd[s][t][ech].x;
@@ -499,7 +532,13 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                         gdu[o] = Elem<Tin>::from_f(du);
                         gddl[o] = Elem<Tin>::from_f(draw);
                         if (HAS_Z) {
-                            const float y = fmaf(eD, e.x, (n0.z + n1.z) + (n2.z + n3.z));
+                            float y;
+                            if (YPRE) {
+                                y = S.yp[k % RING][t][ech];
+                            } else {
+                                const float4 q4 = *reinterpret_cast<const float4*>(&S.nyp[hh][tt][ech][0]);
+                                y = fmaf(eD, e.x, (q4.x + q4.y) + (q4.z + q4.w));
+                            }
                             gdz[o] = Elem<Tin>::from_f(e.z * y);
                         }
                         accD = fmaf(e.w, e.x, accD);
@@ -617,7 +656,7 @@ static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
 
 template <typename Tin, bool HAS_Z>
 static cudaError_t launch_bwd_t(const ScanDev& p, cudaStream_t st) {
-    auto k = scan_bwd_kernel<Tin, HAS_Z>;
+    auto k = (HAS_Z && p.ypre) ? scan_bwd_kernel<Tin, HAS_Z, true> : scan_bwd_kernel<Tin, HAS_Z, false>;
     const int smem = sizeof(BwdSmem<Tin>);
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;

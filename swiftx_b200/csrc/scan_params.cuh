@@ -20,12 +20,13 @@ struct ScanDev {
     const float* dbias;
     const float* h0;
     // 16-byte cp.async is legal for these tiles
-    bool vec_u, vec_dl, vec_z, vec_B, vec_C, vec_dout;
+    bool vec_u, vec_dl, vec_z, vec_B, vec_C, vec_dout, vec_yp;
     // forward outputs
     void* out;
     float* h_last;
     float* ck;               // (b, nck, D, 16)
     float* dsum;             // (b, D) sum over t of delta_eff, optional
+    float* ypre;             // (b, L, D) fp32 pre-gate output: forward writes, backward reads
     // backward
     const void* dout; int64_t dout_sb, dout_sl;
     void* du; void* ddl; void* dz; void* dB; void* dC;

@@ -77,12 +77,14 @@ def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
 
 def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
                  h0=None, out_dtype=None, checkpoints=False, return_last_state=False,
-                 return_delta_sum=False, write_out=True):
+                 return_delta_sum=False, write_out=True, pre_out=None):
     """One kernel launch of the forward scan (no autograd).
 
     Returns (out, checkpoints or None, last_state or None), plus delta_sum (b, D) -- the
     sum over t of delta_eff -- when return_delta_sum.  write_out=False skips the output
-    (out is None), for callers that only need the final state / delta_sum."""
+    (out is None), for callers that only need the final state / delta_sum.  pre_out, a
+    dense fp32 (b, L, D) tensor, receives the pre-gate output when z is given (the
+    backward can then skip recomputing it)."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
     b, L, Dm = u.shape
@@ -100,14 +102,19 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     a.h_last = hl.data_ptr() if hl is not None else None
     a.checkpoints = ck.data_ptr() if ck is not None else None
     a.delta_sum = ds.data_ptr() if ds is not None else None
+    if pre_out is not None and z is not None:
+        if pre_out.dtype != torch.float32 or not pre_out.is_contiguous() or pre_out.shape != (b, L, Dm):
+            raise ValueError("pre_out must be a dense fp32 (b, L, D) tensor")
+        a.out_pre = pre_out.data_ptr()
     _lib.check(lib.swx_scan_fwd(a, _lib.stream_ptr(u.device)), "swx_scan_fwd")
     if return_delta_sum:
         return out, ck, hl, ds
     return out, ck, hl
 
 
-def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, dout):
-    """One call of the backward kernels (no autograd).  Returns a dict of gradients."""
+def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, dout, y_pre=None):
+    """One call of the backward kernels (no autograd).  Returns a dict of gradients.
+    y_pre: the pre-gate output the forward wrote to pre_out (optional, with z)."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
     b, L, Dm = u.shape
@@ -131,6 +138,8 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     for k in ("du", "ddelta", "dz", "dB", "dC", "dA", "dD", "ddelta_bias", "dh0"):
         setattr(a, k, g[k].data_ptr() if g[k] is not None else None)
     a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
+    if y_pre is not None and z is not None:
+        a.out_pre = y_pre.data_ptr()
     _lib.check(lib.swx_scan_bwd(a, _lib.stream_ptr(dev)), "swx_scan_bwd")
     return g
 
@@ -143,13 +152,15 @@ class SelectiveScanFn(torch.autograd.Function):
     def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, out_dtype,
                 return_last_state):
         need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9))
+        pre = (torch.empty(u.shape, device=u.device, dtype=torch.float32)
+               if need_grad and z is not None else None)
         out, ck, hl = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0,
                                    out_dtype, checkpoints=need_grad,
-                                   return_last_state=return_last_state)
+                                   return_last_state=return_last_state, pre_out=pre)
         ctx.delta_softplus = delta_softplus
         ctx.dtypes = [t.dtype if t is not None else None for t in (u, delta, A, B, C, D, z, delta_bias, h0)]
         if need_grad:
-            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, h0, ck)
+            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, h0, ck, pre)
         if return_last_state:
             ctx.mark_non_differentiable(hl)
             return out, hl
@@ -157,8 +168,8 @@ class SelectiveScanFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout, *unused):
-        u, delta, A, B, C, D, z, delta_bias, h0, ck = ctx.saved_tensors
-        g = scan_backward(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, h0, ck, dout)
+        u, delta, A, B, C, D, z, delta_bias, h0, ck, pre = ctx.saved_tensors
+        g = scan_backward(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, h0, ck, dout, y_pre=pre)
         dts = ctx.dtypes
         cast = lambda t, dt: None if t is None or dt is None else t.to(dt)  # noqa: E731
         return (cast(g["du"], dts[0]), cast(g["ddelta"], dts[1]), cast(g["dA"], dts[2]),

@@ -30,7 +30,7 @@ def test_struct_mirrors_match():
     assert lib.swx_scan_args_size() == ctypes.sizeof(_lib.ScanArgs)
     assert lib.swx_conv_args_size() == ctypes.sizeof(_lib.ConvArgs)
     assert lib.swx_decode_args_size() == ctypes.sizeof(_lib.DecodeArgs)
-    assert lib.swx_abi_version() == 2
+    assert lib.swx_abi_version() == 3
 
 
 def test_status_strings():

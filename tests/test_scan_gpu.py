@@ -137,16 +137,19 @@ def test_fwd_bwd_vs_oracle(case):
     if not sp:   # plain delta: pass the positive softplus(delta_raw + bias) as the block does
         inp["delta"] = torch.nn.functional.softplus(inp["delta"] + inp["delta_bias"])
     out_o, hl_o, gr_o, scale = oracle_case(inp, gate, sp, wD)
+    pre = torch.empty(inp["u"].shape, device=DEV, dtype=torch.float32)
     out, ck, hl = scan_forward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"],
                                inp["D"] if wD else None, inp["z"] if gate else None,
                                inp["delta_bias"] if sp else None, sp, checkpoints=True,
-                               return_last_state=True)
+                               return_last_state=True, pre_out=pre)
     assert_close(np64(out), out_o, 1e-4, 1e-5, "out")
     assert_close(np64(hl), hl_o, 1e-4, 1e-5, "h_last")
-    g = scan_backward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"] if wD else None,
-                      inp["z"] if gate else None, inp["delta_bias"] if sp else None, sp, None, ck,
-                      inp["dout"])
-    check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"] if wD else None,
+            inp["z"] if gate else None, inp["delta_bias"] if sp else None, sp, None, ck, inp["dout"])
+    # backward with the saved pre-gate output and with the readout recomputed
+    for y_pre in ((pre, None) if gate else (None,)):
+        g = scan_backward(*args, y_pre=y_pre)
+        check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
 
 
 def test_initial_state_and_grad():
@@ -217,9 +220,10 @@ def test_config1_full_size_vs_oracle():
     inp = config_inputs(8, 2048, 512, 16, seed=0, device=DEV)
     oracle.set_num_threads(max(1, oracle.num_threads()))
     out_o, hl_o, gr_o, scale = oracle_case(inp)
+    pre = torch.empty(inp["u"].shape, device=DEV, dtype=torch.float32)
     out, ck, _ = scan_forward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
-                              inp["delta_bias"], True, checkpoints=True)
+                              inp["delta_bias"], True, checkpoints=True, pre_out=pre)
     assert_close(np64(out), out_o, 1e-4, 1e-5, "out")
     g = scan_backward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
-                      inp["delta_bias"], True, None, ck, inp["dout"])
+                      inp["delta_bias"], True, None, ck, inp["dout"], y_pre=pre)
     check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
