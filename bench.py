@@ -356,45 +356,89 @@ def run_lm_train(args, world, rank, local):
     """Sift byte-level LM training step: 8 layers, d_model 256, expand 2, d_state 16, d_conv 4,
     vocab 256, tied embedding, batch 16 x 512 i.i.d. random bytes per GPU, AdamW lr 3e-4
     (betas 0.9/0.95, weight decay 0.1 on matrices), grad clip 1.0, bf16 autocast as the
-    reference trainer (training/train.py:133-172); data parallel with NCCL all-reduce."""
+    reference trainer (training/train.py:133-172).  Data parallel: gradients live in one
+    flat fp32 buffer that is all-reduced (NCCL, average) once per step.  The forward +
+    backward and the clip + AdamW update are each replayed as a CUDA graph (the step is
+    otherwise bound by kernel-launch overhead); --no-graph runs them eagerly."""
+    import torch.distributed as dist
+
     from swiftx_b200.sift import SiftConfig, SiftLM
     dev = torch.device("cuda", local)
     torch.manual_seed(0)
     model = SiftLM(SiftConfig(vocab_size=256, d_model=256, n_layers=8, d_state=16, d_conv=4, expand=2)).to(dev)
-    decay = [p for p in model.parameters() if p.dim() >= 2 and not getattr(p, "_no_weight_decay", False)]
+    params = list(model.parameters())
+    if world > 1:                                   # identical start on every rank
+        for p in params:
+            dist.broadcast(p.data, src=0)
+    flat = torch.zeros(sum(p.numel() for p in params), device=dev, dtype=torch.float32)
+    off = 0
+    for p in params:
+        p.grad = flat[off:off + p.numel()].view_as(p)
+        off += p.numel()
+    decay = [p for p in params if p.dim() >= 2 and not getattr(p, "_no_weight_decay", False)]
     ids = {id(p) for p in decay}
-    no_decay = [p for p in model.parameters() if id(p) not in ids]
-    net = model
-    if world > 1:
-        from torch.nn.parallel import DistributedDataParallel as DDP
-        net = DDP(model, device_ids=[local], gradient_as_bucket_view=True)
+    no_decay = [p for p in params if id(p) not in ids]
+    graphed = not args.no_graph
     opt = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1}, {"params": no_decay, "weight_decay": 0.0}],
-                            lr=3e-4, betas=(0.9, 0.95), fused=True)
+                            lr=3e-4, betas=(0.9, 0.95), fused=True, capturable=graphed)
     B, L = 16, 512
     g = torch.Generator().manual_seed(1234 + rank)
     host = torch.randint(0, 256, (B, L + 1), generator=g, dtype=torch.long).pin_memory()
     tok = host.to(dev)
 
-    def train_step(t):
+    def fwd_bwd():
+        flat.zero_()
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
-            _, loss = net(t[:, :-1], t[:, 1:])
-        opt.zero_grad(set_to_none=True)
+            _, loss = model(tok[:, :-1], tok[:, 1:])
         loss.backward()
-        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
-        opt.step()
-        return loss
+        return loss.detach()
 
-    ms, clocks = timed_steps(lambda: train_step(tok), args, world, local, dev)
+    def update():
+        torch.nn.utils.clip_grad_norm_(params, 1.0)
+        opt.step()
+
+    def allreduce():
+        if world > 1:
+            dist.all_reduce(flat, op=dist.ReduceOp.AVG)
+
+    if graphed:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(3):
+                fwd_bwd()
+                allreduce()
+                update()
+        torch.cuda.current_stream().wait_stream(side)
+        g_fb, g_up = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g_fb):
+            static_loss = fwd_bwd()
+        with torch.cuda.graph(g_up):
+            update()
+
+        def train_step():
+            g_fb.replay()
+            allreduce()
+            g_up.replay()
+            return static_loss
+    else:
+        def train_step():
+            loss = fwd_bwd()
+            allreduce()
+            update()
+            return loss
+
+    ms, clocks = timed_steps(train_step, args, world, local, dev)
     tokens = B * L * world
 
     def e2e_step():
-        t = host.to(dev, non_blocking=True)
-        return train_step(t).detach().to("cpu", non_blocking=True)
+        tok.copy_(host, non_blocking=True)
+        return train_step().to("cpu", non_blocking=True)
     ms_e2e, _ = timed_steps(e2e_step, args, world, local, dev)
     res = base_line(args, world, METRIC, round(tokens / (ms * 1e-3), 1), "tokens/s", ms, "bf16",
                     {"workload": "Sift LM train step (config 2)", "model": "SiftLM 8L d256 e2 N16 vocab256",
                      "global_batch": B * world, "seq_len": L, "parallelism": f"dp{world}",
-                     "l2": "activations and weights per step exceed L2"})
+                     "cuda_graph": graphed, "l2": "activations and weights per step exceed L2"})
     res["e2e"] = {"value": round(tokens / (ms_e2e * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step":
                   host.numel() * host.element_size(), "d2h_bytes_per_step": 4}
     res["gpu_launches"] = 6 * 8 * args.steps      # per layer: conv fwd, scan fwd, conv bwd x2, scan bwd x2
@@ -502,6 +546,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="lm_train: run the step eagerly, no CUDA graphs")
     ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode"], default="scan",
                     help="scan: config 1 (default, the headline); lm_train: config 2; long_scan: config 3; "
                          "decode: config 4")

@@ -18,7 +18,7 @@
 namespace swx {
 
 constexpr int CONV_MAXK = 6;
-constexpr int CONV_TT = 64;       // steps per thread
+constexpr int CONV_TT = 16;       // steps per thread (short tiles: more threads in flight)
 constexpr int CONV_NT = 128;      // threads (channels) per CTA
 
 struct ConvDev {

@@ -27,6 +27,9 @@
 // shared memory in fixed order; cross-CTA and cross-batch sums are written as
 // partials and summed by a second kernel in fixed order, so every gradient is
 // bit-reproducible (no float atomics, unlike models/triton_scan.py:101-102,108-109).
+#include <mutex>
+#include <vector>
+
 #include "common.cuh"
 #include "scan_params.cuh"
 
@@ -643,11 +646,31 @@ __global__ void scan_bwd_finalize_kernel(const ScanDev p) {
 }
 
 // =============================================================== launchers
+// Opt a kernel into more than 48 KB of dynamic shared memory.  Done once per kernel
+// and device (cached), so later launches -- e.g. inside CUDA-graph capture -- make no
+// runtime configuration calls.
+template <typename K>
+static cudaError_t allow_smem(K kernel, int bytes) {
+    struct Entry { int dev; const void* fn; };
+    static std::mutex mu;
+    static std::vector<Entry> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const void* fn = reinterpret_cast<const void*>(kernel);
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& x : done)
+        if (x.dev == dev && x.fn == fn) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.push_back({dev, fn});
+    return e;
+}
+
 template <typename Tin, typename Tout, bool HAS_Z>
 static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
     auto k = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true> : scan_fwd_kernel<Tin, Tout, HAS_Z, false>;
     const int smem = sizeof(FwdSmem<Tin>);
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = allow_smem(k, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
     k<<<grid, NTH, smem, st>>>(p);
@@ -658,7 +681,7 @@ template <typename Tin, bool HAS_Z>
 static cudaError_t launch_bwd_t(const ScanDev& p, cudaStream_t st) {
     auto k = (HAS_Z && p.ypre) ? scan_bwd_kernel<Tin, HAS_Z, true> : scan_bwd_kernel<Tin, HAS_Z, false>;
     const int smem = sizeof(BwdSmem<Tin>);
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = allow_smem(k, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
     k<<<grid, NTH, smem, st>>>(p);
