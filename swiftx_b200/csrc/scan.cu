@@ -39,6 +39,8 @@ constexpr int SCH = 32;               // channels per CTA
 constexpr int NSCAN = 128;            // recurrence threads
 constexpr int NAUX = 128;             // helper threads
 constexpr int NTH = NSCAN + NAUX;
+constexpr int FNAUX = 256;            // helper threads of the forward (two warps per sub-partition)
+constexpr int FNTH = NSCAN + FNAUX;
 constexpr int FT = 32;                // forward tile (steps)
 constexpr int HT = TCK / 2;           // backward half tile (steps)
 constexpr int RING = 4;               // raw staging slots
@@ -63,7 +65,7 @@ struct FwdSmem {
     Tin C[RING][FT][NS];
     float2 dd[2][FT][SCH];        // (delta_eff, delta_eff * u)
     float yp[2][FT][SCH][4];      // partial readouts of the 4 state groups
-    float red[NAUX];              // per-thread sums of delta_eff
+    float red[FNAUX];              // per-thread sums of delta_eff
 };
 
 template <bool FULL, bool WR, typename Tin>
@@ -108,7 +110,7 @@ __device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], c
 // WR: write the output (pass 1 of the sequence-parallel scan needs only the final state
 // and the per-channel sum of delta_eff, so it skips C, z, the readout and the stores).
 template <typename Tin, typename Tout, bool HAS_Z, bool WR>
-__global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
+__global__ void __launch_bounds__(FNTH, 1) scan_fwd_kernel(const ScanDev p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem<Tin>& S = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
 
@@ -136,7 +138,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
         const int64_t ck_stride = (int64_t)p.D * NS;
         for (int c = 0; c < nchunk; ++c) {
             const int s = c & 1, t0 = c * FT, nt = min(FT, p.L - t0);
-            bar_sync(BAR_D0 + s, NTH);
+            bar_sync(BAR_D0 + s, FNTH);
             float* ckp = (p.ck && dvalid)
                              ? p.ck + (((int64_t)bi * p.nck + t0 / TCK) * p.D + d) * NS + 4 * j
                              : nullptr;
@@ -145,7 +147,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
                 fwd_tile<true, WR>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
             else
                 fwd_tile<false, WR>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
-            bar_arrive(BAR_X0 + s, NTH);
+            bar_arrive(BAR_X0 + s, FNTH);
         }
         if (p.h_last && dvalid) {
             hv[0] = h01.x; hv[1] = h01.y; hv[2] = h23.x; hv[3] = h23.y;
@@ -172,13 +174,13 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
         auto issue = [&](int c) {
             if (c < nchunk) {
                 const int t0 = c * FT, rv = min(FT, p.L - t0), r = c % RING;
-                stage_tile<Tin, SCH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, FT, rv, nd, p.vec_u, at, NAUX);
-                stage_tile<Tin, SCH>(&S.dl[r][0][0], gdl + t0 * p.dl_sl, p.dl_sl, FT, rv, nd, p.vec_dl, at, NAUX);
+                stage_tile<Tin, SCH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, FT, rv, nd, p.vec_u, at, FNAUX);
+                stage_tile<Tin, SCH>(&S.dl[r][0][0], gdl + t0 * p.dl_sl, p.dl_sl, FT, rv, nd, p.vec_dl, at, FNAUX);
                 if (HAS_Z && WR)
-                    stage_tile<Tin, SCH>(&S.z[r][0][0], gz + t0 * p.z_sl, p.z_sl, FT, rv, nd, p.vec_z, at, NAUX);
-                stage_tile<Tin, NS>(&S.B[r][0][0], gB + t0 * p.B_sl, p.B_sl, FT, rv, p.N, p.vec_B, at, NAUX);
+                    stage_tile<Tin, SCH>(&S.z[r][0][0], gz + t0 * p.z_sl, p.z_sl, FT, rv, nd, p.vec_z, at, FNAUX);
+                stage_tile<Tin, NS>(&S.B[r][0][0], gB + t0 * p.B_sl, p.B_sl, FT, rv, p.N, p.vec_B, at, FNAUX);
                 if (WR)
-                    stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, FT, rv, p.N, p.vec_C, at, NAUX);
+                    stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, FT, rv, p.N, p.vec_C, at, FNAUX);
             }
             cp_async_commit();
         };
@@ -188,8 +190,8 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
         auto derive = [&](int c) {
             const int r = c % RING, s = c & 1, nt = min(FT, p.L - c * FT);
 #pragma unroll
-            for (int m = 0; m < FT * SCH / (2 * NAUX); ++m) {
-                const int t = 2 * (at / SCH + m * (NAUX / SCH));
+            for (int m = 0; m < FT * SCH / (2 * FNAUX); ++m) {
+                const int t = 2 * (at / SCH + m * (FNAUX / SCH));
                 const float2 raw = add2(f2(Elem<Tin>::to_f(S.dl[r][t][ech]), Elem<Tin>::to_f(S.dl[r][t + 1][ech])), bias2);
                 float2 dte = raw, dsp;
                 if (p.softplus) softplus2(raw, dte, dsp);
@@ -204,8 +206,8 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
             if (!WR) return;
             const int r = c % RING, s = c & 1, t0 = c * FT, nt = min(FT, p.L - t0);
 #pragma unroll
-            for (int m = 0; m < FT * SCH / (2 * NAUX); ++m) {
-                const int t = 2 * (at / SCH + m * (NAUX / SCH));
+            for (int m = 0; m < FT * SCH / (2 * FNAUX); ++m) {
+                const int t = 2 * (at / SCH + m * (FNAUX / SCH));
                 const float4 q0 = *reinterpret_cast<const float4*>(&S.yp[s][t][ech][0]);
                 const float4 q1 = *reinterpret_cast<const float4*>(&S.yp[s][t + 1][ech][0]);
                 float2 y = f2((q0.x + q0.y) + (q0.z + q0.w), (q1.x + q1.y) + (q1.z + q1.w));
@@ -231,33 +233,33 @@ __global__ void __launch_bounds__(NTH, 1) scan_fwd_kernel(const ScanDev p) {
         issue(1);
         issue(2);
         cp_async_wait<2>();
-        bar_sync(BAR_AUX, NAUX);
+        bar_sync(BAR_AUX, FNAUX);
         derive(0);
-        bar_arrive(BAR_D0, NTH);
+        bar_arrive(BAR_D0, FNTH);
         for (int c = 0; c < nchunk; ++c) {
             if (c >= 1) {
-                bar_sync(BAR_X0 + ((c - 1) & 1), NTH);
+                bar_sync(BAR_X0 + ((c - 1) & 1), FNTH);
                 epilogue(c - 1);
             }
             if (c + 1 < nchunk) {
                 cp_async_wait<1>();
-                bar_sync(BAR_AUX, NAUX);
+                bar_sync(BAR_AUX, FNAUX);
                 derive(c + 1);
-                bar_arrive(BAR_D0 + ((c + 1) & 1), NTH);
+                bar_arrive(BAR_D0 + ((c + 1) & 1), FNTH);
             }
-            bar_sync(BAR_AUX, NAUX);      // raw slot (c-1) % RING no longer read
+            bar_sync(BAR_AUX, FNAUX);      // raw slot (c-1) % RING no longer read
             issue(c + 3);
         }
-        bar_sync(BAR_X0 + ((nchunk - 1) & 1), NTH);
+        bar_sync(BAR_X0 + ((nchunk - 1) & 1), FNTH);
         epilogue(nchunk - 1);
         cp_async_wait<0>();
         if (p.dsum) {                      // sum over the 4 thread groups of a channel
             S.red[at] = dsum;
-            bar_sync(BAR_AUX, NAUX);
+            bar_sync(BAR_AUX, FNAUX);
             if (at < SCH && evalid) {
                 float sum = 0.f;
 #pragma unroll
-                for (int m = 0; m < NAUX / SCH; ++m) sum += S.red[at + m * SCH];
+                for (int m = 0; m < FNAUX / SCH; ++m) sum += S.red[at + m * SCH];
                 p.dsum[(int64_t)bi * p.D + d0 + at] = sum;
             }
         }
@@ -673,7 +675,7 @@ static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
     cudaError_t e = allow_smem(k, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
-    k<<<grid, NTH, smem, st>>>(p);
+    k<<<grid, FNTH, smem, st>>>(p);
     return cudaGetLastError();
 }
 
