@@ -235,21 +235,20 @@ def run_ours(args, world, rank, local):
 
 
 def run_e2e(args, inp, dev, world):
-    from swiftx_b200.selective_scan import scan_backward, scan_forward
+    """The scan workload through the host-buffer API: every step copies its inputs from
+    pinned host memory, runs forward + backward, and copies every result back, with the
+    copies of one row chunk overlapping the kernels of the next (HostScanPipeline)."""
+    from swiftx_b200.host_pipeline import HostScanPipeline
+    b, L, D, N = CFG["b"], CFG["L"], CFG["D"], CFG["N"]
     host = {k: (v.cpu().pin_memory() if v is not None else None) for k, v in inp.items()}
     keys_in = ["u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias"]
     h2d = sum(host[k].numel() * host[k].element_size() for k in keys_in)
+    pipe = HostScanPipeline(b, L, D, N, rows_per_chunk=args.e2e_rows, n_compute=args.e2e_streams, device=dev)
+    res = pipe.allocate_host_outputs()
 
     def step():
-        d = {k: host[k].to(dev, non_blocking=True) for k in keys_in}
-        pre = torch.empty(d["u"].shape, device=dev, dtype=torch.float32)
-        out, ck, _ = scan_forward(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"],
-                                  d["delta_bias"], True, checkpoints=True, pre_out=pre)
-        g = scan_backward(d["u"], d["delta"], d["A"], d["B"], d["C"], d["D"], d["z"],
-                          d["delta_bias"], True, None, ck, d["dout"], y_pre=pre)
-        res = [out] + [v for v in g.values() if v is not None]
-        outs = [r.to("cpu", non_blocking=True) for r in res]
-        return outs, sum(r.numel() * r.element_size() for r in res)
+        pipe.forward_backward(host["u"], host["delta"], host["A"], host["B"], host["C"], host["dout"],
+                              D=host["D"], z=host["z"], delta_bias=host["delta_bias"], out=res)
 
     for _ in range(max(1, args.warmup)):
         step()
@@ -257,17 +256,17 @@ def run_e2e(args, inp, dev, world):
     barrier(world)
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record()
-    d2h = 0
     for _ in range(args.steps):
-        _, d2h = step()
+        step()
     t1.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world, dev)
-    b, L, D, N = CFG["b"], CFG["L"], CFG["D"], CFG["N"]
     fwd_b, bwd_b = alg_bytes(b, L, D, N)
     return {"value": round((fwd_b + bwd_b) * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "swiftx_b200.selective_scan.scan_forward/scan_backward (C ABI) from pinned host buffers"}
+            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": pipe.d2h_bytes(res),
+            "api": "swiftx_b200.host_pipeline.HostScanPipeline.forward_backward (C ABI kernels) on pinned "
+                   f"host tensors; {len(pipe.chunks)} row chunks, H2D / kernels / D2H overlapped on "
+                   f"{2 + pipe.n_compute} streams"}
 
 
 # ----------------------------------------------------------------- CPU oracle (reference arm / baseline)
@@ -547,6 +546,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="lm_train: run the step eagerly, no CUDA graphs")
+    ap.add_argument("--e2e-rows", type=int, default=1, help="scan e2e: batch rows per pipelined chunk")
+    ap.add_argument("--e2e-streams", type=int, default=2, help="scan e2e: compute streams of the pipeline")
     ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode"], default="scan",
                     help="scan: config 1 (default, the headline); lm_train: config 2; long_scan: config 3; "
                          "decode: config 4")

@@ -45,7 +45,8 @@ def test_sizes_of_checkpoints_and_workspace():
     assert lib.swx_scan_checkpoint_floats(8, 2048, 512) == 8 * 128 * 512 * 16
     assert lib.swx_scan_checkpoint_floats(1, 17, 3) == 1 * 2 * 3 * 16
     assert lib.swx_scan_bwd_workspace_bytes(8, 2048, 512) >= 16 * 8 * 2048 * 32 * 4
-    assert lib.swx_conv1d_bwd_workspace_bytes(2, 130, 8, 4) == 2 * 3 * 8 * 5 * 4
+    # one (weight, bias) partial per (row, 16-step time tile, channel): 2 rows x 9 tiles x 8 ch x (4+1) floats
+    assert lib.swx_conv1d_bwd_workspace_bytes(2, 130, 8, 4) == 2 * 9 * 8 * 5 * 4
 
 
 def test_host_side_validation_without_gpu():
