@@ -13,7 +13,10 @@ runs on the sm_100a kernels:
 
 and decode runs the conv-window / state-update kernels around the x_proj / dt_proj GEMVs.
 Fusing the gate is exactly the reference's y * silu(z) when no SiftX pathway mixing is
-configured (models/sift_block.py:132-142); pathway gating is not supported here.
+configured (models/sift_block.py:132-142).  With pathway_gate (SiftX), the per-token
+group weights sit between the scan and the gate, so the scan kernel runs without z
+(D skip and softplus still fused) and the mix and gate follow in torch, as in the
+reference.
 """
 import math
 from dataclasses import dataclass
@@ -52,8 +55,6 @@ class SiftBlock(nn.Module):
                  dt_max=1e-1, conv_bias=True, bias=False, scan_impl="fast", scan_mode="auto",
                  timescales=None, pathway_gate=False):
         super().__init__()
-        if pathway_gate:
-            raise NotImplementedError("SiftX pathway gating is not part of the B200 hot path")
         self.d_model = d_model
         self.d_state = d_state
         self.d_conv = d_conv
@@ -67,16 +68,26 @@ class SiftBlock(nn.Module):
         self.x_proj = nn.Linear(self.d_inner, self.dt_rank + 2 * d_state, bias=False)
         self.dt_proj = nn.Linear(self.dt_rank, self.d_inner, bias=True)
         init_dt_proj(self.dt_proj, self.dt_rank, dt_min, dt_max)
+        # SiftX multi-timescale groups (models/sift_block.py:74-93): contiguous channel
+        # groups with their own dt range, and an optional per-token softmax over groups
         self.timescales = [tuple(t) for t in timescales] if timescales else None
+        self.n_groups = len(self.timescales) if self.timescales else 1
+        self.register_buffer("group_of", torch.zeros(self.d_inner, dtype=torch.long), persistent=False)
         if self.timescales:
             bounds = torch.linspace(0, self.d_inner, len(self.timescales) + 1).round().long().tolist()
             for i, (lo, hi) in enumerate(self.timescales):
                 a, b = bounds[i], bounds[i + 1]
+                self.group_of[a:b] = i
                 tmp = nn.Linear(self.dt_rank, b - a, bias=True)
                 init_dt_proj(tmp, self.dt_rank, lo, hi)
                 with torch.no_grad():
                     self.dt_proj.bias[a:b] = tmp.bias
         self.pathway = None
+        if pathway_gate and self.n_groups > 1:
+            self.pathway = nn.Linear(self.d_inner, self.n_groups)
+            nn.init.zeros_(self.pathway.weight)
+            nn.init.zeros_(self.pathway.bias)
+            self.pathway.bias._no_reinit = True
         self.A_log = nn.Parameter(init_A_log(self.d_inner, d_state))
         self.A_log._no_weight_decay = True
         self.D = nn.Parameter(torch.ones(self.d_inner))
@@ -95,10 +106,20 @@ class SiftBlock(nn.Module):
         x = causal_conv1d_fn(x, self.conv1d.weight, self.conv1d.bias, "silu")
         delta, B, C = self._split(x)
         A = -torch.exp(self.A_log.float())
+        gate = z if self.pathway is None else None
         with torch.autocast(device_type=x.device.type, enabled=False):
-            y = selective_scan_fn(x, delta, A, B, C, self.D.float(), z=z,
+            y = selective_scan_fn(x, delta, A, B, C, self.D.float(), z=gate,
                                   delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
-        return self.out_proj(y.to(xz.dtype))
+        y = y.to(xz.dtype)
+        if self.pathway is not None:
+            y = self._mix_pathways(y, x) * F.silu(z)
+        return self.out_proj(y)
+
+    def _mix_pathways(self, y, x):
+        """SiftX: reweight the channel groups per token, softmax x G (1 at init)
+        (models/sift_block.py:137-142)."""
+        w = torch.softmax(self.pathway(x), dim=-1) * self.n_groups
+        return y * w[..., self.group_of]
 
     def allocate_state(self, batch, device=None, dtype=torch.float32):
         conv_state = torch.zeros(batch, self.d_inner, self.d_conv, device=device, dtype=dtype)
@@ -112,8 +133,11 @@ class SiftBlock(nn.Module):
         x, z = xz.chunk(2, dim=-1)
         xc = decode_conv_step(x, conv_state, self.conv1d.weight, self.conv1d.bias)
         delta, B, C = self._split(xc)
+        gate = z if self.pathway is None else None
         y = decode_ssm_step(xc, delta.float(), B.float(), C.float(), -torch.exp(self.A_log.float()),
-                            ssm_state, Dskip=self.D, z=z, delta_bias=self.dt_proj.bias)
+                            ssm_state, Dskip=self.D, z=gate, delta_bias=self.dt_proj.bias)
+        if self.pathway is not None:
+            y = self._mix_pathways(y, xc) * F.silu(z)
         return self.out_proj(y.to(self.out_proj.weight.dtype))
 
 

@@ -17,6 +17,12 @@ Fixtures:
   gated.npz          scan(u, softplus(dr + bias)) * silu(z) via the block's glue, all grads
   conv.npz           SiftBlock conv1d + SiLU on the strided x half of in_proj, with grads
   decode.npz         SiftBlock.step intermediates (conv window, state update, gated y)
+  pathway.npz        SiftX block (3 timescale groups, pathway gate): weights, forward output
+                     and 9 recurrent steps (models/sift_block.py:111-175)
+
+    python tests/golden/make_golden.py /path/to/reference --only pathway
+
+regenerates one fixture.
 """
 import math
 import os
@@ -66,10 +72,30 @@ def config_inputs(b, L, D, N, seed=0):
     return u, dr, bias, A, Bm, Cm, Dskip, z
 
 
-def main(ref_root):
+def make_pathway(SiftBlock):
+    """9. SiftX block with pathway mixing (models/sift_block.py:74-93, 111-142, 153-175)."""
+    torch.manual_seed(0)
+    blk = SiftBlock(d_model=16, d_state=8, d_conv=4, expand=2, scan_impl="ref",
+                    timescales=[(1e-3, 1e-2), (1e-2, 3e-2), (3e-2, 1e-1)], pathway_gate=True).double()
+    gen = torch.Generator().manual_seed(11)
+    with torch.no_grad():
+        blk.pathway.weight.copy_(0.5 * torch.randn(blk.pathway.weight.shape, dtype=torch.float64, generator=gen))
+        blk.pathway.bias.copy_(0.5 * torch.randn(blk.pathway.bias.shape, dtype=torch.float64, generator=gen))
+        hidden = torch.randn(2, 29, 16, dtype=torch.float64, generator=gen)
+        out = blk(hidden)
+        state = blk.allocate_state(2, dtype=torch.float64)
+        steps = torch.stack([blk.step(hidden[:, t], state) for t in range(9)], 1)
+    params = {"p_" + k.replace(".", "__"): v for k, v in blk.state_dict().items()}
+    save("pathway", hidden=hidden, out=out, steps=steps, group_of=blk.group_of, **params)
+
+
+def main(ref_root, only=None):
     sys.path.insert(0, ref_root)
     from models.selective_scan import selective_scan_fast, selective_scan_ref
     from models.sift_block import SiftBlock
+    if only == "pathway":
+        make_pathway(SiftBlock)
+        return
 
     # 1. hand-computed known answer
     u = torch.tensor([[[2.0], [4.0], [6.0]]])
@@ -172,6 +198,12 @@ def main(ref_root):
          conv_b=blk.conv1d.bias, A=-torch.exp(blk.A_log.float()).double(), D=blk.D, conv_state0=conv0, ssm_state0=ssm0,
          y=cap["y"], conv_state1=state[0], ssm_state1=state[1])
 
+    make_pathway(SiftBlock)
+
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    args = [a for a in sys.argv[1:] if a != "--only"]
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only:
+        args.remove(only)
+    main(args[0] if args else "/root/reference", only)

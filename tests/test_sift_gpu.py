@@ -213,3 +213,109 @@ def test_graph_captured_train_step_matches_eager():
     eager, graphed = run(False), run(True)
     assert graphed[-1] < 0.5 * graphed[0]
     np.testing.assert_allclose(graphed[:10], eager[:10], rtol=1e-3)
+
+
+def make_pathway_block():
+    """SiftX block: three timescale groups over 32 channels (sizes 11/10/11) and the
+    per-token pathway gate, with non-zero pathway weights so the mix is not the identity."""
+    torch.manual_seed(0)
+    blk = SiftBlock(d_model=16, d_state=8, d_conv=4, expand=2, timescales=[(1e-3, 1e-2), (1e-2, 3e-2), (3e-2, 1e-1)],
+                    pathway_gate=True).to(DEV)
+    with torch.no_grad():
+        blk.pathway.weight.normal_(0, 0.5)
+        blk.pathway.bias.normal_(0, 0.5)
+    return blk
+
+
+def _pathway_reference(blk, hidden, scan):
+    """models/sift_block.py:111-142 with pathway mixing, float64 on the CPU; `scan` computes
+    the ungated scan y + D*u from (xc, delta, A, B, C, D)."""
+    p = {k: v.detach().double().cpu() for k, v in blk.state_dict().items()}
+    h = hidden.detach().double().cpu()
+    xz = h @ p["in_proj.weight"].T
+    D = blk.d_inner
+    x, z = xz[..., :D], xz[..., D:]
+    L = x.shape[1]
+    xc = F.silu(F.conv1d(x.transpose(1, 2), p["conv1d.weight"], p["conv1d.bias"], padding=3,
+                         groups=D)[..., :L].transpose(1, 2))
+    dt, B, C = torch.split(xc @ p["x_proj.weight"].T, [blk.dt_rank, blk.d_state, blk.d_state], dim=-1)
+    delta = F.softplus(dt @ p["dt_proj.weight"].T + p["dt_proj.bias"])
+    A = -torch.exp(p["A_log"])
+    y = scan(xc, delta, A, B, C, p["D"])
+    w = torch.softmax(xc @ p["pathway.weight"].T + p["pathway.bias"], dim=-1) * blk.n_groups
+    y = y * w[..., blk.group_of.cpu()] * F.silu(z)
+    return y @ p["out_proj.weight"].T
+
+
+def test_pathway_block_matches_oracle():
+    blk = make_pathway_block()
+    assert blk.group_of.tolist() == [0] * 11 + [1] * 10 + [2] * 11
+    x = torch.randn(2, 29, 16, device=DEV)
+
+    def scan(xc, delta, A, B, C, Dv):
+        return torch.from_numpy(oracle.scan_fwd(xc.numpy(), delta.numpy(), A.numpy(), B.numpy(), C.numpy(),
+                                                Dv.numpy()))
+    np.testing.assert_allclose(blk(x).detach().double().cpu().numpy(), _pathway_reference(blk, x, scan).numpy(),
+                               rtol=1e-4, atol=1e-5)
+
+
+def test_pathway_step_matches_forward():
+    blk = make_pathway_block()
+    x = torch.randn(2, 9, 16, device=DEV)
+    y_full = blk(x)
+    state = blk.allocate_state(2, device=DEV)
+    ys = [blk.step(x[:, t], state) for t in range(9)]
+    assert torch.allclose(y_full, torch.stack(ys, 1), atol=1e-5)
+
+
+def test_pathway_block_grads_match_autograd():
+    blk = make_pathway_block()
+    x = torch.randn(2, 12, 16, device=DEV)
+    blk(x).pow(2).sum().backward()
+    params = {k: v.detach().double().cpu().requires_grad_() for k, v in blk.state_dict().items()}
+
+    def scan(xc, delta, A, B, C, Dv):
+        hst = torch.zeros(xc.shape[0], xc.shape[2], A.shape[1], dtype=torch.float64)
+        ys = []
+        for t in range(xc.shape[1]):
+            hst = torch.exp(delta[:, t, :, None] * A) * hst + delta[:, t, :, None] * B[:, t, None, :] * xc[:, t, :, None]
+            ys.append((hst * C[:, t, None, :]).sum(-1))
+        return torch.stack(ys, 1) + xc * Dv
+
+    # the block of _pathway_reference again, on grad-tracking float64 copies of the parameters
+    h = x.double().cpu()
+    p = params
+    xz = h @ p["in_proj.weight"].T
+    D = blk.d_inner
+    xx, z = xz[..., :D], xz[..., D:]
+    L = xx.shape[1]
+    xc = F.silu(F.conv1d(xx.transpose(1, 2), p["conv1d.weight"], p["conv1d.bias"], padding=3,
+                         groups=D)[..., :L].transpose(1, 2))
+    dt, B, C = torch.split(xc @ p["x_proj.weight"].T, [blk.dt_rank, blk.d_state, blk.d_state], dim=-1)
+    delta = F.softplus(dt @ p["dt_proj.weight"].T + p["dt_proj.bias"])
+    y = scan(xc, delta, -torch.exp(p["A_log"]), B, C, p["D"])
+    w = torch.softmax(xc @ p["pathway.weight"].T + p["pathway.bias"], dim=-1) * blk.n_groups
+    y = y * w[..., blk.group_of.cpu()] * F.silu(z)
+    (y @ p["out_proj.weight"].T).pow(2).sum().backward()
+    got = dict(blk.named_parameters())
+    assert "pathway.weight" in got and "pathway.bias" in got
+    for k, v in p.items():
+        np.testing.assert_allclose(got[k].grad.double().cpu().numpy(), v.grad.numpy(), rtol=1e-3, atol=1e-4,
+                                   err_msg=k)
+
+
+def test_pathway_block_matches_reference_fixture(golden):
+    """The reference's own SiftX block (pathway.npz, made by importing models/sift_block.py):
+    its weights loaded into this block give the same forward output and recurrent steps."""
+    g = golden("pathway")
+    blk = SiftBlock(d_model=16, d_state=8, d_conv=4, expand=2,
+                    timescales=[(1e-3, 1e-2), (1e-2, 3e-2), (3e-2, 1e-1)], pathway_gate=True).to(DEV)
+    sd = {k[2:].replace("__", "."): torch.from_numpy(v).float() for k, v in g.items() if k.startswith("p_")}
+    blk.load_state_dict(sd)
+    assert blk.group_of.cpu().tolist() == g["group_of"].tolist()
+    hidden = torch.from_numpy(g["hidden"]).float().to(DEV)
+    scale = np.abs(g["out"]).max()
+    np.testing.assert_allclose(blk(hidden).detach().double().cpu().numpy(), g["out"], rtol=1e-4, atol=1e-5 * scale)
+    state = blk.allocate_state(2, device=DEV)
+    steps = torch.stack([blk.step(hidden[:, t], state) for t in range(9)], 1)
+    np.testing.assert_allclose(steps.detach().double().cpu().numpy(), g["steps"], rtol=1e-4, atol=1e-5 * scale)
