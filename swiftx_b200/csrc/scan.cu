@@ -39,8 +39,7 @@ constexpr int SCH = 32;               // channels per CTA
 constexpr int NSCAN = 128;            // recurrence threads
 constexpr int NAUX = 128;             // helper threads
 constexpr int NTH = NSCAN + NAUX;
-constexpr int FNAUX = 256;            // helper threads of the forward (two warps per sub-partition)
-constexpr int FNTH = NSCAN + FNAUX;
+constexpr int FNAUX_MAX = 256;        // helper threads of the forward: 128 or 256 (see launch_fwd_t)
 constexpr int FT = 32;                // forward tile (steps)
 constexpr int HT = TCK / 2;           // backward half tile (steps)
 constexpr int RING = 4;               // raw staging slots
@@ -65,7 +64,7 @@ struct FwdSmem {
     Tin C[RING][FT][NS];
     float2 dd[2][FT][SCH];        // (delta_eff, delta_eff * u)
     float yp[2][FT][SCH][4];      // partial readouts of the 4 state groups
-    float red[FNAUX];              // per-thread sums of delta_eff
+    float red[FNAUX_MAX];          // per-thread sums of delta_eff
 };
 
 template <bool FULL, bool WR, typename Tin>
@@ -109,8 +108,10 @@ __device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], c
 
 // WR: write the output (pass 1 of the sequence-parallel scan needs only the final state
 // and the per-channel sum of delta_eff, so it skips C, z, the readout and the stores).
-template <typename Tin, typename Tout, bool HAS_Z, bool WR>
-__global__ void __launch_bounds__(FNTH, 1) scan_fwd_kernel(const ScanDev p) {
+// NA: helper threads (128 = one helper warp per sub-partition, 256 = two).
+template <typename Tin, typename Tout, bool HAS_Z, bool WR, int NA>
+__global__ void __launch_bounds__(NSCAN + NA, 1) scan_fwd_kernel(const ScanDev p) {
+    constexpr int FNAUX = NA, FNTH = NSCAN + NA;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem<Tin>& S = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
 
@@ -668,14 +669,50 @@ static cudaError_t allow_smem(K kernel, int bytes) {
     return e;
 }
 
+// SM count of the current device and how many CTAs of `kernel` fit on one SM at the given
+// block and shared-memory size; queried once per (device, kernel), then cached.
+template <typename K>
+static cudaError_t sm_fit(K kernel, int threads, int smem, int* sms, int* per_sm) {
+    struct Entry { int dev; const void* fn; int sms, per_sm; };
+    static std::mutex mu;
+    static std::vector<Entry> seen;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    const void* fn = reinterpret_cast<const void*>(kernel);
+    std::lock_guard<std::mutex> lock(mu);
+    for (const Entry& x : seen)
+        if (x.dev == dev && x.fn == fn) { *sms = x.sms; *per_sm = x.per_sm; return cudaSuccess; }
+    e = cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(per_sm, kernel, threads, smem);
+    if (e == cudaSuccess) seen.push_back({dev, fn, *sms, *per_sm});
+    return e;
+}
+
+// Helper-warp count of the forward.  A CTA is paced by its helper warps, so two per SM
+// sub-partition (256 helper threads) is faster when each SM holds one CTA.  When the grid
+// has more CTAs than SMs and the 128-helper CTA fits twice on an SM (bf16 inputs: 95
+// registers, 81 KB of shared memory), two co-resident CTAs -- two recurrence warps per
+// sub-partition, one wave instead of two -- are faster.
 template <typename Tin, typename Tout, bool HAS_Z>
 static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
-    auto k = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true> : scan_fwd_kernel<Tin, Tout, HAS_Z, false>;
+    auto k2 = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true, 256> : scan_fwd_kernel<Tin, Tout, HAS_Z, false, 256>;
+    auto k1 = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true, 128> : scan_fwd_kernel<Tin, Tout, HAS_Z, false, 128>;
     const int smem = sizeof(FwdSmem<Tin>);
-    cudaError_t e = allow_smem(k, smem);
-    if (e != cudaSuccess) return e;
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
-    k<<<grid, FNTH, smem, st>>>(p);
+    const long long nblocks = (long long)grid.x * grid.y;
+    cudaError_t e = allow_smem(k1, smem);
+    if (e != cudaSuccess) return e;
+    int sms = 0, per_sm = 0;
+    e = sm_fit(k1, NSCAN + 128, smem, &sms, &per_sm);
+    if (e != cudaSuccess) return e;
+    if (nblocks > sms && per_sm >= 2) {
+        k1<<<grid, NSCAN + 128, smem, st>>>(p);
+    } else {
+        e = allow_smem(k2, smem);
+        if (e != cudaSuccess) return e;
+        k2<<<grid, NSCAN + 256, smem, st>>>(p);
+    }
     return cudaGetLastError();
 }
 
