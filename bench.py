@@ -488,7 +488,8 @@ def run_long_scan(args, world, rank, local):
 def run_decode(args, world, rank, local):
     """Recurrent decode: batch 256 (sharded over the ranks), 24 layers, D=2048, N=16,
     d_conv=4, fp32 state ~ N(0, 0.1); per layer one fused conv-window shift + state update
-    + C readout + gate launch; the 24-layer step is replayed as one CUDA graph."""
+    + C readout + gate launch (the persistent streaming kernel at this shape); the 24-layer
+    step is replayed as one CUDA graph."""
     import math
 
     from swiftx_b200.decode import decode_step
@@ -529,7 +530,7 @@ def run_decode(args, world, rank, local):
     res["latency_ms_per_token"] = round(ms, 4)
     achieved = per_layer * layers / (ms * 1e-3) / 1e9
     peak, kind = measured_peak()
-    res["roofline"] = {"bound": "hbm", "kernel": "decode_kernel", "achieved": round(achieved, 1), "peak": peak,
+    res["roofline"] = {"bound": "hbm", "kernel": "decode_stream_kernel", "achieved": round(achieved, 1), "peak": peak,
                        "peak_kind": kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                        "alg_bytes_per_launch": per_layer}
     res["clocks"] = clocks

@@ -12,6 +12,9 @@
 // a channel (one 16-byte load/store each, fully coalesced across the warp); the readout
 // is reduced over the 4 lanes with two xor-shuffles.
 #include "common.cuh"
+#include "launch_util.cuh"
+
+#include <algorithm>
 
 namespace swx {
 
@@ -153,6 +156,157 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
     }
 }
 
+// ---------------------------------------------------------------- streaming variant
+// For the common shape (width 4, d_state 16, D a multiple of 64, 16-byte aligned rows)
+// the step is a pure stream: per (row, channel) 64 B of state in and out, the conv
+// window in and out, a few per-token scalars.  A launch of one short-lived CTA per tile
+// leaves the memory pipe idle between waves, so here each CTA stays resident, owns one
+// 64-channel block (its per-channel parameters are loaded once) and walks a strided
+// subset of the batch rows, with the inputs of the next DP_STAGES-1 rows in flight in a
+// cp.async ring while it computes the current one.  Outputs go straight to global memory.
+constexpr int DP_CH = 64;                 // channels per tile
+constexpr int DP_NT = 4 * DP_CH;          // thread = (channel, 4-state group)
+constexpr int DP_STAGES = 4;
+
+struct __align__(16) DecTile {
+    float4 ss[DP_CH][4];                  // SSM state, 64 channels x 16
+    float4 cs[DP_CH];                     // conv window, 64 channels x 4 taps
+    float x[DP_CH], z[DP_CH], dr[DP_CH];  // token input (or xc), gate, delta before bias
+    float4 B[4], C[4];
+};
+
+template <bool CONV, bool HAS_Z>
+__global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, int row_groups) {
+    __shared__ DecTile S[DP_STAGES];
+    const int tid = threadIdx.x;
+    const int j = tid & 3, ch = tid >> 2;
+    const int nblk = p.D / DP_CH;
+    const int cb = blockIdx.x % nblk, rg = blockIdx.x / nblk;
+    const int d0 = cb * DP_CH, d = d0 + ch;
+
+    // per-channel parameters, once per CTA
+    const float4 A4 = *reinterpret_cast<const float4*>(p.A + (int64_t)d * NS + 4 * j);
+    float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
+    float cbias = 0.f;
+    if (CONV) {
+        cw = *reinterpret_cast<const float4*>(p.cw + (int64_t)d * 4);
+        cbias = p.cb ? p.cb[d] : 0.f;
+    }
+    const float dsk = p.Dskip ? p.Dskip[d] : 0.f;
+    const float dbi = p.dbias ? p.dbias[d] : 0.f;
+    const float2 A01 = f2(A4.x, A4.y), A23 = f2(A4.z, A4.w);
+
+    // tile copies: every thread one 16-byte piece of the state; threads 0..63 the conv
+    // window, 64..111 x / z / delta, 112..119 B and C
+    auto issue = [&](int r, int slot) {
+        DecTile& T = S[slot];
+        cp_async16(&T.ss[0][0] + tid, p.ssm_state + ((int64_t)r * p.D + d0) * NS + 4 * tid, 16);
+        if (tid < 64) {
+            if (CONV) cp_async16(&T.cs[tid], p.conv_state + ((int64_t)r * p.D + d0 + tid) * 4, 16);
+        } else if (tid < 80) {
+            cp_async16(&T.x[4 * (tid - 64)], p.x + r * p.x_sb + d0 + 4 * (tid - 64), 16);
+        } else if (tid < 96) {
+            if (HAS_Z) cp_async16(&T.z[4 * (tid - 80)], p.z + r * p.z_sb + d0 + 4 * (tid - 80), 16);
+        } else if (tid < 112) {
+            cp_async16(&T.dr[4 * (tid - 96)], p.dl + r * p.dl_sb + d0 + 4 * (tid - 96), 16);
+        } else if (tid < 116) {
+            cp_async16(&T.B[tid - 112], p.B + r * p.B_sb + 4 * (tid - 112), 16);
+        } else if (tid < 120) {
+            cp_async16(&T.C[tid - 116], p.C + r * p.C_sb + 4 * (tid - 116), 16);
+        }
+    };
+
+#pragma unroll
+    for (int k = 0; k < DP_STAGES - 1; ++k) {
+        const int r = rg + k * row_groups;
+        if (r < p.b) issue(r, k);
+        cp_async_commit();
+    }
+    for (int k = 0;; ++k) {
+        const int r = rg + k * row_groups;
+        if (r >= p.b) break;
+        const int rn = rg + (k + DP_STAGES - 1) * row_groups;
+        if (rn < p.b) issue(rn, (k + DP_STAGES - 1) % DP_STAGES);   // slot read at k-1
+        cp_async_commit();
+        cp_async_wait<DP_STAGES - 1>();
+        __syncthreads();
+
+        const DecTile& T = S[k % DP_STAGES];
+        const int64_t bd = (int64_t)r * p.D + d;
+        float xc = T.x[ch];
+        float4 win = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (CONV) {
+            const float4 w = T.cs[ch];
+            win = make_float4(w.y, w.z, w.w, xc);
+            float acc = cbias;
+            acc = fmaf(win.x, cw.x, acc);
+            acc = fmaf(win.y, cw.y, acc);
+            acc = fmaf(win.z, cw.z, acc);
+            acc = fmaf(win.w, cw.w, acc);
+            xc = silu_f(acc);
+        }
+        const float raw = T.dr[ch] + dbi;
+        float dte = raw;
+        if (p.softplus) {
+            float2 sp, dsp;
+            softplus2(bc2(raw), sp, dsp);
+            dte = sp.x;
+        }
+        const float4 h4 = T.ss[ch][j], b4 = T.B[j], c4 = T.C[j];
+        // same operation order as decode_kernel, so both give identical bits
+        const float2 dt = bc2(dte * LOG2E), dx = bc2(dte * xc);
+        const float2 h01 = fma2(ex2x2(mul2(dt, A01)), f2(h4.x, h4.y), mul2(dx, f2(b4.x, b4.y)));
+        const float2 h23 = fma2(ex2x2(mul2(dt, A23)), f2(h4.z, h4.w), mul2(dx, f2(b4.z, b4.w)));
+        float2 yy = mul2(h01, f2(c4.x, c4.y));
+        yy = fma2(h23, f2(c4.z, c4.w), yy);
+        float y = yy.x + yy.y;
+        y += __shfl_xor_sync(0xffffffffu, y, 1);
+        y += __shfl_xor_sync(0xffffffffu, y, 2);
+        *reinterpret_cast<float4*>(p.ssm_state + bd * NS + 4 * j) = make_float4(h01.x, h01.y, h23.x, h23.y);
+        if (j == 0) {
+            if (CONV) {
+                *reinterpret_cast<float4*>(p.conv_state + bd * 4) = win;
+                if (p.xc_out) p.xc_out[bd] = xc;
+            }
+            y = fmaf(dsk, xc, y);
+            if (HAS_Z) y *= silu_f(T.z[ch]);
+            p.out[bd] = y;
+        }
+        __syncthreads();                  // slot k % DP_STAGES is refilled at k+1
+    }
+    cp_async_wait<0>();
+}
+
+// The streaming variant applies when every tile is full and every row is 16-byte aligned.
+static bool stream_ok(const DecDev& p) {
+    auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const bool conv = p.mode & SWX_DECODE_CONV;
+    if (!(p.mode & SWX_DECODE_SSM) || p.N != NS || (conv && p.K != 4) || p.D % DP_CH != 0) return false;
+    if (!al(p.x) || !al(p.z) || !al(p.dl) || !al(p.B) || !al(p.C) || !al(p.A) || !al(p.ssm_state)) return false;
+    if (conv && (!al(p.conv_state) || !al(p.cw))) return false;
+    if (p.x_sb % 4 || p.dl_sb % 4 || p.B_sb % 4 || p.C_sb % 4 || (p.z && p.z_sb % 4)) return false;
+    return true;
+}
+
+template <bool CONV, bool HAS_Z>
+static cudaError_t launch_stream_t(const DecDev& p, cudaStream_t st) {
+    auto k = decode_stream_kernel<CONV, HAS_Z>;
+    int sms = 0, per_sm = 0;
+    cudaError_t e = sm_fit(k, DP_NT, 0, &sms, &per_sm);
+    if (e != cudaSuccess) return e;
+    const int nblk = p.D / DP_CH;
+    const int slots = std::max(1, sms * per_sm);
+    const int row_groups = std::max(1, std::min(p.b, slots / nblk));
+    k<<<nblk * row_groups, DP_NT, 0, st>>>(p, row_groups);
+    return cudaGetLastError();
+}
+
+static cudaError_t launch_stream(const DecDev& p, cudaStream_t st) {
+    const bool conv = p.mode & SWX_DECODE_CONV;
+    if (conv) return p.z ? launch_stream_t<true, true>(p, st) : launch_stream_t<true, false>(p, st);
+    return p.z ? launch_stream_t<false, true>(p, st) : launch_stream_t<false, false>(p, st);
+}
+
 template <int K>
 static void launch_dec(const DecDev& p, cudaStream_t st) {
     dim3 grid((p.D + DEC_CH - 1) / DEC_CH, (p.b + DEC_RB - 1) / DEC_RB);
@@ -188,6 +342,7 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     p.cw = a->conv_weight; p.cb = a->conv_bias; p.A = a->A; p.Dskip = a->Dskip; p.dbias = a->delta_bias;
     p.conv_state = a->conv_state; p.ssm_state = a->ssm_state; p.xc_out = a->xc_out; p.out = a->out;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (swx::stream_ok(p)) return swx::launch_stream(p, st) == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
     switch ((a->mode & SWX_DECODE_CONV) ? p.K : 4) {
         case 1: swx::launch_dec<1>(p, st); break;
         case 2: swx::launch_dec<2>(p, st); break;

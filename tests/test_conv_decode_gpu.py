@@ -122,3 +122,54 @@ def test_decode_vs_oracle_multi_step(N):
         close(y, yo)
         close(csd, cs_o)
         close(ssd, ss_o)
+
+
+def _stream_case(b, D, seed):
+    N, K = 16, 4
+    g = torch.Generator().manual_seed(seed)
+    p = {"A": -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1), "cw": torch.randn(D, K, generator=g) * 0.5,
+         "cb": torch.randn(D, generator=g), "Dskip": torch.randn(D, generator=g),
+         "dbias": torch.randn(D, generator=g) * 0.5 - 3}
+    st = {"cs": torch.randn(b, D, K, generator=g), "ss": torch.randn(b, D, N, generator=g) * 0.1}
+    steps = [{k: torch.randn(b, n, generator=g) for k, n in (("x", D), ("z", D), ("dr", D), ("B", N), ("C", N))}
+             for _ in range(4)]
+    return p, st, steps
+
+
+def _padded(t):
+    """The same values with a row stride that is not a multiple of 4 elements, which
+    sends the launch to the per-CTA kernel instead of the streaming one."""
+    buf = torch.zeros(t.shape[0], t.shape[1] + 1, device=t.device, dtype=t.dtype)
+    buf[:, :t.shape[1]] = t
+    return buf[:, :t.shape[1]]
+
+
+@pytest.mark.parametrize("b,D,gate", [(5, 128, True), (3, 256, False), (19, 64, True)])
+def test_decode_streaming_path(b, D, gate):
+    """D a multiple of 64, N=16, K=4, aligned rows: the persistent streaming kernel.  It
+    matches the float64 oracle over several steps (fused launch), matches the per-CTA
+    kernel bit for bit on the same values, and the split launch (conv kernel, then the
+    state update alone, which also streams) gives the same result."""
+    p, st, steps = _stream_case(b, D, seed=b + D)
+    dv = {k: v.to(DEV) for k, v in p.items()}
+    cs_s, ss_s = st["cs"].to(DEV), st["ss"].to(DEV)            # streaming, fused
+    cs_r, ss_r = st["cs"].to(DEV), st["ss"].to(DEV)            # per-CTA kernel, fused
+    cs_2, ss_2 = st["cs"].to(DEV), st["ss"].to(DEV)            # streaming, split
+    cs_o, ss_o = st["cs"].double().numpy(), st["ss"].double().numpy()
+    for s in steps:
+        d = {k: v.to(DEV) for k, v in s.items()}
+        z = d["z"] if gate else None
+        kw = dict(Dskip=dv["Dskip"], delta_bias=dv["dbias"])
+        y_s = decode_step(d["x"], cs_s, dv["cw"], dv["cb"], d["dr"], d["B"], d["C"], dv["A"], ss_s, z=z, **kw)
+        y_r = decode_step(_padded(d["x"]), cs_r, dv["cw"], dv["cb"], d["dr"], d["B"], d["C"], dv["A"], ss_r,
+                          z=z, **kw)
+        xc = decode_conv_step(d["x"], cs_2, dv["cw"], dv["cb"])
+        y_2 = decode_ssm_step(xc, d["dr"], d["B"], d["C"], dv["A"], ss_2, z=z, **kw)
+        yo, cs_o, ss_o, _ = oracle.decode_step(s["x"], s["z"] if gate else None, s["dr"], s["B"], s["C"], p["cw"],
+                                               p["cb"], p["A"], p["Dskip"], p["dbias"], cs_o, ss_o)
+        close(y_s, yo)
+        close(ss_s, ss_o)
+        close(cs_s, cs_o)
+        assert torch.equal(y_s, y_r) and torch.equal(ss_s, ss_r) and torch.equal(cs_s, cs_r)
+        close(y_2, yo)
+        assert torch.equal(ss_2, ss_s) and torch.equal(cs_2, cs_s)
