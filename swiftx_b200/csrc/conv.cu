@@ -136,17 +136,39 @@ __global__ void __launch_bounds__(CONV_NT) conv_bwd_kernel(const ConvDev p) {
     ws[K] = dbacc;
 }
 
-__global__ void conv_bwd_finalize_kernel(const ConvDev p) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;      // (d, k) with k <= K
+// Fixed-order column sums of the (row, tile) partials ws[(bi * ntiles + tl)][d][k]:
+// one block per 32 consecutive (d, k) columns; warp w adds rows w, w+32, ... (lanes read
+// 32 adjacent columns of a row: one 128-byte load), then the 32 warp sums of a column are
+// added in warp order.
+constexpr int FIN_WARPS = 32;
+__global__ void __launch_bounds__(32 * FIN_WARPS) conv_bwd_finalize_kernel(const ConvDev p) {
+    __shared__ float part[FIN_WARPS][33];
     const int K1 = p.K + 1;
-    if (i >= p.D * K1) return;
-    const int d = i / K1, k = i % K1;
-    float s = 0.f;
-    for (int bi = 0; bi < p.b; ++bi)
-        for (int tl = 0; tl < p.ntiles; ++tl)
-            s += p.ws[(((int64_t)bi * p.ntiles + tl) * p.D + d) * K1 + k];
-    if (k < p.K) p.dw[(int64_t)d * p.K + k] = s;
-    else if (p.dbias) p.dbias[d] = s;
+    const int W = p.D * K1;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int col = blockIdx.x * 32 + lane;
+    const int rows = p.b * p.ntiles;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (col < W) {
+        int r = w;
+        for (; r + 3 * FIN_WARPS < rows; r += 4 * FIN_WARPS) {
+            a0 += p.ws[(int64_t)r * W + col];
+            a1 += p.ws[(int64_t)(r + FIN_WARPS) * W + col];
+            a2 += p.ws[(int64_t)(r + 2 * FIN_WARPS) * W + col];
+            a3 += p.ws[(int64_t)(r + 3 * FIN_WARPS) * W + col];
+        }
+        for (; r < rows; r += FIN_WARPS) a0 += p.ws[(int64_t)r * W + col];
+    }
+    part[w][lane] = (a0 + a1) + (a2 + a3);
+    __syncthreads();
+    if (w == 0 && col < W) {
+        float s = 0.f;
+#pragma unroll 8
+        for (int i = 0; i < FIN_WARPS; ++i) s += part[i][lane];
+        const int d = col / K1, k = col % K1;
+        if (k < p.K) p.dw[(int64_t)d * p.K + k] = s;
+        else if (p.dbias) p.dbias[d] = s;
+    }
 }
 
 template <typename T, int K>
@@ -231,7 +253,7 @@ int swx_conv1d_bwd(const swx_conv_args* a, void* stream) {
     else swx::dispatch_k<__nv_bfloat16>(p, grid, st, true);
     if (cudaGetLastError() != cudaSuccess) return SWX_ERR_CUDA;
     const int n = p.D * (p.K + 1);
-    swx::conv_bwd_finalize_kernel<<<(n + 255) / 256, 256, 0, st>>>(p);
+    swx::conv_bwd_finalize_kernel<<<(n + 31) / 32, 32 * swx::FIN_WARPS, 0, st>>>(p);
     return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
 }
 
