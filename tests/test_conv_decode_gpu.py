@@ -173,3 +173,24 @@ def test_decode_streaming_path(b, D, gate):
         assert torch.equal(y_s, y_r) and torch.equal(ss_s, ss_r) and torch.equal(cs_s, cs_r)
         close(y_2, yo)
         assert torch.equal(ss_2, ss_s) and torch.equal(cs_2, cs_s)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("L,K", [(300, 4), (37, 3)])
+def test_conv_vector_and_scalar_paths_agree(dtype, L, K):
+    """D a multiple of 4 with aligned rows runs the 4-channel forward; the same values in
+    a view whose row stride is odd run the one-channel forward.  Outputs are identical
+    (same per-channel arithmetic), and so are the gradients of the two layouts."""
+    b, D = 3, 128
+    g = torch.Generator().manual_seed(L + K)
+    x = torch.randn(b, L, D, generator=g).to(DEV, dtype)
+    odd = torch.zeros(b, L, D + 1, device=DEV, dtype=dtype)
+    odd[..., :D] = x
+    xo = odd[..., :D]
+    assert xo.stride(1) % 4 != 0
+    w = (torch.randn(D, K, generator=g) * 0.5).to(DEV)
+    bias = torch.randn(D, generator=g).to(DEV)
+    dout = torch.randn(b, L, D, generator=g).to(DEV, dtype)
+    assert torch.equal(conv1d_forward(x, w, bias), conv1d_forward(xo, w, bias))
+    for got, want in zip(conv1d_backward(x, w, bias, dout), conv1d_backward(xo, w, bias, dout)):
+        assert torch.equal(got, want)
