@@ -485,6 +485,40 @@ def run_long_scan(args, world, rank, local):
     return res
 
 
+def run_linear_scan(args, world, rank, local):
+    """parallel_scan forward + backward (h_t = a_t h_{t-1} + x_t and its adjoint) on the
+    (b, L, D, N) = (8, 2048, 512, 16) fp32 tensors the reference's _SelectiveScanFn feeds
+    its _scan: forward reads a, x and writes h; backward reads a, h, dh and writes da, dx
+    (8 x 537 MB per step).  One batch per rank (weak scaling)."""
+    from swiftx_b200 import parallel_scan
+    dev = torch.device("cuda", local)
+    b, L, D, N = 8, 2048, 512, 16
+    g = torch.Generator(device=dev).manual_seed(3000 + rank)
+    a = (torch.rand(b, L, D, N, device=dev, generator=g) * 0.2 + 0.8).requires_grad_()
+    x = torch.randn(b, L, D, N, device=dev, generator=g).requires_grad_()
+    dh = torch.randn(b, L, D, N, device=dev, generator=g)
+
+    def step():
+        a.grad = x.grad = None
+        parallel_scan(a, x).backward(dh)
+
+    ms, clocks = timed_steps(step, args, world, local, dev)
+    elems = b * L * D * N
+    alg = 8 * elems * 4
+    peak, kind = measured_peak()
+    achieved = alg / (ms * 1e-3) / 1e9
+    res = base_line(args, world, METRIC, round(alg * world / (ms * 1e-3) / 1e9, 1), "GB/s", ms, "f32",
+                    {"workload": "linear recurrence parallel_scan fwd+bwd", "batch": b, "seqlen": L,
+                     "width": D * N, "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
+                     "l2": "inputs larger than L2 (2.1 GB per step)", "alg_bytes_per_step": alg})
+    res["roofline"] = {"bound": "hbm", "kernel": "linear_scan_fwd_kernel + linear_scan_bwd_kernel",
+                       "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                       "frac": round(achieved / peak, 4), "traffic": None, "alg_bytes_per_launch": alg // 2}
+    res["clocks"] = clocks
+    res["gpu_launches"] = 2 * args.steps
+    return res
+
+
 def run_decode(args, world, rank, local):
     """Recurrent decode: batch 256 (sharded over the ranks), 24 layers, D=2048, N=16,
     d_conv=4, fp32 state ~ N(0, 0.1); per layer one fused conv-window shift + state update
@@ -549,9 +583,9 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="lm_train: run the step eagerly, no CUDA graphs")
     ap.add_argument("--e2e-rows", type=int, default=1, help="scan e2e: batch rows per pipelined chunk")
     ap.add_argument("--e2e-streams", type=int, default=2, help="scan e2e: compute streams of the pipeline")
-    ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode"], default="scan",
+    ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode", "linear_scan"], default="scan",
                     help="scan: config 1 (default, the headline); lm_train: config 2; long_scan: config 3; "
-                         "decode: config 4")
+                         "decode: config 4; linear_scan: parallel_scan fwd+bwd at the reference's (b, L, D, N)")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
@@ -566,6 +600,8 @@ def main():
         res = run_long_scan(args, world, rank, local)
     elif args.workload == "decode":
         res = run_decode(args, world, rank, local)
+    elif args.workload == "linear_scan":
+        res = run_linear_scan(args, world, rank, local)
     else:
         res = run_ours(args, world, rank, local)
     if rank == 0 and res is not None:

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 3
+#define SWX_ABI_VERSION 4
 
 /* status codes */
 #define SWX_OK 0
@@ -39,6 +39,7 @@ extern "C" {
 /* element types */
 #define SWX_DTYPE_F32 0
 #define SWX_DTYPE_BF16 1
+#define SWX_DTYPE_F64 2   /* linear scan only */
 
 /* Arguments of the scan entry points (forward and backward share one struct). */
 typedef struct swx_scan_args {
@@ -191,6 +192,30 @@ typedef struct swx_decode_args {
 /* Replaces SiftBlock.step's conv-window roll, conv dot + bias + SiLU and in-place
  * state update / readout / gate (models/sift_block.py:153-175). */
 int swx_decode_step(const swx_decode_args* args, void* stream);
+
+/* Linear recurrence along the sequence, for every (batch row, element) chain:
+ *   h_t = a_t * h_{t-1} + x_t,  h_{-1} = 0
+ * a, x: (batch, seqlen, width) with unit element stride and any row / batch stride
+ * (width = the product of the trailing dims); h: dense (batch, seqlen, width).
+ * Replaces parallel_scan / sequential_scan (models/selective_scan.py:66-99), which
+ * compute the same recurrence by a Hillis-Steele scan and by a loop. */
+typedef struct swx_linear_scan_args {
+    int64_t batch, seqlen, width;
+    int32_t dtype;                    /* SWX_DTYPE_F32 or SWX_DTYPE_F64 */
+    int32_t reserved;
+    const void* a; int64_t a_sb, a_sl;
+    const void* x; int64_t x_sb, x_sl;
+    void* h;                          /* forward output; backward input (the forward's h) */
+    const void* dh; int64_t dh_sb, dh_sl;   /* backward: gradient of h */
+    void* da;                         /* backward outputs, dense (batch, seqlen, width) */
+    void* dx;
+} swx_linear_scan_args;
+
+int64_t swx_linear_scan_args_size(void);
+int swx_linear_scan_fwd(const swx_linear_scan_args* args, void* stream);
+/* Adjoint of swx_linear_scan_fwd: g_t = dh_t + a_{t+1} g_{t+1} (g_{seqlen} = 0),
+ * dx_t = g_t, da_t = g_t * h_{t-1} (h_{-1} = 0).  Reads the forward's h. */
+int swx_linear_scan_bwd(const swx_linear_scan_args* args, void* stream);
 
 #ifdef __cplusplus
 }

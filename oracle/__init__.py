@@ -108,6 +108,30 @@ def scan_bwd(u, delta, A, B, C, dout, D=None, z=None, delta_bias=None, delta_sof
     return {k: v for k, v in g.items() if v is not None}
 
 
+def linear_scan(a, x):
+    """h_t = a_t * h_{t-1} + x_t along dim 1 (h starts at 0), the reference's
+    sequential_scan (models/selective_scan.py:91-99).  a, x: (b, L, ...)."""
+    lib = _load()
+    a, x = _arr(a), _arr(x)
+    b, L = a.shape[:2]
+    W = int(np.prod(a.shape[2:])) if a.ndim > 2 else 1
+    h = np.empty(a.shape)
+    lib.orc_linear_scan(b, L, ctypes.c_long(W), _ptr(a), _ptr(x), _ptr(h))
+    return h
+
+
+def linear_scan_bwd(a, h, dh):
+    """Gradients (da, dx) of linear_scan for the upstream gradient dh, given its output h:
+    the reverse recurrence g_t = dh_t + a_{t+1} g_{t+1}, dx = g, da_t = g_t h_{t-1}."""
+    lib = _load()
+    a, h, dh = _arr(a), _arr(h), _arr(dh)
+    b, L = a.shape[:2]
+    W = int(np.prod(a.shape[2:])) if a.ndim > 2 else 1
+    da, dx = np.empty(a.shape), np.empty(a.shape)
+    lib.orc_linear_scan_bwd(b, L, ctypes.c_long(W), _ptr(a), _ptr(h), _ptr(dh), _ptr(da), _ptr(dx))
+    return da, dx
+
+
 def conv1d_fwd(x, weight, bias=None, silu=True):
     """Causal depthwise conv1d (+SiLU).  x: (b,L,D); weight: (D,K) or (D,1,K); bias: (D,)."""
     lib = _load()

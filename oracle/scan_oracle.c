@@ -15,6 +15,7 @@
  *   models/sift_block.py:117-118      causal depthwise conv1d (pad d_conv-1, keep first L) + SiLU
  *   models/sift_block.py:134          y * silu(z) gate
  *   models/sift_block.py:153-175      SiftBlock.step (decode)
+ *   models/selective_scan.py:91-99    sequential_scan (h_t = a_t * h_{t-1} + x_t loop)
  *
  * Layouts follow the reference API: u, delta, z, y are (b, L, D); B, C are
  * (b, L, N); A is (D, N); D-skip, delta_bias are (D,); states are (b, D, N);
@@ -309,5 +310,38 @@ void orc_decode_step(int b, int D, int N, int K, const double* x, const double* 
         }
         if (Dskip) y += Dskip[d] * xc;
         out[(size_t)bi * D + d] = z ? y * silu(z[(size_t)bi * D + d]) : y;
+    }
+}
+
+/* sequential_scan (models/selective_scan.py:91-99): h = a[:, t] * h + x[:, t] along dim 1,
+ * h starting at 0; a, x, h dense (b, L, W) with W the product of the trailing dims. */
+void orc_linear_scan(int b, int L, long W, const double* a, const double* x, double* h) {
+    #pragma omp parallel for schedule(static)
+    for (long q = 0; q < (long)b * W; ++q) {
+        const long bi = q / W, m = q % W;
+        double acc = 0.0;
+        for (int t = 0; t < L; ++t) {
+            const size_t i = ((size_t)bi * L + t) * W + m;
+            acc = a[i] * acc + x[i];
+            h[i] = acc;
+        }
+    }
+}
+
+/* Adjoint of orc_linear_scan given the upstream gradient dh of h: g_t = dh_t + a_{t+1} g_{t+1}
+ * (walked from the last step), dx_t = g_t, da_t = g_t * h_{t-1} with h_{-1} = 0. */
+void orc_linear_scan_bwd(int b, int L, long W, const double* a, const double* h, const double* dh,
+                         double* da, double* dx) {
+    #pragma omp parallel for schedule(static)
+    for (long q = 0; q < (long)b * W; ++q) {
+        const long bi = q / W, m = q % W;
+        double g = 0.0, an = 0.0;
+        for (int t = L - 1; t >= 0; --t) {
+            const size_t i = ((size_t)bi * L + t) * W + m;
+            g = dh[i] + an * g;
+            dx[i] = g;
+            da[i] = t > 0 ? g * h[i - W] : 0.0;
+            an = a[i];
+        }
     }
 }

@@ -20,6 +20,7 @@ SWX_ERR_TIMEOUT = 4
 SWX_STATIC_SCRATCH_BYTES = 8 << 20
 
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
+SWX_DTYPE_F64 = 2
 
 i64 = ctypes.c_int64
 i32 = ctypes.c_int32
@@ -76,6 +77,15 @@ class DecodeArgs(ctypes.Structure):
     ]
 
 
+class LinearScanArgs(ctypes.Structure):
+    """Mirror of ``swx_linear_scan_args``."""
+    _fields_ = [
+        ("batch", i64), ("seqlen", i64), ("width", i64), ("dtype", i32), ("reserved", i32),
+        ("a", vp), ("a_sb", i64), ("a_sl", i64), ("x", vp), ("x_sb", i64), ("x_sl", i64),
+        ("h", vp), ("dh", vp), ("dh_sb", i64), ("dh_sl", i64), ("da", vp), ("dx", vp),
+    ]
+
+
 _lib = None
 
 
@@ -93,7 +103,7 @@ def load():
     lib.swx_status_string.restype = ctypes.c_char_p
     lib.swx_status_string.argtypes = [ctypes.c_int]
     for fn, st in (("swx_scan_args_size", ScanArgs), ("swx_conv_args_size", ConvArgs),
-                   ("swx_decode_args_size", DecodeArgs)):
+                   ("swx_decode_args_size", DecodeArgs), ("swx_linear_scan_args_size", LinearScanArgs)):
         getattr(lib, fn).restype = i64
         if getattr(lib, fn)() != ctypes.sizeof(st):
             raise RuntimeError(f"{st.__name__} layout mismatch between the library and its binding")
@@ -103,7 +113,8 @@ def load():
     lib.swx_scan_bwd_workspace_bytes.argtypes = [i64, i64, i64]
     for name, st in (("swx_scan_fwd", ScanArgs), ("swx_scan_bwd", ScanArgs),
                      ("swx_scan_bwd_static_scratch", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
-                     ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs)):
+                     ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs),
+                     ("swx_linear_scan_fwd", LinearScanArgs), ("swx_linear_scan_bwd", LinearScanArgs)):
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = [ctypes.POINTER(st), vp]

@@ -6,7 +6,9 @@ Mirrors models/selective_scan.py of the reference:
   (models/selective_scan.py:246-265) -- every mode runs the sm_100a kernel;
 * ``selective_scan_ref(u, delta, A, B, C, D=None)`` (:34-60) -- same kernel;
 * ``selective_scan_fn(...)`` -- the extended entry point with the SiLU(z) gate and
-  softplus(delta + delta_bias) folded in (the block glue of models/sift_block.py:108,134).
+  softplus(delta + delta_bias) folded in (the block glue of models/sift_block.py:108,134);
+* ``parallel_scan(a, x)`` / ``sequential_scan(a, x)`` (:66-99) -- the plain linear
+  recurrence h_t = a_t h_{t-1} + x_t along dim 1, on its own kernel.
 
 Shapes: u, delta, z (b, L, D); A (D, N); B, C (b, L, N); D, delta_bias (D,).
 Autograd follows the reference's custom Functions: the forward saves only its inputs
@@ -205,3 +207,76 @@ def selective_scan_ref(u, delta, A, B, C, D=None):
     """Reference-named entry (models/selective_scan.py:34): the exact sequential
     recurrence, computed by the same CUDA kernel."""
     return selective_scan_fn(u, delta, A, B, C, D)
+
+
+# ----------------------------------------------------------------- linear recurrence
+_LS_DTYPES = {torch.float32: 0, torch.float64: _lib.SWX_DTYPE_F64}
+
+
+def _flat3(t):
+    """(b, L, ...) -> (b, L, W) view with unit element stride (copies only if needed)."""
+    b, L = t.shape[:2]
+    v = t.reshape(b, L, -1)
+    return v if v.stride(-1) == 1 else v.contiguous()
+
+
+def _ls_dtype(a, x):
+    dt = torch.promote_types(a.dtype, x.dtype)
+    return dt if dt in _LS_DTYPES else torch.float32
+
+
+class LinearScanFn(torch.autograd.Function):
+    """h_t = a_t * h_{t-1} + x_t along dim 1 on the sm_100a kernel, with its adjoint as the
+    backward (g_t = dh_t + a_{t+1} g_{t+1}; dx = g, da_t = g_t h_{t-1})."""
+
+    @staticmethod
+    def forward(ctx, a, x):
+        _require_cuda(a, x)
+        if a.dim() < 2 or a.shape != x.shape:
+            raise ValueError(f"expected a and x of the same shape (b, L, ...), got {tuple(a.shape)} "
+                             f"and {tuple(x.shape)}")
+        dt = _ls_dtype(a, x)
+        af, xf = _flat3(a.detach().to(dt)), _flat3(x.detach().to(dt))
+        b, L, W = af.shape
+        h = torch.empty((b, L, W), device=a.device, dtype=dt)
+        s = _lib.LinearScanArgs()
+        s.batch, s.seqlen, s.width, s.dtype = b, L, W, _LS_DTYPES[dt]
+        s.a, s.a_sb, s.a_sl = af.data_ptr(), af.stride(0), af.stride(1)
+        s.x, s.x_sb, s.x_sl = xf.data_ptr(), xf.stride(0), xf.stride(1)
+        s.h = h.data_ptr()
+        _lib.check(_lib.load().swx_linear_scan_fwd(s, _lib.stream_ptr(a.device)), "swx_linear_scan_fwd")
+        ctx.save_for_backward(af, h)
+        ctx.shape, ctx.dtypes = a.shape, (a.dtype, x.dtype)
+        return h.view(a.shape).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dh):
+        af, h = ctx.saved_tensors
+        b, L, W = h.shape
+        dhf = _flat3(dh.to(h.dtype))
+        da, dx = torch.empty_like(h), torch.empty_like(h)
+        s = _lib.LinearScanArgs()
+        s.batch, s.seqlen, s.width, s.dtype = b, L, W, _LS_DTYPES[h.dtype]
+        s.a, s.a_sb, s.a_sl = af.data_ptr(), af.stride(0), af.stride(1)
+        s.h = h.data_ptr()
+        s.dh, s.dh_sb, s.dh_sl = dhf.data_ptr(), dhf.stride(0), dhf.stride(1)
+        s.da, s.dx = da.data_ptr(), dx.data_ptr()
+        _lib.check(_lib.load().swx_linear_scan_bwd(s, _lib.stream_ptr(h.device)), "swx_linear_scan_bwd")
+        return da.view(ctx.shape).to(ctx.dtypes[0]), dx.view(ctx.shape).to(ctx.dtypes[1])
+
+
+def parallel_scan(a, x):
+    """Solve h_t = a_t * h_{t-1} + x_t (h before the first step = 0) along dim 1.
+
+    Drop-in for models/selective_scan.py:66-88: a, x of shape (b, L, ...) -> h like x.
+    The reference composes affine maps with a Hillis-Steele scan (log2 L rounds over the
+    whole tensor); on B200 the recurrence is one HBM stream (read a, x; write h) with a
+    thread per (row, element) chain, so the result matches sequential_scan to rounding.
+    Differentiable (the reference's version is not: its in-place updates break autograd).
+    fp32 and fp64 compute natively; other float dtypes compute in fp32."""
+    return LinearScanFn.apply(a, x)
+
+
+def sequential_scan(a, x):
+    """Same recurrence as parallel_scan (models/selective_scan.py:91-99), same kernel."""
+    return LinearScanFn.apply(a, x)

@@ -19,6 +19,8 @@ Fixtures:
   decode.npz         SiftBlock.step intermediates (conv window, state update, gated y)
   pathway.npz        SiftX block (3 timescale groups, pathway gate): weights, forward output
                      and 9 recurrent steps (models/sift_block.py:111-175)
+  linscan.npz        parallel_scan / sequential_scan on tests/test_selective_scan.py:59-64
+                     shapes, and float64 gradients of sequential_scan by autograd
 
     python tests/golden/make_golden.py /path/to/reference --only pathway
 
@@ -89,12 +91,36 @@ def make_pathway(SiftBlock):
     save("pathway", hidden=hidden, out=out, steps=steps, group_of=blk.group_of, **params)
 
 
+def make_linscan(parallel_scan, sequential_scan):
+    """10. The associative and the loop scan (models/selective_scan.py:66-99) on the
+    reference test's inputs (tests/test_selective_scan.py:59-64), plus float64 gradients by
+    autograd through sequential_scan."""
+    out = {}
+    for L in (1, 2, 5, 8, 33, 128):
+        g = torch.Generator().manual_seed(L)
+        a = torch.rand(3, L, 4, 2, generator=g)
+        x = torch.randn(3, L, 4, 2, generator=g)
+        out.update({f"a_{L}": a, f"x_{L}": x, f"hp_{L}": parallel_scan(a, x), f"hs_{L}": sequential_scan(a, x)})
+    g = torch.Generator().manual_seed(99)
+    a = torch.rand(2, 33, 5, 3, dtype=torch.float64, generator=g).requires_grad_()
+    x = torch.randn(2, 33, 5, 3, dtype=torch.float64, generator=g).requires_grad_()
+    w = torch.randn(2, 33, 5, 3, dtype=torch.float64, generator=g)
+    h = sequential_scan(a, x)         # parallel_scan's in-place updates are not differentiable
+    (h * w).sum().backward()
+    out.update(ga=a.detach(), gx=x.detach(), gw=w, gh=h.detach(), gda=a.grad, gdx=x.grad)
+    save("linscan", **out)
+
+
 def main(ref_root, only=None):
     sys.path.insert(0, ref_root)
     from models.selective_scan import selective_scan_fast, selective_scan_ref
     from models.sift_block import SiftBlock
     if only == "pathway":
         make_pathway(SiftBlock)
+        return
+    if only == "linscan":
+        from models.selective_scan import parallel_scan, sequential_scan
+        make_linscan(parallel_scan, sequential_scan)
         return
 
     # 1. hand-computed known answer
@@ -199,6 +225,8 @@ def main(ref_root, only=None):
          y=cap["y"], conv_state1=state[0], ssm_state1=state[1])
 
     make_pathway(SiftBlock)
+    from models.selective_scan import parallel_scan, sequential_scan
+    make_linscan(parallel_scan, sequential_scan)
 
 
 if __name__ == "__main__":

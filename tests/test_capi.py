@@ -30,7 +30,8 @@ def test_struct_mirrors_match():
     assert lib.swx_scan_args_size() == ctypes.sizeof(_lib.ScanArgs)
     assert lib.swx_conv_args_size() == ctypes.sizeof(_lib.ConvArgs)
     assert lib.swx_decode_args_size() == ctypes.sizeof(_lib.DecodeArgs)
-    assert lib.swx_abi_version() == 3
+    assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
+    assert lib.swx_abi_version() == 4
 
 
 def test_status_strings():
@@ -69,6 +70,14 @@ def test_host_side_validation_without_gpu():
     d = _lib.DecodeArgs()
     d.batch, d.dim, d.mode = 1, 4, 0                          # no mode
     assert lib.swx_decode_step(d, None) == _lib.SWX_ERR_INVALID_ARG
+    s = _lib.LinearScanArgs()
+    s.batch, s.seqlen, s.width, s.dtype = 2, 5, 3, 1          # bf16 is not a linear-scan dtype
+    assert lib.swx_linear_scan_fwd(s, None) == _lib.SWX_ERR_UNSUPPORTED
+    s.dtype = 0                                               # missing pointers
+    assert lib.swx_linear_scan_fwd(s, None) == _lib.SWX_ERR_INVALID_ARG
+    assert lib.swx_linear_scan_bwd(s, None) == _lib.SWX_ERR_INVALID_ARG
+    s.seqlen = 0
+    assert lib.swx_linear_scan_fwd(s, None) == _lib.SWX_OK
 
 
 def test_cpu_tensors_are_rejected_not_computed():
@@ -80,3 +89,6 @@ def test_cpu_tensors_are_rejected_not_computed():
         selective_scan_fast(u, u.abs(), -torch.ones(3, 2), torch.randn(1, 4, 2), torch.randn(1, 4, 2))
     with pytest.raises(RuntimeError):
         causal_conv1d_fn(u, torch.randn(3, 1, 4))
+    from swiftx_b200 import parallel_scan
+    with pytest.raises(RuntimeError):
+        parallel_scan(torch.rand(2, 5, 3), torch.randn(2, 5, 3))
