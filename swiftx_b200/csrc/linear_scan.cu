@@ -22,7 +22,7 @@ struct LsDev {
 };
 
 constexpr int LS_NT = 128;
-constexpr int LS_U = 8;
+constexpr int LS_U = 16;
 
 template <typename T>
 __global__ void __launch_bounds__(LS_NT) linear_scan_fwd_kernel(const LsDev p) {
