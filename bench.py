@@ -562,6 +562,23 @@ def run_decode(args, world, rank, local):
                      "d_state": N, "d_conv": K, "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
                      "cuda_graph": True}, scaling="strong")
     res["latency_ms_per_token"] = round(ms, 4)
+    del graph
+    torch.cuda.synchronize()
+    # the whole model's recurrent step (embedding, 24 x [in_proj, conv-window kernel,
+    # x_proj, dt_proj, state-update kernel, out_proj], norms, head) replayed from one graph
+    from swiftx_b200.sift import GraphedStep, SiftConfig, SiftLM
+    lay.clear()
+    torch.manual_seed(0)
+    model = SiftLM(SiftConfig(vocab_size=256, d_model=1024, n_layers=layers, d_state=N, d_conv=K,
+                              expand=2)).to(dev).eval()
+    tok = torch.randint(0, 256, (b,), device=dev, generator=g)
+    res["model_step"] = {"model": f"SiftLM d_model 1024 (D={D}), {layers} layers, N={N}, vocab 256; fp32 state",
+                         "batch": btot, "cuda_graph": "whole step (GraphedStep)"}
+    for name, amp in (("fp32", None), ("bf16_projections", torch.bfloat16)):
+        stepper = GraphedStep(model, b, dev, autocast_dtype=amp)
+        ms_m, _ = timed_steps(lambda: stepper(tok), args, world, local, dev)
+        res["model_step"][name] = {"tokens_per_s": round(btot / (ms_m * 1e-3), 1), "ms_per_token": round(ms_m, 4)}
+        del stepper
     achieved = per_layer * layers / (ms * 1e-3) / 1e9
     peak, kind = measured_peak()
     res["roofline"] = {"bound": "hbm", "kernel": "decode_stream_kernel", "achieved": round(achieved, 1), "peak": peak,
@@ -569,7 +586,6 @@ def run_decode(args, world, rank, local):
                        "alg_bytes_per_launch": per_layer}
     res["clocks"] = clocks
     res["gpu_launches"] = layers * args.steps
-    del graph
     return res
 
 

@@ -233,17 +233,65 @@ class SiftLM(nn.Module):
         return self.lm_head(self.backbone.norm_f(x))
 
     @torch.no_grad()
-    def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None):
-        state = self.allocate_state(idx.shape[0], idx.device)
+    def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None, graphed=False):
+        """Prompt then sampled tokens through the recurrent step (models/sift_model.py
+        generate).  graphed=True replays each step from one CUDA graph (GraphedStep)."""
+        if graphed:
+            stepper = GraphedStep(self, idx.shape[0], idx.device)
+            step = lambda tok: stepper(tok).clone()  # noqa: E731
+        else:
+            state = self.allocate_state(idx.shape[0], idx.device)
+            step = lambda tok: self.step(tok, state)  # noqa: E731
         logits = None
         for t in range(idx.shape[1]):
-            logits = self.step(idx[:, t], state)
+            logits = step(idx[:, t])
         out = [idx]
         for _ in range(max_new_tokens):
             nxt = sample(logits, temperature, top_k)
             out.append(nxt[:, None])
-            logits = self.step(nxt, state)
+            logits = step(nxt)
         return torch.cat(out, dim=1)
+
+
+class GraphedStep:
+    """SiftLM.step for a fixed batch, replayed as one CUDA graph: the embedding, every
+    layer's in_proj, conv-window kernel, x_proj / dt_proj, state-update kernel and
+    out_proj, the norms and the head -- about fifteen launches per layer -- in one graph
+    launch per token.  The recurrent state lives in buffers owned by this object and is
+    updated in place by every call, as SiftLM.step updates its state.
+
+    Calling returns the graph's static logits tensor (overwritten by the next call).
+    autocast_dtype (e.g. torch.bfloat16) runs the projections under autocast, as the
+    reference trainer does; the state and the decode kernels stay fp32."""
+
+    def __init__(self, model, batch, device=None, autocast_dtype=None):
+        dev = torch.device(device) if device is not None else next(model.parameters()).device
+        self.model = model
+        self.state = model.allocate_state(batch, dev)
+        self.token = torch.zeros(batch, dtype=torch.long, device=dev)
+        amp = lambda: torch.autocast("cuda", dtype=autocast_dtype, enabled=autocast_dtype is not None)  # noqa: E731
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side), torch.no_grad(), amp():
+            for _ in range(2):                    # one-time library and kernel setup
+                model.step(self.token, self.state)
+        torch.cuda.current_stream(dev).wait_stream(side)
+        self.reset()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph), torch.no_grad(), amp():
+            self.logits = model.step(self.token, self.state)
+
+    def reset(self):
+        """Zero the recurrent state (a fresh sequence)."""
+        for conv_state, ssm_state in self.state:
+            conv_state.zero_()
+            ssm_state.zero_()
+
+    @torch.no_grad()
+    def __call__(self, token):
+        self.token.copy_(token)
+        self.graph.replay()
+        return self.logits
 
 
 def sample(logits, temperature=1.0, top_k=None):

@@ -319,3 +319,25 @@ def test_pathway_block_matches_reference_fixture(golden):
     state = blk.allocate_state(2, device=DEV)
     steps = torch.stack([blk.step(hidden[:, t], state) for t in range(9)], 1)
     np.testing.assert_allclose(steps.detach().double().cpu().numpy(), g["steps"], rtol=1e-4, atol=1e-5 * scale)
+
+
+def test_graphed_step_matches_eager_step():
+    """GraphedStep replays SiftLM.step from one CUDA graph: the same logits token by token
+    and the same state, and generate(graphed=True) picks the same greedy tokens."""
+    from swiftx_b200.sift import GraphedStep
+    torch.manual_seed(0)
+    m = SiftLM(tiny_cfg()).to(DEV).eval()
+    idx = torch.randint(0, 11, (3, 10), device=DEV)
+    state = m.allocate_state(3, device=DEV)
+    gs = GraphedStep(m, 3)
+    for t in range(10):
+        want = m.step(idx[:, t], state)
+        got = gs(idx[:, t])
+        assert torch.allclose(got, want, atol=1e-5, rtol=1e-5)
+    for (c1, s1), (c2, s2) in zip(state, gs.state):
+        assert torch.allclose(c1, c2, atol=1e-6) and torch.allclose(s1, s2, atol=1e-5)
+    gs.reset()
+    assert all(float(c.abs().sum()) == 0 and float(s.abs().sum()) == 0 for c, s in gs.state)
+    a = m.generate(idx[:, :4], 6, temperature=0)
+    b = m.generate(idx[:, :4], 6, temperature=0, graphed=True)
+    assert torch.equal(a, b)
