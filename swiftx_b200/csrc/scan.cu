@@ -109,9 +109,12 @@ __device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], c
 
 // WR: write the output (pass 1 of the sequence-parallel scan needs only the final state
 // and the per-channel sum of delta_eff, so it skips C, z, the readout and the stores).
-// NA: helper threads (128 = one helper warp per sub-partition, 256 = two).
+// NA: helper threads (128 = one helper warp per sub-partition, 256 = two).  The 128-helper
+// variant is built for two CTAs per SM (at most 128 registers a thread): the output-writing
+// kernels need ~100 anyway, and the sequence-parallel pass 1 (no output) then fits two CTAs
+// per SM at the cost of a few spilled bytes.
 template <typename Tin, typename Tout, bool HAS_Z, bool WR, int NA>
-__global__ void __launch_bounds__(NSCAN + NA, 1) scan_fwd_kernel(const ScanDev p) {
+__global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel(const ScanDev p) {
     constexpr int FNAUX = NA, FNTH = NSCAN + NA;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     FwdSmem<Tin>& S = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
