@@ -492,7 +492,7 @@ def run_linear_scan(args, world, rank, local):
     (8 x 537 MB per step).  One batch per rank (weak scaling)."""
     from swiftx_b200 import parallel_scan
     dev = torch.device("cuda", local)
-    b, L, D, N = 8, 2048, 512, 16
+    b, L, D, N = args.ls_batch, 2048, 512, 16
     g = torch.Generator(device=dev).manual_seed(3000 + rank)
     a = (torch.rand(b, L, D, N, device=dev, generator=g) * 0.2 + 0.8).requires_grad_()
     x = torch.randn(b, L, D, N, device=dev, generator=g).requires_grad_()
@@ -510,7 +510,7 @@ def run_linear_scan(args, world, rank, local):
     res = base_line(args, world, METRIC, round(alg * world / (ms * 1e-3) / 1e9, 1), "GB/s", ms, "f32",
                     {"workload": "linear recurrence parallel_scan fwd+bwd", "batch": b, "seqlen": L,
                      "width": D * N, "parallelism": f"batch-sharded x{world}" if world > 1 else "single GPU",
-                     "l2": "inputs larger than L2 (2.1 GB per step)", "alg_bytes_per_step": alg})
+                     "l2": "inputs larger than L2", "alg_bytes_per_step": alg})
     res["roofline"] = {"bound": "hbm", "kernel": "linear_scan_fwd_kernel + linear_scan_bwd_kernel",
                        "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind, "unit": "GB/s",
                        "frac": round(achieved / peak, 4), "traffic": None, "alg_bytes_per_launch": alg // 2}
@@ -598,6 +598,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="lm_train: run the step eagerly, no CUDA graphs")
     ap.add_argument("--e2e-rows", type=int, default=1, help="scan e2e: batch rows per pipelined chunk")
+    ap.add_argument("--ls-batch", type=int, default=8, help="linear_scan: batch rows (8 = the measured size)")
     ap.add_argument("--e2e-streams", type=int, default=2, help="scan e2e: compute streams of the pipeline")
     ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode", "linear_scan"], default="scan",
                     help="scan: config 1 (default, the headline); lm_train: config 2; long_scan: config 3; "
