@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 4
+#define SWX_ABI_VERSION 5
 
 /* status codes */
 #define SWX_OK 0
@@ -216,6 +216,30 @@ int swx_linear_scan_fwd(const swx_linear_scan_args* args, void* stream);
 /* Adjoint of swx_linear_scan_fwd: g_t = dh_t + a_{t+1} g_{t+1} (g_{seqlen} = 0),
  * dx_t = g_t, da_t = g_t * h_{t-1} (h_{-1} = 0).  Reads the forward's h. */
 int swx_linear_scan_bwd(const swx_linear_scan_args* args, void* stream);
+
+/* RMSNorm of the language model around the mixer (models/sift_model.py:17-26):
+ *   y = (x * rsqrt(mean(x^2) + eps)) * weight  over the last dim, computed in fp32.
+ * x, y, dy, dx: dense (rows, dim), fp32 or bf16; weight, dweight: (dim,) fp32;
+ * rstd: (rows,) fp32, written by the forward when given and read by the backward.
+ * dim <= 1024.  The weight gradient is a fixed-order sum (deterministic). */
+typedef struct swx_rmsnorm_args {
+    int64_t rows, dim;
+    float eps;
+    int32_t dtype;                    /* SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
+    const void* x;
+    const float* weight;
+    void* y;
+    float* rstd;
+    const void* dy;                   /* backward */
+    void* dx;
+    float* dweight;
+    void* workspace; int64_t workspace_bytes;
+} swx_rmsnorm_args;
+
+int64_t swx_rmsnorm_args_size(void);
+int64_t swx_rmsnorm_bwd_workspace_bytes(int64_t dim);
+int swx_rmsnorm_fwd(const swx_rmsnorm_args* args, void* stream);
+int swx_rmsnorm_bwd(const swx_rmsnorm_args* args, void* stream);
 
 #ifdef __cplusplus
 }

@@ -86,6 +86,15 @@ class LinearScanArgs(ctypes.Structure):
     ]
 
 
+class RMSNormArgs(ctypes.Structure):
+    """Mirror of ``swx_rmsnorm_args``."""
+    _fields_ = [
+        ("rows", i64), ("dim", i64), ("eps", ctypes.c_float), ("dtype", i32),
+        ("x", vp), ("weight", vp), ("y", vp), ("rstd", vp), ("dy", vp), ("dx", vp), ("dweight", vp),
+        ("workspace", vp), ("workspace_bytes", i64),
+    ]
+
+
 _lib = None
 
 
@@ -103,7 +112,8 @@ def load():
     lib.swx_status_string.restype = ctypes.c_char_p
     lib.swx_status_string.argtypes = [ctypes.c_int]
     for fn, st in (("swx_scan_args_size", ScanArgs), ("swx_conv_args_size", ConvArgs),
-                   ("swx_decode_args_size", DecodeArgs), ("swx_linear_scan_args_size", LinearScanArgs)):
+                   ("swx_decode_args_size", DecodeArgs), ("swx_linear_scan_args_size", LinearScanArgs),
+                   ("swx_rmsnorm_args_size", RMSNormArgs)):
         getattr(lib, fn).restype = i64
         if getattr(lib, fn)() != ctypes.sizeof(st):
             raise RuntimeError(f"{st.__name__} layout mismatch between the library and its binding")
@@ -114,10 +124,13 @@ def load():
     for name, st in (("swx_scan_fwd", ScanArgs), ("swx_scan_bwd", ScanArgs),
                      ("swx_scan_bwd_static_scratch", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
                      ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs),
-                     ("swx_linear_scan_fwd", LinearScanArgs), ("swx_linear_scan_bwd", LinearScanArgs)):
+                     ("swx_linear_scan_fwd", LinearScanArgs), ("swx_linear_scan_bwd", LinearScanArgs),
+                     ("swx_rmsnorm_fwd", RMSNormArgs), ("swx_rmsnorm_bwd", RMSNormArgs)):
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = [ctypes.POINTER(st), vp]
+    lib.swx_rmsnorm_bwd_workspace_bytes.restype = i64
+    lib.swx_rmsnorm_bwd_workspace_bytes.argtypes = [i64]
     lib.swx_conv1d_bwd_workspace_bytes.restype = i64
     lib.swx_conv1d_bwd_workspace_bytes.argtypes = [i64, i64, i64, i64]
     _lib = lib

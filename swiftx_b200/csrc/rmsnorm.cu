@@ -1,0 +1,172 @@
+// RMSNorm of the LM around the mixer (models/sift_model.py:17-26, the pre-norm of every
+// residual block and the final norm):  y = (x * rsqrt(mean(x^2) + eps)) * w,  in fp32.
+// In the reference this is six elementwise / reduction launches forward and about ten
+// backward per use; here it is one launch each way (plus a fixed-order sum of the weight
+// gradient), which matters in a training step of many small launches.
+//
+// Forward: one warp per row; lanes stride the columns (coalesced 128-byte accesses), the
+// sum of squares is a warp reduction; the per-row rsqrt is saved for the backward.
+// Backward (x^ = x r, g = w dy):  dx = r (g - x^ mean(x^ g)),  dw = sum_rows dy x^.
+// A fixed grid of warps walks the rows in a fixed assignment, accumulating dw per lane in
+// registers; per-warp partials are then summed in warp order (deterministic).
+#include "common.cuh"
+
+#include <algorithm>
+
+namespace swx {
+
+constexpr int NORM_WARPS = 8;                 // warps per CTA
+constexpr int NORM_MAXC = 32;                 // columns per lane in the backward: d <= 1024
+constexpr int NORM_BWD_WARPS = 148 * 2 * NORM_WARPS;   // fixed backward grid (warps)
+
+struct NormDev {
+    int rows, d;
+    float eps;
+    const void* x; const float* w; void* y; float* rstd;
+    const void* dy; void* dx; float* dw_part; float* dw;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_fwd_kernel(const NormDev p) {
+    const int row = blockIdx.x * NORM_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (row >= p.rows) return;
+    const T* x = static_cast<const T*>(p.x) + (int64_t)row * p.d;
+    T* y = static_cast<T*>(p.y) + (int64_t)row * p.d;
+    float ss = 0.f;
+    for (int c = lane; c < p.d; c += 32) {
+        const float v = Elem<T>::to_f(x[c]);
+        ss = fmaf(v, v, ss);
+    }
+    const float r = rsqrtf(warp_sum(ss) / p.d + p.eps);
+    if (lane == 0 && p.rstd) p.rstd[row] = r;
+    for (int c = lane; c < p.d; c += 32) y[c] = Elem<T>::from_f((Elem<T>::to_f(x[c]) * r) * p.w[c]);
+}
+
+template <typename T, int NC>
+__global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const NormDev p) {
+    const int gw = blockIdx.x * NORM_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    float wv[NC], dwacc[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int c = lane + 32 * k;
+        wv[k] = c < p.d ? p.w[c] : 0.f;
+        dwacc[k] = 0.f;
+    }
+    for (int row = gw; row < p.rows; row += NORM_BWD_WARPS) {
+        const T* x = static_cast<const T*>(p.x) + (int64_t)row * p.d;
+        const T* dy = static_cast<const T*>(p.dy) + (int64_t)row * p.d;
+        T* dx = static_cast<T*>(p.dx) + (int64_t)row * p.d;
+        const float r = p.rstd[row];
+        float xh[NC], g[NC], dyv[NC];
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane + 32 * k;
+            const bool ok = c < p.d;
+            xh[k] = ok ? Elem<T>::to_f(x[c]) * r : 0.f;
+            dyv[k] = ok ? Elem<T>::to_f(dy[c]) : 0.f;
+            g[k] = wv[k] * dyv[k];
+            s = fmaf(xh[k], g[k], s);
+        }
+        const float m = warp_sum(s) / p.d;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane + 32 * k;
+            if (c < p.d) dx[c] = Elem<T>::from_f(r * (g[k] - xh[k] * m));
+            dwacc[k] = fmaf(dyv[k], xh[k], dwacc[k]);
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int c = lane + 32 * k;
+        if (c < p.d) p.dw_part[(int64_t)gw * p.d + c] = dwacc[k];
+    }
+}
+
+// dw[c] = sum over the backward grid's warps of dw_part[warp][c], in warp order.
+__global__ void __launch_bounds__(1024) rmsnorm_dw_kernel(const NormDev p) {
+    __shared__ float part[32][33];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + lane;
+    float s = 0.f;
+    if (c < p.d)
+        for (int r = w; r < NORM_BWD_WARPS; r += 32) s += p.dw_part[(int64_t)r * p.d + c];
+    part[w][lane] = s;
+    __syncthreads();
+    if (w == 0 && c < p.d) {
+        float t = 0.f;
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) t += part[i][lane];
+        p.dw[c] = t;
+    }
+}
+
+template <typename T>
+static void launch_bwd(const NormDev& p, cudaStream_t st) {
+    const int nc = (p.d + 31) / 32;
+    const dim3 grid(NORM_BWD_WARPS / NORM_WARPS);
+    if (nc <= 8) rmsnorm_bwd_kernel<T, 8><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    else if (nc <= 16) rmsnorm_bwd_kernel<T, 16><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    else rmsnorm_bwd_kernel<T, NORM_MAXC><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    rmsnorm_dw_kernel<<<(p.d + 31) / 32, 1024, 0, st>>>(p);
+}
+
+}  // namespace swx
+
+namespace {
+int norm_check(const swx_rmsnorm_args* a, bool bwd) {
+    if (!a) return SWX_ERR_INVALID_ARG;
+    if (a->rows < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
+    if (a->dtype != SWX_DTYPE_F32 && a->dtype != SWX_DTYPE_BF16) return SWX_ERR_UNSUPPORTED;
+    if (a->rows > INT32_MAX || a->dim > 32 * swx::NORM_MAXC) return SWX_ERR_UNSUPPORTED;
+    if (a->rows * a->dim == 0) return SWX_OK;
+    if (!a->x || !a->weight) return SWX_ERR_INVALID_ARG;
+    if (!bwd && !a->y) return SWX_ERR_INVALID_ARG;
+    if (bwd && (!a->dy || !a->dx || !a->dweight || !a->rstd || !a->workspace)) return SWX_ERR_INVALID_ARG;
+    return SWX_OK;
+}
+
+swx::NormDev norm_pack(const swx_rmsnorm_args* a) {
+    swx::NormDev p{};
+    p.rows = (int)a->rows; p.d = (int)a->dim; p.eps = a->eps;
+    p.x = a->x; p.w = a->weight; p.y = a->y; p.rstd = a->rstd;
+    p.dy = a->dy; p.dx = a->dx; p.dw_part = static_cast<float*>(a->workspace); p.dw = a->dweight;
+    return p;
+}
+}  // namespace
+
+extern "C" {
+
+int64_t swx_rmsnorm_args_size(void) { return (int64_t)sizeof(swx_rmsnorm_args); }
+
+int64_t swx_rmsnorm_bwd_workspace_bytes(int64_t dim) { return (int64_t)swx::NORM_BWD_WARPS * dim * 4; }
+
+int swx_rmsnorm_fwd(const swx_rmsnorm_args* a, void* stream) {
+    const int s = norm_check(a, false);
+    if (s != SWX_OK || a->rows * a->dim == 0) return s;
+    const swx::NormDev p = norm_pack(a);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const unsigned grid = (unsigned)((p.rows + swx::NORM_WARPS - 1) / swx::NORM_WARPS);
+    if (a->dtype == SWX_DTYPE_F32) swx::rmsnorm_fwd_kernel<float><<<grid, 32 * swx::NORM_WARPS, 0, st>>>(p);
+    else swx::rmsnorm_fwd_kernel<__nv_bfloat16><<<grid, 32 * swx::NORM_WARPS, 0, st>>>(p);
+    return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
+}
+
+int swx_rmsnorm_bwd(const swx_rmsnorm_args* a, void* stream) {
+    const int s = norm_check(a, true);
+    if (s != SWX_OK || a->rows * a->dim == 0) return s;
+    if (a->workspace_bytes < swx_rmsnorm_bwd_workspace_bytes(a->dim)) return SWX_ERR_INVALID_ARG;
+    const swx::NormDev p = norm_pack(a);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (a->dtype == SWX_DTYPE_F32) swx::launch_bwd<float>(p, st);
+    else swx::launch_bwd<__nv_bfloat16>(p, st);
+    return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
+}
+
+}  // extern "C"

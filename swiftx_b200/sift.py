@@ -25,6 +25,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import norm as norm_kernels
 from .conv import causal_conv1d_fn
 from .decode import decode_conv_step, decode_ssm_step
 from .selective_scan import selective_scan_fn
@@ -148,6 +149,10 @@ class RMSNorm(nn.Module):
         self.weight = nn.Parameter(torch.ones(d))
 
     def forward(self, x):
+        """models/sift_model.py:25-26; on CUDA (fp32 / bf16, d <= 1024) one fused kernel
+        each way, otherwise the reference expression itself."""
+        if norm_kernels.supported(x):
+            return norm_kernels.rms_norm(x, self.weight, self.eps)
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
 
 

@@ -31,7 +31,8 @@ def test_struct_mirrors_match():
     assert lib.swx_conv_args_size() == ctypes.sizeof(_lib.ConvArgs)
     assert lib.swx_decode_args_size() == ctypes.sizeof(_lib.DecodeArgs)
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
-    assert lib.swx_abi_version() == 4
+    assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
+    assert lib.swx_abi_version() == 5
 
 
 def test_status_strings():
@@ -78,6 +79,12 @@ def test_host_side_validation_without_gpu():
     assert lib.swx_linear_scan_bwd(s, None) == _lib.SWX_ERR_INVALID_ARG
     s.seqlen = 0
     assert lib.swx_linear_scan_fwd(s, None) == _lib.SWX_OK
+    r = _lib.RMSNormArgs()
+    r.rows, r.dim, r.eps, r.dtype = 4, 2048, 1e-5, 0           # dim > 1024
+    assert lib.swx_rmsnorm_fwd(r, None) == _lib.SWX_ERR_UNSUPPORTED
+    r.dim = 256                                               # missing pointers
+    assert lib.swx_rmsnorm_fwd(r, None) == _lib.SWX_ERR_INVALID_ARG
+    assert lib.swx_rmsnorm_bwd(r, None) == _lib.SWX_ERR_INVALID_ARG
 
 
 def test_cpu_tensors_are_rejected_not_computed():
