@@ -230,7 +230,7 @@ def run_ours(args, world, rank, local):
     if sampler:
         res["clocks"] = sampler.summary()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        res["cpu_baseline"] = cpu_baseline(args, sample_b=1, reps=2)
+        res["cpu_baseline"] = cpu_baseline(args)
     return res
 
 
@@ -270,54 +270,67 @@ def run_e2e(args, inp, dev, world):
 
 
 # ----------------------------------------------------------------- CPU oracle (reference arm / baseline)
-def cpu_baseline(args, sample_b=1, reps=1):
-    """The oracle port of the reference's scan (float64 C, OpenMP over all host threads)
-    on a bounded sample of the workload: `sample_b` of the 8 batch rows, full L and D."""
-    import numpy as np
-
-    import oracle
+def _oracle_inputs():
+    """The default workload's inputs (all 8 rows) as float64 arrays for the oracle."""
     from swiftx_b200.workloads import config_inputs
+    inp = config_inputs(CFG["b"], CFG["L"], CFG["D"], CFG["N"], seed=0)
+    return {k: (v.double().numpy() if v is not None else None) for k, v in inp.items()}
 
-    b, L, D, N = sample_b, CFG["L"], CFG["D"], CFG["N"]
-    inp = config_inputs(b, L, D, N, seed=0)
-    a = {k: (v.double().numpy() if v is not None else None) for k, v in inp.items()}
+
+def _oracle_step(a):
+    """One fwd+bwd of the workload through the oracle port of the reference's scan
+    (float64 C, OpenMP over all host threads); returns the seconds it took."""
+    import oracle
+    t = time.perf_counter()
+    oracle.scan_fwd(a["u"], a["delta"], a["A"], a["B"], a["C"], D=a["D"], z=a["z"],
+                    delta_bias=a["delta_bias"], delta_softplus=True)
+    oracle.scan_bwd(a["u"], a["delta"], a["A"], a["B"], a["C"], a["dout"], D=a["D"], z=a["z"],
+                    delta_bias=a["delta_bias"], delta_softplus=True)
+    return time.perf_counter() - t
+
+
+def cpu_baseline(args, min_seconds=10.0, max_reps=40):
+    """The oracle port timed on the host cores over the whole workload (8 rows), repeated
+    until at least min_seconds of CPU work (at most max_reps fwd+bwd passes)."""
+    import oracle
     oracle.set_num_threads(os.cpu_count() or 1)
+    a = _oracle_inputs()
+    _oracle_step(a)                                   # untimed: page in, thread pool up
     times = []
-    for _ in range(reps):
-        t = time.perf_counter()
-        oracle.scan_fwd(a["u"], a["delta"], a["A"], a["B"], a["C"], D=a["D"], z=a["z"],
-                        delta_bias=a["delta_bias"], delta_softplus=True)
-        oracle.scan_bwd(a["u"], a["delta"], a["A"], a["B"], a["C"], a["dout"], D=a["D"], z=a["z"],
-                        delta_bias=a["delta_bias"], delta_softplus=True)
-        times.append(time.perf_counter() - t)
-    fwd_b, bwd_b = alg_bytes(b, L, D, N)
-    best = min(times)
-    _ = np
-    return {"value": round((fwd_b + bwd_b) / best / 1e9, 4), "unit": "GB/s", "cores": oracle.num_threads(),
-            "kind": "port", "seconds_per_sample": round(best, 3),
-            "sample": f"b={b} of 8 rows, L={L}, D={D}, N={N}, fwd+bwd, best of {reps}"}
+    while sum(times) < min_seconds and len(times) < max_reps:
+        times.append(_oracle_step(a))
+    fwd_b, bwd_b = alg_bytes(CFG["b"], CFG["L"], CFG["D"], CFG["N"])
+    mean = statistics.mean(times)
+    return {"value": round((fwd_b + bwd_b) / mean / 1e9, 4), "unit": "GB/s", "cores": oracle.num_threads(),
+            "kind": "port", "seconds_per_sample": round(mean, 3),
+            "sample": f"the full workload (b={CFG['b']}, L={CFG['L']}, D={CFG['D']}, N={CFG['N']}, fwd+bwd), "
+                      f"mean of {len(times)} passes, {sum(times):.1f} s of CPU time"}
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the oracle port of the reference's CPU scan on the host cores,
+    one full fwd+bwd of the workload per step (rank 0 only)."""
     if rank != 0:
         return None
-    reps = 1
-    times = []
+    import oracle
+    oracle.set_num_threads(os.cpu_count() or 1)
+    a = _oracle_inputs()
     for _ in range(args.warmup):
-        cpu_baseline(args, sample_b=1, reps=1)
-    for _ in range(args.steps):
-        times.append(cpu_baseline(args, sample_b=1, reps=reps))
-    best = max(times, key=lambda r: r["value"])
-    v = statistics.mean(r["value"] for r in times)
+        _oracle_step(a)
+    times = [_oracle_step(a) for _ in range(args.steps)]
+    fwd_b, bwd_b = alg_bytes(CFG["b"], CFG["L"], CFG["D"], CFG["N"])
+    ms = statistics.mean(times) * 1e3
+    v = (fwd_b + bwd_b) / (ms * 1e-3) / 1e9
+    sample = (f"the full workload per step (b={CFG['b']}, L={CFG['L']}, D={CFG['D']}, N={CFG['N']}, fwd+bwd), "
+              f"mean of {len(times)} steps")
     return {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
             "config": {"workload": "selective_scan fwd+bwd, D-skip + SiLU(z) gate + softplus(delta+bias)",
                        "batch": CFG["b"], "seqlen": CFG["L"], "d_inner": CFG["D"], "d_state": CFG["N"]},
-            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": best["cores"], "kind": "port",
-                             "sample": best["sample"]},
+            "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": oracle.num_threads(), "kind": "port",
+                             "sample": sample},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-
 
 
 # ----------------------------------------------------------------- other workloads
