@@ -614,33 +614,36 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
     }
 }
 
-// Second pass: fixed-order sums of the partials.
+// Second pass: fixed-order sums of the partials.  The dB | dC partials are read as whole
+// 32-float rows (one (row, step) of one CTA's channel block: both halves together), so
+// consecutive threads read consecutive words; the per-block sum runs in block order.
 template <typename Tin>
 __global__ void scan_bwd_finalize_kernel(const ScanDev p) {
-    const int64_t nbc = (int64_t)p.b * p.L * p.N;
-    const int64_t total = 2 * nbc + (int64_t)p.D * p.N + p.D;
+    const int64_t nrow = (int64_t)p.b * p.L;                 // (bi, t) rows
+    const int64_t nbc = nrow * 2 * NS;                         // dB | dC words
+    const int64_t total = nbc + (int64_t)p.D * p.N + p.D;
+    const int64_t slab = nrow * 2 * NS;                        // one channel block's partials
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
-        if (i < 2 * nbc) {
-            const int kind = i >= nbc;
-            const int64_t r = kind ? i - nbc : i;
-            const int n = r % p.N;
-            const int64_t bl = r / p.N;               // bi * L + t
-            const int bi = bl / p.L;
-            const int64_t t = bl % p.L;
+        if (i < nbc) {
+            const int col = (int)(i & (2 * NS - 1));
+            const int kind = col >= NS, n = col & (NS - 1);
+            if (n >= p.N) continue;
+            const int64_t bl = i >> 5;                         // bi * L + t
+            const float* src = p.ws_bc + i;
             float s = 0.f;
-            for (int k = 0; k < p.nblk; ++k)
-                s += p.ws_bc[(((int64_t)k * p.b + bi) * p.L + t) * 2 * NS + kind * NS + n];
+#pragma unroll 4
+            for (int k = 0; k < p.nblk; ++k) s += src[(int64_t)k * slab];
             Tin* dst = static_cast<Tin*>(kind ? p.dC : p.dB);
-            dst[r] = Elem<Tin>::from_f(s);
-        } else if (i < 2 * nbc + (int64_t)p.D * p.N) {
-            const int64_t r = i - 2 * nbc;
+            dst[bl * p.N + n] = Elem<Tin>::from_f(s);
+        } else if (i < nbc + (int64_t)p.D * p.N) {
+            const int64_t r = i - nbc;
             const int dd = r / p.N, n = r % p.N;
             float s = 0.f;
             for (int bi = 0; bi < p.b; ++bi) s += p.ws_a[((int64_t)bi * p.D + dd) * NS + n];
             p.dA[r] = s;
         } else {
-            const int dd = i - 2 * nbc - (int64_t)p.D * p.N;
+            const int dd = i - nbc - (int64_t)p.D * p.N;
             float sD = 0.f, sB = 0.f;
             for (int bi = 0; bi < p.b; ++bi) {
                 sD += p.ws_d[(int64_t)bi * p.D + dd];
@@ -690,7 +693,7 @@ static cudaError_t launch_bwd_t(const ScanDev& p, cudaStream_t st) {
     k<<<grid, NTH, smem, st>>>(p);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    const int64_t total = 2LL * p.b * p.L * p.N + (int64_t)p.D * p.N + p.D;
+    const int64_t total = 2LL * NS * p.b * p.L + (int64_t)p.D * p.N + p.D;
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
     scan_bwd_finalize_kernel<Tin><<<blocks, 256, 0, st>>>(p);
     return cudaGetLastError();
