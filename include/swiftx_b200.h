@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 5
+#define SWX_ABI_VERSION 6
 
 /* status codes */
 #define SWX_OK 0
@@ -112,6 +112,11 @@ int swx_scan_fwd(const swx_scan_args* args, void* stream);
  * (models/triton_scan.py:137-155).  Reductions (dA, dB, dC, dD, ddelta_bias) are
  * deterministic: fixed-order sums, no float atomics. */
 int swx_scan_bwd(const swx_scan_args* args, void* stream);
+
+/* How many CTAs per SM swx_scan_bwd would run for these arguments on the current device:
+ * 2 when the grid is larger than the SM count and the variant built for two CTAs per SM
+ * fits (bf16 inputs), else 1; a negative status on error.  Launches nothing. */
+int swx_scan_bwd_ctas_per_sm(const swx_scan_args* args);
 
 /* Capacity of the static scratch used by swx_scan_bwd_static_scratch: 8 MiB, enough
  * for swx_scan_bwd_workspace_bytes(batch, seqlen, dim) of roughly batch*seqlen*dim up

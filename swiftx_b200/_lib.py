@@ -129,6 +129,8 @@ def load():
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = [ctypes.POINTER(st), vp]
+    lib.swx_scan_bwd_ctas_per_sm.restype = ctypes.c_int
+    lib.swx_scan_bwd_ctas_per_sm.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_rmsnorm_bwd_workspace_bytes.restype = i64
     lib.swx_rmsnorm_bwd_workspace_bytes.argtypes = [i64]
     lib.swx_conv1d_bwd_workspace_bytes.restype = i64

@@ -8,6 +8,7 @@
 namespace swx {
 cudaError_t launch_scan_fwd(const ScanDev& p, int in_dtype, int out_dtype, bool has_z, cudaStream_t st);
 cudaError_t launch_scan_bwd(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st);
+cudaError_t scan_bwd_ctas_per_sm(const ScanDev& p, int in_dtype, bool has_z, int* ctas);
 }  // namespace swx
 
 namespace {
@@ -138,6 +139,15 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     p.ws_d = reinterpret_cast<float*>(ws + w.d);
     p.ws_bias = reinterpret_cast<float*>(ws + w.bias);
     return from_cuda(swx::launch_scan_bwd(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
+}
+
+int swx_scan_bwd_ctas_per_sm(const swx_scan_args* a) {
+    int s = check_common(a);
+    if (s != SWX_OK) return -s;
+    const swx::ScanDev p = pack(a);
+    int ctas = 1;
+    if (swx::scan_bwd_ctas_per_sm(p, a->in_dtype, a->z != nullptr, &ctas) != cudaSuccess) return -SWX_ERR_CUDA;
+    return ctas;
 }
 
 }  // extern "C"

@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
 }
 
 // =============================================================== backward
-template <typename Tin>
+template <typename Tin, int HTQ>
 struct BwdSmem {
     Tin u[RING][TCK][SCH];
     Tin dl[RING][TCK][SCH];
@@ -284,10 +284,10 @@ struct BwdSmem {
     float dy[2][TCK][SCH];             // dy = dout * silu(z) (or dout)
     float4 ee[2][TCK][SCH];            // (u, d delta_eff / d delta_raw, dout * silu'(z), dy)
     float yp[RING][TCK][SCH];          // pre-gate output saved by the forward (YPRE)
-    float bc[2][HT][SCH][2 * NS];      // per-channel dB | dC contributions of a half tile; the two
-                                       // 16-wide halves swap on odd channels (bank-conflict-free stores)
-    float2 nsd[2][HT][SCH][4];         // per state group: (sum g*B, sum g*a*h_prev*A)
-    float nyp[2][HT][SCH][4];          // per state group: sum h*C (gate without YPRE)
+    float bc[2][HTQ][SCH][2 * NS];     // per-channel dB | dC contributions of a hand-off tile; the
+                                       // two 16-wide halves swap on odd channels (conflict-free stores)
+    float2 nsd[2][HTQ][SCH][4];        // per state group: (sum g*B, sum g*a*h_prev*A)
+    float nyp[2][HTQ][SCH][4];         // per state group: sum h*C (gate without YPRE)
     float red[2][NAUX];
 };
 
@@ -328,12 +328,13 @@ __device__ __forceinline__ void bwd_recompute(const float2 (*__restrict__ dd)[SC
     }
 }
 
-// One half tile (8 steps, processed last to first) of the reverse recurrence.  The
+// One hand-off tile (HTQ steps, processed last to first) of the reverse recurrence.  The
 // decays are recomputed here (one exp per element; the MUFU pipe has room in the
-// backward), the states and B come from the chunk's registers.
-template <bool FULL, bool YV, typename Tin>
+// backward), the states come from the chunk's registers, B from registers or (NOBV,
+// the two-CTAs-per-SM variant) from shared memory.
+template <bool FULL, bool YV, int HTQ, bool NOBV, typename Tin>
 __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], const float (*__restrict__ dyv)[SCH],
-                                         const Tin (*__restrict__ Cs)[NS],
+                                         const Tin (*__restrict__ Bs)[NS], const Tin (*__restrict__ Cs)[NS],
                                          float (*__restrict__ bc)[SCH][2 * NS], float2 (*__restrict__ nsd)[SCH][4],
                                          float (*__restrict__ nyp)[SCH][4],
                                          int tlo, int nt, int ch, int j, float2 A01, float2 A23,
@@ -344,12 +345,12 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
     const int colB = (ch & 1) * NS + 4 * j;           // swizzled dB / dC columns
     const int colC = ((ch & 1) ^ 1) * NS + 4 * j;
 #pragma unroll
-    for (int tt = HT - 1; tt >= 0; --tt) {
+    for (int tt = HTQ - 1; tt >= 0; --tt) {
         const int t = tlo + tt;
         if (FULL || t < nt) {
             const float2 d = dd[t][ch];
             const float2 dy = bc2(dyv[t][ch]);
-            const float4 b = bv[t];
+            const float4 b = NOBV ? ld4(&Bs[t][4 * j]) : bv[t];
             const float4 c = ld4(&Cs[t][4 * j]);
             const float2 dte = bc2(d.x);
             const float2 a01 = ex2x2(mul2(dte, A01)), a23 = ex2x2(mul2(dte, A23));
@@ -380,11 +381,18 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
 
 // YPRE: the forward saved the pre-gate output, so the gate gradient reads it instead
 // of recomputing the readout (which would need C in the recompute pass).
-template <typename Tin, bool HAS_Z, bool YPRE>
-__global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
+//
+// LOWREG: the variant for grids larger than the SM count, built for two CTAs per SM (at
+// most 128 registers a thread, about 100 KB of shared memory with bf16 inputs): B is
+// reloaded from shared memory in the reverse pass instead of kept in registers, and the
+// per-step results are handed to the helper warps in 4-step tiles instead of 8.
+template <typename Tin, bool HAS_Z, bool YPRE, bool LOWREG>
+__global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const ScanDev p) {
     constexpr bool YV = HAS_Z && !YPRE;
+    constexpr int HTQ = LOWREG ? 4 : HT;       // steps per hand-off tile
+    constexpr int NQ = TCK / HTQ;              // hand-off tiles per chunk
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    BwdSmem<Tin>& S = *reinterpret_cast<BwdSmem<Tin>*>(smem_raw);
+    BwdSmem<Tin, HTQ>& S = *reinterpret_cast<BwdSmem<Tin, HTQ>*>(smem_raw);
 
     const int tid = threadIdx.x;
     const int bi = blockIdx.y;
@@ -425,20 +433,20 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                 bwd_recompute<true, YV>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
             else
                 bwd_recompute<false, YV>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
-            // reverse recurrence: upper half (steps 8..15) into slot 0, lower half into slot 1
+            // reverse recurrence: hand-off tiles from the last steps down, alternating slots
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                const int tlo = hh == 0 ? HT : 0;
-                bar_sync(BAR_E0 + hh, NTH);
+            for (int hh = 0; hh < NQ; ++hh) {
+                const int slot = hh & 1, tlo = (NQ - 1 - hh) * HTQ;
+                bar_sync(BAR_E0 + slot, NTH);
                 if (nt == TCK)
-                    bwd_half<true, YV>(S.dd[s], S.dy[s], S.C[r], S.bc[hh], S.nsd[hh], S.nyp[hh], tlo, nt, ch, j,
-                                       A01, A23, bv, hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23,
-                                       dA01, dA23);
+                    bwd_half<true, YV, HTQ, LOWREG>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[slot], S.nsd[slot],
+                                                    S.nyp[slot], tlo, nt, ch, j, A01, A23, bv, hs01, hs23, yv, hck01,
+                                                    hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
                 else
-                    bwd_half<false, YV>(S.dd[s], S.dy[s], S.C[r], S.bc[hh], S.nsd[hh], S.nyp[hh], tlo, nt, ch, j,
-                                        A01, A23, bv, hs01, hs23, yv, hck01, hck23, An01, An23, g01, g23, an01, an23,
-                                        dA01, dA23);
-                bar_arrive(BAR_X0 + hh, NTH);
+                    bwd_half<false, YV, HTQ, LOWREG>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[slot], S.nsd[slot],
+                                                     S.nyp[slot], tlo, nt, ch, j, A01, A23, bv, hs01, hs23, yv, hck01,
+                                                     hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
+                bar_arrive(BAR_X0 + slot, NTH);
             }
         }
         if (dvalid) {
@@ -519,19 +527,19 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
         };
         auto epilogue = [&](int k, int hh) {
             const int c = nck - 1 - k, s = k & 1, t0 = c * TCK, nt = min(TCK, p.L - t0);
-            const int tlo = hh == 0 ? HT : 0;
+            const int tlo = (NQ - 1 - hh) * HTQ, slot = hh & 1;
             if (evalid) {
 #pragma unroll
-                for (int m = 0; m < HT * SCH / NAUX; ++m) {
+                for (int m = 0; m < HTQ * SCH / NAUX; ++m) {
                     const int tt = at / SCH + m * (NAUX / SCH);
                     const int t = tlo + tt;
                     if (t < nt) {
                         // rotate the state-group order per lane quad: conflict-free 8-byte loads
                         const int rot = (ech >> 2) & 3;
-                        const float2 n0 = S.nsd[hh][tt][ech][(rot + 0) & 3];
-                        const float2 n1 = S.nsd[hh][tt][ech][(rot + 1) & 3];
-                        const float2 n2 = S.nsd[hh][tt][ech][(rot + 2) & 3];
-                        const float2 n3 = S.nsd[hh][tt][ech][(rot + 3) & 3];
+                        const float2 n0 = S.nsd[slot][tt][ech][(rot + 0) & 3];
+                        const float2 n1 = S.nsd[slot][tt][ech][(rot + 1) & 3];
+                        const float2 n2 = S.nsd[slot][tt][ech][(rot + 2) & 3];
+                        const float2 n3 = S.nsd[slot][tt][ech][(rot + 3) & 3];
                         const float sgb = (n0.x + n1.x) + (n2.x + n3.x);
                         const float sda = (n0.y + n1.y) + (n2.y + n3.y);
                         const float dte = S.dd[s][t][ech].x;
@@ -546,7 +554,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                             if (YPRE) {
                                 y = S.yp[k % RING][t][ech];
                             } else {
-                                const float4 q4 = *reinterpret_cast<const float4*>(&S.nyp[hh][tt][ech][0]);
+                                const float4 q4 = *reinterpret_cast<const float4*>(&S.nyp[slot][tt][ech][0]);
                                 y = fmaf(eD, e.x, (q4.x + q4.y) + (q4.z + q4.w));
                             }
                             gdz[o] = Elem<Tin>::from_f(e.z * y);
@@ -556,22 +564,42 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                     }
                 }
             }
-            // CTA partial of dB | dC: fixed-order sum over the 32 channels
-            {
+            // CTA partial of dB | dC: fixed-order sum over the 32 channels.  8-step tiles: one
+            // thread per (step, column pair); 4-step tiles: two, each summing 16 channels,
+            // joined by one shuffle.
+            if (HTQ == 8) {
                 const int o2 = at & 15, tt = at >> 4, t = tlo + tt;
                 if (t < nt) {
                     float2 s0 = f2(0.f, 0.f), s1 = s0, s2 = s0, s3 = s0;
                     const int col0 = 2 * o2, col1 = (2 * o2) ^ NS;   // even / odd channel columns
 #pragma unroll
                     for (int cc = 0; cc < SCH; cc += 4) {
-                        s0 = add2(s0, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 0][col0]));
-                        s1 = add2(s1, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 1][col1]));
-                        s2 = add2(s2, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 2][col0]));
-                        s3 = add2(s3, *reinterpret_cast<const float2*>(&S.bc[hh][tt][cc + 3][col1]));
+                        s0 = add2(s0, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 0][col0]));
+                        s1 = add2(s1, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 1][col1]));
+                        s2 = add2(s2, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 2][col0]));
+                        s3 = add2(s3, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 3][col1]));
                     }
                     *reinterpret_cast<float2*>(wbc + (int64_t)(t0 + t) * 2 * NS + 2 * o2) =
                         add2(add2(s0, s1), add2(s2, s3));
                 }
+            } else {
+                const int half = at & 1, item = at >> 1;
+                const int o2 = item & 15, tt = (item >> 4) & (HTQ - 1), t = tlo + tt;
+                float2 s0 = f2(0.f, 0.f), s1 = s0, s2 = s0, s3 = s0;
+                const int col0 = 2 * o2, col1 = (2 * o2) ^ NS;
+#pragma unroll
+                for (int cc = 16 * half; cc < 16 * half + 16; cc += 4) {
+                    s0 = add2(s0, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 0][col0]));
+                    s1 = add2(s1, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 1][col1]));
+                    s2 = add2(s2, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 2][col0]));
+                    s3 = add2(s3, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 3][col1]));
+                }
+                float2 sum = add2(add2(s0, s1), add2(s2, s3));
+                const float2 other = f2(__shfl_xor_sync(0xffffffffu, sum.x, 1),
+                                        __shfl_xor_sync(0xffffffffu, sum.y, 1));
+                sum = half ? add2(other, sum) : add2(sum, other);
+                if (half == 0 && t < nt)
+                    *reinterpret_cast<float2*>(wbc + (int64_t)(t0 + t) * 2 * NS + 2 * o2) = sum;
             }
         };
 
@@ -582,7 +610,7 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
         bar_sync(BAR_AUX, NAUX);
         derive(0);
         bar_arrive(BAR_D0, NTH);
-        bar_arrive(BAR_E0, NTH);          // both half-tile slots start empty
+        bar_arrive(BAR_E0, NTH);          // both hand-off slots start empty
         bar_arrive(BAR_E0 + 1, NTH);
         for (int k = 0; k < nck; ++k) {
             if (k + 1 < nck) {
@@ -592,10 +620,11 @@ __global__ void __launch_bounds__(NTH, 1) scan_bwd_kernel(const ScanDev p) {
                 bar_arrive(BAR_D0 + ((k + 1) & 1), NTH);
             }
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) {
-                bar_sync(BAR_X0 + hh, NTH);
+            for (int hh = 0; hh < NQ; ++hh) {
+                bar_sync(BAR_X0 + (hh & 1), NTH);
                 epilogue(k, hh);
-                if (k + 1 < nck) bar_arrive(BAR_E0 + hh, NTH);
+                // the slot is free again for the tile two hand-offs later, if there is one
+                if (k * NQ + hh + 2 < NQ * nck) bar_arrive(BAR_E0 + (hh & 1), NTH);
             }
             bar_sync(BAR_AUX, NAUX);      // raw slot (k-1) % RING no longer read
             issue(k + 3);
@@ -683,14 +712,40 @@ static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// Grids larger than the SM count run the two-CTAs-per-SM variant when two of its CTAs
+// fit on an SM (bf16 inputs), so the grid runs in one wave instead of two.
+template <typename Tin, bool HAS_Z>
+static cudaError_t bwd_ctas_per_sm_t(const ScanDev& p, int* ctas) {
+    const bool ypre = HAS_Z && p.ypre;
+    auto k2 = ypre ? scan_bwd_kernel<Tin, HAS_Z, true, true> : scan_bwd_kernel<Tin, HAS_Z, false, true>;
+    const int smem2 = sizeof(BwdSmem<Tin, 4>);
+    const long long nblocks = (long long)((p.D + SCH - 1) / SCH) * p.b;
+    cudaError_t e = allow_smem(k2, smem2);
+    if (e != cudaSuccess) return e;
+    int sms = 0, per_sm = 0;
+    e = sm_fit(k2, NTH, smem2, &sms, &per_sm);
+    if (e != cudaSuccess) return e;
+    *ctas = (nblocks > sms && per_sm >= 2) ? 2 : 1;
+    return cudaSuccess;
+}
+
 template <typename Tin, bool HAS_Z>
 static cudaError_t launch_bwd_t(const ScanDev& p, cudaStream_t st) {
-    auto k = (HAS_Z && p.ypre) ? scan_bwd_kernel<Tin, HAS_Z, true> : scan_bwd_kernel<Tin, HAS_Z, false>;
-    const int smem = sizeof(BwdSmem<Tin>);
-    cudaError_t e = allow_smem(k, smem);
-    if (e != cudaSuccess) return e;
+    const bool ypre = HAS_Z && p.ypre;
+    auto k1 = ypre ? scan_bwd_kernel<Tin, HAS_Z, true, false> : scan_bwd_kernel<Tin, HAS_Z, false, false>;
+    auto k2 = ypre ? scan_bwd_kernel<Tin, HAS_Z, true, true> : scan_bwd_kernel<Tin, HAS_Z, false, true>;
+    const int smem1 = sizeof(BwdSmem<Tin, HT>), smem2 = sizeof(BwdSmem<Tin, 4>);
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
-    k<<<grid, NTH, smem, st>>>(p);
+    int ctas = 1;
+    cudaError_t e = bwd_ctas_per_sm_t<Tin, HAS_Z>(p, &ctas);
+    if (e != cudaSuccess) return e;
+    if (ctas == 2) {
+        k2<<<grid, NTH, smem2, st>>>(p);
+    } else {
+        e = allow_smem(k1, smem1);
+        if (e != cudaSuccess) return e;
+        k1<<<grid, NTH, smem1, st>>>(p);
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
     const int64_t total = 2LL * NS * p.b * p.L + (int64_t)p.D * p.N + p.D;
@@ -711,6 +766,12 @@ cudaError_t launch_scan_fwd(const ScanDev& p, int in_dtype, int out_dtype, bool 
                      : launch_fwd_t<__nv_bfloat16, float, false>(p, st);
     return has_z ? launch_fwd_t<__nv_bfloat16, __nv_bfloat16, true>(p, st)
                  : launch_fwd_t<__nv_bfloat16, __nv_bfloat16, false>(p, st);
+}
+
+cudaError_t scan_bwd_ctas_per_sm(const ScanDev& p, int in_dtype, bool has_z, int* ctas) {
+    if (in_dtype == SWX_DTYPE_F32)
+        return has_z ? bwd_ctas_per_sm_t<float, true>(p, ctas) : bwd_ctas_per_sm_t<float, false>(p, ctas);
+    return has_z ? bwd_ctas_per_sm_t<__nv_bfloat16, true>(p, ctas) : bwd_ctas_per_sm_t<__nv_bfloat16, false>(p, ctas);
 }
 
 cudaError_t launch_scan_bwd(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st) {

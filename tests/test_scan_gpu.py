@@ -227,3 +227,46 @@ def test_config1_full_size_vs_oracle():
     g = scan_backward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
                       inp["delta_bias"], True, None, ck, inp["dout"], y_pre=pre)
     check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
+
+
+@pytest.mark.parametrize("use_pre", [True, False])
+def test_bwd_two_ctas_per_sm_variant(use_pre):
+    """bf16 inputs with more CTAs than SMs (5 rows x 32 channel blocks) run the backward
+    built for two CTAs per SM (4-step hand-off tiles, B read from shared memory).  Its
+    per-row gradients equal, bit for bit, those of the one-CTA-per-SM backward on the same
+    rows (two smaller calls), its sums agree to fp32 re-association, and it matches the
+    oracle at the bf16 tolerance."""
+    from swiftx_b200 import _lib
+    from swiftx_b200.selective_scan import _fill_inputs, _prep
+    b, L, D, N = 5, 100, 1024, 16
+    inp = config_inputs(b, L, D, N, seed=41, device=DEV, dtype=torch.bfloat16)
+    rowwise = ("u", "delta", "z", "B", "C", "dout")
+
+    def run(rows):
+        sub = {k: (v[rows] if k in rowwise else v) for k, v in inp.items()}
+        args = (sub["u"], sub["delta"], sub["A"], sub["B"], sub["C"], sub["D"], sub["z"], sub["delta_bias"], True)
+        pre = torch.empty(sub["u"].shape, device=DEV, dtype=torch.float32) if use_pre else None
+        _, ck, _ = scan_forward(*args, checkpoints=True, pre_out=pre)
+        a = _lib.ScanArgs()
+        u, dl, A, Bm, Cm, Dv, z, bias, h0, in_dt = _prep(*args[:8], None)
+        _fill_inputs(a, u, dl, A, Bm, Cm, Dv, z, bias, h0, True, in_dt)
+        a.out_pre = pre.data_ptr() if pre is not None else None
+        ctas = _lib.load().swx_scan_bwd_ctas_per_sm(a)
+        return scan_backward(*args, None, ck, sub["dout"], y_pre=pre), ctas
+
+    g_all, ctas_all = run(slice(0, 5))
+    g_a, ctas_a = run(slice(0, 2))
+    g_b, ctas_b = run(slice(2, 5))
+    assert (ctas_all, ctas_a, ctas_b) == (2, 1, 1)
+    for k in ("du", "ddelta", "dz"):
+        assert torch.equal(g_all[k], torch.cat([g_a[k], g_b[k]])), k
+    for k in ("dB", "dC"):
+        want = torch.cat([g_a[k], g_b[k]]).float()
+        assert torch.allclose(g_all[k].float(), want, rtol=1e-2, atol=1e-2 * float(want.abs().max())), k
+    for k in ("dA", "dD", "ddelta_bias"):
+        want = (g_a[k] + g_b[k]).double().cpu().numpy()
+        np.testing.assert_allclose(np64(g_all[k]), want, rtol=1e-5, atol=1e-5 * np.abs(want).max(), err_msg=k)
+    out_o, _, gr_o, scale = oracle_case(inp)
+    for k in ("du", "ddelta", "dz", "dB", "dC", "dA", "dD", "ddelta_bias"):
+        want = gr_o[k]
+        assert_close(np64(g_all[k]), want, 3e-2, 3e-2 * np.abs(want).max() + 1e-5 * np.abs(scale[k]).max(), k)
