@@ -32,7 +32,7 @@ extern "C" {
 /* status codes */
 #define SWX_OK 0
 #define SWX_ERR_INVALID_ARG 1   /* bad shape, size, stride or missing pointer */
-#define SWX_ERR_UNSUPPORTED 2   /* dtype / layout this build does not handle */
+#define SWX_ERR_UNSUPPORTED 2   /* dtype / layout the library does not handle */
 #define SWX_ERR_CUDA 3          /* a CUDA launch or runtime call failed */
 #define SWX_ERR_TIMEOUT 4       /* a bounded device-side wait gave up */
 

@@ -4,7 +4,7 @@
  * This file restates, in plain C and float64, the algorithms of the reference
  * (BhanuPrakash6640/SwiftX) for the selective scan, its backward pass, the
  * depthwise causal conv1d + SiLU that feeds it, and the recurrent decode step.
- * It is the checker the CUDA kernels are compared against.  Only the test
+ * It is what the CUDA kernels are compared against.  Only the test
  * suite, the smoke check and the CPU-baseline leg of the benchmark load it;
  * the product library never links or calls it.
  *

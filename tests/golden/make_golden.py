@@ -13,7 +13,7 @@ Fixtures:
   fwd_L{1,7,64}.npz  tests/test_selective_scan.py:68-74 shapes (b=2, D=8, N=16, seed 1)
   bwd_f64.npz        tests/test_selective_scan.py:77-86 shapes (float64, b=2, L=20, D=5, N=6, seed 2)
   tail_*.npz         tests/test_triton_scan.py:15 tail shapes, forward + all grads
-  config0.npz        the CPU config: b=2, L=256, D=128, N=16, seed 0, forward only
+  fwd_b2_L256_D128.npz  b=2, L=256, D=128, N=16, seed 0, forward only (the CPU-sized case)
   gated.npz          scan(u, softplus(dr + bias)) * silu(z) via the block's glue, all grads
   conv.npz           SiftBlock conv1d + SiLU on the strided x half of in_proj, with grads
   decode.npz         SiftBlock.step intermediates (conv window, state update, gated y)
@@ -171,7 +171,7 @@ def main(ref_root, only=None):
     delta = F.softplus(dr + bias)
     y64 = selective_scan_ref(u.double(), delta.double(), A.double(), Bm.double(), Cm.double(), Ds.double())
     y32 = selective_scan_fast(u, delta, A, Bm, Cm, Ds, mode="fused")
-    save("config0", u=u, delta_raw=dr, delta_bias=bias, delta=delta, A=A, B=Bm, C=Cm, D=Ds, y=y64,
+    save("fwd_b2_L256_D128", u=u, delta_raw=dr, delta_bias=bias, delta=delta, A=A, B=Bm, C=Cm, D=Ds, y=y64,
          y_fused_f32=y32)
 
     # 6. gated scan with softplus(delta_raw + bias): the block's glue around the reference scan

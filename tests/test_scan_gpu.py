@@ -110,8 +110,8 @@ def test_golden_gated_softplus(golden):
         assert_close(np64(gr), g[k], 1e-4, 1e-4, k)
 
 
-def test_golden_config0(golden):
-    g = golden("config0")
+def test_golden_cpu_sized_forward(golden):
+    g = golden("fwd_b2_L256_D128")
     t = {k: torch.tensor(v, device=DEV, dtype=torch.float32) for k, v in g.items()}
     y = selective_scan_fn(t["u"], t["delta_raw"], t["A"], t["B"], t["C"], t["D"],
                           delta_bias=t["delta_bias"], delta_softplus=True)
@@ -215,7 +215,7 @@ def test_cpu_tensors_raise():
         selective_scan_fast(u, delta, A, B, C, Ds)
 
 
-def test_config1_full_size_vs_oracle():
+def test_full_size_8x2048x512_vs_oracle():
     """The benchmark configuration itself (b=8, L=2048, D=512, N=16, gated, softplus)."""
     inp = config_inputs(8, 2048, 512, 16, seed=0, device=DEV)
     oracle.set_num_threads(max(1, oracle.num_threads()))
