@@ -53,7 +53,7 @@ def measured_peak():
 
 def profiled_traffic():
     """dram bytes per launch of the backward kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "scan_bwd_kernel_c1.md")
+    p = os.path.join(ROOT, "profiles", "scan_bwd_kernel_8x2048x512.md")
     try:
         with open(p) as f:
             for line in f:
