@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 6
+#define SWX_ABI_VERSION 7
 
 /* status codes */
 #define SWX_OK 0
@@ -224,13 +224,17 @@ int swx_linear_scan_bwd(const swx_linear_scan_args* args, void* stream);
 
 /* RMSNorm of the language model around the mixer (models/sift_model.py:17-26):
  *   y = (x * rsqrt(mean(x^2) + eps)) * weight  over the last dim, computed in fp32.
- * x, y, dy, dx: dense (rows, dim), fp32 or bf16; weight, dweight: (dim,) fp32;
+ * x, dx: dense (rows, dim) in dtype; y, dy: dense (rows, dim) in out_dtype (fp32 or
+ * bf16: a bf16 y is the fp32 result rounded once, as a cast after the norm would give);
+ * weight, dweight: (dim,) fp32;
  * rstd: (rows,) fp32, written by the forward when given and read by the backward.
  * dim <= 1024.  The weight gradient is a fixed-order sum (deterministic). */
 typedef struct swx_rmsnorm_args {
     int64_t rows, dim;
     float eps;
-    int32_t dtype;                    /* SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
+    int32_t dtype;                    /* x, dx: SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
+    int32_t out_dtype;                /* y, dy: SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
+    int32_t reserved;
     const void* x;
     const float* weight;
     void* y;

@@ -32,12 +32,12 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-template <typename T>
+template <typename T, typename TY>
 __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_fwd_kernel(const NormDev p) {
     const int row = blockIdx.x * NORM_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= p.rows) return;
     const T* x = static_cast<const T*>(p.x) + (int64_t)row * p.d;
-    T* y = static_cast<T*>(p.y) + (int64_t)row * p.d;
+    TY* y = static_cast<TY*>(p.y) + (int64_t)row * p.d;
     float ss = 0.f;
     for (int c = lane; c < p.d; c += 32) {
         const float v = Elem<T>::to_f(x[c]);
@@ -45,10 +45,10 @@ __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_fwd_kernel(const Norm
     }
     const float r = rsqrtf(warp_sum(ss) / p.d + p.eps);
     if (lane == 0 && p.rstd) p.rstd[row] = r;
-    for (int c = lane; c < p.d; c += 32) y[c] = Elem<T>::from_f((Elem<T>::to_f(x[c]) * r) * p.w[c]);
+    for (int c = lane; c < p.d; c += 32) y[c] = Elem<TY>::from_f((Elem<T>::to_f(x[c]) * r) * p.w[c]);
 }
 
-template <typename T, int NC>
+template <typename T, typename TY, int NC>
 __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const NormDev p) {
     const int gw = blockIdx.x * NORM_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     float wv[NC], dwacc[NC];
@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const Norm
     }
     for (int row = gw; row < p.rows; row += NORM_BWD_WARPS) {
         const T* x = static_cast<const T*>(p.x) + (int64_t)row * p.d;
-        const T* dy = static_cast<const T*>(p.dy) + (int64_t)row * p.d;
+        const TY* dy = static_cast<const TY*>(p.dy) + (int64_t)row * p.d;
         T* dx = static_cast<T*>(p.dx) + (int64_t)row * p.d;
         const float r = p.rstd[row];
         float xh[NC], g[NC], dyv[NC];
@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const Norm
             const int c = lane + 32 * k;
             const bool ok = c < p.d;
             xh[k] = ok ? Elem<T>::to_f(x[c]) * r : 0.f;
-            dyv[k] = ok ? Elem<T>::to_f(dy[c]) : 0.f;
+            dyv[k] = ok ? Elem<TY>::to_f(dy[c]) : 0.f;
             g[k] = wv[k] * dyv[k];
             s = fmaf(xh[k], g[k], s);
         }
@@ -107,14 +107,26 @@ __global__ void __launch_bounds__(1024) rmsnorm_dw_kernel(const NormDev p) {
     }
 }
 
-template <typename T>
+template <typename T, typename TY>
 static void launch_bwd(const NormDev& p, cudaStream_t st) {
     const int nc = (p.d + 31) / 32;
     const dim3 grid(NORM_BWD_WARPS / NORM_WARPS);
-    if (nc <= 8) rmsnorm_bwd_kernel<T, 8><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
-    else if (nc <= 16) rmsnorm_bwd_kernel<T, 16><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
-    else rmsnorm_bwd_kernel<T, NORM_MAXC><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    if (nc <= 8) rmsnorm_bwd_kernel<T, TY, 8><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    else if (nc <= 16) rmsnorm_bwd_kernel<T, TY, 16><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    else rmsnorm_bwd_kernel<T, TY, NORM_MAXC><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
     rmsnorm_dw_kernel<<<(p.d + 31) / 32, 1024, 0, st>>>(p);
+}
+
+template <typename T>
+static void launch_fwd_x(const NormDev& p, int out_dtype, unsigned grid, cudaStream_t st) {
+    if (out_dtype == SWX_DTYPE_F32) rmsnorm_fwd_kernel<T, float><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    else rmsnorm_fwd_kernel<T, __nv_bfloat16><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+}
+
+template <typename T>
+static void launch_bwd_x(const NormDev& p, int out_dtype, cudaStream_t st) {
+    if (out_dtype == SWX_DTYPE_F32) launch_bwd<T, float>(p, st);
+    else launch_bwd<T, __nv_bfloat16>(p, st);
 }
 
 }  // namespace swx
@@ -124,6 +136,7 @@ int norm_check(const swx_rmsnorm_args* a, bool bwd) {
     if (!a) return SWX_ERR_INVALID_ARG;
     if (a->rows < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
     if (a->dtype != SWX_DTYPE_F32 && a->dtype != SWX_DTYPE_BF16) return SWX_ERR_UNSUPPORTED;
+    if (a->out_dtype != SWX_DTYPE_F32 && a->out_dtype != SWX_DTYPE_BF16) return SWX_ERR_UNSUPPORTED;
     if (a->rows > INT32_MAX || a->dim > 32 * swx::NORM_MAXC) return SWX_ERR_UNSUPPORTED;
     if (a->rows * a->dim == 0) return SWX_OK;
     if (!a->x || !a->weight) return SWX_ERR_INVALID_ARG;
@@ -153,8 +166,8 @@ int swx_rmsnorm_fwd(const swx_rmsnorm_args* a, void* stream) {
     const swx::NormDev p = norm_pack(a);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     const unsigned grid = (unsigned)((p.rows + swx::NORM_WARPS - 1) / swx::NORM_WARPS);
-    if (a->dtype == SWX_DTYPE_F32) swx::rmsnorm_fwd_kernel<float><<<grid, 32 * swx::NORM_WARPS, 0, st>>>(p);
-    else swx::rmsnorm_fwd_kernel<__nv_bfloat16><<<grid, 32 * swx::NORM_WARPS, 0, st>>>(p);
+    if (a->dtype == SWX_DTYPE_F32) swx::launch_fwd_x<float>(p, a->out_dtype, grid, st);
+    else swx::launch_fwd_x<__nv_bfloat16>(p, a->out_dtype, grid, st);
     return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
 }
 
@@ -164,8 +177,8 @@ int swx_rmsnorm_bwd(const swx_rmsnorm_args* a, void* stream) {
     if (a->workspace_bytes < swx_rmsnorm_bwd_workspace_bytes(a->dim)) return SWX_ERR_INVALID_ARG;
     const swx::NormDev p = norm_pack(a);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (a->dtype == SWX_DTYPE_F32) swx::launch_bwd<float>(p, st);
-    else swx::launch_bwd<__nv_bfloat16>(p, st);
+    if (a->dtype == SWX_DTYPE_F32) swx::launch_bwd_x<float>(p, a->out_dtype, st);
+    else swx::launch_bwd_x<__nv_bfloat16>(p, a->out_dtype, st);
     return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
 }
 

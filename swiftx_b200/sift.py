@@ -150,9 +150,15 @@ class RMSNorm(nn.Module):
 
     def forward(self, x):
         """models/sift_model.py:25-26; on CUDA (fp32 / bf16, d <= 1024) one fused kernel
-        each way, otherwise the reference expression itself."""
+        each way, otherwise the reference expression itself.  Under bf16 autocast the
+        result comes out in bf16: its consumers here (in_proj, the head) are Linear layers
+        that autocast would cast it to bf16 anyway, and the kernel rounds the same fp32
+        value once, so the cast (and its backward) is folded into the kernel."""
         if norm_kernels.supported(x):
-            return norm_kernels.rms_norm(x, self.weight, self.eps)
+            out_dtype = None
+            if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+                out_dtype = torch.bfloat16
+            return norm_kernels.rms_norm(x, self.weight, self.eps, out_dtype)
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
 
 

@@ -32,7 +32,7 @@ def test_struct_mirrors_match():
     assert lib.swx_decode_args_size() == ctypes.sizeof(_lib.DecodeArgs)
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
     assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
-    assert lib.swx_abi_version() == 6
+    assert lib.swx_abi_version() == 7
 
 
 def test_status_strings():

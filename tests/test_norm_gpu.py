@@ -53,3 +53,21 @@ def test_bf16_and_determinism():
 def test_rejects_unsupported():
     with pytest.raises(ValueError):
         rms_norm(torch.randn(2, 2048, device=DEV), torch.ones(2048, device=DEV))
+
+
+def test_bf16_output_is_the_rounded_fp32_result():
+    """out_dtype=bf16 gives the fp32 result rounded once, and its backward (bf16 upstream
+    gradient) equals the fp32 backward fed the same gradient values."""
+    g = torch.Generator().manual_seed(4)
+    x = (torch.randn(40, 256, generator=g) * 2).to(DEV)
+    w = torch.randn(256, generator=g).to(DEV)
+    dy = torch.randn(40, 256, generator=g).to(DEV).bfloat16()
+    x1, w1 = x.clone().requires_grad_(), w.clone().requires_grad_()
+    yb = rms_norm(x1, w1, out_dtype=torch.bfloat16)
+    assert yb.dtype == torch.bfloat16 and x1.grad is None
+    x2, w2 = x.clone().requires_grad_(), w.clone().requires_grad_()
+    yf = rms_norm(x2, w2)
+    assert torch.equal(yb, yf.bfloat16())
+    yb.backward(dy)
+    yf.backward(dy.float())
+    assert torch.equal(x1.grad, x2.grad) and torch.equal(w1.grad, w2.grad)
