@@ -583,8 +583,9 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
                         add2(add2(s0, s1), add2(s2, s3));
                 }
             } else {
-                const int half = at & 1, item = at >> 1;
-                const int o2 = item & 15, tt = (item >> 4) & (HTQ - 1), t = tlo + tt;
+                // lanes 0-15 sum channels 0-15 and lanes 16-31 channels 16-31 of the same 16
+                // column pairs, so each half-warp reads one contiguous 128-byte row
+                const int half = (at >> 4) & 1, o2 = at & 15, tt = (at >> 5) & (HTQ - 1), t = tlo + tt;
                 float2 s0 = f2(0.f, 0.f), s1 = s0, s2 = s0, s3 = s0;
                 const int col0 = 2 * o2, col1 = (2 * o2) ^ NS;
 #pragma unroll
@@ -595,8 +596,8 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
                     s3 = add2(s3, *reinterpret_cast<const float2*>(&S.bc[slot][tt][cc + 3][col1]));
                 }
                 float2 sum = add2(add2(s0, s1), add2(s2, s3));
-                const float2 other = f2(__shfl_xor_sync(0xffffffffu, sum.x, 1),
-                                        __shfl_xor_sync(0xffffffffu, sum.y, 1));
+                const float2 other = f2(__shfl_xor_sync(0xffffffffu, sum.x, 16),
+                                        __shfl_xor_sync(0xffffffffu, sum.y, 16));
                 sum = half ? add2(other, sum) : add2(sum, other);
                 if (half == 0 && t < nt)
                     *reinterpret_cast<float2*>(wbc + (int64_t)(t0 + t) * 2 * NS + 2 * o2) = sum;
