@@ -229,21 +229,25 @@ def test_full_size_8x2048x512_vs_oracle():
     check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
 
 
-@pytest.mark.parametrize("use_pre", [True, False])
-def test_bwd_two_ctas_per_sm_variant(use_pre):
-    """bf16 inputs with more CTAs than SMs (5 rows x 32 channel blocks) run the backward
-    built for two CTAs per SM (4-step hand-off tiles, B read from shared memory).  Its
+@pytest.mark.parametrize("shape,gate,use_pre", [((5, 100, 1024, 16), True, True),
+                                                ((5, 100, 1024, 16), True, False),
+                                                ((10, 37, 520, 5), False, False)])
+def test_bwd_two_ctas_per_sm_variant(shape, gate, use_pre):
+    """bf16 inputs with more CTAs than SMs (rows x channel blocks > 148; the second shape
+    also has N < 16, no gate and a partial last channel block) run the backward built for
+    two CTAs per SM (4-step hand-off tiles, B read from shared memory).  Its
     per-row gradients equal, bit for bit, those of the one-CTA-per-SM backward on the same
     rows (two smaller calls), its sums agree to fp32 re-association, and it matches the
     oracle at the bf16 tolerance."""
     from swiftx_b200 import _lib
     from swiftx_b200.selective_scan import _fill_inputs, _prep
-    b, L, D, N = 5, 100, 1024, 16
-    inp = config_inputs(b, L, D, N, seed=41, device=DEV, dtype=torch.bfloat16)
+    b, L, D, N = shape
+    inp = config_inputs(b, L, D, N, seed=41, gate=gate, device=DEV, dtype=torch.bfloat16)
     rowwise = ("u", "delta", "z", "B", "C", "dout")
+    cut = 2 if b == 5 else 4
 
     def run(rows):
-        sub = {k: (v[rows] if k in rowwise else v) for k, v in inp.items()}
+        sub = {k: (v[rows] if k in rowwise and v is not None else v) for k, v in inp.items()}
         args = (sub["u"], sub["delta"], sub["A"], sub["B"], sub["C"], sub["D"], sub["z"], sub["delta_bias"], True)
         pre = torch.empty(sub["u"].shape, device=DEV, dtype=torch.float32) if use_pre else None
         _, ck, _ = scan_forward(*args, checkpoints=True, pre_out=pre)
@@ -254,19 +258,22 @@ def test_bwd_two_ctas_per_sm_variant(use_pre):
         ctas = _lib.load().swx_scan_bwd_ctas_per_sm(a)
         return scan_backward(*args, None, ck, sub["dout"], y_pre=pre), ctas
 
-    g_all, ctas_all = run(slice(0, 5))
-    g_a, ctas_a = run(slice(0, 2))
-    g_b, ctas_b = run(slice(2, 5))
+    g_all, ctas_all = run(slice(0, b))
+    g_a, ctas_a = run(slice(0, cut))
+    g_b, ctas_b = run(slice(cut, b))
     assert (ctas_all, ctas_a, ctas_b) == (2, 1, 1)
     for k in ("du", "ddelta", "dz"):
-        assert torch.equal(g_all[k], torch.cat([g_a[k], g_b[k]])), k
+        if g_all[k] is not None:
+            assert torch.equal(g_all[k], torch.cat([g_a[k], g_b[k]])), k
     for k in ("dB", "dC"):
         want = torch.cat([g_a[k], g_b[k]]).float()
         assert torch.allclose(g_all[k].float(), want, rtol=1e-2, atol=1e-2 * float(want.abs().max())), k
     for k in ("dA", "dD", "ddelta_bias"):
         want = (g_a[k] + g_b[k]).double().cpu().numpy()
         np.testing.assert_allclose(np64(g_all[k]), want, rtol=1e-5, atol=1e-5 * np.abs(want).max(), err_msg=k)
-    out_o, _, gr_o, scale = oracle_case(inp)
+    out_o, _, gr_o, scale = oracle_case(inp, gate=gate)
     for k in ("du", "ddelta", "dz", "dB", "dC", "dA", "dD", "ddelta_bias"):
+        if k not in gr_o:
+            continue
         want = gr_o[k]
         assert_close(np64(g_all[k]), want, 3e-2, 3e-2 * np.abs(want).max() + 1e-5 * np.abs(scale[k]).max(), k)
