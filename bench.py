@@ -475,7 +475,9 @@ def run_lm_train(args, world, rank, local):
                      "cuda_graph": graphed, "l2": "activations and weights per step exceed L2"})
     res["e2e"] = {"value": round(tokens / (ms_e2e * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step":
                   host.numel() * host.element_size(), "d2h_bytes_per_step": 4}
-    res["gpu_launches"] = 6 * 8 * args.steps      # per layer: conv fwd, scan fwd, conv bwd x2, scan bwd x2
+    # per layer: conv fwd, scan fwd, conv bwd x2, scan bwd x2; 9 RMSNorms (8 layers + norm_f):
+    # fwd, bwd, weight-gradient sum; token embedding backward: slice partials + slice sum
+    res["gpu_launches"] = (6 * 8 + 9 * 3 + 2) * args.steps
     res["clocks"] = clocks
     return res
 

@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 7
+#define SWX_ABI_VERSION 8
 
 /* status codes */
 #define SWX_OK 0
@@ -249,6 +249,26 @@ int64_t swx_rmsnorm_args_size(void);
 int64_t swx_rmsnorm_bwd_workspace_bytes(int64_t dim);
 int swx_rmsnorm_fwd(const swx_rmsnorm_args* args, void* stream);
 int swx_rmsnorm_bwd(const swx_rmsnorm_args* args, void* stream);
+
+/* Weight gradient of the LM's token embedding (nn.Embedding, models/sift_model.py;
+ * torch's embedding_dense_backward is what it replaces):
+ *   dweight[v, :] = sum over tokens i with idx[i] == v of dy[i, :]
+ * idx: (ntok,) int64; dy: dense (ntok, dim) fp32; dweight: dense (vocab, dim) fp32,
+ * overwritten.  vocab <= 1024.  Tokens are summed in a fixed order (token slices, then
+ * slices in order), so the result is deterministic for a given shape.  An id outside
+ * [0, vocab) is skipped and, when status is given, sets *status = 1 (device int). */
+typedef struct swx_embedding_args {
+    int64_t ntok, vocab, dim;
+    const int64_t* idx;
+    const float* dy;
+    float* dweight;
+    int32_t* status;                  /* optional */
+    void* workspace; int64_t workspace_bytes;
+} swx_embedding_args;
+
+int64_t swx_embedding_args_size(void);
+int64_t swx_embedding_bwd_workspace_bytes(int64_t ntok, int64_t vocab, int64_t dim);
+int swx_embedding_bwd(const swx_embedding_args* args, void* stream);
 
 #ifdef __cplusplus
 }

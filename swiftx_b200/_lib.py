@@ -95,6 +95,14 @@ class RMSNormArgs(ctypes.Structure):
     ]
 
 
+class EmbeddingArgs(ctypes.Structure):
+    """Mirror of ``swx_embedding_args``."""
+    _fields_ = [
+        ("ntok", i64), ("vocab", i64), ("dim", i64), ("idx", vp), ("dy", vp), ("dweight", vp),
+        ("status", vp), ("workspace", vp), ("workspace_bytes", i64),
+    ]
+
+
 _lib = None
 
 
@@ -113,7 +121,7 @@ def load():
     lib.swx_status_string.argtypes = [ctypes.c_int]
     for fn, st in (("swx_scan_args_size", ScanArgs), ("swx_conv_args_size", ConvArgs),
                    ("swx_decode_args_size", DecodeArgs), ("swx_linear_scan_args_size", LinearScanArgs),
-                   ("swx_rmsnorm_args_size", RMSNormArgs)):
+                   ("swx_rmsnorm_args_size", RMSNormArgs), ("swx_embedding_args_size", EmbeddingArgs)):
         getattr(lib, fn).restype = i64
         if getattr(lib, fn)() != ctypes.sizeof(st):
             raise RuntimeError(f"{st.__name__} layout mismatch between the library and its binding")
@@ -125,7 +133,8 @@ def load():
                      ("swx_scan_bwd_static_scratch", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
                      ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs),
                      ("swx_linear_scan_fwd", LinearScanArgs), ("swx_linear_scan_bwd", LinearScanArgs),
-                     ("swx_rmsnorm_fwd", RMSNormArgs), ("swx_rmsnorm_bwd", RMSNormArgs)):
+                     ("swx_rmsnorm_fwd", RMSNormArgs), ("swx_rmsnorm_bwd", RMSNormArgs),
+                     ("swx_embedding_bwd", EmbeddingArgs)):
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = [ctypes.POINTER(st), vp]
@@ -133,6 +142,8 @@ def load():
     lib.swx_scan_bwd_ctas_per_sm.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_rmsnorm_bwd_workspace_bytes.restype = i64
     lib.swx_rmsnorm_bwd_workspace_bytes.argtypes = [i64]
+    lib.swx_embedding_bwd_workspace_bytes.restype = i64
+    lib.swx_embedding_bwd_workspace_bytes.argtypes = [i64, i64, i64]
     lib.swx_conv1d_bwd_workspace_bytes.restype = i64
     lib.swx_conv1d_bwd_workspace_bytes.argtypes = [i64, i64, i64, i64]
     _lib = lib

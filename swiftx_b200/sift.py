@@ -12,6 +12,8 @@ runs on the sm_100a kernels:
      gate (kernel) -> out_proj (cuBLAS)
 
 and decode runs the conv-window / state-update kernels around the x_proj / dt_proj GEMVs.
+RMSNorm runs on its fused kernels and, in training, the token embedding's weight
+gradient on the sort-free swx_embedding_bwd.
 Fusing the gate is exactly the reference's y * silu(z) when no SiftX pathway mixing is
 configured (models/sift_block.py:132-142).  With pathway_gate (SiftX), the per-token
 group weights sit between the scan and the gate, so the scan kernel runs without z
@@ -25,6 +27,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import embedding as embedding_kernels
 from . import norm as norm_kernels
 from .conv import causal_conv1d_fn
 from .decode import decode_conv_step, decode_ssm_step
@@ -228,7 +231,12 @@ class SiftLM(nn.Module):
             self.lm_head.weight = self.embedding.weight
 
     def forward(self, idx, targets=None):
-        logits = self.lm_head(self.backbone(self.embedding(idx)))
+        w = self.embedding.weight
+        if embedding_kernels.supported(idx, w) and torch.is_grad_enabled():
+            x = embedding_kernels.embedding(idx, w)
+        else:
+            x = self.embedding(idx)
+        logits = self.lm_head(self.backbone(x))
         loss = None
         if targets is not None:
             loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), targets.reshape(-1))

@@ -32,7 +32,8 @@ def test_struct_mirrors_match():
     assert lib.swx_decode_args_size() == ctypes.sizeof(_lib.DecodeArgs)
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
     assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
-    assert lib.swx_abi_version() == 7
+    assert lib.swx_embedding_args_size() == ctypes.sizeof(_lib.EmbeddingArgs)
+    assert lib.swx_abi_version() == 8
 
 
 def test_status_strings():
@@ -49,6 +50,10 @@ def test_sizes_of_checkpoints_and_workspace():
     assert lib.swx_scan_bwd_workspace_bytes(8, 2048, 512) >= 16 * 8 * 2048 * 32 * 4
     # one (weight, bias) partial per (row, 16-step time tile, channel): 2 rows x 9 tiles x 8 ch x (4+1) floats
     assert lib.swx_conv1d_bwd_workspace_bytes(2, 130, 8, 4) == 2 * 9 * 8 * 5 * 4
+    # one (vocab, dim) fp32 partial per token slice; slices hold >= 128 tokens
+    assert lib.swx_embedding_bwd_workspace_bytes(0, 256, 256) == 0
+    assert lib.swx_embedding_bwd_workspace_bytes(300, 10, 64) == 3 * 10 * 64 * 4
+    assert lib.swx_embedding_bwd_workspace_bytes(-1, 10, 64) < 0
 
 
 def test_host_side_validation_without_gpu():
@@ -85,6 +90,13 @@ def test_host_side_validation_without_gpu():
     r.dim = 256                                               # missing pointers
     assert lib.swx_rmsnorm_fwd(r, None) == _lib.SWX_ERR_INVALID_ARG
     assert lib.swx_rmsnorm_bwd(r, None) == _lib.SWX_ERR_INVALID_ARG
+    e = _lib.EmbeddingArgs()
+    e.ntok, e.vocab, e.dim = 8, 2000, 32                      # vocab > 1024
+    assert lib.swx_embedding_bwd(e, None) == _lib.SWX_ERR_UNSUPPORTED
+    e.vocab = 256                                             # missing pointers
+    assert lib.swx_embedding_bwd(e, None) == _lib.SWX_ERR_INVALID_ARG
+    e.vocab = 0                                               # empty weight: nothing to do
+    assert lib.swx_embedding_bwd(e, None) == _lib.SWX_OK
 
 
 def test_cpu_tensors_are_rejected_not_computed():
