@@ -258,37 +258,57 @@ def run_ours(args, world, rank, local):
 
 def run_e2e(args, inp, dev, world):
     """The scan workload through the host-buffer API: every step copies its inputs from
-    pinned host memory, runs forward + backward, and copies every result back, with the
-    copies of one row chunk overlapping the kernels of the next (HostScanPipeline)."""
+    pinned host memory, runs forward + backward, and copies every result back
+    (HostScanPipeline).  The headline runs consecutive steps chained -- the next step's
+    inputs stream in while the previous step's kernels and copies out finish, as a
+    loader feeding batch after batch does; every step still moves all of its own bytes
+    inside the timed region, and the timed region starts on an idle device and ends
+    when the last step's results are on the host.  The unchained figure (each step
+    queued behind the current stream, row chunks overlapped within the step) is
+    reported beside it."""
     from swiftx_b200.host_pipeline import HostScanPipeline
     b, L, D, N = CFG["b"], CFG["L"], CFG["D"], CFG["N"]
     host = {k: (v.cpu().pin_memory() if v is not None else None) for k, v in inp.items()}
     keys_in = ["u", "delta", "z", "B", "C", "dout", "A", "D", "delta_bias"]
     h2d = sum(host[k].numel() * host[k].element_size() for k in keys_in)
-    pipe = HostScanPipeline(b, L, D, N, rows_per_chunk=args.e2e_rows, n_compute=args.e2e_streams, device=dev)
-    res = pipe.allocate_host_outputs()
 
-    def step():
-        pipe.forward_backward(host["u"], host["delta"], host["A"], host["B"], host["C"], host["dout"],
-                              D=host["D"], z=host["z"], delta_bias=host["delta_bias"], out=res)
+    def measure(pipe):
+        res = pipe.allocate_host_outputs()
 
-    for _ in range(max(1, args.warmup)):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(args.steps):
-        step()
-    t1.record()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(t0.elapsed_time(t1) / args.steps, world, dev)
+        def step():
+            pipe.forward_backward(host["u"], host["delta"], host["A"], host["B"], host["C"], host["dout"],
+                                  D=host["D"], z=host["z"], delta_bias=host["delta_bias"], out=res)
+
+        for _ in range(max(1, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(t0.elapsed_time(t1) / args.steps, world, dev), pipe.d2h_bytes(res)
+
     fwd_b, bwd_b = alg_bytes(b, L, D, N)
-    return {"value": round((fwd_b + bwd_b) * world / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-            "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": pipe.d2h_bytes(res),
+    gbs = lambda ms: round((fwd_b + bwd_b) * world / (ms * 1e-3) / 1e9, 2)  # noqa: E731
+    chained = HostScanPipeline(b, L, D, N, rows_per_chunk=args.e2e_rows, n_compute=args.e2e_streams,
+                               nbuf=args.e2e_bufs, device=dev, chain_calls=True)
+    ms, d2h = measure(chained)
+    desc = (f"{len(chained.chunks)} row chunk(s) of {chained.rows} rows, {chained.nbuf} device buffer sets")
+    del chained
+    plain = HostScanPipeline(b, L, D, N, rows_per_chunk=1, n_compute=2, nbuf=3, device=dev)
+    ms_plain, _ = measure(plain)
+    del plain
+    return {"value": gbs(ms), "unit": "GB/s", "ms_per_step": round(ms, 3), "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
             "api": "swiftx_b200.host_pipeline.HostScanPipeline.forward_backward (C ABI kernels) on pinned "
-                   f"host tensors; {len(pipe.chunks)} row chunks, H2D / kernels / D2H overlapped on "
-                   f"{2 + pipe.n_compute} streams"}
+                   f"host tensors; {desc}; consecutive steps chained (the next step's inputs stream in under "
+                   "the previous step's kernels and copies out)",
+            "unchained": {"value": gbs(ms_plain), "ms_per_step": round(ms_plain, 3),
+                          "api": "same call, each step queued behind the current stream; 8 one-row chunks "
+                                 "whose copies and kernels overlap within the step"}}
 
 
 # ----------------------------------------------------------------- CPU oracle (reference arm / baseline)
@@ -634,9 +654,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="lm_train: run the step eagerly, no CUDA graphs")
-    ap.add_argument("--e2e-rows", type=int, default=1, help="scan e2e: batch rows per pipelined chunk")
+    ap.add_argument("--e2e-rows", type=int, default=8, help="scan e2e: batch rows per pipelined chunk")
     ap.add_argument("--ls-batch", type=int, default=8, help="linear_scan: batch rows (8 = the measured size)")
-    ap.add_argument("--e2e-streams", type=int, default=2, help="scan e2e: compute streams of the pipeline")
+    ap.add_argument("--e2e-streams", type=int, default=1, help="scan e2e: compute streams of the pipeline")
+    ap.add_argument("--e2e-bufs", type=int, default=2, help="scan e2e: device buffer sets of the pipeline")
     ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode", "linear_scan"], default="scan",
                     help="scan: fused scan fwd+bwd at b=8 L=2048 D=512 N=16 (default); lm_train: Sift LM training step; "
                          "long_scan: b=4 L=65536 D=2048 forward; decode: batch-256 24-layer recurrent step; "

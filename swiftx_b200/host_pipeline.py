@@ -7,6 +7,9 @@ into chunks, and every chunk goes
 
     H2D (copy stream) -> forward + backward kernels (compute stream) -> D2H (copy stream)
 
+(the forward starts once u, delta, z, B, C are in, while dout is still on its way, and
+the output's copy out starts as soon as the forward ends)
+
 over ``nbuf`` rotating sets of device buffers, so that the copy of chunk k+1 in, the
 kernels of chunk k and the copy of chunk k-1 out run at the same time.  PCIe is full
 duplex and the two copy directions use separate copy engines, so a step costs about
@@ -37,11 +40,19 @@ class HostScanPipeline:
 
     batch, seqlen, dim, dstate: the (b, L, D, N) of every call; dtype: float32 or
     bfloat16 for u, delta, z, B, C, dout and the row gradients; has_z / has_D /
-    has_bias: which optional operands the calls pass."""
+    has_bias: which optional operands the calls pass.
+
+    chain_calls: when False (default) every call is queued behind the current stream,
+    as a torch copy would be.  When True, a call's copies in wait only for this
+    pipeline's own earlier work, so the next call's inputs stream in while the previous
+    call's last kernels and copies out finish (a loader feeding one batch after the
+    other); the host inputs must then be ready when the call is made, not produced by
+    work still queued on the current stream.  Either way the current stream waits for
+    the call's results."""
 
     def __init__(self, batch, seqlen, dim, dstate, *, dtype=torch.float32, has_z=True, has_D=True,
                  has_bias=True, delta_softplus=True, rows_per_chunk=None, nbuf=3, n_compute=2,
-                 device=None):
+                 device=None, chain_calls=False):
         if dtype not in _FLOAT_IN:
             raise ValueError(f"dtype must be float32 or bfloat16, got {dtype}")
         if not 1 <= dstate <= 16:
@@ -58,7 +69,8 @@ class HostScanPipeline:
         self.softplus = bool(delta_softplus)
         self.rows = rows_per_chunk or max(1, -(-batch // 8))
         self.chunks = [(r, min(batch, r + self.rows)) for r in range(0, batch, self.rows)]
-        self.nbuf = max(1, min(nbuf, len(self.chunks)))
+        # buffer sets beyond the chunk count only help when calls overlap one another
+        self.nbuf = max(1, nbuf if chain_calls else min(nbuf, len(self.chunks)))
         self.n_compute = max(1, min(n_compute, self.nbuf))
         R, L, D, N, dev = self.rows, seqlen, dim, dstate, self.dev
         e = lambda *s, dt=dtype: torch.empty(s, device=dev, dtype=dt)  # noqa: E731
@@ -74,23 +86,36 @@ class HostScanPipeline:
             s["ws"] = e(max(self.ws_bytes, 1), dt=torch.uint8)
             self.sets.append(s)
         nc = len(self.chunks)
-        self.dA_part = e(nc, D, N, dt=torch.float32)
-        self.dD_part = e(nc, D, dt=torch.float32) if has_D else None
-        self.dbias_part = e(nc, D, dt=torch.float32) if has_bias else None
-        self.dA = e(D, N, dt=torch.float32)
-        self.dD = e(D, dt=torch.float32) if has_D else None
-        self.dbias = e(D, dt=torch.float32) if has_bias else None
-        self.A = e(D, N, dt=torch.float32)
-        self.Dv = e(D, dt=torch.float32) if has_D else None
-        self.bias = e(D, dt=torch.float32) if has_bias else None
+        # Per-call state that a chained call may still be using while the next one starts
+        # (parameters, per-chunk partials of the batch sums, the sums themselves): two
+        # copies, alternated by call parity.
+        self.par = []
+        for _ in range(2):
+            self.par.append({
+                "A": e(D, N, dt=torch.float32),
+                "Dv": e(D, dt=torch.float32) if has_D else None,
+                "bias": e(D, dt=torch.float32) if has_bias else None,
+                "dA_part": e(nc, D, N, dt=torch.float32),
+                "dD_part": e(nc, D, dt=torch.float32) if has_D else None,
+                "dbias_part": e(nc, D, dt=torch.float32) if has_bias else None,
+                "dA": e(D, N, dt=torch.float32),
+                "dD": e(D, dt=torch.float32) if has_D else None,
+                "dbias": e(D, dt=torch.float32) if has_bias else None,
+                "ev_params": torch.cuda.Event(),   # parameters on the device
+                "ev_done": None,                   # the call's last copy out finished
+            })
+        self.calls = 0
+        self.turn = 0                              # chunks issued so far, over all calls
+        self.chain_calls = bool(chain_calls)
         self.h2d = torch.cuda.Stream(dev)
         self.d2h = torch.cuda.Stream(dev)
         self.comp = [torch.cuda.Stream(dev) for _ in range(self.n_compute)]
-        self.ev_in = [torch.cuda.Event() for _ in range(nc)]      # chunk's inputs on the device
-        self.ev_fwd = [torch.cuda.Event() for _ in range(nc)]     # chunk's forward done
-        self.ev_comp = [torch.cuda.Event() for _ in range(nc)]    # chunk's kernels done
-        self.ev_out = [torch.cuda.Event() for _ in range(nc)]     # chunk's results on the host
-        self.ev_params = torch.cuda.Event()
+        # per buffer set, re-recorded at every use (a wait sees the latest record)
+        self.ev_in_free = [None] * self.nbuf      # set's inputs no longer read (kernels done)
+        self.ev_out_free = [None] * self.nbuf     # set's results copied out
+        self.ev_in_fwd = [torch.cuda.Event() for _ in range(self.nbuf)]   # forward inputs in
+        self.ev_in = [torch.cuda.Event() for _ in range(self.nbuf)]       # all inputs in
+        self.ev_fwd = [torch.cuda.Event() for _ in range(self.nbuf)]      # forward done
 
     # ------------------------------------------------------------------ host buffers
     def allocate_host_outputs(self):
@@ -116,8 +141,9 @@ class HostScanPipeline:
             raise ValueError(f"{name}: expected contiguous {dtype} {shape}, got {t.dtype} {tuple(t.shape)}")
 
     # ------------------------------------------------------------------ one step
-    def _args(self, s, rows, fwd):
-        """swx_scan_args over the device buffers of set `s` for a chunk of `rows` rows."""
+    def _args(self, s, pr, rows, fwd):
+        """swx_scan_args over the device buffers of set `s` (parameters from `pr`) for a
+        chunk of `rows` rows."""
         a = _lib.ScanArgs()
         a.batch, a.seqlen, a.dim, a.dstate = rows, self.L, self.D, self.N
         a.in_dtype = a.out_dtype = _lib.DTYPE_CODES[self.dtype]
@@ -130,9 +156,9 @@ class HostScanPipeline:
             a.out_pre = s["pre"].data_ptr()
         a.B, a.B_sb, a.B_sl = s["B"].data_ptr(), L * N, N
         a.C, a.C_sb, a.C_sl = s["C"].data_ptr(), L * N, N
-        a.A = self.A.data_ptr()
-        a.Dskip = self.Dv.data_ptr() if self.has_D else None
-        a.delta_bias = self.bias.data_ptr() if self.has_bias else None
+        a.A = pr["A"].data_ptr()
+        a.Dskip = pr["Dv"].data_ptr() if self.has_D else None
+        a.delta_bias = pr["bias"].data_ptr() if self.has_bias else None
         a.checkpoints = s["ck"].data_ptr()
         if fwd:
             a.out = s["out"].data_ptr()
@@ -170,71 +196,82 @@ class HostScanPipeline:
         res = out if out is not None else self.allocate_host_outputs()
         host_in = {"u": u, "delta": delta, "z": z, "B": B, "C": C, "dout": dout}
         lib, main = self.lib, torch.cuda.current_stream(self.dev)
+        pr = self.par[self.calls % 2]
+        self.calls += 1
 
-        self.h2d.wait_stream(main)
-        self.d2h.wait_stream(main)
-        for cs in self.comp:
-            cs.wait_stream(main)
+        if not self.chain_calls:
+            self.h2d.wait_stream(main)
+            self.d2h.wait_stream(main)
+            for cs in self.comp:
+                cs.wait_stream(main)
         with torch.cuda.stream(self.h2d):
-            self.A.copy_(A, non_blocking=True)
+            if pr["ev_done"] is not None:                 # the call two back is finished with pr
+                self.h2d.wait_event(pr["ev_done"])
+            pr["A"].copy_(A, non_blocking=True)
             if self.has_D:
-                self.Dv.copy_(D, non_blocking=True)
+                pr["Dv"].copy_(D, non_blocking=True)
             if self.has_bias:
-                self.bias.copy_(delta_bias, non_blocking=True)
-            self.ev_params.record(self.h2d)
+                pr["bias"].copy_(delta_bias, non_blocking=True)
+            pr["ev_params"].record(self.h2d)
         for cs in self.comp:
-            cs.wait_event(self.ev_params)
+            cs.wait_event(pr["ev_params"])
 
         for k, (r0, r1) in enumerate(self.chunks):
             n = r1 - r0
-            s = self.sets[k % self.nbuf]
-            cs = self.comp[k % self.n_compute]
+            si = self.turn % self.nbuf
+            s = self.sets[si]
+            cs = self.comp[self.turn % self.n_compute]
+            self.turn += 1
             with torch.cuda.stream(self.h2d):
-                if k >= self.nbuf:
-                    self.h2d.wait_event(self.ev_comp[k - self.nbuf])     # set's inputs no longer read
+                if self.ev_in_free[si] is not None:
+                    self.h2d.wait_event(self.ev_in_free[si])     # set's inputs no longer read
                 for name in _INPUTS:
+                    if name == "dout":                 # the forward need not wait for it
+                        self.ev_in_fwd[si].record(self.h2d)
                     if name in s:
                         s[name][:n].copy_(host_in[name][r0:r1], non_blocking=True)
-                self.ev_in[k].record(self.h2d)
-            cs.wait_event(self.ev_in[k])
-            if k >= self.nbuf:
-                cs.wait_event(self.ev_out[k - self.nbuf])                # set's results copied out
+                self.ev_in[si].record(self.h2d)
+            cs.wait_event(self.ev_in_fwd[si])
+            if self.ev_out_free[si] is not None:
+                cs.wait_event(self.ev_out_free[si])              # set's results copied out
             sp = _lib.vp(cs.cuda_stream)
-            _lib.check(lib.swx_scan_fwd(self._args(s, n, True), sp), "swx_scan_fwd")
-            self.ev_fwd[k].record(cs)
+            _lib.check(lib.swx_scan_fwd(self._args(s, pr, n, True), sp), "swx_scan_fwd")
+            self.ev_fwd[si].record(cs)
             with torch.cuda.stream(self.d2h):          # the output leaves while the backward runs
-                self.d2h.wait_event(self.ev_fwd[k])
+                self.d2h.wait_event(self.ev_fwd[si])
                 res["out"][r0:r1].copy_(s["out"][:n], non_blocking=True)
-            a = self._args(s, n, False)
-            a.dA = self.dA_part[k].data_ptr()
-            a.dD = self.dD_part[k].data_ptr() if self.has_D else None
-            a.ddelta_bias = self.dbias_part[k].data_ptr() if self.has_bias else None
+            cs.wait_event(self.ev_in[si])
+            a = self._args(s, pr, n, False)
+            a.dA = pr["dA_part"][k].data_ptr()
+            a.dD = pr["dD_part"][k].data_ptr() if self.has_D else None
+            a.ddelta_bias = pr["dbias_part"][k].data_ptr() if self.has_bias else None
             _lib.check(lib.swx_scan_bwd(a, sp), "swx_scan_bwd")
-            self.ev_comp[k].record(cs)
+            self.ev_in_free[si] = cs.record_event()
             with torch.cuda.stream(self.d2h):
-                self.d2h.wait_event(self.ev_comp[k])
+                self.d2h.wait_event(self.ev_in_free[si])
                 for name in _ROW_GRADS:
                     if name in s:
                         res[name][r0:r1].copy_(s[name][:n], non_blocking=True)
-                self.ev_out[k].record(self.d2h)
+                self.ev_out_free[si] = self.d2h.record_event()
 
         # batch-summed gradients: chunk partials added in chunk order, then one copy out
         c0 = self.comp[0]
         for cs in self.comp[1:]:
             c0.wait_stream(cs)
         with torch.cuda.stream(c0):
-            torch.sum(self.dA_part, 0, out=self.dA)
+            torch.sum(pr["dA_part"], 0, out=pr["dA"])
             if self.has_D:
-                torch.sum(self.dD_part, 0, out=self.dD)
+                torch.sum(pr["dD_part"], 0, out=pr["dD"])
             if self.has_bias:
-                torch.sum(self.dbias_part, 0, out=self.dbias)
+                torch.sum(pr["dbias_part"], 0, out=pr["dbias"])
         with torch.cuda.stream(self.d2h):
             self.d2h.wait_stream(c0)
-            res["dA"].copy_(self.dA, non_blocking=True)
+            res["dA"].copy_(pr["dA"], non_blocking=True)
             if self.has_D:
-                res["dD"].copy_(self.dD, non_blocking=True)
+                res["dD"].copy_(pr["dD"], non_blocking=True)
             if self.has_bias:
-                res["ddelta_bias"].copy_(self.dbias, non_blocking=True)
+                res["ddelta_bias"].copy_(pr["dbias"], non_blocking=True)
+            pr["ev_done"] = self.d2h.record_event()
         main.wait_stream(self.d2h)
         main.wait_stream(self.h2d)
         return res

@@ -117,3 +117,28 @@ def test_pipeline_rejects_bad_arguments():
         pipe.forward_backward(host["u"][:, :20], *args[1:], **kw)
     with pytest.raises(ValueError, match="required"):
         pipe.forward_backward(*args, D=host["D"], z=None, delta_bias=host["delta_bias"])
+
+
+@pytest.mark.parametrize("rows,nbuf,n_compute", [(1, 3, 2), (2, 2, 2), (1, 4, 3)])
+def test_chained_calls_overlap_without_mixing_batches(rows, nbuf, n_compute):
+    # Four calls queued back to back (no host sync) on two different problems -- other
+    # inputs, other A / D / delta_bias -- so that the next call's copies in run while the
+    # previous call's kernels and copies out finish; each result set must be its own
+    # problem's whole-batch result.
+    b, L, Dm, N = 5, 150, 64, 16
+    inps = [config_inputs(b, L, Dm, N, seed=41 + i, device=DEV) for i in range(2)]
+    refs = [_device_reference(x, True, True, True) for x in inps]
+    hosts = [{k: v.cpu().pin_memory() for k, v in x.items()} for x in inps]
+    pipe = HostScanPipeline(b, L, Dm, N, rows_per_chunk=rows, nbuf=nbuf, n_compute=n_compute, chain_calls=True)
+    results = []
+    for i in range(4):
+        h = hosts[i % 2]
+        res = pipe.allocate_host_outputs()
+        for t in res.values():
+            t.fill_(float("nan"))
+        pipe.forward_backward(h["u"], h["delta"], h["A"], h["B"], h["C"], h["dout"], D=h["D"], z=h["z"],
+                              delta_bias=h["delta_bias"], out=res)
+        results.append(res)
+    torch.cuda.synchronize()
+    for i, res in enumerate(results):
+        _compare(res, refs[i % 2])
