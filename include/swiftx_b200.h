@@ -15,7 +15,7 @@
  *   B, C, dB, dC                           : (b, L, N)   innermost stride 1
  *   A, dA : (D, N) dense;  Dskip, delta_bias, dD, ddelta_bias : (D,)
  *   h0, h_last, dh0 : (b, D, N) dense fp32
- * Strides are in elements.  N <= 16.
+ * Strides are in elements.  N <= 16, b <= 65535.
  */
 #ifndef SWIFTX_B200_H
 #define SWIFTX_B200_H
@@ -143,7 +143,8 @@ int swx_scan_bwd_static_scratch(const swx_scan_args* args, void* stream);
 /* Causal depthwise conv1d (+ SiLU).  x: (b, L, D) with element strides (x_sb, x_sl) and
  * unit channel stride (e.g. the x half of the in_proj output, row stride 2D);
  * weight (D, width) dense fp32 (= nn.Conv1d weight (D, 1, width)); bias (D,) optional;
- * out, dout-sized gradients (b, L, D) dense, same dtype as x.  width <= 6. */
+ * out, dout-sized gradients (b, L, D) dense, same dtype as x.  width <= 6,
+ * b <= 65535, L <= 65535 * 16. */
 typedef struct swx_conv_args {
     int64_t batch, seqlen, dim, width;
     int32_t dtype;           /* SWX_DTYPE_F32 | SWX_DTYPE_BF16 for x, out, dout, dx */

@@ -44,7 +44,8 @@ int check_common(const swx_scan_args* a) {
     if (!a) return SWX_ERR_INVALID_ARG;
     if (a->batch < 0 || a->seqlen < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
     if (a->dstate < 1 || a->dstate > swx::NS) return SWX_ERR_UNSUPPORTED;
-    if (a->batch > INT32_MAX || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
+    // batch rows index the grid's y dimension (at most 65535)
+    if (a->batch > 65535 || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
     if (elem_size(a->in_dtype) == 0) return SWX_ERR_UNSUPPORTED;
     if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
     if (!a->u || !a->delta || !a->B || !a->C || !a->A) return SWX_ERR_INVALID_ARG;

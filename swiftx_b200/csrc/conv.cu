@@ -311,7 +311,9 @@ int conv_check(const swx_conv_args* a) {
     if (a->batch < 0 || a->seqlen < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
     if (a->width < 1 || a->width > swx::CONV_MAXK) return SWX_ERR_UNSUPPORTED;
     if (conv_es(a->dtype) == 0) return SWX_ERR_UNSUPPORTED;
-    if (a->batch > 65535 || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
+    // batch rows and time tiles index the grid's z and y dimensions (at most 65535 each)
+    if (a->batch > 65535 || (a->seqlen + swx::CONV_TT - 1) / swx::CONV_TT > 65535 || a->dim > INT32_MAX)
+        return SWX_ERR_UNSUPPORTED;
     if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
     if (!a->x || !a->weight) return SWX_ERR_INVALID_ARG;
     return SWX_OK;

@@ -70,8 +70,13 @@ def test_host_side_validation_without_gpu():
     assert lib.swx_scan_bwd(a, None) == _lib.SWX_ERR_INVALID_ARG
     a.seqlen = 0                                              # empty problem: nothing to do
     assert lib.swx_scan_fwd(a, None) == _lib.SWX_OK
+    a.batch, a.seqlen = 65536, 4                              # more rows than the grid's y dimension
+    assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_UNSUPPORTED
+    assert lib.swx_scan_bwd(a, None) == _lib.SWX_ERR_UNSUPPORTED
     c = _lib.ConvArgs()
     c.batch, c.seqlen, c.dim, c.width = 1, 4, 4, 9            # width > 6
+    assert lib.swx_conv1d_fwd(c, None) == _lib.SWX_ERR_UNSUPPORTED
+    c.width, c.seqlen = 4, 65535 * 16 + 1                     # more time tiles than the grid's y dimension
     assert lib.swx_conv1d_fwd(c, None) == _lib.SWX_ERR_UNSUPPORTED
     d = _lib.DecodeArgs()
     d.batch, d.dim, d.mode = 1, 4, 0                          # no mode
