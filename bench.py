@@ -414,21 +414,14 @@ def run_lm_train(args, world, rank, local):
     flat fp32 buffer that is all-reduced (NCCL, average) once per step.  The forward +
     backward and the clip + AdamW update are each replayed as a CUDA graph (the step is
     otherwise bound by kernel-launch overhead); --no-graph runs them eagerly."""
-    import torch.distributed as dist
-
+    from swiftx_b200.data_parallel import FlatGradients, broadcast_parameters
     from swiftx_b200.sift import SiftConfig, SiftLM
     dev = torch.device("cuda", local)
     torch.manual_seed(0)
     model = SiftLM(SiftConfig(vocab_size=256, d_model=256, n_layers=8, d_state=16, d_conv=4, expand=2)).to(dev)
     params = list(model.parameters())
-    if world > 1:                                   # identical start on every rank
-        for p in params:
-            dist.broadcast(p.data, src=0)
-    flat = torch.zeros(sum(p.numel() for p in params), device=dev, dtype=torch.float32)
-    off = 0
-    for p in params:
-        p.grad = flat[off:off + p.numel()].view_as(p)
-        off += p.numel()
+    broadcast_parameters(params)                    # identical start on every rank
+    grads = FlatGradients(params)
     decay = [p for p in params if p.dim() >= 2 and not getattr(p, "_no_weight_decay", False)]
     ids = {id(p) for p in decay}
     no_decay = [p for p in params if id(p) not in ids]
@@ -441,7 +434,7 @@ def run_lm_train(args, world, rank, local):
     tok = host.to(dev)
 
     def fwd_bwd():
-        flat.zero_()
+        grads.zero_()
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
             _, loss = model(tok[:, :-1], tok[:, 1:])
         loss.backward()
@@ -452,8 +445,7 @@ def run_lm_train(args, world, rank, local):
         opt.step()
 
     def allreduce():
-        if world > 1:
-            dist.all_reduce(flat, op=dist.ReduceOp.AVG)
+        grads.all_reduce_()
 
     if graphed:
         side = torch.cuda.Stream()

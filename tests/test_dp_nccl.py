@@ -22,28 +22,21 @@ def _batch(world):
     return torch.randint(0, 11, (world * ROWS_PER_RANK, SEQ + 1), generator=g)
 
 
-def _train(tok, dev, allreduce=None):
+def _train(tok, dev):
+    from swiftx_b200.data_parallel import FlatGradients, broadcast_parameters
     from swiftx_b200.sift import SiftConfig, SiftLM
     torch.manual_seed(0)
     m = SiftLM(SiftConfig(vocab_size=11, d_model=32, n_layers=2, d_state=8)).to(dev)
     params = list(m.parameters())
-    if allreduce is not None:
-        import torch.distributed as dist
-        for p in params:
-            dist.broadcast(p.data, src=0)
-    flat = torch.zeros(sum(p.numel() for p in params), device=dev)
-    off = 0
-    for p in params:
-        p.grad = flat[off:off + p.numel()].view_as(p)
-        off += p.numel()
+    broadcast_parameters(params)
+    grads = FlatGradients(params)
     opt = torch.optim.SGD(params, lr=0.1)
     tok = tok.to(dev)
     for _ in range(STEPS):
-        flat.zero_()
+        grads.zero_()
         _, loss = m(tok[:, :-1], tok[:, 1:])
         loss.backward()
-        if allreduce is not None:
-            allreduce(flat)
+        grads.all_reduce_()
         torch.nn.utils.clip_grad_norm_(params, 1.0)
         opt.step()
     torch.cuda.synchronize()
@@ -61,8 +54,7 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         tok = _batch(world)[rank * ROWS_PER_RANK:(rank + 1) * ROWS_PER_RANK]
-        out = _train(tok, torch.device("cuda", rank),
-                     allreduce=lambda t: dist.all_reduce(t, op=dist.ReduceOp.AVG))
+        out = _train(tok, torch.device("cuda", rank))
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
