@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 8
+#define SWX_ABI_VERSION 9
 
 /* status codes */
 #define SWX_OK 0
@@ -229,13 +229,23 @@ int swx_linear_scan_bwd(const swx_linear_scan_args* args, void* stream);
  * bf16: a bf16 y is the fp32 result rounded once, as a cast after the norm would give);
  * weight, dweight: (dim,) fp32;
  * rstd: (rows,) fp32, written by the forward when given and read by the backward.
- * dim <= 1024.  The weight gradient is a fixed-order sum (deterministic). */
+ * dim <= 1024.  The weight gradient is a fixed-order sum (deterministic).
+ *
+ * Residual form (the pre-norm residual stream, x_{i+1} = x_i + mixer_i(...), fused with
+ * the next norm; models/sift_model.py:58):
+ *   forward, residual given: s = x + residual (fp32 arithmetic, residual in res_dtype) is
+ *     written to sum (dtype) and y = norm(s);
+ *   backward: pass the saved s as x; dsum (rows, dim) fp32, optional, is the gradient of s
+ *     from its other consumers and is added to dx; dres, optional, receives dx again in
+ *     res_dtype (the gradient of the residual input).
+ * With fp32 x both directions give bit-identical values to the separate add, norm,
+ * gradient sum and cast (with bf16 x the gradient sum is rounded once instead of twice). */
 typedef struct swx_rmsnorm_args {
     int64_t rows, dim;
     float eps;
-    int32_t dtype;                    /* x, dx: SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
+    int32_t dtype;                    /* x, dx, sum: SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
     int32_t out_dtype;                /* y, dy: SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
-    int32_t reserved;
+    int32_t res_dtype;                /* residual, dres: SWX_DTYPE_F32 or SWX_DTYPE_BF16 */
     const void* x;
     const float* weight;
     void* y;
@@ -244,6 +254,10 @@ typedef struct swx_rmsnorm_args {
     void* dx;
     float* dweight;
     void* workspace; int64_t workspace_bytes;
+    const void* residual;             /* forward, residual form */
+    void* sum;
+    const float* dsum;                /* backward, residual form */
+    void* dres;
 } swx_rmsnorm_args;
 
 int64_t swx_rmsnorm_args_size(void);

@@ -90,8 +90,8 @@ class RMSNormArgs(ctypes.Structure):
     """Mirror of ``swx_rmsnorm_args``."""
     _fields_ = [
         ("rows", i64), ("dim", i64), ("eps", ctypes.c_float), ("dtype", i32), ("out_dtype", i32),
-        ("reserved", i32), ("x", vp), ("weight", vp), ("y", vp), ("rstd", vp), ("dy", vp), ("dx", vp), ("dweight", vp),
-        ("workspace", vp), ("workspace_bytes", i64),
+        ("res_dtype", i32), ("x", vp), ("weight", vp), ("y", vp), ("rstd", vp), ("dy", vp), ("dx", vp), ("dweight", vp),
+        ("workspace", vp), ("workspace_bytes", i64), ("residual", vp), ("sum", vp), ("dsum", vp), ("dres", vp),
     ]
 
 

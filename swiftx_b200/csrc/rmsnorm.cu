@@ -4,11 +4,16 @@
 // backward per use; here it is one launch each way (plus a fixed-order sum of the weight
 // gradient), which matters in a training step of many small launches.
 //
-// Forward: one warp per row; lanes stride the columns (coalesced 128-byte accesses), the
-// sum of squares is a warp reduction; the per-row rsqrt is saved for the backward.
+// Forward: one warp per row held in registers; lanes stride the columns (coalesced
+// 128-byte accesses), the sum of squares is a warp reduction; the per-row rsqrt is saved
+// for the backward.
 // Backward (x^ = x r, g = w dy):  dx = r (g - x^ mean(x^ g)),  dw = sum_rows dy x^.
 // A fixed grid of warps walks the rows in a fixed assignment, accumulating dw per lane in
 // registers; per-warp partials are then summed in warp order (deterministic).
+// Residual form (x_{i+1} = x_i + h_i feeding the next norm): the forward adds the residual
+// input first and writes the sum; the backward adds the sum's other incoming gradient to
+// dx and writes it a second time in the residual input's type -- the separate add, its
+// backward and the gradient cast folded into the norm's two launches.
 #include "common.cuh"
 
 #include <algorithm>
@@ -16,7 +21,7 @@
 namespace swx {
 
 constexpr int NORM_WARPS = 8;                 // warps per CTA
-constexpr int NORM_MAXC = 32;                 // columns per lane in the backward: d <= 1024
+constexpr int NORM_MAXC = 32;                 // columns per lane (the row in registers): d <= 1024
 constexpr int NORM_BWD_WARPS = 148 * 2 * NORM_WARPS;   // fixed backward grid (warps)
 
 struct NormDev {
@@ -24,7 +29,19 @@ struct NormDev {
     float eps;
     const void* x; const float* w; void* y; float* rstd;
     const void* dy; void* dx; float* dw_part; float* dw;
+    const void* res; void* sum;        // residual form, forward: s = x + res -> sum
+    const float* dsum; void* dres;     // residual form, backward: dx += dsum; dres = dx
+    int res_bf16;                      // res / dres element type
 };
+
+__device__ __forceinline__ float load_res(const void* base, int64_t i, int bf16) {
+    return bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(base)[i]) : static_cast<const float*>(base)[i];
+}
+
+__device__ __forceinline__ void store_res(void* base, int64_t i, float v, int bf16) {
+    if (bf16) static_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(v);
+    else static_cast<float*>(base)[i] = v;
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -32,20 +49,42 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
-template <typename T, typename TY>
+// The row stays in registers (NC columns per lane), so x (and the residual) are read once.
+template <typename T, typename TY, int NC>
 __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_fwd_kernel(const NormDev p) {
     const int row = blockIdx.x * NORM_WARPS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (row >= p.rows) return;
-    const T* x = static_cast<const T*>(p.x) + (int64_t)row * p.d;
-    TY* y = static_cast<TY*>(p.y) + (int64_t)row * p.d;
+    const int64_t o = (int64_t)row * p.d;
+    const T* x = static_cast<const T*>(p.x) + o;
+    TY* y = static_cast<TY*>(p.y) + o;
+    float v[NC];
     float ss = 0.f;
-    for (int c = lane; c < p.d; c += 32) {
-        const float v = Elem<T>::to_f(x[c]);
-        ss = fmaf(v, v, ss);
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int c = lane + 32 * k;
+        v[k] = 0.f;
+        if (c < p.d) {
+            v[k] = Elem<T>::to_f(x[c]);
+            // residual form: normalise s = x + res (rounded to T, as a stored sum would be)
+            if (p.res) v[k] = Elem<T>::to_f(Elem<T>::from_f(v[k] + load_res(p.res, o + c, p.res_bf16)));
+        }
+        ss = fmaf(v[k], v[k], ss);
+    }
+    if (p.res) {
+        T* sum = static_cast<T*>(p.sum) + o;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const int c = lane + 32 * k;
+            if (c < p.d) sum[c] = Elem<T>::from_f(v[k]);
+        }
     }
     const float r = rsqrtf(warp_sum(ss) / p.d + p.eps);
     if (lane == 0 && p.rstd) p.rstd[row] = r;
-    for (int c = lane; c < p.d; c += 32) y[c] = Elem<TY>::from_f((Elem<T>::to_f(x[c]) * r) * p.w[c]);
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        const int c = lane + 32 * k;
+        if (c < p.d) y[c] = Elem<TY>::from_f((v[k] * r) * p.w[c]);
+    }
 }
 
 template <typename T, typename TY, int NC>
@@ -63,7 +102,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const Norm
         const TY* dy = static_cast<const TY*>(p.dy) + (int64_t)row * p.d;
         T* dx = static_cast<T*>(p.dx) + (int64_t)row * p.d;
         const float r = p.rstd[row];
-        float xh[NC], g[NC], dyv[NC];
+        float xh[NC], g[NC], dyv[NC], dsv[NC];
         float s = 0.f;
 #pragma unroll
         for (int k = 0; k < NC; ++k) {
@@ -71,6 +110,7 @@ __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const Norm
             const bool ok = c < p.d;
             xh[k] = ok ? Elem<T>::to_f(x[c]) * r : 0.f;
             dyv[k] = ok ? Elem<TY>::to_f(dy[c]) : 0.f;
+            dsv[k] = (ok && p.dsum) ? p.dsum[(int64_t)row * p.d + c] : 0.f;     // loaded with x, dy
             g[k] = wv[k] * dyv[k];
             s = fmaf(xh[k], g[k], s);
         }
@@ -78,7 +118,14 @@ __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const Norm
 #pragma unroll
         for (int k = 0; k < NC; ++k) {
             const int c = lane + 32 * k;
-            if (c < p.d) dx[c] = Elem<T>::from_f(r * (g[k] - xh[k] * m));
+            if (c < p.d) {
+                float v = r * (g[k] - xh[k] * m);
+                // an explicit add (never contracted into an FMA with the product above), so
+                // dx is the separately rounded norm gradient plus dsum, as an unfused add gives
+                if (p.dsum) v = __fadd_rn(v, dsv[k]);
+                dx[c] = Elem<T>::from_f(v);
+                if (p.dres) store_res(p.dres, (int64_t)row * p.d + c, v, p.res_bf16);
+            }
             dwacc[k] = fmaf(dyv[k], xh[k], dwacc[k]);
         }
     }
@@ -117,10 +164,18 @@ static void launch_bwd(const NormDev& p, cudaStream_t st) {
     rmsnorm_dw_kernel<<<(p.d + 31) / 32, 1024, 0, st>>>(p);
 }
 
+template <typename T, typename TY>
+static void launch_fwd(const NormDev& p, unsigned grid, cudaStream_t st) {
+    const int nc = (p.d + 31) / 32;
+    if (nc <= 8) rmsnorm_fwd_kernel<T, TY, 8><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    else if (nc <= 16) rmsnorm_fwd_kernel<T, TY, 16><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    else rmsnorm_fwd_kernel<T, TY, NORM_MAXC><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+}
+
 template <typename T>
 static void launch_fwd_x(const NormDev& p, int out_dtype, unsigned grid, cudaStream_t st) {
-    if (out_dtype == SWX_DTYPE_F32) rmsnorm_fwd_kernel<T, float><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
-    else rmsnorm_fwd_kernel<T, __nv_bfloat16><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
+    if (out_dtype == SWX_DTYPE_F32) launch_fwd<T, float>(p, grid, st);
+    else launch_fwd<T, __nv_bfloat16>(p, grid, st);
 }
 
 template <typename T>
@@ -138,9 +193,12 @@ int norm_check(const swx_rmsnorm_args* a, bool bwd) {
     if (a->dtype != SWX_DTYPE_F32 && a->dtype != SWX_DTYPE_BF16) return SWX_ERR_UNSUPPORTED;
     if (a->out_dtype != SWX_DTYPE_F32 && a->out_dtype != SWX_DTYPE_BF16) return SWX_ERR_UNSUPPORTED;
     if (a->rows > INT32_MAX || a->dim > 32 * swx::NORM_MAXC) return SWX_ERR_UNSUPPORTED;
+    const bool res_form = bwd ? a->dres != nullptr : a->residual != nullptr;
+    if (res_form && a->res_dtype != SWX_DTYPE_F32 && a->res_dtype != SWX_DTYPE_BF16) return SWX_ERR_UNSUPPORTED;
     if (a->rows * a->dim == 0) return SWX_OK;
     if (!a->x || !a->weight) return SWX_ERR_INVALID_ARG;
     if (!bwd && !a->y) return SWX_ERR_INVALID_ARG;
+    if (!bwd && a->residual && !a->sum) return SWX_ERR_INVALID_ARG;
     if (bwd && (!a->dy || !a->dx || !a->dweight || !a->rstd || !a->workspace)) return SWX_ERR_INVALID_ARG;
     return SWX_OK;
 }
@@ -150,6 +208,8 @@ swx::NormDev norm_pack(const swx_rmsnorm_args* a) {
     p.rows = (int)a->rows; p.d = (int)a->dim; p.eps = a->eps;
     p.x = a->x; p.w = a->weight; p.y = a->y; p.rstd = a->rstd;
     p.dy = a->dy; p.dx = a->dx; p.dw_part = static_cast<float*>(a->workspace); p.dw = a->dweight;
+    p.res = a->residual; p.sum = a->sum; p.dsum = a->dsum; p.dres = a->dres;
+    p.res_bf16 = a->res_dtype == SWX_DTYPE_BF16 ? 1 : 0;
     return p;
 }
 }  // namespace

@@ -12,8 +12,8 @@ runs on the sm_100a kernels:
      gate (kernel) -> out_proj (cuBLAS)
 
 and decode runs the conv-window / state-update kernels around the x_proj / dt_proj GEMVs.
-RMSNorm runs on its fused kernels and, in training, the token embedding's weight
-gradient on the sort-free swx_embedding_bwd.
+RMSNorm runs on its fused kernels, each residual add folded into the next norm, and,
+in training, the token embedding's weight gradient on the sort-free swx_embedding_bwd.
 Fusing the gate is exactly the reference's y * silu(z) when no SiftX pathway mixing is
 configured (models/sift_block.py:132-142).  With pathway_gate (SiftX), the per-token
 group weights sit between the scan and the gate, so the scan kernel runs without z
@@ -158,11 +158,26 @@ class RMSNorm(nn.Module):
         that autocast would cast it to bf16 anyway, and the kernel rounds the same fp32
         value once, so the cast (and its backward) is folded into the kernel."""
         if norm_kernels.supported(x):
-            out_dtype = None
-            if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
-                out_dtype = torch.bfloat16
-            return norm_kernels.rms_norm(x, self.weight, self.eps, out_dtype)
+            return norm_kernels.rms_norm(x, self.weight, self.eps, _norm_out_dtype())
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.eps) * self.weight
+
+    def forward_residual(self, x, res):
+        """(x + res, self(x + res)): the residual stream's add and this norm, on one fused
+        kernel each way when the sum keeps x's dtype (fp32 residual stream), else the
+        plain add and forward."""
+        if norm_kernels.supported(x) and res.dtype in (torch.float32, torch.bfloat16) \
+                and torch.promote_types(x.dtype, res.dtype) == x.dtype and res.shape == x.shape:
+            return norm_kernels.add_rms_norm(x, res, self.weight, self.eps, _norm_out_dtype())
+        s = x + res
+        return s, self(s)
+
+
+def _norm_out_dtype():
+    """bf16 under bf16 autocast (the norm's consumers are Linear layers that would cast to
+    bf16 anyway), else the input's dtype."""
+    if torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+        return torch.bfloat16
+    return None
 
 
 @dataclass
@@ -201,6 +216,7 @@ class SiftBackbone(nn.Module):
         super().__init__()
         self.layers = nn.ModuleList([ResidualBlock(cfg) for _ in range(cfg.n_layers)])
         self.norm_f = RMSNorm(cfg.d_model)
+        self.fuse_residual_norm = True
         self._init_weights(cfg.n_layers)
 
     def _init_weights(self, n_layers):
@@ -214,9 +230,17 @@ class SiftBackbone(nn.Module):
                 w /= math.sqrt(n_layers)
 
     def forward(self, x):
-        for layer in self.layers:
-            x = layer(x)
-        return self.norm_f(x)
+        if not self.fuse_residual_norm or not self.layers:
+            for layer in self.layers:
+                x = layer(x)
+            return self.norm_f(x)
+        # x_{i+1} = x_i + mixer_i(norm_i(x_i)), with each add folded into the next norm
+        # (RMSNorm.forward_residual): the same values as the per-layer form above
+        h = self.layers[0].mixer(self.layers[0].norm(x))
+        for layer in self.layers[1:]:
+            x, n = layer.norm.forward_residual(x, h)
+            h = layer.mixer(n)
+        return self.norm_f.forward_residual(x, h)[1]
 
 
 class SiftLM(nn.Module):

@@ -33,7 +33,7 @@ def test_struct_mirrors_match():
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
     assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
     assert lib.swx_embedding_args_size() == ctypes.sizeof(_lib.EmbeddingArgs)
-    assert lib.swx_abi_version() == 8
+    assert lib.swx_abi_version() == 9
 
 
 def test_status_strings():
@@ -95,6 +95,12 @@ def test_host_side_validation_without_gpu():
     r.dim = 256                                               # missing pointers
     assert lib.swx_rmsnorm_fwd(r, None) == _lib.SWX_ERR_INVALID_ARG
     assert lib.swx_rmsnorm_bwd(r, None) == _lib.SWX_ERR_INVALID_ARG
+    r.residual, r.res_dtype = 1, 7                            # residual form: unknown residual dtype
+    assert lib.swx_rmsnorm_fwd(r, None) == _lib.SWX_ERR_UNSUPPORTED
+    r.res_dtype = 1                                           # residual without a sum output
+    r.x, r.weight, r.y = 8, 8, 8
+    assert lib.swx_rmsnorm_fwd(r, None) == _lib.SWX_ERR_INVALID_ARG
+    r.residual = r.x = r.weight = r.y = None
     e = _lib.EmbeddingArgs()
     e.ntok, e.vocab, e.dim = 8, 2000, 32                      # vocab > 1024
     assert lib.swx_embedding_bwd(e, None) == _lib.SWX_ERR_UNSUPPORTED

@@ -71,3 +71,64 @@ def test_bf16_output_is_the_rounded_fp32_result():
     yb.backward(dy)
     yf.backward(dy.float())
     assert torch.equal(x1.grad, x2.grad) and torch.equal(w1.grad, w2.grad)
+
+
+@pytest.mark.parametrize("res_dtype,out_dtype,with_ds", [
+    (torch.bfloat16, torch.bfloat16, True),       # the LM under autocast: bf16 mixer output, bf16 norm output
+    (torch.float32, None, True),
+    (torch.bfloat16, None, False),                # the final norm: nothing else reads the sum
+])
+def test_add_rms_norm_equals_separate_add_and_norm(res_dtype, out_dtype, with_ds):
+    # Residual form against the separate ops on the same kernels: x + res (torch), then
+    # rms_norm; backward through autograd's add (gradient sum, cast to res's dtype).  With
+    # an fp32 residual stream every value must agree bit for bit.
+    from swiftx_b200.norm import add_rms_norm
+    g = torch.Generator().manual_seed(11)
+    shape = (4, 300, 256)
+    x = (torch.randn(shape, generator=g) * 2).to(DEV)
+    res = torch.randn(shape, generator=g).to(DEV).to(res_dtype)
+    w = torch.randn(256, generator=g).to(DEV)
+    dy = torch.randn(shape, generator=g).to(DEV).to(out_dtype or torch.float32)
+    ds = torch.randn(shape, generator=g).to(DEV) if with_ds else None
+
+    def run(fused):
+        xa, ra, wa = x.clone().requires_grad_(), res.clone().requires_grad_(), w.clone().requires_grad_()
+        if fused:
+            s, y = add_rms_norm(xa, ra, wa, 1e-5, out_dtype)
+        else:
+            s = xa + ra
+            y = rms_norm(s, wa, 1e-5, out_dtype)
+        outs, grads = [y], [dy]
+        if with_ds:
+            outs.append(s)
+            grads.append(ds)
+        torch.autograd.backward(outs, grads)
+        return s.detach(), y.detach(), xa.grad, ra.grad, wa.grad
+
+    for a, b, name in zip(run(True), run(False), ("sum", "y", "dx", "dres", "dweight")):
+        assert a.dtype == b.dtype, name
+        assert torch.equal(a, b), name
+
+
+def test_backbone_fused_residual_norm_matches_per_layer_form():
+    # SiftBackbone folds each residual add into the next norm; the per-layer form
+    # (ResidualBlock.forward) must give the same logits and gradients, bit for bit,
+    # under bf16 autocast as in the LM training step.
+    from swiftx_b200.sift import SiftConfig, SiftLM
+    torch.manual_seed(0)
+    m = SiftLM(SiftConfig(vocab_size=64, d_model=128, n_layers=3, d_state=16)).to(DEV)
+    tok = torch.randint(0, 64, (2, 97), device=DEV)
+
+    def run(fuse):
+        m.backbone.fuse_residual_norm = fuse
+        m.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, loss = m(tok[:, :-1], tok[:, 1:])
+        loss.backward()
+        return logits.detach().float(), [p.grad.clone() for p in m.parameters()]
+
+    l1, g1 = run(True)
+    l0, g0 = run(False)
+    assert torch.equal(l1, l0)
+    for a, b in zip(g1, g0):
+        assert torch.equal(a, b)
