@@ -292,9 +292,10 @@ struct BwdSmem {
 };
 
 // Recompute the 16 states of a chunk from its checkpoint (and, without a saved pre-gate
-// output, the partial readouts).  FULL chunks are branch-free so the scheduler can
-// overlap the steps' loads and exponentials with the state chain.
-template <bool FULL, bool YV, typename Tin>
+// output, the partial readouts); bv receives each step's decays (AREG) or its B.  FULL
+// chunks are branch-free so the scheduler can overlap the steps' loads and exponentials
+// with the state chain.
+template <bool FULL, bool YV, bool AREG, typename Tin>
 __device__ __forceinline__ void bwd_recompute(const float2 (*__restrict__ dd)[SCH], const Tin (*__restrict__ Bs)[NS],
                                               const Tin (*__restrict__ Cs)[NS], int nt, int ch, int j,
                                               float2 A01, float2 A23, float2 hck01, float2 hck23,
@@ -306,10 +307,11 @@ __device__ __forceinline__ void bwd_recompute(const float2 (*__restrict__ dd)[SC
         if (FULL || t < nt) {
             const float2 dv = dd[t][ch];
             const float4 b = ld4(&Bs[t][4 * j]);
-            bv[t] = b;
             const float2 dt = bc2(dv.x), du = bc2(dv.y);
-            h01 = fma2(ex2x2(mul2(dt, A01)), h01, mul2(du, f2(b.x, b.y)));
-            h23 = fma2(ex2x2(mul2(dt, A23)), h23, mul2(du, f2(b.z, b.w)));
+            const float2 a01 = ex2x2(mul2(dt, A01)), a23 = ex2x2(mul2(dt, A23));
+            bv[t] = AREG ? make_float4(a01.x, a01.y, a23.x, a23.y) : b;
+            h01 = fma2(a01, h01, mul2(du, f2(b.x, b.y)));
+            h23 = fma2(a23, h23, mul2(du, f2(b.z, b.w)));
             hs01[t] = h01;
             hs23[t] = h23;
             if (YV) {
@@ -329,10 +331,12 @@ __device__ __forceinline__ void bwd_recompute(const float2 (*__restrict__ dd)[SC
 }
 
 // One hand-off tile (HTQ steps, processed last to first) of the reverse recurrence.  The
-// decays are recomputed here (one exp per element; the MUFU pipe has room in the
-// backward), the states come from the chunk's registers, B from registers or (NOBV,
-// the two-CTAs-per-SM variant) from shared memory.
-template <bool FULL, bool YV, int HTQ, bool NOBV, typename Tin>
+// states come from the chunk's registers.  AREG (one CTA per SM): the recompute pass
+// left each step's decays in bv, so this pass needs no exponential, and B comes from
+// shared memory.  Otherwise bv holds B (or, NOBV, the two-CTAs-per-SM variant at most
+// 128 registers a thread, B comes from shared memory too) and the decays are
+// recomputed here (one exp per element).  Both give the same bits.
+template <bool FULL, bool YV, int HTQ, bool NOBV, bool AREG, typename Tin>
 __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], const float (*__restrict__ dyv)[SCH],
                                          const Tin (*__restrict__ Bs)[NS], const Tin (*__restrict__ Cs)[NS],
                                          float (*__restrict__ bc)[SCH][2 * NS], float2 (*__restrict__ nsd)[SCH][4],
@@ -344,16 +348,35 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
                                          float2& an01, float2& an23, float2& dA01, float2& dA23) {
     const int colB = (ch & 1) * NS + 4 * j;           // swizzled dB / dC columns
     const int colC = ((ch & 1) ^ 1) * NS + 4 * j;
+    constexpr bool BSM = NOBV || AREG;                // B from shared memory
+    // the next (earlier) step's shared-memory inputs are loaded before this step's stores
+    float2 dn = dd[tlo + HTQ - 1][ch];
+    float dyn = dyv[tlo + HTQ - 1][ch];
+    float4 cn = ld4(&Cs[tlo + HTQ - 1][4 * j]);
+    float4 bn = BSM ? ld4(&Bs[tlo + HTQ - 1][4 * j]) : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int tt = HTQ - 1; tt >= 0; --tt) {
         const int t = tlo + tt;
+        const float2 d = dn;
+        const float2 dy = bc2(dyn);
+        const float4 c = cn;
+        const float4 b = BSM ? bn : bv[t];
+        if (tt > 0) {
+            dn = dd[t - 1][ch];
+            dyn = dyv[t - 1][ch];
+            cn = ld4(&Cs[t - 1][4 * j]);
+            if (BSM) bn = ld4(&Bs[t - 1][4 * j]);
+        }
         if (FULL || t < nt) {
-            const float2 d = dd[t][ch];
-            const float2 dy = bc2(dyv[t][ch]);
-            const float4 b = NOBV ? ld4(&Bs[t][4 * j]) : bv[t];
-            const float4 c = ld4(&Cs[t][4 * j]);
             const float2 dte = bc2(d.x);
-            const float2 a01 = ex2x2(mul2(dte, A01)), a23 = ex2x2(mul2(dte, A23));
+            float2 a01, a23;
+            if (AREG) {
+                a01 = f2(bv[t].x, bv[t].y);
+                a23 = f2(bv[t].z, bv[t].w);
+            } else {
+                a01 = ex2x2(mul2(dte, A01));
+                a23 = ex2x2(mul2(dte, A23));
+            }
             g01 = fma2(an01, g01, mul2(dy, f2(c.x, c.y)));
             g23 = fma2(an23, g23, mul2(dy, f2(c.z, c.w)));
             const float2 du = bc2(d.y);
@@ -391,6 +414,7 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
     constexpr bool YV = HAS_Z && !YPRE;
     constexpr int HTQ = LOWREG ? 4 : HT;       // steps per hand-off tile
     constexpr int NQ = TCK / HTQ;              // hand-off tiles per chunk
+    constexpr bool AREG = !LOWREG;             // decays kept in registers (see bwd_half)
     extern __shared__ __align__(16) unsigned char smem_raw[];
     BwdSmem<Tin, HTQ>& S = *reinterpret_cast<BwdSmem<Tin, HTQ>*>(smem_raw);
 
@@ -430,20 +454,20 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
             float4 bv[TCK];
             float yv[TCK];
             if (nt == TCK)
-                bwd_recompute<true, YV>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
+                bwd_recompute<true, YV, AREG>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
             else
-                bwd_recompute<false, YV>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
+                bwd_recompute<false, YV, AREG>(S.dd[s], S.B[r], S.C[r], nt, ch, j, A01, A23, hck01, hck23, hs01, hs23, bv, yv);
             // reverse recurrence: hand-off tiles from the last steps down, alternating slots
 #pragma unroll
             for (int hh = 0; hh < NQ; ++hh) {
                 const int slot = hh & 1, tlo = (NQ - 1 - hh) * HTQ;
                 bar_sync(BAR_E0 + slot, NTH);
                 if (nt == TCK)
-                    bwd_half<true, YV, HTQ, LOWREG>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[slot], S.nsd[slot],
+                    bwd_half<true, YV, HTQ, LOWREG, AREG>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[slot], S.nsd[slot],
                                                     S.nyp[slot], tlo, nt, ch, j, A01, A23, bv, hs01, hs23, yv, hck01,
                                                     hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
                 else
-                    bwd_half<false, YV, HTQ, LOWREG>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[slot], S.nsd[slot],
+                    bwd_half<false, YV, HTQ, LOWREG, AREG>(S.dd[s], S.dy[s], S.B[r], S.C[r], S.bc[slot], S.nsd[slot],
                                                      S.nyp[slot], tlo, nt, ch, j, A01, A23, bv, hs01, hs23, yv, hck01,
                                                      hck23, An01, An23, g01, g23, an01, an23, dA01, dA23);
                 bar_arrive(BAR_X0 + slot, NTH);
