@@ -413,7 +413,10 @@ def run_lm_train(args, world, rank, local):
     reference trainer (training/train.py:133-172).  Data parallel: gradients live in one
     flat fp32 buffer that is all-reduced (NCCL, average) once per step.  The forward +
     backward and the clip + AdamW update are each replayed as a CUDA graph (the step is
-    otherwise bound by kernel-launch overhead); --no-graph runs them eagerly."""
+    otherwise bound by kernel-launch overhead); --no-graph runs them eagerly.  The backward
+    assigns each parameter's gradient (FlatGradients(accumulate=False)): no zero fill and
+    no per-parameter accumulation add; with more than one rank one multi-tensor copy packs
+    them into the all-reduced buffer."""
     from swiftx_b200.data_parallel import FlatGradients, broadcast_parameters
     from swiftx_b200.sift import SiftConfig, SiftLM
     dev = torch.device("cuda", local)
@@ -421,7 +424,7 @@ def run_lm_train(args, world, rank, local):
     model = SiftLM(SiftConfig(vocab_size=256, d_model=256, n_layers=8, d_state=16, d_conv=4, expand=2)).to(dev)
     params = list(model.parameters())
     broadcast_parameters(params)                    # identical start on every rank
-    grads = FlatGradients(params)
+    grads = FlatGradients(params, accumulate=False)     # the backward assigns gradients (no adds)
     decay = [p for p in params if p.dim() >= 2 and not getattr(p, "_no_weight_decay", False)]
     ids = {id(p) for p in decay}
     no_decay = [p for p in params if id(p) not in ids]
@@ -438,6 +441,7 @@ def run_lm_train(args, world, rank, local):
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
             _, loss = model(tok[:, :-1], tok[:, 1:])
         loss.backward()
+        grads.pack_()                                   # into the flat buffer when ranks > 1
         return loss.detach()
 
     def update():

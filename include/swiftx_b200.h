@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 9
+#define SWX_ABI_VERSION 10
 
 /* status codes */
 #define SWX_OK 0
@@ -41,20 +41,25 @@ extern "C" {
 #define SWX_DTYPE_BF16 1
 #define SWX_DTYPE_F64 2   /* linear scan only */
 
+/* swx_scan_args.flags: A holds log(-A) -- the model's A_log parameter, A = -exp(A_log)
+   (models/sift_block.py:121 forms A that way before every scan call).  The kernels form A
+   themselves and the backward's dA receives the gradient with respect to A_log. */
+#define SWX_SCAN_A_LOG 1
+
 /* Arguments of the scan entry points (forward and backward share one struct). */
 typedef struct swx_scan_args {
     int64_t batch, seqlen, dim, dstate;
     int32_t in_dtype;        /* u, delta, z, B, C, dout and the (b,L,*) gradients */
     int32_t out_dtype;       /* out */
     int32_t delta_softplus;  /* delta_eff = softplus(delta + delta_bias) when nonzero */
-    int32_t reserved;
+    int32_t flags;           /* SWX_SCAN_* bits below; other bits must be zero */
     /* inputs */
     const void* u;     int64_t u_sb, u_sl;
     const void* delta; int64_t delta_sb, delta_sl;
     const void* z;     int64_t z_sb, z_sl;      /* optional SiLU gate */
     const void* B;     int64_t B_sb, B_sl;
     const void* C;     int64_t C_sb, C_sl;
-    const float* A;            /* (D, N) */
+    const float* A;            /* (D, N); log(-A) with SWX_SCAN_A_LOG */
     const float* Dskip;        /* optional */
     const float* delta_bias;   /* optional */
     const float* h0;           /* optional initial state */
@@ -68,7 +73,7 @@ typedef struct swx_scan_args {
     const void* dout;  int64_t dout_sb, dout_sl;
     void* du; void* ddelta; void* dz;   /* (b, L, D) dense, in_dtype; dz only with z */
     void* dB; void* dC;                 /* (b, L, N) dense, in_dtype */
-    float* dA;                          /* (D, N) */
+    float* dA;                          /* (D, N); d/dA_log with SWX_SCAN_A_LOG */
     float* dD;                          /* optional (with Dskip) */
     float* ddelta_bias;                 /* optional (with delta_bias) */
     float* dh0;                         /* optional (with h0) */

@@ -19,6 +19,9 @@ SWX_ERR_TIMEOUT = 4
 # capacity of the static scratch of swx_scan_bwd_static_scratch (SWX_STATIC_SCRATCH_BYTES)
 SWX_STATIC_SCRATCH_BYTES = 8 << 20
 
+# swx_scan_args.flags: A holds log(-A) (SWX_SCAN_A_LOG)
+SWX_SCAN_A_LOG = 1
+
 DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 SWX_DTYPE_F64 = 2
 
@@ -31,7 +34,7 @@ class ScanArgs(ctypes.Structure):
     """Mirror of ``swx_scan_args``."""
     _fields_ = [
         ("batch", i64), ("seqlen", i64), ("dim", i64), ("dstate", i64),
-        ("in_dtype", i32), ("out_dtype", i32), ("delta_softplus", i32), ("reserved", i32),
+        ("in_dtype", i32), ("out_dtype", i32), ("delta_softplus", i32), ("flags", i32),
         ("u", vp), ("u_sb", i64), ("u_sl", i64),
         ("delta", vp), ("delta_sb", i64), ("delta_sl", i64),
         ("z", vp), ("z_sb", i64), ("z_sl", i64),

@@ -47,6 +47,7 @@ int check_common(const swx_scan_args* a) {
     // batch rows index the grid's y dimension (at most 65535)
     if (a->batch > 65535 || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
     if (elem_size(a->in_dtype) == 0) return SWX_ERR_UNSUPPORTED;
+    if (a->flags & ~SWX_SCAN_A_LOG) return SWX_ERR_INVALID_ARG;
     if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
     if (!a->u || !a->delta || !a->B || !a->C || !a->A) return SWX_ERR_INVALID_ARG;
     return SWX_OK;
@@ -58,6 +59,7 @@ swx::ScanDev pack(const swx_scan_args* a) {
     p.b = (int)a->batch; p.L = (int)a->seqlen; p.D = (int)a->dim; p.N = (int)a->dstate;
     p.nck = (int)((a->seqlen + swx::TCK - 1) / swx::TCK);
     p.softplus = a->delta_softplus ? 1 : 0;
+    p.a_log = (a->flags & SWX_SCAN_A_LOG) ? 1 : 0;
     p.u = a->u; p.u_sb = a->u_sb; p.u_sl = a->u_sl;
     p.dl = a->delta; p.dl_sb = a->delta_sb; p.dl_sl = a->delta_sl;
     p.z = a->z; p.z_sb = a->z_sb; p.z_sl = a->z_sl;

@@ -55,6 +55,13 @@ __device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
                        __uint_as_float(v.y << 16), __uint_as_float(v.y & 0xffff0000u));
 }
 
+// A[d, n] (flat index i of the (D, N) array), formed as -expf(A_log) when the caller
+// passed log(-A) -- expf is the function torch.exp evaluates for fp32 on CUDA.
+__device__ __forceinline__ float load_A(const ScanDev& p, int64_t i) {
+    const float a = p.A[i];
+    return p.a_log ? -expf(a) : a;
+}
+
 // =============================================================== forward
 template <typename Tin>
 struct FwdSmem {
@@ -135,7 +142,7 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
         for (int i = 0; i < 4; ++i) {
             const int n = 4 * j + i;
             const bool ok = dvalid && n < p.N;
-            av[i] = ok ? p.A[(int64_t)d * p.N + n] * LOG2E : 0.f;
+            av[i] = ok ? load_A(p, (int64_t)d * p.N + n) * LOG2E : 0.f;
             hv[i] = (ok && p.h0) ? p.h0[((int64_t)bi * p.D + d) * p.N + n] : 0.f;
         }
         const float2 A01 = f2(av[0], av[1]), A23 = f2(av[2], av[3]);
@@ -433,7 +440,7 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
             const int n = 4 * j + i;
-            av[i] = (dvalid && n < p.N) ? p.A[(int64_t)d * p.N + n] : 0.f;
+            av[i] = (dvalid && n < p.N) ? load_A(p, (int64_t)d * p.N + n) : 0.f;
         }
         const float2 An01 = f2(av[0], av[1]), An23 = f2(av[2], av[3]);
         const float2 A01 = mul2(An01, bc2(LOG2E)), A23 = mul2(An23, bc2(LOG2E));
@@ -695,7 +702,7 @@ __global__ void scan_bwd_finalize_kernel(const ScanDev p) {
             const int dd = r / p.N, n = r % p.N;
             float s = 0.f;
             for (int bi = 0; bi < p.b; ++bi) s += p.ws_a[((int64_t)bi * p.D + dd) * NS + n];
-            p.dA[r] = s;
+            p.dA[r] = p.a_log ? s * load_A(p, r) : s;       // d/dA_log = dA * A
         } else {
             const int dd = i - nbc - (int64_t)p.D * p.N;
             float sD = 0.f, sB = 0.f;

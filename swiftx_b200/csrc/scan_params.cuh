@@ -9,6 +9,7 @@ struct ScanDev {
     int b, L, D, N;
     int nck;                 // number of 16-step checkpoint slabs = ceil(L / 16)
     int softplus;
+    int a_log;               // A holds log(-A): the kernels use -expf(A[i]); dA is d/d log(-A)
     // inputs (element strides; channel / state stride is 1)
     const void* u;  int64_t u_sb, u_sl;
     const void* dl; int64_t dl_sb, dl_sl;

@@ -24,33 +24,66 @@ def broadcast_parameters(params, src=0, group=None):
 class FlatGradients:
     """One flat buffer holding every parameter's gradient as a view.
 
-    params: the parameters, in a fixed order (the same on every rank).  After
-    construction ``p.grad`` of each is a view into ``self.flat``; autograd accumulates
-    into those views in place, so ``zero_()`` (not ``optimizer.zero_grad``, which would
-    drop the views) clears them between steps."""
+    params: the parameters, in a fixed order (the same on every rank).  Two ways to fill it:
 
-    def __init__(self, params, device=None, dtype=torch.float32):
+    * accumulate=True: ``p.grad`` of each parameter is a view into ``self.flat`` from
+      construction on; autograd accumulates into those views in place, so ``zero_()``
+      (not ``optimizer.zero_grad``, which would drop the views) clears them between steps.
+    * accumulate=False: ``zero_()`` drops every ``p.grad``, so the backward assigns each
+      parameter its gradient as computed -- no zero fill of the buffer and no
+      per-parameter accumulation kernel (one elementwise add per parameter per step
+      otherwise).  ``pack_()`` then copies them into the buffer with one multi-tensor copy
+      and points ``p.grad`` at its views, when there is an all-reduce to feed.
+
+    In both modes, after ``zero_()``, a backward, ``pack_()`` and ``all_reduce_()``, every
+    ``p.grad`` holds the gradient averaged over the ranks."""
+
+    def __init__(self, params, device=None, dtype=torch.float32, accumulate=True):
         self.params = list(params)
         if not self.params:
             raise ValueError("FlatGradients needs at least one parameter")
         dev = device if device is not None else self.params[0].device
         n = sum(p.numel() for p in self.params)
         self.flat = torch.zeros(n, device=dev, dtype=dtype)
+        self.accumulate = accumulate
+        self.views = []
         off = 0
         for p in self.params:
             if p.dtype != dtype:
                 raise ValueError(f"parameter dtype {p.dtype} differs from the gradient buffer's {dtype}")
-            p.grad = self.flat[off:off + p.numel()].view_as(p)
+            self.views.append(self.flat[off:off + p.numel()].view_as(p))
             off += p.numel()
+        if accumulate:
+            for p, v in zip(self.params, self.views):
+                p.grad = v
 
     def zero_(self):
-        self.flat.zero_()
+        """Before a backward: clear the buffer (accumulate mode) or drop every p.grad."""
+        if self.accumulate:
+            self.flat.zero_()
+        else:
+            for p in self.params:
+                p.grad = None
+
+    def pack_(self, group=None):
+        """After a backward (accumulate=False): when the process group has more than one
+        rank, copy every p.grad into the buffer (a parameter without a gradient gets
+        zeros) and point p.grad at the buffer's views.  Otherwise, and in accumulate mode,
+        the gradients are already where the optimizer reads them: nothing to do."""
+        if self.accumulate or _world(group) == 1:
+            return
+        have = [(v, p.grad) for v, p in zip(self.views, self.params) if p.grad is not None]
+        for v, p in zip(self.views, self.params):
+            if p.grad is None:
+                v.zero_()
+        if have:
+            torch._foreach_copy_([v for v, _ in have], [g for _, g in have])
+        for p, v in zip(self.params, self.views):
+            p.grad = v
 
     def all_reduce_(self, group=None):
         """Average the gradient buffer over the ranks of ``group`` (no-op on one rank)."""
-        if not (dist.is_available() and dist.is_initialized()):
-            return
-        world = dist.get_world_size(group)
+        world = _world(group)
         if world == 1:
             return
         if dist.get_backend(group) == "nccl":
@@ -58,3 +91,10 @@ class FlatGradients:
         else:                                   # gloo has no AVG: sum, then scale
             dist.all_reduce(self.flat, op=dist.ReduceOp.SUM, group=group)
             self.flat.div_(world)
+
+
+def _world(group=None):
+    """Ranks in ``group``: 1 without an initialised process group."""
+    if not (dist.is_available() and dist.is_initialized()):
+        return 1
+    return dist.get_world_size(group)

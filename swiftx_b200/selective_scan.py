@@ -42,11 +42,12 @@ def _in_dtype(*ts):
     return dt if dt in _FLOAT_IN else torch.float32
 
 
-def _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, softplus, in_dt):
+def _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, softplus, in_dt, A_is_log=False):
     b, L, Dm = u.shape
     a.batch, a.seqlen, a.dim, a.dstate = b, L, Dm, A.shape[1]
     a.in_dtype = _lib.DTYPE_CODES[in_dt]
     a.delta_softplus = 1 if softplus else 0
+    a.flags = _lib.SWX_SCAN_A_LOG if A_is_log else 0
     a.u, a.u_sb, a.u_sl = u.data_ptr(), u.stride(0), u.stride(1)
     a.delta, a.delta_sb, a.delta_sl = delta.data_ptr(), delta.stride(0), delta.stride(1)
     if z is not None:
@@ -79,14 +80,15 @@ def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
 
 def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
                  h0=None, out_dtype=None, checkpoints=False, return_last_state=False,
-                 return_delta_sum=False, write_out=True, pre_out=None):
+                 return_delta_sum=False, write_out=True, pre_out=None, A_is_log=False):
     """One kernel launch of the forward scan (no autograd).
 
     Returns (out, checkpoints or None, last_state or None), plus delta_sum (b, D) -- the
     sum over t of delta_eff -- when return_delta_sum.  write_out=False skips the output
     (out is None), for callers that only need the final state / delta_sum.  pre_out, a
     dense fp32 (b, L, D) tensor, receives the pre-gate output when z is given (the
-    backward can then skip recomputing it)."""
+    backward can then skip recomputing it).  A_is_log: A holds log(-A) (see
+    selective_scan_fn)."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
     b, L, Dm = u.shape
@@ -98,7 +100,7 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     hl = torch.empty((b, Dm, N), device=u.device, dtype=torch.float32) if return_last_state else None
     ds = torch.empty((b, Dm), device=u.device, dtype=torch.float32) if return_delta_sum else None
     a = _lib.ScanArgs()
-    _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt)
+    _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt, A_is_log)
     a.out_dtype = _lib.DTYPE_CODES[out_dt]
     a.out = out.data_ptr() if out is not None else None
     a.h_last = hl.data_ptr() if hl is not None else None
@@ -114,9 +116,11 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     return out, ck, hl
 
 
-def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, dout, y_pre=None):
+def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, dout, y_pre=None,
+                  A_is_log=False):
     """One call of the backward kernels (no autograd).  Returns a dict of gradients.
-    y_pre: the pre-gate output the forward wrote to pre_out (optional, with z)."""
+    y_pre: the pre-gate output the forward wrote to pre_out (optional, with z).
+    A_is_log: A holds log(-A), and "dA" is the gradient with respect to it."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
     b, L, Dm = u.shape
@@ -133,7 +137,7 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     wsb = lib.swx_scan_bwd_workspace_bytes(b, L, Dm)
     ws = torch.empty(max(wsb, 1), device=dev, dtype=torch.uint8)
     a = _lib.ScanArgs()
-    _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt)
+    _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt, A_is_log)
     a.out_dtype = a.in_dtype
     a.checkpoints = ck.data_ptr()
     a.dout, a.dout_sb, a.dout_sl = dout.data_ptr(), dout.stride(0), dout.stride(1)
@@ -152,14 +156,15 @@ class SelectiveScanFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, out_dtype,
-                return_last_state):
+                return_last_state, A_is_log):
         need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9))
         pre = (torch.empty(u.shape, device=u.device, dtype=torch.float32)
                if need_grad and z is not None else None)
         out, ck, hl = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0,
                                    out_dtype, checkpoints=need_grad,
-                                   return_last_state=return_last_state, pre_out=pre)
+                                   return_last_state=return_last_state, pre_out=pre, A_is_log=A_is_log)
         ctx.delta_softplus = delta_softplus
+        ctx.A_is_log = A_is_log
         ctx.dtypes = [t.dtype if t is not None else None for t in (u, delta, A, B, C, D, z, delta_bias, h0)]
         if need_grad:
             ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, h0, ck, pre)
@@ -171,23 +176,29 @@ class SelectiveScanFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dout, *unused):
         u, delta, A, B, C, D, z, delta_bias, h0, ck, pre = ctx.saved_tensors
-        g = scan_backward(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, h0, ck, dout, y_pre=pre)
+        g = scan_backward(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, h0, ck, dout, y_pre=pre,
+                          A_is_log=ctx.A_is_log)
         dts = ctx.dtypes
         cast = lambda t, dt: None if t is None or dt is None else t.to(dt)  # noqa: E731
         return (cast(g["du"], dts[0]), cast(g["ddelta"], dts[1]), cast(g["dA"], dts[2]),
                 cast(g["dB"], dts[3]), cast(g["dC"], dts[4]), cast(g["dD"], dts[5]),
                 cast(g["dz"], dts[6]), cast(g["ddelta_bias"], dts[7]), None,
-                cast(g["dh0"], dts[8]), None, None)
+                cast(g["dh0"], dts[8]), None, None, None)
 
 
 def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
-                      h0=None, out_dtype=None, return_last_state=False):
+                      h0=None, out_dtype=None, return_last_state=False, A_is_log=False):
     """Fused selective scan with optional SiLU(z) gate and softplus(delta + delta_bias).
 
     out = (scan(u, delta_eff, A, B, C) + D*u) * silu(z),  delta_eff = softplus(delta + delta_bias).
-    Returns out (and the final state (b, D, N) when return_last_state)."""
+    Returns out (and the final state (b, D, N) when return_last_state).
+
+    A_is_log=True: the tensor passed as A holds log(-A) -- the block's A_log parameter --
+    and the kernels form A = -exp(A_log) themselves (models/sift_block.py:121 does it in
+    two elementwise ops before each call, plus two more in the backward); its gradient
+    is returned with respect to A_log."""
     return SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, bool(delta_softplus), h0,
-                                 out_dtype, bool(return_last_state))
+                                 out_dtype, bool(return_last_state), bool(A_is_log))
 
 
 _MODES = ("auto", "parallel", "sequential", "fused", "triton")

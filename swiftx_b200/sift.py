@@ -8,8 +8,8 @@ runs on the sm_100a kernels:
 
   in_proj (cuBLAS) -> causal conv1d + SiLU (kernel, reads the strided x half in place)
   -> x_proj (cuBLAS) -> dt_proj without bias (cuBLAS)
-  -> fused selective scan with softplus(delta + dt_proj.bias), D skip and the SiLU(z)
-     gate (kernel) -> out_proj (cuBLAS)
+  -> fused selective scan with A = -exp(A_log), softplus(delta + dt_proj.bias), D skip
+     and the SiLU(z) gate (kernel) -> out_proj (cuBLAS)
 
 and decode runs the conv-window / state-update kernels around the x_proj / dt_proj GEMVs.
 RMSNorm runs on its fused kernels, each residual add folded into the next norm, and,
@@ -109,11 +109,11 @@ class SiftBlock(nn.Module):
         x, z = xz.chunk(2, dim=-1)                        # strided views, row stride 2D
         x = causal_conv1d_fn(x, self.conv1d.weight, self.conv1d.bias, "silu")
         delta, B, C = self._split(x)
-        A = -torch.exp(self.A_log.float())
         gate = z if self.pathway is None else None
         with torch.autocast(device_type=x.device.type, enabled=False):
-            y = selective_scan_fn(x, delta, A, B, C, self.D.float(), z=gate,
-                                  delta_bias=self.dt_proj.bias.float(), delta_softplus=True)
+            # A = -exp(A_log) is formed inside the scan kernels (A_is_log)
+            y = selective_scan_fn(x, delta, self.A_log.float(), B, C, self.D.float(), z=gate,
+                                  delta_bias=self.dt_proj.bias.float(), delta_softplus=True, A_is_log=True)
         y = y.to(xz.dtype)
         if self.pathway is not None:
             y = self._mix_pathways(y, x) * F.silu(z)

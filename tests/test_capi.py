@@ -33,7 +33,7 @@ def test_struct_mirrors_match():
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
     assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
     assert lib.swx_embedding_args_size() == ctypes.sizeof(_lib.EmbeddingArgs)
-    assert lib.swx_abi_version() == 9
+    assert lib.swx_abi_version() == 10
 
 
 def test_status_strings():
@@ -65,7 +65,9 @@ def test_host_side_validation_without_gpu():
     assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_UNSUPPORTED
     a.dstate, a.in_dtype = 16, 7                              # unknown dtype
     assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_UNSUPPORTED
-    a.in_dtype = 0                                            # missing pointers
+    a.in_dtype, a.flags = 0, 2                                # unknown flag bit
+    assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_INVALID_ARG
+    a.flags = _lib.SWX_SCAN_A_LOG                             # missing pointers
     assert lib.swx_scan_fwd(a, None) == _lib.SWX_ERR_INVALID_ARG
     assert lib.swx_scan_bwd(a, None) == _lib.SWX_ERR_INVALID_ARG
     a.seqlen = 0                                              # empty problem: nothing to do

@@ -1,10 +1,12 @@
 """Data-parallel gradient plumbing (swiftx_b200.data_parallel) on CPU ranks over gloo.
 
 Two ranks start from rank 0's parameters (broadcast), train a small MLP for three steps
-on their halves of a global batch with every gradient a view into one flat buffer that
-is averaged across the ranks each step, then clip and SGD.  Both ranks must end with
-identical parameters, equal (to fp32 re-association) to one process training on the
-whole batch.  The same class drives the GPU LM's data-parallel step over NCCL."""
+on their halves of a global batch with every gradient in one flat buffer that is
+averaged across the ranks each step, then clip and SGD -- with the gradients accumulated
+into the buffer's views, and with them assigned by the backward and packed into the
+buffer.  Both ranks must end with identical parameters, equal (to fp32 re-association)
+to one process training on the whole batch.  The same class drives the GPU LM's
+data-parallel step over NCCL."""
 import os
 import socket
 
@@ -24,42 +26,45 @@ def _data():
     return torch.randn(WORLD * ROWS_PER_RANK, 10, generator=g), torch.randn(WORLD * ROWS_PER_RANK, 3, generator=g)
 
 
-def _train(x, y, seed):
+def _train(x, y, seed, accumulate=True):
     torch.manual_seed(seed)                   # ranks other than 0 start elsewhere until the broadcast
     m = torch.nn.Sequential(torch.nn.Linear(10, 16), torch.nn.Tanh(), torch.nn.Linear(16, 3))
     params = list(m.parameters())
     broadcast_parameters(params)
-    grads = FlatGradients(params)
+    grads = FlatGradients(params, accumulate=accumulate)
     opt = torch.optim.SGD(params, lr=0.2)
     for _ in range(STEPS):
         grads.zero_()
         torch.nn.functional.mse_loss(m(x), y).backward()
+        grads.pack_()
         grads.all_reduce_()
         torch.nn.utils.clip_grad_norm_(params, 1.0)
         opt.step()
-    assert all(p.grad._base is grads.flat for p in params)      # autograd kept the views
+    if accumulate or (dist.is_initialized() and dist.get_world_size() > 1):
+        assert all(p.grad._base is grads.flat for p in params)  # the optimizer read the buffer
     return torch.cat([p.detach().reshape(-1) for p in params]).numpy()
 
 
-def _worker(rank, port, q):
+def _worker(rank, port, accumulate, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=WORLD)
     try:
         x, y = _data()
         rows = slice(rank * ROWS_PER_RANK, (rank + 1) * ROWS_PER_RANK)
-        q.put((rank, _train(x[rows], y[rows], seed=rank)))
+        q.put((rank, _train(x[rows], y[rows], seed=rank, accumulate=accumulate)))
     finally:
         dist.destroy_process_group()
 
 
-def test_flat_gradients_average_over_gloo_ranks():
+@pytest.mark.parametrize("accumulate", [True, False], ids=["accumulate", "assign"])
+def test_flat_gradients_average_over_gloo_ranks(accumulate):
     with socket.socket() as s:
         s.bind(("127.0.0.1", 0))
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, port, accumulate, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=120) for _ in range(WORLD))
@@ -68,7 +73,7 @@ def test_flat_gradients_average_over_gloo_ranks():
         assert p.exitcode == 0
     assert np.array_equal(got[1], got[0]), "ranks diverged"
     x, y = _data()
-    whole = _train(x, y, seed=0)               # one process, whole batch, no process group
+    whole = _train(x, y, seed=0, accumulate=accumulate)    # one process, whole batch, no process group
     np.testing.assert_allclose(got[0], whole, rtol=1e-5, atol=1e-6)
 
 
@@ -87,3 +92,18 @@ def test_flat_gradients_bind_views_and_reject_mixed_dtypes():
         FlatGradients([torch.nn.Parameter(torch.randn(2, dtype=torch.float64))])
     with pytest.raises(ValueError, match="at least one"):
         FlatGradients([])
+
+
+def test_assign_mode_leaves_gradients_to_autograd_on_one_rank():
+    a = torch.nn.Parameter(torch.randn(3, 4))
+    b = torch.nn.Parameter(torch.randn(5))
+    fg = FlatGradients([a, b], accumulate=False)
+    assert a.grad is None and b.grad is None
+    for k in range(2):                         # no accumulation across steps
+        fg.zero_()
+        assert a.grad is None
+        ((k + 1) * a.sum() + (b * b).sum()).backward()
+        fg.pack_()                             # one rank: the assigned gradients stay
+        np.testing.assert_allclose(a.grad.numpy(), k + 1.0)
+        np.testing.assert_allclose(b.grad.numpy(), (2 * b).detach().numpy())
+        assert a.grad._base is not fg.flat

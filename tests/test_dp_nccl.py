@@ -1,6 +1,7 @@
 """Data-parallel training of the Sift LM over NCCL on 2+ GPUs (skipped with fewer), the
-way bench.py's LM workload runs it: every gradient is a view into one flat buffer that is
-all-reduced (average) once per step, then the clip and the optimizer step.  After three
+way bench.py's LM workload runs it: the gradients land in one flat buffer (accumulated
+into its views, or assigned by the backward and packed into it) that is all-reduced
+(average) once per step, then the clip and the optimizer step.  After three
 steps on their halves of a global batch the ranks must hold identical parameters, equal
 (to fp32 re-association) to one GPU training on the whole batch.  The optimizer here is
 plain SGD, whose update is linear in the gradient, so rounding-level gradient
@@ -22,20 +23,21 @@ def _batch(world):
     return torch.randint(0, 11, (world * ROWS_PER_RANK, SEQ + 1), generator=g)
 
 
-def _train(tok, dev):
+def _train(tok, dev, accumulate=True):
     from swiftx_b200.data_parallel import FlatGradients, broadcast_parameters
     from swiftx_b200.sift import SiftConfig, SiftLM
     torch.manual_seed(0)
     m = SiftLM(SiftConfig(vocab_size=11, d_model=32, n_layers=2, d_state=8)).to(dev)
     params = list(m.parameters())
     broadcast_parameters(params)
-    grads = FlatGradients(params)
+    grads = FlatGradients(params, accumulate=accumulate)
     opt = torch.optim.SGD(params, lr=0.1)
     tok = tok.to(dev)
     for _ in range(STEPS):
         grads.zero_()
         _, loss = m(tok[:, :-1], tok[:, 1:])
         loss.backward()
+        grads.pack_()
         grads.all_reduce_()
         torch.nn.utils.clip_grad_norm_(params, 1.0)
         opt.step()
@@ -43,7 +45,7 @@ def _train(tok, dev):
     return torch.cat([p.detach().reshape(-1) for p in params]).cpu().numpy()
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, accumulate, q):
     import datetime
 
     import torch.distributed as dist
@@ -54,13 +56,14 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         tok = _batch(world)[rank * ROWS_PER_RANK:(rank + 1) * ROWS_PER_RANK]
-        out = _train(tok, torch.device("cuda", rank))
+        out = _train(tok, torch.device("cuda", rank), accumulate)
         q.put((rank, out))
     finally:
         dist.destroy_process_group()
 
 
-def test_data_parallel_training_over_nccl():
+@pytest.mark.parametrize("accumulate", [True, False], ids=["accumulate", "assign"])
+def test_data_parallel_training_over_nccl(accumulate):
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -70,7 +73,7 @@ def test_data_parallel_training_over_nccl():
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, accumulate, q)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=180) for _ in range(world))
@@ -79,5 +82,5 @@ def test_data_parallel_training_over_nccl():
         assert p.exitcode == 0
     for r in range(1, world):
         assert np.array_equal(got[r], got[0]), f"rank {r} diverged from rank 0"
-    whole = _train(_batch(world), torch.device("cuda", 0))
+    whole = _train(_batch(world), torch.device("cuda", 0), accumulate)
     np.testing.assert_allclose(got[0], whole, rtol=1e-4, atol=1e-5)

@@ -198,6 +198,34 @@ def test_deterministic_backward():
             assert torch.equal(g1[k], g2[k]), k
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["fp32", "bf16"])
+def test_a_log_formed_in_kernel_matches_torch_chain(dtype):
+    """A_is_log=True (the kernels form A = -exp(A_log) and return d/dA_log) against the
+    block's torch expression A = -torch.exp(A_log) feeding the plain call, through
+    autograd: the same values (the kernel's expf is the function torch.exp evaluates), so
+    outputs and every gradient agree to rounding; a 1x2 channel tail and N < 16 included."""
+    b, L, D, N = 2, 77, 66, 12
+    inp = config_inputs(b, L, D, N, seed=11, device=DEV, dtype=dtype)
+    g = torch.Generator(device="cpu").manual_seed(3)
+    A_log = (torch.log(torch.arange(1, N + 1, dtype=torch.float32)).repeat(D, 1)
+             + 0.1 * torch.randn(D, N, generator=g)).to(DEV)
+    keys = ["u", "delta", "B", "C", "D", "z", "delta_bias"]
+    res = []
+    for in_kernel in (False, True):
+        t = {k: inp[k].clone().requires_grad_() for k in keys}
+        al = A_log.clone().requires_grad_()
+        A = al if in_kernel else -torch.exp(al)
+        out = selective_scan_fn(t["u"], t["delta"], A, t["B"], t["C"], t["D"], z=t["z"],
+                                delta_bias=t["delta_bias"], delta_softplus=True, A_is_log=in_kernel)
+        out.backward(inp["dout"])
+        res.append((out.detach(), al.grad, {k: t[k].grad for k in keys}))
+    (o0, a0, g0), (o1, a1, g1) = res
+    assert_close(np64(o1), np64(o0), 1e-6, 1e-7, "out")
+    assert_close(np64(a1), np64(a0), 1e-6, 1e-6 * float(a0.abs().max()), "dA_log")
+    for k in keys:
+        assert_close(np64(g1[k]), np64(g0[k]), 1e-6, 1e-6 * float(g0[k].abs().max()), k)
+
+
 def test_bf16_inputs_fp32_state():
     b, L, D, N = 2, 200, 64, 16
     inp = config_inputs(b, L, D, N, seed=9, device=DEV, dtype=torch.bfloat16)

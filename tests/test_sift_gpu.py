@@ -161,26 +161,28 @@ def test_generate_length():
     assert out.shape == (2, 8)
 
 
-def test_graph_captured_train_step_matches_eager():
+@pytest.mark.parametrize("accumulate", [True, False], ids=["accumulate", "assign"])
+def test_graph_captured_train_step_matches_eager(accumulate):
     """The training step replayed from CUDA graphs (forward+backward, then clip+AdamW)
     follows the same loss trajectory as the eager step (the kernels launch on the
-    capturing stream and allocate from the graph's pool)."""
+    capturing stream and allocate from the graph's pool), with the gradients accumulated
+    into a flat buffer's views and with them assigned by the backward (bench.py's LM
+    step), where the update graph reads the gradients from the first graph's pool."""
+    from swiftx_b200.data_parallel import FlatGradients
+
     def run(graphed):
         torch.manual_seed(0)
         m = SiftLM(tiny_cfg()).to(DEV)
         params = list(m.parameters())
-        flat = torch.zeros(sum(p.numel() for p in params), device=DEV)
-        off = 0
-        for p in params:
-            p.grad = flat[off:off + p.numel()].view_as(p)
-            off += p.numel()
+        grads = FlatGradients(params, accumulate=accumulate)
         opt = torch.optim.AdamW(params, lr=3e-3, fused=True, capturable=graphed)
         idx = torch.randint(0, 11, (4, 17), device=DEV, generator=torch.Generator(device=DEV).manual_seed(1))
 
         def fwd_bwd():
-            flat.zero_()
+            grads.zero_()
             _, loss = m(idx[:, :-1], idx[:, 1:])
             loss.backward()
+            grads.pack_()
             return loss.detach()
 
         def update():
