@@ -9,7 +9,8 @@
 // for the backward.
 // Backward (x^ = x r, g = w dy):  dx = r (g - x^ mean(x^ g)),  dw = sum_rows dy x^.
 // A fixed grid of warps walks the rows in a fixed assignment, accumulating dw per lane in
-// registers; per-warp partials are then summed in warp order (deterministic).
+// registers; each CTA sums its warps' partials in warp order and a second kernel sums the
+// CTAs' partials in CTA order (deterministic).
 // Residual form (x_{i+1} = x_i + h_i feeding the next norm): the forward adds the residual
 // input first and writes the sum; the backward adds the sum's other incoming gradient to
 // dx and writes it a second time in the residual input's type -- the separate add, its
@@ -22,7 +23,8 @@ namespace swx {
 
 constexpr int NORM_WARPS = 8;                 // warps per CTA
 constexpr int NORM_MAXC = 32;                 // columns per lane (the row in registers): d <= 1024
-constexpr int NORM_BWD_WARPS = 148 * 2 * NORM_WARPS;   // fixed backward grid (warps)
+constexpr int NORM_BWD_CTAS = 148 * 2;                 // fixed backward grid
+constexpr int NORM_BWD_WARPS = NORM_BWD_CTAS * NORM_WARPS;
 
 struct NormDev {
     int rows, d;
@@ -129,21 +131,28 @@ __global__ void __launch_bounds__(32 * NORM_WARPS) rmsnorm_bwd_kernel(const Norm
             dwacc[k] = fmaf(dyv[k], xh[k], dwacc[k]);
         }
     }
+    // the CTA's dw partial: its warps' partials summed in warp order
+    __shared__ float red[NORM_WARPS][NC * 32];
+    const int wi = threadIdx.x >> 5;
 #pragma unroll
-    for (int k = 0; k < NC; ++k) {
-        const int c = lane + 32 * k;
-        if (c < p.d) p.dw_part[(int64_t)gw * p.d + c] = dwacc[k];
+    for (int k = 0; k < NC; ++k) red[wi][lane + 32 * k] = dwacc[k];
+    __syncthreads();
+    for (int c = threadIdx.x; c < p.d; c += 32 * NORM_WARPS) {
+        float t = 0.f;
+#pragma unroll
+        for (int i = 0; i < NORM_WARPS; ++i) t += red[i][c];
+        p.dw_part[(int64_t)blockIdx.x * p.d + c] = t;
     }
 }
 
-// dw[c] = sum over the backward grid's warps of dw_part[warp][c], in warp order.
+// dw[c] = sum over the backward grid's CTAs of dw_part[cta][c], in a fixed order.
 __global__ void __launch_bounds__(1024) rmsnorm_dw_kernel(const NormDev p) {
     __shared__ float part[32][33];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
     float s = 0.f;
     if (c < p.d)
-        for (int r = w; r < NORM_BWD_WARPS; r += 32) s += p.dw_part[(int64_t)r * p.d + c];
+        for (int r = w; r < NORM_BWD_CTAS; r += 32) s += p.dw_part[(int64_t)r * p.d + c];
     part[w][lane] = s;
     __syncthreads();
     if (w == 0 && c < p.d) {
@@ -157,7 +166,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_dw_kernel(const NormDev p) {
 template <typename T, typename TY>
 static void launch_bwd(const NormDev& p, cudaStream_t st) {
     const int nc = (p.d + 31) / 32;
-    const dim3 grid(NORM_BWD_WARPS / NORM_WARPS);
+    const dim3 grid(NORM_BWD_CTAS);
     if (nc <= 8) rmsnorm_bwd_kernel<T, TY, 8><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
     else if (nc <= 16) rmsnorm_bwd_kernel<T, TY, 16><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
     else rmsnorm_bwd_kernel<T, TY, NORM_MAXC><<<grid, 32 * NORM_WARPS, 0, st>>>(p);
@@ -218,7 +227,7 @@ extern "C" {
 
 int64_t swx_rmsnorm_args_size(void) { return (int64_t)sizeof(swx_rmsnorm_args); }
 
-int64_t swx_rmsnorm_bwd_workspace_bytes(int64_t dim) { return (int64_t)swx::NORM_BWD_WARPS * dim * 4; }
+int64_t swx_rmsnorm_bwd_workspace_bytes(int64_t dim) { return (int64_t)swx::NORM_BWD_CTAS * dim * 4; }
 
 int swx_rmsnorm_fwd(const swx_rmsnorm_args* a, void* stream) {
     const int s = norm_check(a, false);

@@ -34,6 +34,54 @@ from .decode import decode_conv_step, decode_ssm_step
 from .selective_scan import selective_scan_fn
 
 
+# bf16 copies of the projection weights for the current SiftLM forward under bf16 autocast
+# (id(fp32 weight) -> bf16 view), or None: see _Bf16Linear and SiftLM.forward.
+_W16 = None
+
+
+class _Bf16Linear(torch.autograd.Function):
+    """y = x @ W^T on a bf16 copy of the fp32 weight made beforehand -- the GEMM bf16
+    autocast runs -- without autocast's per-call weight cast, and with the weight gradient
+    returned in fp32 straight from the GEMM (mm with an fp32 output) instead of a bf16
+    gradient cast back to the parameter's dtype: two elementwise launches fewer per
+    projection and step, and dW is not rounded to bf16 on its way to the fp32 parameter."""
+
+    @staticmethod
+    def forward(ctx, x, weight, w16):
+        ctx.save_for_backward(x, w16)
+        return F.linear(x, w16)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w16 = ctx.saved_tensors
+        dx = dy.matmul(w16) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            dw = torch.mm(dy.reshape(-1, dy.shape[-1]).t(), x.reshape(-1, x.shape[-1]), out_dtype=torch.float32)
+        return dx, dw, None
+
+
+def _linear(x, weight, bias=None):
+    """F.linear(x, weight, bias), through _Bf16Linear when the running SiftLM forward made
+    a bf16 copy of ``weight`` (bias-free projections under bf16 autocast)."""
+    w16 = _W16.get(id(weight)) if _W16 is not None and bias is None else None
+    if w16 is None or x.dtype != torch.bfloat16:
+        return F.linear(x, weight, bias)
+    return _Bf16Linear.apply(x, weight, w16)
+
+
+def _bf16_copies(weights):
+    """bf16 copies of fp32 weights in two launches (one concatenation, one cast) instead
+    of one cast per weight: {id(weight): bf16 view}."""
+    with torch.no_grad():
+        flat = torch.cat([w.reshape(-1) for w in weights]).to(torch.bfloat16)
+    out, off = {}, 0
+    for w in weights:
+        out[id(w)] = flat[off:off + w.numel()].view_as(w)
+        off += w.numel()
+    return out
+
+
 def init_A_log(d_inner, d_state):
     """S4D-real: A_n = -(n+1) for every channel, stored as log(-A) (models/ssm.py:43-51)."""
     A = torch.arange(1, d_state + 1, dtype=torch.float32).repeat(d_inner, 1)
@@ -99,13 +147,18 @@ class SiftBlock(nn.Module):
         self.out_proj = nn.Linear(self.d_inner, d_model, bias=bias)
 
     def _split(self, x):
-        x_dbl = self.x_proj(x)
+        x_dbl = _linear(x, self.x_proj.weight)
         dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
-        return F.linear(dt, self.dt_proj.weight), B, C      # dt_proj bias fused into the scan
+        return _linear(dt, self.dt_proj.weight), B, C       # dt_proj bias fused into the scan
+
+    def projection_weights(self):
+        """The fp32 weights of the bias-free projections (in_proj, x_proj, dt_proj, out_proj)."""
+        return [m.weight for m in (self.in_proj, self.x_proj, self.dt_proj, self.out_proj)
+                if m is self.dt_proj or m.bias is None]
 
     def forward(self, hidden):
         """hidden: (b, L, d_model) -> (b, L, d_model)"""
-        xz = self.in_proj(hidden)
+        xz = _linear(hidden, self.in_proj.weight, self.in_proj.bias)
         x, z = xz.chunk(2, dim=-1)                        # strided views, row stride 2D
         x = causal_conv1d_fn(x, self.conv1d.weight, self.conv1d.bias, "silu")
         delta, B, C = self._split(x)
@@ -117,7 +170,7 @@ class SiftBlock(nn.Module):
         y = y.to(xz.dtype)
         if self.pathway is not None:
             y = self._mix_pathways(y, x) * F.silu(z)
-        return self.out_proj(y)
+        return _linear(y, self.out_proj.weight, self.out_proj.bias)
 
     def _mix_pathways(self, y, x):
         """SiftX: reweight the channel groups per token, softmax x G (1 at init)
@@ -253,14 +306,31 @@ class SiftLM(nn.Module):
         self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)
         if cfg.tie_embeddings:
             self.lm_head.weight = self.embedding.weight
+        self.bf16_weight_copies = True      # under bf16 autocast: see forward
 
     def forward(self, idx, targets=None):
+        """Under bf16 autocast on CUDA (and bf16_weight_copies) the projection weights and
+        the head's are cast to bf16 once per forward, in two launches, and the projections
+        run through _Bf16Linear: the same bf16 GEMMs as autocast, without its per-call
+        weight casts, and with fp32 weight gradients from the GEMM itself."""
+        global _W16
         w = self.embedding.weight
         if embedding_kernels.supported(idx, w) and torch.is_grad_enabled():
             x = embedding_kernels.embedding(idx, w)
         else:
             x = self.embedding(idx)
-        logits = self.lm_head(self.backbone(x))
+        prev = _W16
+        if self.bf16_weight_copies and w.is_cuda and torch.is_autocast_enabled("cuda") \
+                and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+            ws = [p for layer in self.backbone.layers for p in layer.mixer.projection_weights()]
+            if self.lm_head.bias is None:
+                ws.append(self.lm_head.weight)
+            if all(p.dtype == torch.float32 for p in ws):
+                _W16 = _bf16_copies(ws)
+        try:
+            logits = _linear(self.backbone(x), self.lm_head.weight, self.lm_head.bias)
+        finally:
+            _W16 = prev
         loss = None
         if targets is not None:
             loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), targets.reshape(-1))

@@ -217,6 +217,32 @@ def test_graph_captured_train_step_matches_eager(accumulate):
     np.testing.assert_allclose(graphed[:10], eager[:10], rtol=1e-3)
 
 
+def test_bf16_weight_copies_match_autocast():
+    """SiftLM under bf16 autocast with its per-forward bf16 weight copies (_Bf16Linear)
+    against plain autocast: the same bf16 GEMMs, so identical logits; gradients agree to
+    bf16 rounding (autocast rounds each projection's weight gradient to bf16 before casting
+    it back to fp32, the copies' path returns the GEMM's fp32 result)."""
+    torch.manual_seed(0)
+    m = SiftLM(SiftConfig(vocab_size=64, d_model=128, n_layers=2, d_state=16)).to(DEV)
+    tok = torch.randint(0, 64, (2, 97), device=DEV)
+
+    def run(copies):
+        m.bf16_weight_copies = copies
+        m.zero_grad(set_to_none=True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits, loss = m(tok[:, :-1], tok[:, 1:])
+        loss.backward()
+        return logits.detach().float(), {n: p.grad.clone() for n, p in m.named_parameters()}
+
+    l1, g1 = run(True)
+    l0, g0 = run(False)
+    assert torch.equal(l1, l0)
+    for n in g0:
+        assert g1[n].dtype == torch.float32, n
+        tol = 2e-2 * float(g0[n].abs().max())
+        np.testing.assert_allclose(g1[n].cpu().numpy(), g0[n].cpu().numpy(), rtol=2e-2, atol=tol, err_msg=n)
+
+
 def make_pathway_block():
     """SiftX block: three timescale groups over 32 channels (sizes 11/10/11) and the
     per-token pathway gate, with non-zero pathway weights so the mix is not the identity."""
