@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 10
+#define SWX_ABI_VERSION 11
 
 /* status codes */
 #define SWX_OK 0
@@ -177,6 +177,9 @@ int64_t swx_conv1d_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t di
 /* ------------------------------------------------------------------ decode step */
 #define SWX_DECODE_CONV 1   /* roll the conv window, append x, xc = silu(conv + bias) */
 #define SWX_DECODE_SSM 2    /* h = exp(delta*A)*h + delta*B*xc ; out = (<h,C> + D*xc)*silu(z) */
+/* swx_decode_args.flags: A holds log(-A), the block's A_log parameter (SiftBlock.step forms
+   A = -exp(A_log) before every token, models/sift_block.py:168); the kernel forms A itself */
+#define SWX_DECODE_A_LOG 1
 
 /* One token of recurrent generation, fp32.  Row strides are in elements; the channel
  * (and state) stride is 1.  States are updated in place. */
@@ -191,13 +194,15 @@ typedef struct swx_decode_args {
     const float* C; int64_t C_sb;     /* (b, N) */
     const float* conv_weight;         /* (D, width) */
     const float* conv_bias;           /* (D,) optional */
-    const float* A;                   /* (D, N) */
+    const float* A;                   /* (D, N); log(-A) with SWX_DECODE_A_LOG */
     const float* Dskip;               /* (D,) optional */
     const float* delta_bias;          /* (D,) optional */
     float* conv_state;                /* (b, D, width) in/out */
     float* ssm_state;                 /* (b, D, N) in/out */
     float* xc_out;                    /* (b, D) optional: the post-conv activation */
     float* out;                       /* (b, D) */
+    int32_t flags;                    /* SWX_DECODE_A_LOG; other bits must be zero */
+    int32_t reserved;
 } swx_decode_args;
 
 /* Replaces SiftBlock.step's conv-window roll, conv dot + bias + SiLU and in-place

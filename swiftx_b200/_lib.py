@@ -66,6 +66,7 @@ class ConvArgs(ctypes.Structure):
 
 SWX_DECODE_CONV = 1
 SWX_DECODE_SSM = 2
+SWX_DECODE_A_LOG = 1      # swx_decode_args.flags: A holds log(-A)
 
 
 class DecodeArgs(ctypes.Structure):
@@ -77,6 +78,7 @@ class DecodeArgs(ctypes.Structure):
         ("delta", vp), ("delta_sb", i64), ("B", vp), ("B_sb", i64), ("C", vp), ("C_sb", i64),
         ("conv_weight", vp), ("conv_bias", vp), ("A", vp), ("Dskip", vp), ("delta_bias", vp),
         ("conv_state", vp), ("ssm_state", vp), ("xc_out", vp), ("out", vp),
+        ("flags", i32), ("reserved", i32),
     ]
 
 

@@ -20,6 +20,7 @@ namespace swx {
 
 struct DecDev {
     int b, D, N, K, softplus, mode;
+    int a_log;                       // A holds log(-A): the kernels use -expf(A[i])
     const float* x; int64_t x_sb;
     const float* z; int64_t z_sb;
     const float* dl; int64_t dl_sb;
@@ -29,6 +30,14 @@ struct DecDev {
     const float* A; const float* Dskip; const float* dbias;
     float* conv_state; float* ssm_state; float* xc_out; float* out;
 };
+
+// Four consecutive entries of A from offset i (16-byte aligned), formed as -expf(A_log)
+// when the caller passed log(-A) -- expf is the function torch.exp evaluates for fp32.
+__device__ __forceinline__ float4 load_A4(const DecDev& p, int64_t i) {
+    float4 a = *reinterpret_cast<const float4*>(p.A + i);
+    if (p.a_log) a = make_float4(-expf(a.x), -expf(a.y), -expf(a.z), -expf(a.w));
+    return a;
+}
 
 constexpr int DEC_NT = 256;          // 64 channels x 4 state groups per CTA
 constexpr int DEC_CH = DEC_NT / 4;
@@ -57,7 +66,7 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
     float4 A4 = make_float4(0.f, 0.f, 0.f, 0.f);
     float dsk = 0.f, dbi = 0.f;
     if (ssm) {
-        if (full) A4 = *reinterpret_cast<const float4*>(p.A + (int64_t)dc * NS + 4 * j);
+        if (full) A4 = load_A4(p, (int64_t)dc * NS + 4 * j);
         dsk = p.Dskip ? p.Dskip[dc] : 0.f;
         dbi = p.dbias ? p.dbias[dc] : 0.f;
     }
@@ -139,8 +148,8 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
             for (int i = 0; i < 4; ++i) {
                 const int n = 4 * j + i;
                 if (n < p.N) {
-                    const float h = fmaf(ex2(dte * p.A[(int64_t)dc * p.N + n] * LOG2E), hp[n],
-                                         dxc * p.B[bc * p.B_sb + n]);
+                    const float an = p.a_log ? -expf(p.A[(int64_t)dc * p.N + n]) : p.A[(int64_t)dc * p.N + n];
+                    const float h = fmaf(ex2(dte * an * LOG2E), hp[n], dxc * p.B[bc * p.B_sb + n]);
                     y = fmaf(h, p.C[bc * p.C_sb + n], y);
                     if (valid[r]) hp[n] = h;
                 }
@@ -185,7 +194,7 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
     const int d0 = cb * DP_CH, d = d0 + ch;
 
     // per-channel parameters, once per CTA
-    const float4 A4 = *reinterpret_cast<const float4*>(p.A + (int64_t)d * NS + 4 * j);
+    const float4 A4 = load_A4(p, (int64_t)d * NS + 4 * j);
     float4 cw = make_float4(0.f, 0.f, 0.f, 0.f);
     float cbias = 0.f;
     if (CONV) {
@@ -320,6 +329,7 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     if (!a) return SWX_ERR_INVALID_ARG;
     if (a->batch < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
     if (a->mode < 1 || a->mode > 3) return SWX_ERR_INVALID_ARG;
+    if (a->flags & ~SWX_DECODE_A_LOG) return SWX_ERR_INVALID_ARG;
     if ((a->mode & SWX_DECODE_CONV) && (a->width < 1 || a->width > 6)) return SWX_ERR_UNSUPPORTED;
     if ((a->mode & SWX_DECODE_SSM) && (a->dstate < 1 || a->dstate > swx::NS)) return SWX_ERR_UNSUPPORTED;
     if (a->batch * a->dim == 0) return SWX_OK;
@@ -337,6 +347,7 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     swx::DecDev p{};
     p.b = (int)a->batch; p.D = (int)a->dim; p.N = (int)a->dstate; p.K = (int)a->width;
     p.softplus = a->delta_softplus ? 1 : 0; p.mode = a->mode;
+    p.a_log = (a->flags & SWX_DECODE_A_LOG) ? 1 : 0;
     p.x = a->x; p.x_sb = a->x_sb; p.z = a->z; p.z_sb = a->z_sb;
     p.dl = a->delta; p.dl_sb = a->delta_sb; p.B = a->B; p.B_sb = a->B_sb; p.C = a->C; p.C_sb = a->C_sb;
     p.cw = a->conv_weight; p.cb = a->conv_bias; p.A = a->A; p.Dskip = a->Dskip; p.dbias = a->delta_bias;

@@ -23,13 +23,14 @@ def _row(t):
 
 def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, delta=None, B=None,
           C=None, A=None, Dskip=None, delta_bias=None, ssm_state=None, delta_softplus=True,
-          want_xc=False):
+          want_xc=False, A_is_log=False):
     lib = _lib.load()
     x, z, delta, B, C = map(_row, (x, z, delta, B, C))
     b, D = x.shape
     a = _lib.DecodeArgs()
     a.batch, a.dim, a.mode = b, D, mode
     a.delta_softplus = 1 if delta_softplus else 0
+    a.flags = _lib.SWX_DECODE_A_LOG if A_is_log else 0
     a.x, a.x_sb = x.data_ptr(), x.stride(0)
     keep = []
     if mode & _lib.SWX_DECODE_CONV:
@@ -75,16 +76,20 @@ def decode_conv_step(x, conv_state, conv_weight, conv_bias=None):
 
 
 def decode_ssm_step(xc, delta, B, C, A, ssm_state, Dskip=None, z=None, delta_bias=None,
-                    delta_softplus=True):
-    """Returns out (b, D); ssm_state (b, D, N) is updated in place."""
+                    delta_softplus=True, A_is_log=False):
+    """Returns out (b, D); ssm_state (b, D, N) is updated in place.  A_is_log: A holds
+    log(-A) (the block's A_log parameter) and the kernel forms A = -exp(A_log) itself."""
     return _call(_lib.SWX_DECODE_SSM, xc, z=z, delta=delta, B=B, C=C, A=A, Dskip=Dskip,
-                 delta_bias=delta_bias, ssm_state=ssm_state, delta_softplus=delta_softplus)[0]
+                 delta_bias=delta_bias, ssm_state=ssm_state, delta_softplus=delta_softplus,
+                 A_is_log=A_is_log)[0]
 
 
 def decode_step(x, conv_state, conv_weight, conv_bias, delta, B, C, A, ssm_state, Dskip=None,
-                z=None, delta_bias=None, delta_softplus=True, return_xc=False):
+                z=None, delta_bias=None, delta_softplus=True, return_xc=False, A_is_log=False):
     """Fused conv-window shift + conv + SiLU + state update + readout + gate.
-    Returns out (b, D) (and xc when asked); both states are updated in place."""
+    Returns out (b, D) (and xc when asked); both states are updated in place.
+    A_is_log: A holds log(-A), as in decode_ssm_step."""
     out, xc = _call(_lib.SWX_DECODE_CONV | _lib.SWX_DECODE_SSM, x, conv_state, conv_weight, conv_bias,
-                    z, delta, B, C, A, Dskip, delta_bias, ssm_state, delta_softplus, want_xc=return_xc)
+                    z, delta, B, C, A, Dskip, delta_bias, ssm_state, delta_softplus, want_xc=return_xc,
+                    A_is_log=A_is_log)
     return (out, xc) if return_xc else out

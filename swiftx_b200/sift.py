@@ -191,8 +191,9 @@ class SiftBlock(nn.Module):
         xc = decode_conv_step(x, conv_state, self.conv1d.weight, self.conv1d.bias)
         delta, B, C = self._split(xc)
         gate = z if self.pathway is None else None
-        y = decode_ssm_step(xc, delta.float(), B.float(), C.float(), -torch.exp(self.A_log.float()),
-                            ssm_state, Dskip=self.D, z=gate, delta_bias=self.dt_proj.bias)
+        # A = -exp(A_log) is formed inside the kernel (A_is_log)
+        y = decode_ssm_step(xc, delta.float(), B.float(), C.float(), self.A_log, ssm_state, Dskip=self.D,
+                            z=gate, delta_bias=self.dt_proj.bias, A_is_log=True)
         if self.pathway is not None:
             y = self._mix_pathways(y, xc) * F.silu(z)
         return self.out_proj(y.to(self.out_proj.weight.dtype))

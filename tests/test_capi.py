@@ -33,7 +33,7 @@ def test_struct_mirrors_match():
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
     assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
     assert lib.swx_embedding_args_size() == ctypes.sizeof(_lib.EmbeddingArgs)
-    assert lib.swx_abi_version() == 10
+    assert lib.swx_abi_version() == 11
 
 
 def test_status_strings():
@@ -82,6 +82,8 @@ def test_host_side_validation_without_gpu():
     assert lib.swx_conv1d_fwd(c, None) == _lib.SWX_ERR_UNSUPPORTED
     d = _lib.DecodeArgs()
     d.batch, d.dim, d.mode = 1, 4, 0                          # no mode
+    assert lib.swx_decode_step(d, None) == _lib.SWX_ERR_INVALID_ARG
+    d.mode, d.flags = _lib.SWX_DECODE_SSM, 2                  # unknown flag bit
     assert lib.swx_decode_step(d, None) == _lib.SWX_ERR_INVALID_ARG
     s = _lib.LinearScanArgs()
     s.batch, s.seqlen, s.width, s.dtype = 2, 5, 3, 1          # bf16 is not a linear-scan dtype

@@ -194,3 +194,30 @@ def test_conv_vector_and_scalar_paths_agree(dtype, L, K):
     assert torch.equal(conv1d_forward(x, w, bias), conv1d_forward(xo, w, bias))
     for got, want in zip(conv1d_backward(x, w, bias, dout), conv1d_backward(xo, w, bias, dout)):
         assert torch.equal(got, want)
+
+
+@pytest.mark.parametrize("b,D,N", [(5, 128, 16), (3, 96, 16), (4, 64, 5)])
+def test_decode_a_log_formed_in_kernel(b, D, N):
+    """A_is_log=True (the kernel forms A = -exp(A_log), SiftBlock.step's call) against the
+    block's torch expression A = -torch.exp(A_log) passed as A: the same values (the
+    kernel's expf is the function torch.exp evaluates), on the streaming kernel (D a
+    multiple of 64, N=16), the per-CTA kernel (D=96) and the N < 16 path, over three
+    steps of the fused conv + state update."""
+    g = torch.Generator().manual_seed(b * D + N)
+    A_log = (torch.log(torch.arange(1, N + 1, dtype=torch.float32)).repeat(D, 1)
+             + 0.1 * torch.randn(D, N, generator=g)).to(DEV)
+    cw, cb = (torch.randn(D, 4, generator=g) * 0.5).to(DEV), torch.randn(D, generator=g).to(DEV)
+    Dsk, dbias = torch.randn(D, generator=g).to(DEV), (torch.randn(D, generator=g) * 0.5 - 3).to(DEV)
+    cs0, ss0 = torch.randn(b, D, 4, generator=g), torch.randn(b, D, N, generator=g) * 0.1
+    states = [(cs0.clone().to(DEV), ss0.clone().to(DEV)) for _ in range(2)]
+    for _ in range(3):
+        x, z, dr = (torch.randn(b, D, generator=g).to(DEV) for _ in range(3))
+        B, C = torch.randn(b, N, generator=g).to(DEV), torch.randn(b, N, generator=g).to(DEV)
+        outs = []
+        for (cs, ss), in_kernel in zip(states, (False, True)):
+            A = A_log if in_kernel else -torch.exp(A_log)
+            outs.append(decode_step(x, cs, cw, cb, dr, B, C, A, ss, Dskip=Dsk, z=z, delta_bias=dbias,
+                                    A_is_log=in_kernel))
+        close(outs[1], n64(outs[0]), rtol=1e-6, atol=1e-7)
+        close(states[1][1], n64(states[0][1]), rtol=1e-6, atol=1e-7)
+        assert torch.equal(states[1][0], states[0][0])
