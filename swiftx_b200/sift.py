@@ -62,19 +62,27 @@ class _Bf16Linear(torch.autograd.Function):
 
 
 def _linear(x, weight, bias=None):
-    """F.linear(x, weight, bias), through _Bf16Linear when the running SiftLM forward made
-    a bf16 copy of ``weight`` (bias-free projections under bf16 autocast)."""
+    """F.linear(x, weight, bias), through _Bf16Linear when the running SiftLM forward (or a
+    GraphedStep) made a bf16 copy of ``weight`` (bias-free projections under bf16
+    autocast).  An fp32 input is cast to bf16 first, as autocast casts it."""
     w16 = _W16.get(id(weight)) if _W16 is not None and bias is None else None
+    if w16 is not None and x.dtype == torch.float32 and torch.is_autocast_enabled("cuda") \
+            and torch.get_autocast_dtype("cuda") == torch.bfloat16:
+        x = x.to(torch.bfloat16)
     if w16 is None or x.dtype != torch.bfloat16:
         return F.linear(x, weight, bias)
     return _Bf16Linear.apply(x, weight, w16)
 
 
-def _bf16_copies(weights):
+def _bf16_copies(weights, flat=None):
     """bf16 copies of fp32 weights in two launches (one concatenation, one cast) instead
-    of one cast per weight: {id(weight): bf16 view}."""
+    of one cast per weight: {id(weight): bf16 view}.  ``flat``: an existing bf16 buffer of
+    the right size to refresh in place (its views stay valid)."""
     with torch.no_grad():
-        flat = torch.cat([w.reshape(-1) for w in weights]).to(torch.bfloat16)
+        if flat is None:
+            flat = torch.cat([w.reshape(-1) for w in weights]).to(torch.bfloat16)
+        else:
+            flat.copy_(torch.cat([w.reshape(-1) for w in weights]))
     out, off = {}, 0
     for w in weights:
         out[id(w)] = flat[off:off + w.numel()].view_as(w)
@@ -186,7 +194,7 @@ class SiftBlock(nn.Module):
     def step(self, hidden, state):
         """hidden: (b, d_model) one token; state (conv_state, ssm_state) updated in place."""
         conv_state, ssm_state = state
-        xz = self.in_proj(hidden).float()
+        xz = _linear(hidden, self.in_proj.weight, self.in_proj.bias).float()
         x, z = xz.chunk(2, dim=-1)
         xc = decode_conv_step(x, conv_state, self.conv1d.weight, self.conv1d.bias)
         delta, B, C = self._split(xc)
@@ -196,7 +204,7 @@ class SiftBlock(nn.Module):
                             z=gate, delta_bias=self.dt_proj.bias, A_is_log=True)
         if self.pathway is not None:
             y = self._mix_pathways(y, xc) * F.silu(z)
-        return self.out_proj(y.to(self.out_proj.weight.dtype))
+        return _linear(y.to(self.out_proj.weight.dtype), self.out_proj.weight, self.out_proj.bias)
 
 
 class RMSNorm(nn.Module):
@@ -323,10 +331,8 @@ class SiftLM(nn.Module):
         prev = _W16
         if self.bf16_weight_copies and w.is_cuda and torch.is_autocast_enabled("cuda") \
                 and torch.get_autocast_dtype("cuda") == torch.bfloat16:
-            ws = [p for layer in self.backbone.layers for p in layer.mixer.projection_weights()]
-            if self.lm_head.bias is None:
-                ws.append(self.lm_head.weight)
-            if all(p.dtype == torch.float32 for p in ws):
+            ws = self.projection_weights()
+            if ws is not None:
                 _W16 = _bf16_copies(ws)
         try:
             logits = _linear(self.backbone(x), self.lm_head.weight, self.lm_head.bias)
@@ -337,6 +343,14 @@ class SiftLM(nn.Module):
             loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)).float(), targets.reshape(-1))
         return logits, loss
 
+    def projection_weights(self):
+        """The fp32 weights that have bf16 copies under bf16 autocast: every block's
+        bias-free projections and the head's (None when one is not fp32)."""
+        ws = [p for layer in self.backbone.layers for p in layer.mixer.projection_weights()]
+        if self.lm_head.bias is None:
+            ws.append(self.lm_head.weight)
+        return ws if all(p.dtype == torch.float32 for p in ws) else None
+
     def allocate_state(self, batch, device=None):
         return [l.mixer.allocate_state(batch, device) for l in self.backbone.layers]
 
@@ -344,7 +358,7 @@ class SiftLM(nn.Module):
         x = self.embedding(token)
         for layer, s in zip(self.backbone.layers, state):
             x = layer.step(x, s)
-        return self.lm_head(self.backbone.norm_f(x))
+        return _linear(self.backbone.norm_f(x), self.lm_head.weight, self.lm_head.bias)
 
     @torch.no_grad()
     def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None, graphed=False):
@@ -376,24 +390,49 @@ class GraphedStep:
 
     Calling returns the graph's static logits tensor (overwritten by the next call).
     autocast_dtype (e.g. torch.bfloat16) runs the projections under autocast, as the
-    reference trainer does; the state and the decode kernels stay fp32."""
+    reference trainer does; the state and the decode kernels stay fp32.  Under bf16
+    autocast (and model.bf16_weight_copies) the projection and head weights are cast to
+    bf16 once, here, into a buffer the graph reads, instead of at every token as autocast
+    does (the same bf16 values, without re-reading every fp32 weight per step); after
+    changing the model's weights, call refresh_weights()."""
 
     def __init__(self, model, batch, device=None, autocast_dtype=None):
+        global _W16
         dev = torch.device(device) if device is not None else next(model.parameters()).device
         self.model = model
         self.state = model.allocate_state(batch, dev)
         self.token = torch.zeros(batch, dtype=torch.long, device=dev)
         amp = lambda: torch.autocast("cuda", dtype=autocast_dtype, enabled=autocast_dtype is not None)  # noqa: E731
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side), torch.no_grad(), amp():
-            for _ in range(2):                    # one-time library and kernel setup
-                model.step(self.token, self.state)
-        torch.cuda.current_stream(dev).wait_stream(side)
-        self.reset()
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph), torch.no_grad(), amp():
-            self.logits = model.step(self.token, self.state)
+        self._weights, self._w16_flat, w16 = None, None, None
+        if autocast_dtype == torch.bfloat16 and model.bf16_weight_copies and dev.type == "cuda":
+            self._weights = model.projection_weights()
+            if self._weights is not None:
+                w16 = self.refresh_weights()
+        prev = _W16
+        _W16 = w16
+        try:
+            side = torch.cuda.Stream(dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side), torch.no_grad(), amp():
+                for _ in range(2):                    # one-time library and kernel setup
+                    model.step(self.token, self.state)
+            torch.cuda.current_stream(dev).wait_stream(side)
+            self.reset()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph), torch.no_grad(), amp():
+                self.logits = model.step(self.token, self.state)
+        finally:
+            _W16 = prev
+
+    def refresh_weights(self):
+        """Re-take the bf16 copies of the projection weights (after the model's weights
+        changed), in place; a no-op without them.  Returns {id(weight): bf16 view}."""
+        if self._weights is None:
+            return None
+        if self._w16_flat is None:
+            n = sum(w.numel() for w in self._weights)
+            self._w16_flat = torch.empty(n, dtype=torch.bfloat16, device=self._weights[0].device)
+        return _bf16_copies(self._weights, flat=self._w16_flat)
 
     def reset(self):
         """Zero the recurrent state (a fresh sequence)."""

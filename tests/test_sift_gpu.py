@@ -369,3 +369,37 @@ def test_graphed_step_matches_eager_step():
     a = m.generate(idx[:, :4], 6, temperature=0)
     b = m.generate(idx[:, :4], 6, temperature=0, graphed=True)
     assert torch.equal(a, b)
+
+
+def test_graphed_step_bf16_weight_copies():
+    """GraphedStep under bf16 autocast reads bf16 copies of the projection weights taken
+    when it was built: its logits agree with the eager step under autocast (which casts
+    every weight at every call) to bf16 rounding, go stale once a weight changes, and
+    agree again after refresh_weights()."""
+    from swiftx_b200.sift import GraphedStep
+    torch.manual_seed(0)
+    m = SiftLM(tiny_cfg()).to(DEV).eval()
+    idx = torch.randint(0, 11, (3, 6), device=DEV)
+
+    def eager():
+        st = m.allocate_state(3, device=DEV)
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return torch.stack([m.step(idx[:, t], st).float() for t in range(6)])
+
+    def graphed(gs):
+        gs.reset()
+        return torch.stack([gs(idx[:, t]).float().clone() for t in range(6)])
+
+    def rel(a, b):
+        return float((a - b).abs().max() / b.abs().max())
+
+    gs = GraphedStep(m, 3, autocast_dtype=torch.bfloat16)
+    assert gs._w16_flat is not None
+    assert rel(graphed(gs), eager()) < 1e-2
+    with torch.no_grad():
+        for layer in m.backbone.layers:
+            layer.mixer.out_proj.weight.mul_(10.0)
+    want = eager()
+    assert rel(graphed(gs), want) > 0.1            # the copies are from before the change
+    gs.refresh_weights()
+    assert rel(graphed(gs), want) < 1e-2
