@@ -693,8 +693,8 @@ __global__ void scan_bwd_finalize_kernel(const ScanDev p) {
             const int64_t bl = i >> 5;                         // bi * L + t
             const float* src = p.ws_bc + i;
             float s = 0.f;
-#pragma unroll 4
-            for (int k = 0; k < p.nblk; ++k) s += src[(int64_t)k * slab];
+#pragma unroll 16
+            for (int k = 0; k < p.nblk; ++k) s += src[(int64_t)k * slab];   // loads in flight, adds in order
             Tin* dst = static_cast<Tin*>(kind ? p.dC : p.dB);
             dst[bl * p.N + n] = Elem<Tin>::from_f(s);
         } else if (i < nbc + (int64_t)p.D * p.N) {
