@@ -151,8 +151,14 @@ __global__ void __launch_bounds__(1024) rmsnorm_dw_kernel(const NormDev p) {
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int c = blockIdx.x * 32 + lane;
     float s = 0.f;
-    if (c < p.d)
-        for (int r = w; r < NORM_BWD_CTAS; r += 32) s += p.dw_part[(int64_t)r * p.d + c];
+    if (c < p.d) {
+        // rows w, w + 32, ... in order; a fixed trip count so every load is issued up front
+#pragma unroll
+        for (int i = 0; i < (NORM_BWD_CTAS + 31) / 32; ++i) {
+            const int r = w + 32 * i;
+            if (r < NORM_BWD_CTAS) s += p.dw_part[(int64_t)r * p.d + c];
+        }
+    }
     part[w][lane] = s;
     __syncthreads();
     if (w == 0 && c < p.d) {
