@@ -29,7 +29,8 @@ def _data():
 def _train(x, y, seed, accumulate=True):
     torch.manual_seed(seed)                   # ranks other than 0 start elsewhere until the broadcast
     m = torch.nn.Sequential(torch.nn.Linear(10, 16), torch.nn.Tanh(), torch.nn.Linear(16, 3))
-    params = list(m.parameters())
+    unused = torch.nn.Parameter(torch.randn(4))   # no gradient reaches it: packed as zeros
+    params = list(m.parameters()) + [unused]
     broadcast_parameters(params)
     grads = FlatGradients(params, accumulate=accumulate)
     opt = torch.optim.SGD(params, lr=0.2)
