@@ -35,7 +35,11 @@ from .selective_scan import selective_scan_fn
 
 
 # bf16 copies of the projection weights for the current SiftLM forward under bf16 autocast
-# (id(fp32 weight) -> bf16 view), or None: see _Bf16Linear and SiftLM.forward.
+# (id(fp32 weight) -> bf16 view), or None: see _Bf16Linear and SiftLM.forward.  Set only
+# for the duration of one SiftLM.forward or GraphedStep build and restored afterwards.  A
+# projection whose weight has no entry (another model's, or the table already restored
+# by a concurrent forward in another thread) takes the plain F.linear path, which
+# computes the same bf16 GEMM under autocast.
 _W16 = None
 
 
