@@ -39,7 +39,7 @@ extern "C" {
 /* element types */
 #define SWX_DTYPE_F32 0
 #define SWX_DTYPE_BF16 1
-#define SWX_DTYPE_F64 2   /* linear scan only */
+#define SWX_DTYPE_F64 2   /* float64: the scan (in_dtype = out_dtype = F64) and the linear scan */
 
 /* swx_scan_args.flags: A holds log(-A) -- the model's A_log parameter, A = -exp(A_log)
    (models/sift_block.py:121 forms A that way before every scan call).  The kernels form A
@@ -50,7 +50,13 @@ extern "C" {
 typedef struct swx_scan_args {
     int64_t batch, seqlen, dim, dstate;
     int32_t in_dtype;        /* u, delta, z, B, C, dout and the (b,L,*) gradients */
-    int32_t out_dtype;       /* out */
+    int32_t out_dtype;       /* out; SWX_DTYPE_F64 exactly when in_dtype is.  With float64
+                                inputs every floating-point pointer below (A, Dskip,
+                                delta_bias, h0, h_last, checkpoints, delta_sum, out_pre,
+                                dA, dD, ddelta_bias, dh0) holds float64 values, and the
+                                checkpoint buffer holds swx_scan_checkpoint_floats()
+                                float64 values; float64 is the correctness path of the
+                                reference's float64 gradchecks, not a fast path */
     int32_t delta_softplus;  /* delta_eff = softplus(delta + delta_bias) when nonzero */
     int32_t flags;           /* SWX_SCAN_* bits below; other bits must be zero */
     /* inputs */
@@ -96,10 +102,13 @@ int64_t swx_conv_args_size(void);
 int64_t swx_decode_args_size(void);
 
 /* Number of fp32 values of the forward's state checkpoints (one (D, 16) slab per
- * 16 time steps per batch row). */
+ * 16 time steps per batch row); -1 for a negative size or batch*seqlen*dim > 2^40. */
 int64_t swx_scan_checkpoint_floats(int64_t batch, int64_t seqlen, int64_t dim);
-/* Bytes of scratch the backward needs for its deterministic cross-CTA reductions. */
+/* Bytes of scratch the backward needs for its deterministic cross-CTA reductions; -1 for
+ * a negative size or batch*seqlen*dim > 2^40 (the scan entry points reject those too). */
 int64_t swx_scan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim);
+/* The same for float64 inputs (in_dtype SWX_DTYPE_F64), whose partial sums are float64. */
+int64_t swx_scan_bwd_workspace_bytes_f64(int64_t batch, int64_t seqlen, int64_t dim);
 
 /* Forward selective scan:
  *   delta_eff = softplus(delta + delta_bias) | delta + delta_bias | delta
@@ -136,8 +145,12 @@ int swx_scan_bwd_ctas_per_sm(const swx_scan_args* args);
  * comes from a fixed array in the library's device memory, which every GPU that loads
  * the library holds until the process exits.  Returns SWX_ERR_INVALID_ARG (without
  * launching) when swx_scan_bwd_workspace_bytes() exceeds SWX_STATIC_SCRATCH_BYTES.
- * The first call on each device looks the array's address up (cudaGetSymbolAddress,
- * with that device current); make that first call before any stream capture.  All
+ * Arguments are checked as swx_scan_bwd checks them, before any size arithmetic.
+ * The first call in each (device, CUDA context) pair looks the array's address up
+ * (cudaGetSymbolAddress, with that device current) and caches it under the pair; make
+ * that first call before any stream capture.  After cudaDeviceReset, or under another
+ * driver context, the library's module is loaded anew and the next call repeats the
+ * lookup for the new context (again: outside stream capture).  All
  * calls on a device share the one array: calls that overlap on the GPU (other streams,
  * other host threads) race and must be serialised by the caller.  Every scratch byte
  * that is read is first written by the same call, so nothing needs clearing between

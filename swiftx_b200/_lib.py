@@ -22,8 +22,8 @@ SWX_STATIC_SCRATCH_BYTES = 8 << 20
 # swx_scan_args.flags: A holds log(-A) (SWX_SCAN_A_LOG)
 SWX_SCAN_A_LOG = 1
 
-DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1}
 SWX_DTYPE_F64 = 2
+DTYPE_CODES = {torch.float32: 0, torch.bfloat16: 1, torch.float64: SWX_DTYPE_F64}
 
 i64 = ctypes.c_int64
 i32 = ctypes.c_int32
@@ -132,8 +132,9 @@ def load():
             raise RuntimeError(f"{st.__name__} layout mismatch between the library and its binding")
     lib.swx_scan_checkpoint_floats.restype = i64
     lib.swx_scan_checkpoint_floats.argtypes = [i64, i64, i64]
-    lib.swx_scan_bwd_workspace_bytes.restype = i64
-    lib.swx_scan_bwd_workspace_bytes.argtypes = [i64, i64, i64]
+    for fn in ("swx_scan_bwd_workspace_bytes", "swx_scan_bwd_workspace_bytes_f64"):
+        getattr(lib, fn).restype = i64
+        getattr(lib, fn).argtypes = [i64, i64, i64]
     for name, st in (("swx_scan_fwd", ScanArgs), ("swx_scan_bwd", ScanArgs),
                      ("swx_scan_bwd_static_scratch", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
                      ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs),

@@ -9,11 +9,15 @@ namespace swx {
 cudaError_t launch_scan_fwd(const ScanDev& p, int in_dtype, int out_dtype, bool has_z, cudaStream_t st);
 cudaError_t launch_scan_bwd(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st);
 cudaError_t scan_bwd_ctas_per_sm(const ScanDev& p, int in_dtype, bool has_z, int* ctas);
+cudaError_t launch_scan_fwd_f64(const ScanDev& p, cudaStream_t st);
+cudaError_t launch_scan_bwd_f64(const ScanDev& p, cudaStream_t st);
 }  // namespace swx
 
 namespace {
 
-int elem_size(int dt) { return dt == SWX_DTYPE_F32 ? 4 : (dt == SWX_DTYPE_BF16 ? 2 : 0); }
+int elem_size(int dt) {
+    return dt == SWX_DTYPE_F32 ? 4 : (dt == SWX_DTYPE_BF16 ? 2 : (dt == SWX_DTYPE_F64 ? 8 : 0));
+}
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
@@ -29,20 +33,32 @@ struct WsLayout {
     int64_t bc, a, d, bias, total;
 };
 
-WsLayout ws_layout(int64_t b, int64_t L, int64_t D) {
+// es: bytes of one partial sum (4 for fp32 / bf16 inputs, 8 for float64 inputs).
+WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
     const int64_t nblk = (D + 31) / 32;
     WsLayout w;
     w.bc = 0;
-    w.a = w.bc + round_up(nblk * b * L * 2 * swx::NS * 4);
-    w.d = w.a + round_up(b * D * swx::NS * 4);
-    w.bias = w.d + round_up(b * D * 4);
-    w.total = w.bias + round_up(b * D * 4);
+    w.a = w.bc + round_up(nblk * b * L * 2 * swx::NS * es);
+    w.d = w.a + round_up(b * D * swx::NS * es);
+    w.bias = w.d + round_up(b * D * es);
+    w.total = w.bias + round_up(b * D * es);
     return w;
+}
+
+// b * L * D elements at most (2^40, far beyond any device's memory): every size product
+// the launchers and workspace layouts form stays well inside int64.
+constexpr int64_t kMaxElems = int64_t(1) << 40;
+
+bool sizes_ok(int64_t b, int64_t L, int64_t D) {
+    if (b < 0 || L < 0 || D < 0) return false;
+    if (L != 0 && b > kMaxElems / L) return false;
+    const int64_t bl = b * L;
+    return D == 0 || bl <= kMaxElems / D;
 }
 
 int check_common(const swx_scan_args* a) {
     if (!a) return SWX_ERR_INVALID_ARG;
-    if (a->batch < 0 || a->seqlen < 0 || a->dim < 0) return SWX_ERR_INVALID_ARG;
+    if (!sizes_ok(a->batch, a->seqlen, a->dim)) return SWX_ERR_INVALID_ARG;
     if (a->dstate < 1 || a->dstate > swx::NS) return SWX_ERR_UNSUPPORTED;
     // batch rows index the grid's y dimension (at most 65535)
     if (a->batch > 65535 || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
@@ -86,6 +102,11 @@ int from_cuda(cudaError_t e) { return e == cudaSuccess ? SWX_OK : SWX_ERR_CUDA; 
 
 }  // namespace
 
+namespace swx {
+// Argument checks shared by every scan entry point (see check_common).
+int scan_check_args(const swx_scan_args* a) { return check_common(a); }
+}  // namespace swx
+
 extern "C" {
 
 int swx_abi_version(void) { return SWX_ABI_VERSION; }
@@ -106,11 +127,18 @@ const char* swx_status_string(int status) {
 }
 
 int64_t swx_scan_checkpoint_floats(int64_t batch, int64_t seqlen, int64_t dim) {
+    if (!sizes_ok(batch, seqlen, dim)) return -1;
     return batch * ((seqlen + swx::TCK - 1) / swx::TCK) * dim * swx::NS;
 }
 
 int64_t swx_scan_bwd_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim) {
+    if (!sizes_ok(batch, seqlen, dim)) return -1;
     return ws_layout(batch, seqlen, dim).total;
+}
+
+int64_t swx_scan_bwd_workspace_bytes_f64(int64_t batch, int64_t seqlen, int64_t dim) {
+    if (!sizes_ok(batch, seqlen, dim)) return -1;
+    return ws_layout(batch, seqlen, dim, 8).total;
 }
 
 int swx_scan_fwd(const swx_scan_args* a, void* stream) {
@@ -121,6 +149,11 @@ int swx_scan_fwd(const swx_scan_args* a, void* stream) {
     if (!a->out && !a->h_last && !a->delta_sum && !a->checkpoints) return SWX_OK;   // nothing requested
     if (a->checkpoints && !aligned16(a->checkpoints)) return SWX_ERR_INVALID_ARG;
     swx::ScanDev p = pack(a);
+    if (a->in_dtype == SWX_DTYPE_F64) {
+        if (a->out_dtype != SWX_DTYPE_F64) return SWX_ERR_UNSUPPORTED;
+        return from_cuda(swx::launch_scan_fwd_f64(p, static_cast<cudaStream_t>(stream)));
+    }
+    if (a->out_dtype == SWX_DTYPE_F64) return SWX_ERR_UNSUPPORTED;
     return from_cuda(swx::launch_scan_fwd(p, a->in_dtype, a->out_dtype, a->z != nullptr,
                                           static_cast<cudaStream_t>(stream)));
 }
@@ -133,7 +166,8 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
         return SWX_ERR_INVALID_ARG;
     if (a->z && !a->dz) return SWX_ERR_INVALID_ARG;
     if (!aligned16(a->checkpoints) || !a->workspace || !aligned16(a->workspace)) return SWX_ERR_INVALID_ARG;
-    const WsLayout w = ws_layout(a->batch, a->seqlen, a->dim);
+    const bool f64 = a->in_dtype == SWX_DTYPE_F64;
+    const WsLayout w = ws_layout(a->batch, a->seqlen, a->dim, f64 ? 8 : 4);
     if (a->workspace_bytes < w.total) return SWX_ERR_INVALID_ARG;
     swx::ScanDev p = pack(a);
     char* ws = static_cast<char*>(a->workspace);
@@ -141,12 +175,14 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     p.ws_a = reinterpret_cast<float*>(ws + w.a);
     p.ws_d = reinterpret_cast<float*>(ws + w.d);
     p.ws_bias = reinterpret_cast<float*>(ws + w.bias);
+    if (f64) return from_cuda(swx::launch_scan_bwd_f64(p, static_cast<cudaStream_t>(stream)));
     return from_cuda(swx::launch_scan_bwd(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
 }
 
 int swx_scan_bwd_ctas_per_sm(const swx_scan_args* a) {
     int s = check_common(a);
     if (s != SWX_OK) return -s;
+    if (a->in_dtype == SWX_DTYPE_F64) return 1;
     const swx::ScanDev p = pack(a);
     int ctas = 1;
     if (swx::scan_bwd_ctas_per_sm(p, a->in_dtype, a->z != nullptr, &ctas) != cudaSuccess) return -SWX_ERR_CUDA;

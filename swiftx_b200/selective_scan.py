@@ -14,7 +14,9 @@ Shapes: u, delta, z (b, L, D); A (D, N); B, C (b, L, N); D, delta_bias (D,).
 Autograd follows the reference's custom Functions: the forward saves only its inputs
 plus state checkpoints every 16 steps, the backward recomputes
 (models/selective_scan.py:124, models/triton_scan.py:133), and gradients come back
-in the input dtype with dA / dD in fp32 (models/triton_scan.py:153-155).
+in the input dtype with dA / dD in fp32 (models/triton_scan.py:153-155).  float64
+inputs are computed in float64 and return float64 (as the reference's scan keeps the
+input dtype, models/selective_scan.py:52), so its float64 gradchecks hold.
 
 There is no CPU path: CPU tensors raise.  The kernel library must be built.
 """
@@ -22,7 +24,7 @@ import torch
 
 from . import _lib
 
-_FLOAT_IN = (torch.float32, torch.bfloat16)
+_FLOAT_IN = (torch.float32, torch.bfloat16, torch.float64)
 
 
 def _require_cuda(*ts):
@@ -40,6 +42,12 @@ def _rows(t):
 def _in_dtype(*ts):
     dt = ts[0].dtype
     return dt if dt in _FLOAT_IN else torch.float32
+
+
+def _param_dtype(in_dt):
+    """dtype of A, D, delta_bias, h0 and their gradients: float64 with float64 inputs
+    (computed in float64 throughout), else fp32."""
+    return torch.float64 if in_dt == torch.float64 else torch.float32
 
 
 def _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, softplus, in_dt, A_is_log=False):
@@ -65,8 +73,9 @@ def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
     in_dt = _in_dtype(u)
     cast = lambda t: None if t is None else _rows(t.to(in_dt))  # noqa: E731
     u, delta, B, C, z = cast(u), cast(delta), cast(B), cast(C), cast(z)
-    f32 = lambda t: None if t is None else t.detach().float().contiguous()  # noqa: E731
-    A, D, delta_bias, h0 = f32(A), f32(D), f32(delta_bias), f32(h0)
+    pdt = _param_dtype(in_dt)
+    par = lambda t: None if t is None else t.detach().to(pdt).contiguous()  # noqa: E731
+    A, D, delta_bias, h0 = par(A), par(D), par(delta_bias), par(h0)
     if u.dim() != 3 or delta.shape != u.shape or B.dim() != 3 or C.shape != B.shape:
         raise ValueError("expected u, delta (b, L, D) and B, C (b, L, N)")
     b, L, Dm = u.shape
@@ -93,12 +102,13 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
     b, L, Dm = u.shape
     N = A.shape[1]
-    out_dt = out_dtype or in_dt
+    pdt = _param_dtype(in_dt)
+    out_dt = torch.float64 if in_dt == torch.float64 else (out_dtype or in_dt)
     out = torch.empty((b, L, Dm), device=u.device, dtype=out_dt) if write_out else None
-    ck = (torch.empty(lib.swx_scan_checkpoint_floats(b, L, Dm), device=u.device, dtype=torch.float32)
+    ck = (torch.empty(lib.swx_scan_checkpoint_floats(b, L, Dm), device=u.device, dtype=pdt)
           if checkpoints else None)
-    hl = torch.empty((b, Dm, N), device=u.device, dtype=torch.float32) if return_last_state else None
-    ds = torch.empty((b, Dm), device=u.device, dtype=torch.float32) if return_delta_sum else None
+    hl = torch.empty((b, Dm, N), device=u.device, dtype=pdt) if return_last_state else None
+    ds = torch.empty((b, Dm), device=u.device, dtype=pdt) if return_delta_sum else None
     a = _lib.ScanArgs()
     _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt, A_is_log)
     a.out_dtype = _lib.DTYPE_CODES[out_dt]
@@ -107,8 +117,8 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     a.checkpoints = ck.data_ptr() if ck is not None else None
     a.delta_sum = ds.data_ptr() if ds is not None else None
     if pre_out is not None and z is not None:
-        if pre_out.dtype != torch.float32 or not pre_out.is_contiguous() or pre_out.shape != (b, L, Dm):
-            raise ValueError("pre_out must be a dense fp32 (b, L, D) tensor")
+        if pre_out.dtype != pdt or not pre_out.is_contiguous() or pre_out.shape != (b, L, Dm):
+            raise ValueError(f"pre_out must be a dense {pdt} (b, L, D) tensor")
         a.out_pre = pre_out.data_ptr()
     _lib.check(lib.swx_scan_fwd(a, _lib.stream_ptr(u.device)), "swx_scan_fwd")
     if return_delta_sum:
@@ -127,14 +137,16 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     N = A.shape[1]
     dout = _rows(dout.to(in_dt))
     dev = u.device
+    pdt = _param_dtype(in_dt)
     e = lambda *s, dt=in_dt: torch.empty(s, device=dev, dtype=dt)  # noqa: E731
     g = {"du": e(b, L, Dm), "ddelta": e(b, L, Dm), "dB": e(b, L, N), "dC": e(b, L, N),
-         "dA": e(Dm, N, dt=torch.float32)}
+         "dA": e(Dm, N, dt=pdt)}
     g["dz"] = e(b, L, Dm) if z is not None else None
-    g["dD"] = e(Dm, dt=torch.float32) if D is not None else None
-    g["ddelta_bias"] = e(Dm, dt=torch.float32) if delta_bias is not None else None
-    g["dh0"] = e(b, Dm, N, dt=torch.float32) if h0 is not None else None
-    wsb = lib.swx_scan_bwd_workspace_bytes(b, L, Dm)
+    g["dD"] = e(Dm, dt=pdt) if D is not None else None
+    g["ddelta_bias"] = e(Dm, dt=pdt) if delta_bias is not None else None
+    g["dh0"] = e(b, Dm, N, dt=pdt) if h0 is not None else None
+    wsb = (lib.swx_scan_bwd_workspace_bytes_f64 if in_dt == torch.float64
+           else lib.swx_scan_bwd_workspace_bytes)(b, L, Dm)
     ws = torch.empty(max(wsb, 1), device=dev, dtype=torch.uint8)
     a = _lib.ScanArgs()
     _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, delta_softplus, in_dt, A_is_log)
@@ -158,7 +170,7 @@ class SelectiveScanFn(torch.autograd.Function):
     def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, out_dtype,
                 return_last_state, A_is_log):
         need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9))
-        pre = (torch.empty(u.shape, device=u.device, dtype=torch.float32)
+        pre = (torch.empty(u.shape, device=u.device, dtype=_param_dtype(_in_dtype(u)))
                if need_grad and z is not None else None)
         out, ck, hl = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0,
                                    out_dtype, checkpoints=need_grad,

@@ -234,4 +234,8 @@ if __name__ == "__main__":
     only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
     if only:
         args.remove(only)
-    main(args[0] if args else "/root/reference", only)
+    ref = args[0] if args else os.environ.get("SWIFTX_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py <path to the reference checkout> [--only NAME] "
+                 "(or set SWIFTX_REFERENCE)")
+    main(ref, only)

@@ -58,10 +58,12 @@ def test_chunked_equals_whole(bounds):
 
 def test_long_sequence_bf16_eight_chunks():
     """The long-sequence configuration's layout (bf16 u/delta/B/C/z, fp32 state and
-    output) at reduced size, split like 8 ranks."""
+    output) at reduced size, split like 8 ranks, against the oracle run on the same
+    bf16-rounded values (rtol 2e-2, bf16 inputs with fp32 state)."""
     b, L, D = 2, 8 * 512, 256
     inp = config_inputs(b, L, D, 16, seed=4, device=DEV, dtype=torch.bfloat16)
-    whole, _, _ = scan_forward(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"],
-                               inp["delta_bias"], True, out_dtype=torch.float32)
     got = chunked_scan(inp, list(range(0, L + 1, 512)))
-    np.testing.assert_allclose(got.cpu().numpy(), whole.cpu().numpy(), rtol=1e-3, atol=1e-4)
+    n = lambda t: t.double().cpu().numpy()  # noqa: E731
+    want = oracle.scan_fwd(*(n(inp[k]) for k in ("u", "delta", "A", "B", "C")), D=n(inp["D"]), z=n(inp["z"]),
+                           delta_bias=n(inp["delta_bias"]), delta_softplus=True)
+    np.testing.assert_allclose(n(got), want, rtol=2e-2, atol=1e-3 * np.abs(want).max())
