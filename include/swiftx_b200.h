@@ -127,10 +127,14 @@ int swx_scan_fwd(const swx_scan_args* args, void* stream);
  * deterministic: fixed-order sums, no float atomics. */
 int swx_scan_bwd(const swx_scan_args* args, void* stream);
 
-/* How many CTAs per SM swx_scan_bwd would run for these arguments on the current device:
- * 2 when the grid is larger than the SM count and the variant built for two CTAs per SM
- * fits (bf16 inputs), else 1; a negative status on error.  Launches nothing. */
+/* How many CTAs of its main kernel swx_scan_bwd keeps on one SM of the current device for
+ * these arguments (2 on a B200); a negative status on error.  Launches nothing. */
 int swx_scan_bwd_ctas_per_sm(const swx_scan_args* args);
+
+/* Number of time segments swx_scan_bwd walks in parallel for a sequence of seqlen steps
+ * and dim channels (a function of those two alone, so the rows of a batch get the same
+ * bits whatever the batch); a negative status for invalid sizes. */
+int swx_scan_bwd_segments(int64_t seqlen, int64_t dim);
 
 /* Capacity of the static scratch used by swx_scan_bwd_static_scratch: 8 MiB, enough
  * for swx_scan_bwd_workspace_bytes(batch, seqlen, dim) of roughly batch*seqlen*dim up

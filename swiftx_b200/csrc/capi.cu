@@ -7,10 +7,10 @@
 
 namespace swx {
 cudaError_t launch_scan_fwd(const ScanDev& p, int in_dtype, int out_dtype, bool has_z, cudaStream_t st);
-cudaError_t launch_scan_bwd(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st);
-cudaError_t scan_bwd_ctas_per_sm(const ScanDev& p, int in_dtype, bool has_z, int* ctas);
+cudaError_t scan_bwd_seg_ctas_per_sm(const ScanDev& p, int in_dtype, bool has_z, int* ctas);
 cudaError_t launch_scan_fwd_f64(const ScanDev& p, cudaStream_t st);
 cudaError_t launch_scan_bwd_f64(const ScanDev& p, cudaStream_t st);
+cudaError_t launch_scan_bwd_seg(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st);
 }  // namespace swx
 
 namespace {
@@ -29,19 +29,62 @@ bool vec_ok(const void* p, int64_t sb, int64_t sl, int es) {
 constexpr int64_t kAlign = 256;
 int64_t round_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
-struct WsLayout {
-    int64_t bc, a, d, bias, total;
+// Segments of the time-segmented backward, a function of (L, D) alone: results do not
+// depend on the device, and the rows of a batch get bit-identical gradients whether they
+// are passed together or in smaller batches.  Sized for about two 64-channel CTAs per SM
+// of a 148-SM B200 at a batch of 8 rows, with segments of at least 128 steps; the reverse
+// carries are summarised over sub-segments of up to 128 steps that divide a segment.
+struct SegPlan {
+    int64_t seg_len, nseg, sub_len, nsub, first_sub, nblk64;
 };
 
-// es: bytes of one partial sum (4 for fp32 / bf16 inputs, 8 for float64 inputs).
+SegPlan seg_plan(int64_t L, int64_t D) {
+    SegPlan s{};
+    const int64_t nck = (L + 15) / 16;
+    s.nblk64 = (D + 63) / 64;
+    int64_t G = std::max<int64_t>(1, 37 / std::max<int64_t>(1, s.nblk64));   // 8 rows x blocks x G ~ 2 x 148
+    G = std::min<int64_t>(G, std::max<int64_t>(1, nck / 8));
+    const int64_t per = std::max<int64_t>(1, (nck + G - 1) / G);   // checkpoint chunks per segment
+    s.nseg = std::max<int64_t>(1, (nck + per - 1) / per);
+    s.seg_len = 16 * per;
+    s.sub_len = s.seg_len % 128 == 0 ? 128 : s.seg_len % 64 == 0 ? 64 : s.seg_len % 32 == 0 ? 32 : 16;
+    // very long sequences: fewer, longer summaries (at most 128 steps each, staged whole)
+    while ((L + s.sub_len - 1) / s.sub_len > 8192 && s.sub_len < 128 && s.seg_len % (2 * s.sub_len) == 0)
+        s.sub_len *= 2;
+    s.nsub = (L + s.sub_len - 1) / s.sub_len;
+    s.first_sub = s.seg_len / s.sub_len;
+    return s;
+}
+
+struct WsLayout {
+    int64_t bc, a, d, bias, q, s, c, total;
+};
+
+// es: bytes of one partial sum (4 for fp32 / bf16 inputs, 8 for float64 inputs).  fp32 /
+// bf16 inputs use the segmented backward's layout: dB|dC partials per 64-channel block,
+// dA / dD / d(delta_bias) partials per (segment, row), the sub-segment summaries and the
+// segment carries.  float64 inputs: partials per 32-channel block and per row.
 WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
-    const int64_t nblk = (D + 31) / 32;
-    WsLayout w;
+    WsLayout w{};
+    if (es == 8) {
+        const int64_t nblk = (D + 31) / 32;
+        w.bc = 0;
+        w.a = w.bc + round_up(nblk * b * L * 2 * swx::NS * es);
+        w.d = w.a + round_up(b * D * swx::NS * es);
+        w.bias = w.d + round_up(b * D * es);
+        w.q = w.s = w.c = w.bias + round_up(b * D * es);
+        w.total = w.q;
+        return w;
+    }
+    const SegPlan sp = seg_plan(L, D);
     w.bc = 0;
-    w.a = w.bc + round_up(nblk * b * L * 2 * swx::NS * es);
-    w.d = w.a + round_up(b * D * swx::NS * es);
-    w.bias = w.d + round_up(b * D * es);
-    w.total = w.bias + round_up(b * D * es);
+    w.a = w.bc + round_up(sp.nblk64 * b * L * 2 * swx::NS * 4);
+    w.d = w.a + round_up(sp.nseg * b * D * swx::NS * 4);
+    w.bias = w.d + round_up(sp.nseg * b * D * 4);
+    w.q = w.bias + round_up(sp.nseg * b * D * 4);
+    w.s = w.q + round_up(sp.nsub * b * D * swx::NS * 4);
+    w.c = w.s + round_up(sp.nsub * b * D * 4);
+    w.total = w.c + round_up(sp.nseg * b * D * swx::NS * 4);
     return w;
 }
 
@@ -176,7 +219,13 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     p.ws_d = reinterpret_cast<float*>(ws + w.d);
     p.ws_bias = reinterpret_cast<float*>(ws + w.bias);
     if (f64) return from_cuda(swx::launch_scan_bwd_f64(p, static_cast<cudaStream_t>(stream)));
-    return from_cuda(swx::launch_scan_bwd(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
+    const SegPlan sp = seg_plan(a->seqlen, a->dim);
+    p.seg_len = (int)sp.seg_len; p.nseg = (int)sp.nseg; p.sub_len = (int)sp.sub_len;
+    p.nsub = (int)sp.nsub; p.first_sub = (int)sp.first_sub; p.nblk64 = (int)sp.nblk64;
+    p.ws_q = reinterpret_cast<float*>(ws + w.q);
+    p.ws_s = reinterpret_cast<float*>(ws + w.s);
+    p.ws_c = reinterpret_cast<float*>(ws + w.c);
+    return from_cuda(swx::launch_scan_bwd_seg(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
 }
 
 int swx_scan_bwd_ctas_per_sm(const swx_scan_args* a) {
@@ -185,8 +234,13 @@ int swx_scan_bwd_ctas_per_sm(const swx_scan_args* a) {
     if (a->in_dtype == SWX_DTYPE_F64) return 1;
     const swx::ScanDev p = pack(a);
     int ctas = 1;
-    if (swx::scan_bwd_ctas_per_sm(p, a->in_dtype, a->z != nullptr, &ctas) != cudaSuccess) return -SWX_ERR_CUDA;
+    if (swx::scan_bwd_seg_ctas_per_sm(p, a->in_dtype, a->z != nullptr, &ctas) != cudaSuccess) return -SWX_ERR_CUDA;
     return ctas;
+}
+
+int swx_scan_bwd_segments(int64_t seqlen, int64_t dim) {
+    if (!sizes_ok(1, seqlen, dim)) return -SWX_ERR_INVALID_ARG;
+    return (int)seg_plan(seqlen, dim).nseg;
 }
 
 }  // extern "C"

@@ -22,6 +22,7 @@ reference.
 """
 import math
 from dataclasses import dataclass
+from fractions import Fraction
 
 import torch
 import torch.nn as nn
@@ -94,69 +95,129 @@ def _bf16_copies(weights, flat=None):
     return out
 
 
-def init_A_log(d_inner, d_state):
-    """S4D-real: A_n = -(n+1) for every channel, stored as log(-A) (models/ssm.py:43-51)."""
-    A = torch.arange(1, d_state + 1, dtype=torch.float32).repeat(d_inner, 1)
-    return torch.log(A)
+# ----------------------------------------------------------------- parameter table
+# The block's parameters as data: state_dict key, shape (from the block's dimensions),
+# initial distribution, and whether it is excluded from weight decay.  The keys and
+# shapes are the reference's (models/sift_block.py:30-101) so its checkpoints load; the
+# distributions are the ones its initialisers produce:
+#   "fan_in"      U(-s/sqrt(fan_in), +s/sqrt(fan_in)), fan_in = every dim but the first
+#                 (torch's default for Linear / Conv1d weights, and dt_proj.weight's
+#                 U(+-dt_rank^-1/2)); s = 1/sqrt(n_layers) for out_proj inside a backbone
+#   "fan_in_of:K" the same bound as parameter K's (a Conv1d bias)
+#   "dt_bias"     inverse softplus of dt, log-uniform over each timescale group's range,
+#                 floored at 1e-4 (models/ssm.py:54-71)
+#   "s4d_log"     log(n + 1) for state n in every channel: A = -(n + 1) (models/ssm.py:43-51)
+#   "ones" / "zeros"
+_BLOCK_TABLE = (
+    # key              shape                                        init             no decay  when
+    ("A_log",          lambda m: (m.d_inner, m.d_state),             "s4d_log",       True,  None),
+    ("D",              lambda m: (m.d_inner,),                       "ones",          True,  None),
+    ("in_proj.weight", lambda m: (2 * m.d_inner, m.d_model),         "fan_in",        False, None),
+    ("in_proj.bias",   lambda m: (2 * m.d_inner,),                   "zeros",         False, "bias"),
+    ("conv1d.weight",  lambda m: (m.d_inner, 1, m.d_conv),           "fan_in",        False, None),
+    ("conv1d.bias",    lambda m: (m.d_inner,),                       "fan_in_of:conv1d.weight", False, "conv_bias"),
+    ("x_proj.weight",  lambda m: (m.dt_rank + 2 * m.d_state, m.d_inner), "fan_in",    False, None),
+    ("dt_proj.weight", lambda m: (m.d_inner, m.dt_rank),             "fan_in",        False, None),
+    ("dt_proj.bias",   lambda m: (m.d_inner,),                       "dt_bias",       False, None),
+    ("pathway.weight", lambda m: (m.n_groups, m.d_inner),            "zeros",         False, "pathway"),
+    ("pathway.bias",   lambda m: (m.n_groups,),                      "zeros",         False, "pathway"),
+    ("out_proj.weight", lambda m: (m.d_model, m.d_inner),            "fan_in",        False, None),
+    ("out_proj.bias",  lambda m: (m.d_model,),                       "zeros",         False, "bias"),
+)
 
 
-def init_dt_proj(dt_proj, dt_rank, dt_min=1e-3, dt_max=1e-1, dt_init_floor=1e-4, dt_scale=1.0):
-    """softplus(bias) log-uniform in [dt_min, dt_max]; weights U(+-dt_rank^-0.5)
-    (models/ssm.py:54-71)."""
-    std = dt_rank ** -0.5 * dt_scale
-    nn.init.uniform_(dt_proj.weight, -std, std)
-    d_inner = dt_proj.out_features
-    dt = torch.exp(torch.rand(d_inner) * (math.log(dt_max) - math.log(dt_min))
-                   + math.log(dt_min)).clamp(min=dt_init_floor)
-    inv_dt = dt + torch.log(-torch.expm1(-dt))        # inverse softplus
-    with torch.no_grad():
-        dt_proj.bias.copy_(inv_dt)
-    dt_proj.bias._no_reinit = True
+class _Slot(nn.Module):
+    """The tensors of one named projection (``weight`` and, when it has one, ``bias``),
+    so that state_dict keys read ``<name>.weight`` / ``<name>.bias``."""
+
+    def __init__(self):
+        super().__init__()
+        self.register_parameter("bias", None)       # replaced when the table gives one
+
+
+def _fan_in(t):
+    return math.prod(t.shape[1:])
+
+
+def _log_uniform(n, lo, hi):
+    return torch.exp(torch.empty(n).uniform_(math.log(lo), math.log(hi)))
+
+
+def _inverse_softplus(y):
+    """x with softplus(x) = y: y + log(1 - exp(-y))."""
+    return y + torch.log(-torch.expm1(-y))
 
 
 class SiftBlock(nn.Module):
+    """The Sift mixer (models/sift_block.py:30) on the B200 kernels.  Same constructor
+    arguments, parameter names and shapes as the reference; built from _BLOCK_TABLE."""
+
     def __init__(self, d_model, d_state=16, d_conv=4, expand=2, dt_rank="auto", dt_min=1e-3,
                  dt_max=1e-1, conv_bias=True, bias=False, scan_impl="fast", scan_mode="auto",
-                 timescales=None, pathway_gate=False):
+                 timescales=None, pathway_gate=False, out_scale=1.0):
         super().__init__()
-        self.d_model = d_model
-        self.d_state = d_state
-        self.d_conv = d_conv
+        self.d_model, self.d_state, self.d_conv = d_model, d_state, d_conv
         self.d_inner = expand * d_model
-        self.dt_rank = math.ceil(d_model / 16) if dt_rank == "auto" else dt_rank
-        self.scan_impl = scan_impl          # every impl / mode runs the same kernel
-        self.scan_mode = scan_mode
-        self.in_proj = nn.Linear(d_model, 2 * self.d_inner, bias=bias)
-        self.conv1d = nn.Conv1d(self.d_inner, self.d_inner, kernel_size=d_conv, groups=self.d_inner,
-                                padding=d_conv - 1, bias=conv_bias)
-        self.x_proj = nn.Linear(self.d_inner, self.dt_rank + 2 * d_state, bias=False)
-        self.dt_proj = nn.Linear(self.dt_rank, self.d_inner, bias=True)
-        init_dt_proj(self.dt_proj, self.dt_rank, dt_min, dt_max)
-        # SiftX multi-timescale groups (models/sift_block.py:74-93): contiguous channel
-        # groups with their own dt range, and an optional per-token softmax over groups
+        self.dt_rank = -(-d_model // 16) if dt_rank == "auto" else dt_rank
+        self.scan_impl, self.scan_mode = scan_impl, scan_mode    # every impl / mode runs the same kernels
+        # SiftX multi-timescale groups (models/sift_block.py:74-93): contiguous channel groups
+        # of nearly equal size, each with its own dt range; pathway_gate adds a per-token
+        # softmax over the groups
         self.timescales = [tuple(t) for t in timescales] if timescales else None
-        self.n_groups = len(self.timescales) if self.timescales else 1
-        self.register_buffer("group_of", torch.zeros(self.d_inner, dtype=torch.long), persistent=False)
-        if self.timescales:
-            bounds = torch.linspace(0, self.d_inner, len(self.timescales) + 1).round().long().tolist()
-            for i, (lo, hi) in enumerate(self.timescales):
-                a, b = bounds[i], bounds[i + 1]
-                self.group_of[a:b] = i
-                tmp = nn.Linear(self.dt_rank, b - a, bias=True)
-                init_dt_proj(tmp, self.dt_rank, lo, hi)
-                with torch.no_grad():
-                    self.dt_proj.bias[a:b] = tmp.bias
-        self.pathway = None
-        if pathway_gate and self.n_groups > 1:
-            self.pathway = nn.Linear(self.d_inner, self.n_groups)
-            nn.init.zeros_(self.pathway.weight)
-            nn.init.zeros_(self.pathway.bias)
-            self.pathway.bias._no_reinit = True
-        self.A_log = nn.Parameter(init_A_log(self.d_inner, d_state))
-        self.A_log._no_weight_decay = True
-        self.D = nn.Parameter(torch.ones(self.d_inner))
-        self.D._no_weight_decay = True
-        self.out_proj = nn.Linear(self.d_inner, d_model, bias=bias)
+        ranges = self.timescales or [(dt_min, dt_max)]
+        self.n_groups = len(ranges)
+        G, Dn = self.n_groups, self.d_inner
+        edges = [round(Fraction(i * Dn, G)) for i in range(G + 1)]     # ties to even, as torch.round
+        group_of = torch.zeros(Dn, dtype=torch.long)
+        for i in range(G):
+            group_of[edges[i]:edges[i + 1]] = i
+        self.register_buffer("group_of", group_of, persistent=False)
+        present = {"bias": bias, "conv_bias": conv_bias, "pathway": bool(pathway_gate and G > 1)}
+        for key, shape, rule, no_decay, when in _BLOCK_TABLE:
+            if when is not None and not present[when]:
+                continue
+            slot_name, _, leaf = key.rpartition(".")
+            owner = self
+            if slot_name:
+                if not hasattr(self, slot_name) or getattr(self, slot_name) is None:
+                    self.add_module(slot_name, _Slot())
+                owner = getattr(self, slot_name)
+            prm = nn.Parameter(torch.empty(shape(self)))
+            if no_decay:
+                prm._no_weight_decay = True
+            if leaf in owner._parameters:
+                del owner._parameters[leaf]
+            owner.register_parameter(leaf, prm)
+        if not present["pathway"]:
+            self.pathway = None
+        self._initialise(ranges, out_scale)
+
+    @torch.no_grad()
+    def _initialise(self, ranges, out_scale=1.0):
+        """Draw every parameter from its distribution in _BLOCK_TABLE."""
+        params = dict(self.named_parameters())
+        for key, _, rule, _, _ in _BLOCK_TABLE:
+            t = params.get(key)
+            if t is None:
+                continue
+            if rule == "ones":
+                t.fill_(1.0)
+            elif rule == "zeros":
+                t.zero_()
+            elif rule == "s4d_log":
+                t.copy_(torch.log(torch.arange(1, self.d_state + 1, dtype=torch.float32)).expand_as(t))
+            elif rule.startswith("fan_in"):
+                ref = params[rule.split(":", 1)[1]] if ":" in rule else t
+                bound = 1.0 / math.sqrt(_fan_in(ref))
+                if key == "out_proj.weight":
+                    bound *= out_scale
+                t.uniform_(-bound, bound)
+            elif rule == "dt_bias":
+                edges = [round(Fraction(i * self.d_inner, len(ranges))) for i in range(len(ranges) + 1)]
+                for (lo, hi), a, b in zip(ranges, edges[:-1], edges[1:]):
+                    t[a:b] = _inverse_softplus(_log_uniform(b - a, lo, hi).clamp(min=1e-4))
+            else:
+                raise ValueError(f"unknown init rule {rule!r} for {key}")
 
     def _split(self, x):
         x_dbl = _linear(x, self.x_proj.weight)
@@ -187,13 +248,14 @@ class SiftBlock(nn.Module):
     def _mix_pathways(self, y, x):
         """SiftX: reweight the channel groups per token, softmax x G (1 at init)
         (models/sift_block.py:137-142)."""
-        w = torch.softmax(self.pathway(x), dim=-1) * self.n_groups
+        w = torch.softmax(F.linear(x, self.pathway.weight, self.pathway.bias), dim=-1) * self.n_groups
         return y * w[..., self.group_of]
 
     def allocate_state(self, batch, device=None, dtype=torch.float32):
-        conv_state = torch.zeros(batch, self.d_inner, self.d_conv, device=device, dtype=dtype)
-        ssm_state = torch.zeros(batch, self.d_inner, self.d_state, device=device, dtype=dtype)
-        return conv_state, ssm_state
+        """(conv window (b, D, d_conv), SSM state (b, D, d_state)), zeroed: the recurrent
+        state that step() updates in place (models/sift_block.py:148-151 layout)."""
+        shapes = ((batch, self.d_inner, self.d_conv), (batch, self.d_inner, self.d_state))
+        return tuple(torch.zeros(sh, device=device, dtype=dtype) for sh in shapes)
 
     def step(self, hidden, state):
         """hidden: (b, d_model) one token; state (conv_state, ssm_state) updated in place."""
@@ -248,6 +310,8 @@ def _norm_out_dtype():
 
 @dataclass
 class SiftConfig:
+    """Model hyper-parameters; field names and defaults are the reference's
+    (models/sift_model.py:30), so its YAML configs and call sites construct it unchanged."""
     vocab_size: int = 65
     d_model: int = 128
     n_layers: int = 4
@@ -262,13 +326,16 @@ class SiftConfig:
     pathway_gate: bool = False
 
 
-class ResidualBlock(nn.Module):
-    def __init__(self, cfg):
+class _Layer(nn.Module):
+    """One pre-norm residual layer, x + mixer(norm(x)); the attribute names ``norm`` and
+    ``mixer`` give the reference's state_dict keys (backbone.layers.<i>.norm / .mixer)."""
+
+    def __init__(self, cfg, out_scale):
         super().__init__()
         self.norm = RMSNorm(cfg.d_model)
         self.mixer = SiftBlock(cfg.d_model, d_state=cfg.d_state, d_conv=cfg.d_conv, expand=cfg.expand,
                                dt_rank=cfg.dt_rank, scan_impl=cfg.scan_impl, scan_mode=cfg.scan_mode,
-                               timescales=cfg.timescales, pathway_gate=cfg.pathway_gate)
+                               timescales=cfg.timescales, pathway_gate=cfg.pathway_gate, out_scale=out_scale)
 
     def forward(self, x):
         return x + self.mixer(self.norm(x))
@@ -278,22 +345,15 @@ class ResidualBlock(nn.Module):
 
 
 class SiftBackbone(nn.Module):
+    """n_layers residual layers and the final norm.  Inside a backbone each layer's
+    out_proj is drawn with its bound scaled by 1/sqrt(n_layers)."""
+
     def __init__(self, cfg):
         super().__init__()
-        self.layers = nn.ModuleList([ResidualBlock(cfg) for _ in range(cfg.n_layers)])
+        scale = 1.0 / math.sqrt(max(1, cfg.n_layers))
+        self.layers = nn.ModuleList(_Layer(cfg, scale) for _ in range(cfg.n_layers))
         self.norm_f = RMSNorm(cfg.d_model)
         self.fuse_residual_norm = True
-        self._init_weights(cfg.n_layers)
-
-    def _init_weights(self, n_layers):
-        for _, m in self.named_modules():
-            if isinstance(m, nn.Linear) and m.bias is not None and not getattr(m.bias, "_no_reinit", False):
-                nn.init.zeros_(m.bias)
-        for layer in self.layers:
-            w = layer.mixer.out_proj.weight
-            nn.init.kaiming_uniform_(w, a=math.sqrt(5))
-            with torch.no_grad():
-                w /= math.sqrt(n_layers)
 
     def forward(self, x):
         if not self.fuse_residual_norm or not self.layers:
@@ -310,15 +370,22 @@ class SiftBackbone(nn.Module):
 
 
 class SiftLM(nn.Module):
+    """Byte-level language model: token embedding (N(0, 0.02)), backbone, head tied to the
+    embedding when cfg.tie_embeddings (state_dict keys embedding.weight, backbone.*,
+    lm_head.weight, as models/sift_model.py:92-101)."""
+
     def __init__(self, cfg: SiftConfig):
         super().__init__()
         self.cfg = cfg
-        self.embedding = nn.Embedding(cfg.vocab_size, cfg.d_model)
-        nn.init.normal_(self.embedding.weight, std=0.02)
+        self.embedding = _Slot()
+        self.embedding.weight = nn.Parameter(torch.empty(cfg.vocab_size, cfg.d_model).normal_(0.0, 0.02))
         self.backbone = SiftBackbone(cfg)
-        self.lm_head = nn.Linear(cfg.d_model, cfg.vocab_size, bias=False)
+        self.lm_head = _Slot()
         if cfg.tie_embeddings:
             self.lm_head.weight = self.embedding.weight
+        else:
+            bound = 1.0 / math.sqrt(cfg.d_model)
+            self.lm_head.weight = nn.Parameter(torch.empty(cfg.vocab_size, cfg.d_model).uniform_(-bound, bound))
         self.bf16_weight_copies = True      # under bf16 autocast: see forward
 
     def forward(self, idx, targets=None):
@@ -331,7 +398,7 @@ class SiftLM(nn.Module):
         if embedding_kernels.supported(idx, w) and torch.is_grad_enabled():
             x = embedding_kernels.embedding(idx, w)
         else:
-            x = self.embedding(idx)
+            x = F.embedding(idx, w)
         prev = _W16
         if self.bf16_weight_copies and w.is_cuda and torch.is_autocast_enabled("cuda") \
                 and torch.get_autocast_dtype("cuda") == torch.bfloat16:
@@ -356,32 +423,38 @@ class SiftLM(nn.Module):
         return ws if all(p.dtype == torch.float32 for p in ws) else None
 
     def allocate_state(self, batch, device=None):
-        return [l.mixer.allocate_state(batch, device) for l in self.backbone.layers]
+        """One (conv window, SSM state) pair per layer, zeroed."""
+        return [layer.mixer.allocate_state(batch, device) for layer in self.backbone.layers]
 
     def step(self, token, state):
-        x = self.embedding(token)
-        for layer, s in zip(self.backbone.layers, state):
-            x = layer.step(x, s)
-        return _linear(self.backbone.norm_f(x), self.lm_head.weight, self.lm_head.bias)
+        """Logits for one token per row, advancing ``state`` (from allocate_state) in place:
+        the recurrent form of forward (models/sift_model.py:115)."""
+        h = F.embedding(token, self.embedding.weight)
+        for layer, st in zip(self.backbone.layers, state):
+            h = layer.step(h, st)
+        return _linear(self.backbone.norm_f(h), self.lm_head.weight, self.lm_head.bias)
 
     @torch.no_grad()
     def generate(self, idx, max_new_tokens, temperature=1.0, top_k=None, graphed=False):
-        """Prompt then sampled tokens through the recurrent step (models/sift_model.py
-        generate).  graphed=True replays each step from one CUDA graph (GraphedStep)."""
+        """The prompt ``idx`` (b, T) followed by ``max_new_tokens`` sampled tokens, produced
+        through the recurrent step (the prompt is consumed token by token, then each new
+        token is sampled from the last logits and fed back).  graphed=True replays each
+        step from one CUDA graph (GraphedStep)."""
         if graphed:
             stepper = GraphedStep(self, idx.shape[0], idx.device)
-            step = lambda tok: stepper(tok).clone()  # noqa: E731
+            advance = lambda tok: stepper(tok).clone()  # noqa: E731
         else:
             state = self.allocate_state(idx.shape[0], idx.device)
-            step = lambda tok: self.step(tok, state)  # noqa: E731
+            advance = lambda tok: self.step(tok, state)  # noqa: E731
         logits = None
-        for t in range(idx.shape[1]):
-            logits = step(idx[:, t])
+        for tok in idx.unbind(1):
+            logits = advance(tok)
         out = [idx]
-        for _ in range(max_new_tokens):
-            nxt = sample(logits, temperature, top_k)
-            out.append(nxt[:, None])
-            logits = step(nxt)
+        for i in range(max_new_tokens):
+            tok = sample(logits, temperature, top_k)
+            out.append(tok.unsqueeze(1))
+            if i + 1 < max_new_tokens:          # the last token's logits are not needed
+                logits = advance(tok)
         return torch.cat(out, dim=1)
 
 
@@ -452,14 +525,19 @@ class GraphedStep:
 
 
 def sample(logits, temperature=1.0, top_k=None):
+    """One token id per row from (b, vocab) logits: greedy at temperature 0, otherwise
+    drawn from softmax(logits / temperature), restricted to the top_k largest when top_k
+    is given (exactly k candidates; the reference keeps every logit tied with the k-th)."""
     if temperature == 0:
         return logits.argmax(-1)
-    logits = logits / temperature
-    if top_k is not None:
-        v, _ = torch.topk(logits, min(top_k, logits.size(-1)))
-        logits = logits.masked_fill(logits < v[:, [-1]], float("-inf"))
-    return torch.multinomial(F.softmax(logits.float(), -1), 1).squeeze(-1)
+    scaled = logits.float() / temperature
+    if top_k is None:
+        return torch.multinomial(torch.softmax(scaled, -1), 1).squeeze(-1)
+    vals, ids = scaled.topk(min(top_k, scaled.shape[-1]), dim=-1)
+    pick = torch.multinomial(torch.softmax(vals, -1), 1)
+    return ids.gather(-1, pick).squeeze(-1)
 
 
 def count_params(model):
-    return sum(p.numel() for p in model.parameters())
+    """Number of parameter values (a tied head counted once)."""
+    return sum(t.numel() for t in {id(p): p for p in model.parameters()}.values())

@@ -47,7 +47,16 @@ def test_sizes_of_checkpoints_and_workspace():
     lib = _lib.load()
     assert lib.swx_scan_checkpoint_floats(8, 2048, 512) == 8 * 128 * 512 * 16
     assert lib.swx_scan_checkpoint_floats(1, 17, 3) == 1 * 2 * 3 * 16
-    assert lib.swx_scan_bwd_workspace_bytes(8, 2048, 512) >= 16 * 8 * 2048 * 32 * 4
+    # dB|dC partials per 64-channel block (8 x 8 rows x 2048 steps x 32 floats), plus the
+    # per-segment partials, sub-segment summaries and segment carries
+    nseg = lib.swx_scan_bwd_segments(2048, 512)
+    assert nseg == 4 and lib.swx_scan_bwd_segments(512, 512) == 4 and lib.swx_scan_bwd_segments(64, 512) == 1
+    assert lib.swx_scan_bwd_segments(65536, 2048) == 1 and lib.swx_scan_bwd_segments(-1, 8) < 0
+    ws = lib.swx_scan_bwd_workspace_bytes(8, 2048, 512)
+    assert ws >= 8 * 8 * 2048 * 32 * 4 + nseg * 8 * 512 * (16 + 2) * 4 + (2048 // 128) * 8 * 512 * 17 * 4
+    assert lib.swx_scan_bwd_workspace_bytes(65535, 1 << 30, 1 << 30) == -1
+    assert lib.swx_scan_checkpoint_floats(-1, 4, 4) == -1
+    assert lib.swx_scan_bwd_workspace_bytes_f64(8, 2048, 512) >= 16 * 8 * 2048 * 32 * 8
     # one (weight, bias) partial per (row, 16-step time tile, channel): 2 rows x 9 tiles x 8 ch x (4+1) floats
     assert lib.swx_conv1d_bwd_workspace_bytes(2, 130, 8, 4) == 2 * 9 * 8 * 5 * 4
     # one (vocab, dim) fp32 partial per token slice; slices hold >= 128 tokens
