@@ -312,6 +312,12 @@ int64_t swx_embedding_args_size(void);
 int64_t swx_embedding_bwd_workspace_bytes(int64_t ntok, int64_t vocab, int64_t dim);
 int swx_embedding_bwd(const swx_embedding_args* args, void* stream);
 
+/* Diagnostic: y[i] = 2^x[i] computed by the FMA-pipe exponential the scan backward uses
+ * for part of its decays (a degree-5 minimax polynomial after rounding x to an integer
+ * part; x clamped to [-125, 127]), so its accuracy can be checked on the device.  x, y:
+ * device fp32 arrays of n values.  Not part of any reference interface. */
+int swx_exp2_fma_eval(const float* x, float* y, int64_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -148,6 +148,8 @@ def load():
     lib.swx_scan_bwd_ctas_per_sm.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_scan_bwd_segments.restype = ctypes.c_int
     lib.swx_scan_bwd_segments.argtypes = [i64, i64]
+    lib.swx_exp2_fma_eval.restype = ctypes.c_int
+    lib.swx_exp2_fma_eval.argtypes = [vp, vp, i64, vp]
     lib.swx_rmsnorm_bwd_workspace_bytes.restype = i64
     lib.swx_rmsnorm_bwd_workspace_bytes.argtypes = [i64]
     lib.swx_embedding_bwd_workspace_bytes.restype = i64

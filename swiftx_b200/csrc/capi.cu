@@ -57,13 +57,12 @@ SegPlan seg_plan(int64_t L, int64_t D) {
 }
 
 struct WsLayout {
-    int64_t bc, a, d, bias, q, s, c, total;
+    int64_t bc, a, d, bias, q, s, total;
 };
 
 // es: bytes of one partial sum (4 for fp32 / bf16 inputs, 8 for float64 inputs).  fp32 /
 // bf16 inputs use the segmented backward's layout: dB|dC partials per 64-channel block,
-// dA / dD / d(delta_bias) partials per (segment, row), the sub-segment summaries and the
-// segment carries.  float64 inputs: partials per 32-channel block and per row.
+// dA / dD / d(delta_bias) partials per (segment, row) and the sub-segment summaries.  float64 inputs: partials per 32-channel block and per row.
 WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
     WsLayout w{};
     if (es == 8) {
@@ -72,7 +71,7 @@ WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
         w.a = w.bc + round_up(nblk * b * L * 2 * swx::NS * es);
         w.d = w.a + round_up(b * D * swx::NS * es);
         w.bias = w.d + round_up(b * D * es);
-        w.q = w.s = w.c = w.bias + round_up(b * D * es);
+        w.q = w.s = w.bias + round_up(b * D * es);
         w.total = w.q;
         return w;
     }
@@ -83,8 +82,7 @@ WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
     w.bias = w.d + round_up(sp.nseg * b * D * 4);
     w.q = w.bias + round_up(sp.nseg * b * D * 4);
     w.s = w.q + round_up(sp.nsub * b * D * swx::NS * 4);
-    w.c = w.s + round_up(sp.nsub * b * D * 4);
-    w.total = w.c + round_up(sp.nseg * b * D * swx::NS * 4);
+    w.total = w.s + round_up(sp.nsub * b * D * 4);
     return w;
 }
 
@@ -224,7 +222,6 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     p.nsub = (int)sp.nsub; p.first_sub = (int)sp.first_sub; p.nblk64 = (int)sp.nblk64;
     p.ws_q = reinterpret_cast<float*>(ws + w.q);
     p.ws_s = reinterpret_cast<float*>(ws + w.s);
-    p.ws_c = reinterpret_cast<float*>(ws + w.c);
     return from_cuda(swx::launch_scan_bwd_seg(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
 }
 

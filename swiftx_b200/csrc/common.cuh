@@ -74,6 +74,32 @@ __device__ __forceinline__ float2 ex2x2(float2 x) { return make_float2(ex2(x.x),
 
 __device__ __forceinline__ float2 rcp2(float2 x) { return make_float2(rcp(x.x), rcp(x.y)); }
 
+// 2^x of two values on the FMA pipe instead of the MUFU unit (which runs at 16 results per
+// clock per SM, an eighth of the FMA pipe): x = j + r with j = rint(x) from the
+// round-to-integer constant 1.5 * 2^23 and |r| <= 1/2, then a degree-5 polynomial for
+// 2^r on [-1/2, 1/2] -- the minimax fit of the relative error by a Remez exchange
+// (fit_exp2_poly.py; 7.5e-8 for the float64 fit, about 2e-7 as evaluated in fp32, the
+// order of ex2.approx) -- and 2^j added to the exponent field.
+// x is clamped to [-125, 127]: below that a decay of ~2^-125 stands for 0 (its
+// contribution is far below fp32 resolution of the sums it enters), above it the result
+// stays finite where ex2.approx overflows.
+__device__ __forceinline__ float2 ex2x2_fma(float2 x) {
+    x.x = fminf(fmaxf(x.x, -125.f), 127.f);
+    x.y = fminf(fmaxf(x.y, -125.f), 127.f);
+    const float2 t = add2(x, bc2(12582912.f));          // 1.5 * 2^23 + rint(x)
+    const float2 j = add2(t, bc2(-12582912.f));         // rint(x), exact
+    const float2 r = fma2(j, bc2(-1.f), x);              // x - j, exact
+    float2 q = bc2(1.3276472454890609e-3f);
+    q = fma2(q, r, bc2(9.675540961325169e-3f));
+    q = fma2(q, r, bc2(5.550713092088699e-2f));
+    q = fma2(q, r, bc2(2.4022120237350464e-1f));
+    q = fma2(q, r, bc2(6.931469440460205e-1f));
+    q = fma2(q, r, bc2(1.0000001192092896f));
+    // low mantissa bits of t hold j: (bits(t) << 23) = j << 23 (mod 2^32)
+    return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                       __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+}
+
 // softplus of two values (torch threshold 20) and its derivative sigmoid(x), sharing
 // e = exp(x).  For e < 1/16, log1p(e) is its alternating Taylor series through e^6
 // (relative truncation error below e^6/7 < 3e-9) because lg2.approx has an absolute

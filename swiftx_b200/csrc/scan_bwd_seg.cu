@@ -7,12 +7,11 @@
 //   1. summary (scan_bwd_summary_kernel): every sub-segment of sub_len steps after the
 //      first segment is walked backwards from a zero carry; it leaves its local outgoing
 //      carry Q = a_t0 g_t0 and the sum of its delta_eff (its decay is exp(A * sum)).
-//   2. carry (scan_bwd_carry_kernel): per (row, channel, state), the carries are chained
-//      from the end of the sequence, c <- Q + exp(A * S) c, and the value that enters each
-//      segment is kept.
-//   3. main (scan_bwd_seg_kernel): each CTA owns 64 channels of one row for one segment
-//      and walks its 16-step checkpoint chunks last to first, starting from that carry.
-//   4. finalize: fixed-order sums of the partials (dB, dC over channel blocks; dA, dD,
+//   2. main (scan_bwd_seg_kernel): each CTA owns 64 channels of one row for one segment.
+//      Its prologue chains the carries of the later sub-segments from the end of the
+//      sequence, c <- Q + exp(A * S) c, to the value that enters its segment; then it
+//      walks its 16-step checkpoint chunks last to first, starting from that carry.
+//   3. finalize: fixed-order sums of the partials (dB, dC over channel blocks; dA, dD,
 //      d(delta_bias) over segments and rows).
 //
 // Main kernel layout: a warp covers 16 channels x 16 states; lane (q, j) = (lane >> 2,
@@ -67,49 +66,63 @@ __device__ __forceinline__ void store2(__nv_bfloat16* q, float2 v) {
 // ===================================================================== 1. summaries
 // Thread = one channel of one row, all 16 states; walks its sub-segment backwards from a
 // zero carry.  The sub-segment's C rows (the same for every thread of the CTA) are staged
-// in shared memory once; each thread's delta / dout / z values are loaded four steps at a
-// time, one block ahead of the arithmetic.
-constexpr int SUM_MAXLEN = 128;           // longest sub-segment staged whole (sub_len <= 128)
+// in shared memory once; the CTA's delta / dout / z rows arrive in 16-step blocks through
+// a two-slot cp.async pipeline, one block ahead of the arithmetic.  The decays of the
+// first SUM_FMA_PAIRS state pairs are computed on the FMA pipe (ex2x2_fma), the others on
+// the MUFU unit, which this kernel otherwise saturates.
+constexpr int SUM_MAXLEN = 128;           // longest sub-segment (sub_len <= 128)
+constexpr int SUM_BLK = 16;               // steps per staged block
+constexpr int SUM_FMA_PAIRS = 2;          // of the 8 state pairs
 
 template <typename Tin>
-struct SumIn {
-    float raw[4], dov[4], zv[4];
+struct SumSmem {
+    float C[SUM_MAXLEN][NS];
+    Tin dl[2][SUM_BLK][SUM_THREADS];
+    Tin dout[2][SUM_BLK][SUM_THREADS];
+    Tin z[2][SUM_BLK][SUM_THREADS];
 };
 
 template <typename Tin, bool HAS_Z>
-__device__ __forceinline__ void sum_load(SumIn<Tin>& x, const Tin* gdl, const Tin* gdo, const Tin* gz,
-                                         const ScanDev& p, int tb, int t0, float bias) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int64_t t = max(tb - i, t0);
-        x.raw[i] = Elem<Tin>::to_f(gdl[t * p.dl_sl]) + bias;
-        x.dov[i] = Elem<Tin>::to_f(gdo[t * p.dout_sl]);
-        x.zv[i] = HAS_Z ? Elem<Tin>::to_f(gz[t * p.z_sl]) : 0.f;
-    }
-}
-
-template <typename Tin, bool HAS_Z>
 __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const ScanDev p) {
-    __shared__ __align__(16) float Cs[SUM_MAXLEN][NS];
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    SumSmem<Tin>& S = *reinterpret_cast<SumSmem<Tin>*>(smem_raw);
+    const int tid = threadIdx.x;
     const int nxb = (p.D + SUM_THREADS - 1) / SUM_THREADS;
     const int64_t blk = blockIdx.x;                      // (sub-segment, row, channel block)
-    const int d = (int)(blk % nxb) * SUM_THREADS + threadIdx.x;
+    const int d0 = (int)(blk % nxb) * SUM_THREADS;
+    const int d = d0 + tid;
     const int bi = (int)((blk / nxb) % p.b);
     const int ss = p.first_sub + (int)(blk / ((int64_t)nxb * p.b));
+    const int nd = min(SUM_THREADS, p.D - d0);
     const bool ok = d < p.D;
     const int dc = ok ? d : p.D - 1;
     const int t0 = ss * p.sub_len, t1 = min(p.L, t0 + p.sub_len), nt = t1 - t0;
-    const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + dc;
-    const Tin* gdo = static_cast<const Tin*>(p.dout) + bi * p.dout_sb + dc;
-    const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + dc : nullptr;
+    const int nblk = (nt + SUM_BLK - 1) / SUM_BLK;
+    const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + d0;
+    const Tin* gdo = static_cast<const Tin*>(p.dout) + bi * p.dout_sb + d0;
+    const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + d0 : nullptr;
     const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
-    const float bias = p.dbias ? p.dbias[dc] : 0.f;
-    SumIn<Tin> cur, nxt;
-    sum_load<Tin, HAS_Z>(cur, gdl, gdo, gz, p, t1 - 1, t0, bias);
-    for (int i = threadIdx.x; i < nt * NS; i += SUM_THREADS) {
+
+    // block k of the walk covers steps [hi - SUM_BLK, hi), hi = t1 - k * SUM_BLK, clipped at t0
+    auto issue = [&](int k) {
+        if (k < nblk) {
+            const int hi = t1 - k * SUM_BLK, lo = max(t0, hi - SUM_BLK), rv = hi - lo, r = k & 1;
+            stage_tile<Tin, SUM_THREADS>(&S.dl[r][0][0], gdl + (int64_t)lo * p.dl_sl, p.dl_sl, SUM_BLK, rv, nd,
+                                         p.vec_dl, tid, SUM_THREADS);
+            stage_tile<Tin, SUM_THREADS>(&S.dout[r][0][0], gdo + (int64_t)lo * p.dout_sl, p.dout_sl, SUM_BLK, rv,
+                                         nd, p.vec_dout, tid, SUM_THREADS);
+            if (HAS_Z)
+                stage_tile<Tin, SUM_THREADS>(&S.z[r][0][0], gz + (int64_t)lo * p.z_sl, p.z_sl, SUM_BLK, rv, nd,
+                                             p.vec_z, tid, SUM_THREADS);
+        }
+        cp_async_commit();
+    };
+    issue(0);
+    for (int i = tid; i < nt * NS; i += SUM_THREADS) {
         const int row = i / NS, n = i % NS;
-        Cs[row][n] = n < p.N ? Elem<Tin>::to_f(gC[(int64_t)(t0 + row) * p.C_sl + n]) : 0.f;
+        S.C[row][n] = n < p.N ? Elem<Tin>::to_f(gC[(int64_t)(t0 + row) * p.C_sl + n]) : 0.f;
     }
+    const float bias = p.dbias ? p.dbias[dc] : 0.f;
     float2 A2[NS / 2], g[NS / 2], an[NS / 2];
 #pragma unroll
     for (int i = 0; i < NS / 2; ++i) {
@@ -118,31 +131,38 @@ __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const Sca
         A2[i] = f2(a0, a1);
         g[i] = an[i] = f2(0.f, 0.f);
     }
-    __syncthreads();
     float ssum = 0.f;
-    for (int tb = t1 - 1; tb >= t0; tb -= 4) {
-        if (tb - 4 >= t0) sum_load<Tin, HAS_Z>(nxt, gdl, gdo, gz, p, tb - 4, t0, bias);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int t = tb - i;
+    for (int k = 0; k < nblk; ++k) {
+        issue(k + 1);
+        cp_async_wait<1>();
+        __syncthreads();
+        const int hi = t1 - k * SUM_BLK, r = k & 1;
+        const int base = max(t0, hi - SUM_BLK);          // step of staged row 0
+#pragma unroll 4
+        for (int i = SUM_BLK - 1; i >= 0; --i) {
+            const int t = hi - SUM_BLK + i;
             if (t < t0) break;
-            float dte = cur.raw[i];
-            if (p.softplus) dte = softplus_f(cur.raw[i]);
+            const int row = t - base;
+            const float raw = Elem<Tin>::to_f(S.dl[r][row][tid]) + bias;
+            const float dov = Elem<Tin>::to_f(S.dout[r][row][tid]);
+            const float dte = p.softplus ? softplus_f(raw) : raw;
             ssum += dte;
-            const float dy = HAS_Z ? cur.dov[i] * silu_f(cur.zv[i]) : cur.dov[i];
-            const float4* cr = reinterpret_cast<const float4*>(&Cs[t - t0][0]);
+            const float dy = HAS_Z ? dov * silu_f(Elem<Tin>::to_f(S.z[r][row][tid])) : dov;
+            const float4* cr = reinterpret_cast<const float4*>(&S.C[t - t0][0]);
             const float2 dt2 = bc2(dte), dy2 = bc2(dy);
 #pragma unroll
             for (int v = 0; v < NS / 4; ++v) {
                 const float4 c4 = cr[v];
                 g[2 * v] = fma2(an[2 * v], g[2 * v], mul2(dy2, f2(c4.x, c4.y)));
                 g[2 * v + 1] = fma2(an[2 * v + 1], g[2 * v + 1], mul2(dy2, f2(c4.z, c4.w)));
-                an[2 * v] = ex2x2(mul2(dt2, A2[2 * v]));
-                an[2 * v + 1] = ex2x2(mul2(dt2, A2[2 * v + 1]));
+                const float2 x0 = mul2(dt2, A2[2 * v]), x1 = mul2(dt2, A2[2 * v + 1]);
+                an[2 * v] = 2 * v < SUM_FMA_PAIRS ? ex2x2_fma(x0) : ex2x2(x0);
+                an[2 * v + 1] = 2 * v + 1 < SUM_FMA_PAIRS ? ex2x2_fma(x1) : ex2x2(x1);
             }
         }
-        cur = nxt;
+        __syncthreads();                                  // slot r is refilled two blocks on
     }
+    cp_async_wait<0>();
     if (ok) {
         float* q = p.ws_q + (((int64_t)ss * p.b + bi) * p.D + d) * NS;
 #pragma unroll
@@ -154,32 +174,7 @@ __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const Sca
     }
 }
 
-// ===================================================================== 2. carries
-// Thread = (row, channel, state).  Walks the sub-segment summaries from the end of the
-// sequence: c <- Q_ss + exp(A * S_ss) * c, and stores c where a segment begins.
-__global__ void scan_bwd_carry_kernel(const ScanDev p) {
-    const int64_t total = (int64_t)p.b * p.D * NS;
-    const int sub_per_seg = p.seg_len / p.sub_len;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int n = (int)(i % NS);
-        const int64_t bd = i / NS;                      // bi * D + d
-        const int d = (int)(bd % p.D);
-        const float a2 = n < p.N ? load_A_sg(p, (int64_t)d * p.N + n) * LOG2E : 0.f;
-        float c = 0.f;
-        p.ws_c[((int64_t)(p.nseg - 1) * p.b * p.D + bd) * NS + n] = 0.f;
-        for (int ss = p.nsub - 1; ss >= p.first_sub; --ss) {
-            const int64_t o = (int64_t)ss * p.b * p.D + bd;
-            c = fmaf(ex2(a2 * p.ws_s[o]), c, p.ws_q[o * NS + n]);
-            if (ss % sub_per_seg == 0) {
-                const int m = ss / sub_per_seg - 1;      // the segment that ends where ss begins
-                p.ws_c[((int64_t)m * p.b * p.D + bd) * NS + n] = c;
-            }
-        }
-    }
-}
-
-// ===================================================================== 3. main kernel
+// ===================================================================== 2. main kernel
 template <typename Tin, bool YV>
 struct SegSmem {
     Tin u[SG_RING][TCK][SG_CH];
@@ -453,13 +448,24 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
         Ls.An[2 * c + 1] = f2(av[2], av[3]);
         Ls.A2[2 * c] = mul2(Ls.An[2 * c], bc2(LOG2E));
         Ls.A2[2 * c + 1] = mul2(Ls.An[2 * c + 1], bc2(LOG2E));
-        // the carry entering this segment from the later ones (zero for the last segment):
-        // g starts as that carry and the first step's "a_{t+1}" is 1
-        float4 cv = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (v && p.nseg > 1)
-            cv = *reinterpret_cast<const float4*>(p.ws_c + (((int64_t)seg * p.b + bi) * p.D + ca + c) * NS + 4 * j);
-        Ls.g[2 * c] = f2(cv.x, cv.y);
-        Ls.g[2 * c + 1] = f2(cv.z, cv.w);
+        // the carry entering this segment from the later ones (zero for the last segment),
+        // chained from the end of the sequence over the later sub-segments' summaries:
+        // c <- Q_ss + exp(A * S_ss) * c.  g starts as that carry and the first step's
+        // "a_{t+1}" is 1
+        float2 c01 = bc2(0.f), c23 = bc2(0.f);
+        if (v) {
+            const int lo = (seg + 1) * (p.seg_len / p.sub_len);
+#pragma unroll 4
+            for (int ss = p.nsub - 1; ss >= lo; --ss) {
+                const int64_t o = ((int64_t)ss * p.b + bi) * p.D + ca + c;
+                const float2 sv = bc2(p.ws_s[o]);
+                const float4 qv = *reinterpret_cast<const float4*>(p.ws_q + o * NS + 4 * j);
+                c01 = fma2(ex2x2(mul2(Ls.A2[2 * c], sv)), c01, f2(qv.x, qv.y));
+                c23 = fma2(ex2x2(mul2(Ls.A2[2 * c + 1], sv)), c23, f2(qv.z, qv.w));
+            }
+        }
+        Ls.g[2 * c] = c01;
+        Ls.g[2 * c + 1] = c23;
         Ls.an[2 * c] = Ls.an[2 * c + 1] = bc2(1.f);
         Ls.dA[2 * c] = Ls.dA[2 * c + 1] = bc2(0.f);
     }
@@ -627,7 +633,7 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
     }
 }
 
-// ===================================================================== 4. finalize
+// ===================================================================== 3. finalize
 template <typename Tin>
 __global__ void scan_bwd_seg_finalize_kernel(const ScanDev p) {
     const int64_t nrow = (int64_t)p.b * p.L;
@@ -674,11 +680,10 @@ static cudaError_t launch_seg_t(const ScanDev& p, cudaStream_t st) {
         const int64_t nsum = p.nsub - p.first_sub;
         const int64_t gs = (int64_t)((p.D + SUM_THREADS - 1) / SUM_THREADS) * p.b * nsum;
         if (gs > INT32_MAX) return cudaErrorInvalidConfiguration;
-        scan_bwd_summary_kernel<Tin, HAS_Z><<<(unsigned)gs, SUM_THREADS, 0, st>>>(p);
-        if ((e = cudaGetLastError()) != cudaSuccess) return e;
-        const int64_t tot = (int64_t)p.b * p.D * NS;
-        const int blocks = (int)std::min<int64_t>((tot + 255) / 256, 148 * 16);
-        scan_bwd_carry_kernel<<<blocks, 256, 0, st>>>(p);
+        auto ks = scan_bwd_summary_kernel<Tin, HAS_Z>;
+        const int ssm = sizeof(SumSmem<Tin>);
+        if ((e = allow_smem(ks, ssm)) != cudaSuccess) return e;
+        ks<<<(unsigned)gs, SUM_THREADS, ssm, st>>>(p);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
     const bool ypre = HAS_Z && p.ypre;

@@ -39,13 +39,12 @@ struct ScanDev {
     int nblk;                // CTAs along D
     // time-segmented backward (scan_bwd_seg.cu): the sequence is cut into nseg segments
     // of seg_len steps (a multiple of 16, the last one may be shorter), walked in
-    // parallel; the reverse carry entering each segment comes from per-sub-segment
-    // summaries (sub_len steps, dividing seg_len) combined by a small kernel
+    // parallel; the reverse carry entering each segment is chained from per-sub-segment
+    // summaries (sub_len steps, dividing seg_len)
     int seg_len, nseg, sub_len, nsub, first_sub;
     int nblk64;              // 64-channel blocks along D
     float* ws_q;             // (nsub, b, D, 16) local carry a_t0 * g_t0 of each sub-segment
     float* ws_s;             // (nsub, b, D) sum of delta_eff over each sub-segment
-    float* ws_c;             // (nseg, b, D, 16) carry entering each segment from the later ones
 };
 
 }  // namespace swx
