@@ -9,6 +9,11 @@ plus one backward over one batch of seeded synthetic inputs.
 
 With N > 1 (torchrun, one rank per GPU) each rank runs its own batch (weak scaling:
 batch rows are independent channels of the scan, no collective on the data path).
+The default line also carries, measured at the same N, the other two halves of the
+metric: "lm_train" (Sift LM training tokens/s, data parallel with one NCCL all-reduce of
+the gradients per step; its all-reduce time alone is reported) and "long_scan" (the
+b=4, L=65536, D=2048 bf16 forward, sequence parallel over the ranks: chunk forward,
+peer-to-peer boundary exchange, correction; its phase split is reported).
 Metric: algorithmic GB/s (each input read once, each output written once; 375.4 MB
 per step at b=8) summed over ranks, timed on the device with CUDA events, max over
 ranks.  Prints one JSON line on rank 0.
@@ -253,6 +258,15 @@ def run_ours(args, world, rank, local):
         res["clocks"] = sampler.summary()
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         res["cpu_baseline"] = cpu_baseline(args)
+    if not args.scan_only:
+        # the other two halves of the headline metric, at the same N: Sift LM training
+        # (data parallel, gradient all-reduce) and the long-sequence scan (sequence parallel)
+        for name, fn in (("lm_train", run_lm_train), ("long_scan", run_long_scan)):
+            sub = fn(args, world, rank, local)
+            keep = ("value", "unit", "ms_per_step", "scaling", "dtype", "config", "clocks", "e2e", "allreduce_ms",
+                    "allreduce_bytes", "phases_ms", "gpu_launches")
+            res[name] = {k: sub[k] for k in keep if k in sub}
+        res["gpu_launches"] += res["lm_train"]["gpu_launches"] + res["long_scan"]["gpu_launches"]
     return res
 
 
@@ -480,6 +494,8 @@ def run_lm_train(args, world, rank, local):
 
     ms, clocks = timed_steps(train_step, args, world, local, dev)
     tokens = B * L * world
+    # the gradient all-reduce alone (the step's only collective), same buffer, same count
+    ms_ar, _ = timed_steps(allreduce, args, world, local, dev) if world > 1 else (0.0, None)
 
     def e2e_step():
         tok.copy_(host, non_blocking=True)
@@ -491,6 +507,8 @@ def run_lm_train(args, world, rank, local):
                      "cuda_graph": graphed, "l2": "activations and weights per step exceed L2"})
     res["e2e"] = {"value": round(tokens / (ms_e2e * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step":
                   host.numel() * host.element_size(), "d2h_bytes_per_step": 4}
+    res["allreduce_ms"] = round(ms_ar, 4)
+    res["allreduce_bytes"] = grads.flat.numel() * grads.flat.element_size() if world > 1 else 0
     # per layer: conv fwd, scan fwd, conv bwd x2, scan bwd x2; 9 RMSNorms (8 layers + norm_f):
     # fwd, bwd, weight-gradient sum; token embedding backward: slice partials + slice sum
     res["gpu_launches"] = (6 * 8 + 9 * 3 + 2) * args.steps
@@ -501,11 +519,12 @@ def run_lm_train(args, world, rank, local):
 def run_long_scan(args, world, rank, local):
     """Long-sequence forward scan, bf16 u/delta/B/C/z, fp32 state and output, gated:
     b=4, L=65536, D=2048, N=16, split along the sequence over the ranks (sequence
-    parallel: pass 1 boundary values, NCCL all_gather, prefix combine, pass 2)."""
+    parallel: each rank's full forward from a zero state, the boundary values sent peer to
+    peer to the later ranks, prefix combine, initial-state correction on ranks > 0)."""
     import math
 
-    from swiftx_b200.selective_scan import scan_forward
-    from swiftx_b200.seqpar import sequence_parallel_scan
+    from swiftx_b200.selective_scan import scan_correct, scan_forward
+    from swiftx_b200.seqpar import combine_prefix, exchange_boundaries, sequence_parallel_scan
     dev = torch.device("cuda", local)
     b, L, D, N = 4, 65536, 2048, 16
     Lr = L // world
@@ -534,7 +553,28 @@ def run_long_scan(args, world, rank, local):
                      "d_state": N, "parallelism": f"sequence-parallel x{world}" if world > 1 else "single GPU",
                      "alg_bytes": alg}, scaling="strong")
     res["clocks"] = clocks
-    res["gpu_launches"] = (2 if world > 1 else 1) * args.steps
+    # phase split of one step on this rank (CUDA events; max over ranks): the chunk's
+    # forward, the peer-to-peer exchange of boundary values, the combine + correction
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    barrier(world)
+    torch.cuda.synchronize()
+    ev[0].record()
+    out, _, h_end, dsum = scan_forward(u, dr, A, Bm, Cm, Dsk, z, bias, True, out_dtype=torch.float32,
+                                       return_last_state=True, return_delta_sum=True)
+    ev[1].record()
+    if world > 1:
+        h_ends, dsums = exchange_boundaries(h_end, dsum)
+    ev[2].record()
+    if world > 1 and rank > 0:
+        scan_correct(out, combine_prefix(h_ends, dsums, A, rank), u, dr, A, Bm, Cm, z=z, delta_bias=bias,
+                     delta_softplus=True)
+    ev[3].record()
+    torch.cuda.synchronize()
+    split = [max_over_ranks(ev[i].elapsed_time(ev[i + 1]), world, dev) for i in range(3)]
+    res["phases_ms"] = {"chunk_forward": round(split[0], 4), "exchange": round(split[1], 4),
+                        "combine_and_correct": round(split[2], 4)}
+    # kernel launches per step on the slowest rank: forward; correction = block sums + correct
+    res["gpu_launches"] = (1 + (2 if world > 1 else 0)) * args.steps
     return res
 
 
@@ -649,6 +689,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--scan-only", action="store_true",
+                    help="default workload: skip the lm_train and long_scan sub-objects")
     ap.add_argument("--no-graph", action="store_true", help="lm_train: run the step eagerly, no CUDA graphs")
     ap.add_argument("--e2e-rows", type=int, default=8, help="scan e2e: batch rows per pipelined chunk")
     ap.add_argument("--ls-batch", type=int, default=8, help="linear_scan: batch rows (8 = the measured size)")

@@ -127,14 +127,35 @@ int swx_scan_fwd(const swx_scan_args* args, void* stream);
  * deterministic: fixed-order sums, no float atomics. */
 int swx_scan_bwd(const swx_scan_args* args, void* stream);
 
+/* Initial-state correction of a chunk scanned from a zero state, for a sequence split
+ * across ranks or streams: the scan is linear in its initial state, so
+ *   out_t += silu(z_t) * sum_n C_t[n] * exp(A[d, n] * S_t) * h_in[n],  S_t = sum_{s<=t} delta_eff_s
+ * (without z the factor silu(z_t) is 1) turns the output of swx_scan_fwd with h0 = NULL
+ * into the output it would have had with h0 = h_in.  Arguments as swx_scan_fwd: delta,
+ * delta_bias, delta_softplus, z, C, A (SWX_SCAN_A_LOG allowed) and dims; args->h0 is
+ * h_in (b, D, N) fp32 (required); args->out (b, L, D) dense in out_dtype is updated in
+ * place; u, B, Dskip are not read (u and B must still be given, as for swx_scan_fwd).
+ * workspace: >= swx_scan_correct_workspace_bytes().  No reference counterpart: the
+ * reference has no sequence parallelism; this is the correction pass of the sequence-
+ * parallel design (each rank scans its chunk from zero, then corrects). */
+int swx_scan_correct(const swx_scan_args* args, void* stream);
+int64_t swx_scan_correct_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim);
+
+/* swx_scan_bwd runs one of two kernels.  The time-segmented one (the default) cuts the
+ * sequence into segments walked in parallel, with the reverse carries between them from
+ * sub-segment summaries; its segment plan is a function of (seqlen, dim) alone, so the
+ * rows of a batch get the same bits whatever the batch.  bf16 problems whose grid of
+ * 32-channel x row CTAs fills every SM at two CTAs per SM run a kernel that walks whole
+ * rows instead (faster there).  Both reduce in fixed order (deterministic). */
+
 /* How many CTAs of its main kernel swx_scan_bwd keeps on one SM of the current device for
  * these arguments (2 on a B200); a negative status on error.  Launches nothing. */
 int swx_scan_bwd_ctas_per_sm(const swx_scan_args* args);
 
-/* Number of time segments swx_scan_bwd walks in parallel for a sequence of seqlen steps
- * and dim channels (a function of those two alone, so the rows of a batch get the same
- * bits whatever the batch); a negative status for invalid sizes. */
-int swx_scan_bwd_segments(int64_t seqlen, int64_t dim);
+/* Number of time segments swx_scan_bwd walks in parallel for these arguments on the
+ * current device; 0 when it runs the whole-row kernel (and for float64 inputs); a
+ * negative status on error.  Launches nothing. */
+int swx_scan_bwd_segments(const swx_scan_args* args);
 
 /* Capacity of the static scratch used by swx_scan_bwd_static_scratch: 8 MiB, enough
  * for swx_scan_bwd_workspace_bytes(batch, seqlen, dim) of roughly batch*seqlen*dim up

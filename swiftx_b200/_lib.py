@@ -132,11 +132,12 @@ def load():
             raise RuntimeError(f"{st.__name__} layout mismatch between the library and its binding")
     lib.swx_scan_checkpoint_floats.restype = i64
     lib.swx_scan_checkpoint_floats.argtypes = [i64, i64, i64]
-    for fn in ("swx_scan_bwd_workspace_bytes", "swx_scan_bwd_workspace_bytes_f64"):
+    for fn in ("swx_scan_bwd_workspace_bytes", "swx_scan_bwd_workspace_bytes_f64", "swx_scan_correct_workspace_bytes"):
         getattr(lib, fn).restype = i64
         getattr(lib, fn).argtypes = [i64, i64, i64]
     for name, st in (("swx_scan_fwd", ScanArgs), ("swx_scan_bwd", ScanArgs),
-                     ("swx_scan_bwd_static_scratch", ScanArgs), ("swx_conv1d_fwd", ConvArgs),
+                     ("swx_scan_bwd_static_scratch", ScanArgs), ("swx_scan_correct", ScanArgs),
+                     ("swx_conv1d_fwd", ConvArgs),
                      ("swx_conv1d_bwd", ConvArgs), ("swx_decode_step", DecodeArgs),
                      ("swx_linear_scan_fwd", LinearScanArgs), ("swx_linear_scan_bwd", LinearScanArgs),
                      ("swx_rmsnorm_fwd", RMSNormArgs), ("swx_rmsnorm_bwd", RMSNormArgs),
@@ -147,7 +148,7 @@ def load():
     lib.swx_scan_bwd_ctas_per_sm.restype = ctypes.c_int
     lib.swx_scan_bwd_ctas_per_sm.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_scan_bwd_segments.restype = ctypes.c_int
-    lib.swx_scan_bwd_segments.argtypes = [i64, i64]
+    lib.swx_scan_bwd_segments.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_exp2_fma_eval.restype = ctypes.c_int
     lib.swx_exp2_fma_eval.argtypes = [vp, vp, i64, vp]
     lib.swx_rmsnorm_bwd_workspace_bytes.restype = i64

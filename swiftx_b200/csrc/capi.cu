@@ -11,6 +11,11 @@ cudaError_t scan_bwd_seg_ctas_per_sm(const ScanDev& p, int in_dtype, bool has_z,
 cudaError_t launch_scan_fwd_f64(const ScanDev& p, cudaStream_t st);
 cudaError_t launch_scan_bwd_f64(const ScanDev& p, cudaStream_t st);
 cudaError_t launch_scan_bwd_seg(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st);
+cudaError_t launch_scan_bwd_rows(const ScanDev& p, bool has_z, cudaStream_t st);
+cudaError_t scan_bwd_rows_applicable(const ScanDev& p, int in_dtype, bool has_z, bool* yes);
+cudaError_t launch_scan_correct(const ScanDev& p, int in_dtype, int out_dtype, bool has_z, float* ws,
+                                cudaStream_t st);
+int64_t scan_correct_workspace_floats(int64_t b, int64_t L, int64_t D);
 }  // namespace swx
 
 namespace {
@@ -60,15 +65,18 @@ struct WsLayout {
     int64_t bc, a, d, bias, q, s, total;
 };
 
-// es: bytes of one partial sum (4 for fp32 / bf16 inputs, 8 for float64 inputs).  fp32 /
-// bf16 inputs use the segmented backward's layout: dB|dC partials per 64-channel block,
-// dA / dD / d(delta_bias) partials per (segment, row) and the sub-segment summaries.  float64 inputs: partials per 32-channel block and per row.
+// es: bytes of one partial sum (4 for fp32 / bf16 inputs, 8 for float64 inputs).
+// fp32 / bf16 inputs: one layout serves both backward kernels -- dB|dC partials per
+// channel block (32-channel blocks of the row kernel, which need the most), dA / dD /
+// d(delta_bias) partials per (segment, row) (per row for the row kernel), and the
+// segmented kernel's sub-segment summaries.  float64 inputs: partials per 32-channel
+// block and per row.
 WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
     WsLayout w{};
+    const int64_t nblk32 = (D + 31) / 32;
     if (es == 8) {
-        const int64_t nblk = (D + 31) / 32;
         w.bc = 0;
-        w.a = w.bc + round_up(nblk * b * L * 2 * swx::NS * es);
+        w.a = w.bc + round_up(nblk32 * b * L * 2 * swx::NS * es);
         w.d = w.a + round_up(b * D * swx::NS * es);
         w.bias = w.d + round_up(b * D * es);
         w.q = w.s = w.bias + round_up(b * D * es);
@@ -77,7 +85,7 @@ WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
     }
     const SegPlan sp = seg_plan(L, D);
     w.bc = 0;
-    w.a = w.bc + round_up(sp.nblk64 * b * L * 2 * swx::NS * 4);
+    w.a = w.bc + round_up(nblk32 * b * L * 2 * swx::NS * 4);
     w.d = w.a + round_up(sp.nseg * b * D * swx::NS * 4);
     w.bias = w.d + round_up(sp.nseg * b * D * 4);
     w.q = w.bias + round_up(sp.nseg * b * D * 4);
@@ -217,6 +225,10 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     p.ws_d = reinterpret_cast<float*>(ws + w.d);
     p.ws_bias = reinterpret_cast<float*>(ws + w.bias);
     if (f64) return from_cuda(swx::launch_scan_bwd_f64(p, static_cast<cudaStream_t>(stream)));
+    bool rows = false;
+    if (swx::scan_bwd_rows_applicable(p, a->in_dtype, a->z != nullptr, &rows) != cudaSuccess) return SWX_ERR_CUDA;
+    if (rows)
+        return from_cuda(swx::launch_scan_bwd_rows(p, a->z != nullptr, static_cast<cudaStream_t>(stream)));
     const SegPlan sp = seg_plan(a->seqlen, a->dim);
     p.seg_len = (int)sp.seg_len; p.nseg = (int)sp.nseg; p.sub_len = (int)sp.sub_len;
     p.nsub = (int)sp.nsub; p.first_sub = (int)sp.first_sub; p.nblk64 = (int)sp.nblk64;
@@ -225,19 +237,46 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     return from_cuda(swx::launch_scan_bwd_seg(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
 }
 
+int64_t swx_scan_correct_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim) {
+    if (!sizes_ok(batch, seqlen, dim)) return -1;
+    return round_up(swx::scan_correct_workspace_floats(batch, seqlen, dim) * 4);
+}
+
+int swx_scan_correct(const swx_scan_args* a, void* stream) {
+    int s = check_common(a);
+    if (s != SWX_OK) return s;
+    if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
+    if (a->in_dtype == SWX_DTYPE_F64 || elem_size(a->out_dtype) == 0 || a->out_dtype == SWX_DTYPE_F64)
+        return SWX_ERR_UNSUPPORTED;
+    if (!a->out || !a->h0 || !a->workspace) return SWX_ERR_INVALID_ARG;
+    if ((a->seqlen + 255) / 256 > 65535) return SWX_ERR_UNSUPPORTED;
+    if (a->workspace_bytes < swx_scan_correct_workspace_bytes(a->batch, a->seqlen, a->dim)) return SWX_ERR_INVALID_ARG;
+    swx::ScanDev p = pack(a);
+    return from_cuda(swx::launch_scan_correct(p, a->in_dtype, a->out_dtype, a->z != nullptr,
+                                              static_cast<float*>(a->workspace), static_cast<cudaStream_t>(stream)));
+}
+
 int swx_scan_bwd_ctas_per_sm(const swx_scan_args* a) {
     int s = check_common(a);
     if (s != SWX_OK) return -s;
     if (a->in_dtype == SWX_DTYPE_F64) return 1;
     const swx::ScanDev p = pack(a);
+    bool rows = false;
+    if (swx::scan_bwd_rows_applicable(p, a->in_dtype, a->z != nullptr, &rows) != cudaSuccess) return -SWX_ERR_CUDA;
+    if (rows) return 2;
     int ctas = 1;
     if (swx::scan_bwd_seg_ctas_per_sm(p, a->in_dtype, a->z != nullptr, &ctas) != cudaSuccess) return -SWX_ERR_CUDA;
     return ctas;
 }
 
-int swx_scan_bwd_segments(int64_t seqlen, int64_t dim) {
-    if (!sizes_ok(1, seqlen, dim)) return -SWX_ERR_INVALID_ARG;
-    return (int)seg_plan(seqlen, dim).nseg;
+int swx_scan_bwd_segments(const swx_scan_args* a) {
+    int s = check_common(a);
+    if (s != SWX_OK) return -s;
+    if (a->in_dtype == SWX_DTYPE_F64) return 0;
+    const swx::ScanDev p = pack(a);
+    bool rows = false;
+    if (swx::scan_bwd_rows_applicable(p, a->in_dtype, a->z != nullptr, &rows) != cudaSuccess) return -SWX_ERR_CUDA;
+    return rows ? 0 : (int)seg_plan(a->seqlen, a->dim).nseg;
 }
 
 }  // extern "C"

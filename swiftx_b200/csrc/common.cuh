@@ -80,10 +80,10 @@ __device__ __forceinline__ float2 rcp2(float2 x) { return make_float2(rcp(x.x), 
 // 2^r on [-1/2, 1/2] -- the minimax fit of the relative error by a Remez exchange
 // (fit_exp2_poly.py; 7.5e-8 for the float64 fit, about 2e-7 as evaluated in fp32, the
 // order of ex2.approx) -- and 2^j added to the exponent field.
-// x is clamped to [-125, 127]: below that a decay of ~2^-125 stands for 0 (its
-// contribution is far below fp32 resolution of the sums it enters), above it the result
-// stays finite where ex2.approx overflows.
+// Below -125 the result is 0, as ex2.approx.ftz flushes results under 2^-126; x is
+// clamped at 127 above (finite where ex2.approx overflows).
 __device__ __forceinline__ float2 ex2x2_fma(float2 x) {
+    const bool z0 = x.x < -125.f, z1 = x.y < -125.f;
     x.x = fminf(fmaxf(x.x, -125.f), 127.f);
     x.y = fminf(fmaxf(x.y, -125.f), 127.f);
     const float2 t = add2(x, bc2(12582912.f));          // 1.5 * 2^23 + rint(x)
@@ -96,8 +96,9 @@ __device__ __forceinline__ float2 ex2x2_fma(float2 x) {
     q = fma2(q, r, bc2(6.931469440460205e-1f));
     q = fma2(q, r, bc2(1.0000001192092896f));
     // low mantissa bits of t hold j: (bits(t) << 23) = j << 23 (mod 2^32)
-    return make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
-                       __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+    const float2 y = make_float2(__int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23)),
+                                 __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23)));
+    return make_float2(z0 ? 0.f : y.x, z1 ? 0.f : y.y);
 }
 
 // softplus of two values (torch threshold 20) and its derivative sigmoid(x), sharing

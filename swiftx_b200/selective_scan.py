@@ -162,6 +162,30 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     return g
 
 
+def scan_correct(out, h_in, u, delta, A, B, C, z=None, delta_bias=None, delta_softplus=False,
+                 A_is_log=False):
+    """In place: turn ``out``, the forward of a chunk scanned from a zero state, into the
+    forward of the same chunk scanned from ``h_in`` (b, D, N):
+    out_t += silu(z_t) * sum_n C_t[n] exp(A[:, n] S_t) h_in[n], S_t the running sum of
+    delta_eff (swx_scan_correct).  u and B are only shape-checked.  Returns out."""
+    lib = _lib.load()
+    u, delta, A, B, C, _, z, delta_bias, h_in, in_dt = _prep(u, delta, A, B, C, None, z, delta_bias, h_in)
+    if in_dt == torch.float64:
+        raise ValueError("scan_correct: float64 is not supported")
+    b, L, Dm = u.shape
+    if out.shape != (b, L, Dm) or not out.is_contiguous() or out.dtype not in _lib.DTYPE_CODES:
+        raise ValueError("out must be a dense (b, L, D) fp32 or bf16 tensor")
+    wsb = lib.swx_scan_correct_workspace_bytes(b, L, Dm)
+    ws = torch.empty(max(wsb, 1), device=u.device, dtype=torch.uint8)
+    a = _lib.ScanArgs()
+    _fill_inputs(a, u, delta, A, B, C, None, z, delta_bias, h_in, delta_softplus, in_dt, A_is_log)
+    a.out_dtype = _lib.DTYPE_CODES[out.dtype]
+    a.out = out.data_ptr()
+    a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
+    _lib.check(lib.swx_scan_correct(a, _lib.stream_ptr(u.device)), "swx_scan_correct")
+    return out
+
+
 class SelectiveScanFn(torch.autograd.Function):
     """Custom autograd Function over the fused kernels (same save/recompute trade as
     _FusedScanFn / TritonScanFn in the reference)."""

@@ -1,33 +1,36 @@
 """Sequence-parallel selective scan across the ranks of a process group.
 
-A long sequence is split into contiguous chunks, one per rank in rank order.  The
-recurrence h_t = a_t h_{t-1} + x_t is affine in the initial state, so with h0 = 0 each
-rank's chunk ends in a local state h_end and carries the decay P = prod_t a_t =
-exp(A * sum_t delta_eff_t) (per batch row, channel and state).  The true initial state
-of chunk g is the prefix  h_in_g = P_{g-1} h_in_{g-1} + h_end_{g-1},  h_in_0 = 0.
+A long sequence is split into contiguous chunks, one per rank in rank order.  The scan
+is linear in its initial state: with h0 = 0 each rank's chunk ends in a local state
+h_end and carries the decay P = exp(A * sum_t delta_eff_t) (per batch row, channel and
+state), and the true initial state of chunk g is the prefix
+    h_in_g = P_{g-1} h_in_{g-1} + h_end_{g-1},   h_in_0 = 0.
 
-  pass 1: local scan without output -> (h_end, sum_t delta_eff)       [kernel, WR=false]
-  exchange: all_gather of the 2*b*D*N fp32 boundary values over NCCL (NVLink)
-  combine: the prefix above for the ranks before this one (tiny, on the GPU)
-  pass 2: full scan of the chunk from h_in (gate, D skip, output)     [kernel]
-
-The two passes are the cost of chunking: both walk every element's decay.
+  pass 1: the chunk's full forward from h0 = 0 (gated output, h_end, sum of delta_eff)
+  exchange: each rank sends its 2 b D N-sized boundary values peer to peer to every later
+            rank (NCCL send/recv over NVLink, grouped; no collective over all ranks)
+  combine: the prefix above over the earlier ranks, in rank order (tiny, on the GPU)
+  correct: out_t += silu(z_t) sum_n C_t[n] exp(A[:, n] S_t) h_in[n], S_t the running
+           sum of delta_eff (swx_scan_correct) -- no step waits for the previous one
+           except through S_t, so it runs at the throughput of its exponentials, not as
+           a second serial walk of the chunk.
+Rank 0 needs no correction.
 """
 import torch
 import torch.distributed as dist
 
-from .selective_scan import scan_forward
+from .selective_scan import scan_correct, scan_forward
 
 
-def _kernel_local_scan(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, write_out, out_dtype):
-    if not write_out:
-        _, _, h_end, dsum = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0=h0,
-                                         out_dtype=out_dtype, return_last_state=True,
-                                         return_delta_sum=True, write_out=False)
-        return None, h_end, dsum
-    out, _, _ = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0=h0,
-                             out_dtype=out_dtype)
-    return out, None, None
+def _kernel_local_scan(u, delta, A, B, C, D, z, delta_bias, delta_softplus, out_dtype):
+    out, _, h_end, dsum = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus,
+                                       out_dtype=out_dtype, return_last_state=True, return_delta_sum=True)
+    return out, h_end, dsum
+
+
+def _kernel_correct(out, h_in, u, delta, A, B, C, z, delta_bias, delta_softplus):
+    return scan_correct(out, h_in, u, delta, A, B, C, z=z, delta_bias=delta_bias,
+                        delta_softplus=delta_softplus)
 
 
 def combine_prefix(h_end_all, dsum_all, A, rank):
@@ -42,29 +45,40 @@ def combine_prefix(h_end_all, dsum_all, A, rank):
     return h
 
 
+def exchange_boundaries(h_end, dsum, group=None):
+    """Peer-to-peer exchange of the boundary values: this rank's (h_end, dsum) go to every
+    later rank and the earlier ranks' come back.  Returns the lists (h_end, dsum) of
+    ranks 0..rank (this rank's own last)."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    pack = torch.cat([h_end.reshape(-1), dsum.reshape(-1).to(h_end.dtype)])
+    recv = [torch.empty_like(pack) for _ in range(rank)]
+    ranks = dist.get_process_group_ranks(group) if group is not None else list(range(world))
+    ops = [dist.P2POp(dist.isend, pack, ranks[d], group) for d in range(rank + 1, world)]
+    ops += [dist.P2POp(dist.irecv, recv[s], ranks[s], group) for s in range(rank)]
+    if ops:
+        for r in dist.batch_isend_irecv(ops):
+            r.wait()
+    nh = h_end.numel()
+    packs = recv + [pack]
+    return ([q[:nh].view_as(h_end) for q in packs], [q[nh:].view_as(dsum) for q in packs])
+
+
 def sequence_parallel_scan(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=True,
-                           group=None, out_dtype=torch.float32, local_scan=None):
+                           group=None, out_dtype=torch.float32, local_scan=None, correct=None):
     """Forward selective scan of a sequence split across the ranks of `group`.
 
     Each rank passes its own chunk (b, L_rank, D) / (b, L_rank, N) of u, delta, z, B, C,
     in rank order along the sequence; A, D, delta_bias are replicated.  Returns this
-    rank's (b, L_rank, D) output.  `local_scan` replaces the per-chunk kernel call (the
-    tests use it to drive the host logic on CPU ranks)."""
+    rank's (b, L_rank, D) output.  `local_scan` and `correct` replace the two kernel calls
+    (the tests use them to drive the host logic on CPU ranks)."""
     scan = local_scan or _kernel_local_scan
-    world = dist.get_world_size(group)
-    rank = dist.get_rank(group)
-    b, _, Dm = u.shape
-    N = A.shape[1]
-    h0 = None
-    if world > 1:
-        _, h_end, dsum = scan(u, delta, A, B, C, D, z, delta_bias, delta_softplus, None, False, out_dtype)
-        pack = torch.cat([h_end.reshape(-1), dsum.reshape(-1).to(h_end.dtype)])
-        parts = [torch.empty_like(pack) for _ in range(world)]
-        dist.all_gather(parts, pack, group=group)
-        nh = b * Dm * N
-        h_ends = [q[:nh].view(b, Dm, N) for q in parts]
-        dsums = [q[nh:].view(b, Dm) for q in parts]
+    fix = correct or _kernel_correct
+    out, h_end, dsum = scan(u, delta, A, B, C, D, z, delta_bias, delta_softplus, out_dtype)
+    if dist.get_world_size(group) > 1:
+        rank = dist.get_rank(group)
+        h_ends, dsums = exchange_boundaries(h_end, dsum, group)
         if rank > 0:
-            h0 = combine_prefix(h_ends, dsums, A, rank)
-    out, _, _ = scan(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, True, out_dtype)
+            h_in = combine_prefix(h_ends, dsums, A, rank)
+            out = fix(out, h_in, u, delta, A, B, C, z, delta_bias, delta_softplus)
     return out

@@ -49,9 +49,16 @@ def test_sizes_of_checkpoints_and_workspace():
     assert lib.swx_scan_checkpoint_floats(1, 17, 3) == 1 * 2 * 3 * 16
     # dB|dC partials per 64-channel block (8 x 8 rows x 2048 steps x 32 floats), plus the
     # per-segment partials, sub-segment summaries and segment carries
-    nseg = lib.swx_scan_bwd_segments(2048, 512)
-    assert nseg == 4 and lib.swx_scan_bwd_segments(512, 512) == 4 and lib.swx_scan_bwd_segments(64, 512) == 1
-    assert lib.swx_scan_bwd_segments(65536, 2048) == 1 and lib.swx_scan_bwd_segments(-1, 8) < 0
+    def segments(b, L, D):                    # fp32 inputs: the segmented kernel, no device query
+        a = _lib.ScanArgs()
+        a.batch, a.seqlen, a.dim, a.dstate = b, L, D, 16
+        a.in_dtype = a.out_dtype = 0
+        a.u = a.delta = a.B = a.C = a.A = 256      # placeholders: the query reads no memory
+        return lib.swx_scan_bwd_segments(ctypes.byref(a))
+    nseg = segments(8, 2048, 512)
+    assert nseg == 4 and segments(16, 512, 512) == 4 and segments(8, 64, 512) == 1
+    assert segments(4, 65536, 2048) == 1 and segments(1, -1, 8) < 0
+    assert segments(1, 2048, 512) == nseg                        # a function of (L, D) alone
     ws = lib.swx_scan_bwd_workspace_bytes(8, 2048, 512)
     assert ws >= 8 * 8 * 2048 * 32 * 4 + nseg * 8 * 512 * (16 + 2) * 4 + (2048 // 128) * 8 * 512 * 17 * 4
     assert lib.swx_scan_bwd_workspace_bytes(65535, 1 << 30, 1 << 30) == -1

@@ -257,51 +257,71 @@ def test_full_size_8x2048x512_vs_oracle():
     check_grads({k: v for k, v in g.items() if v is not None}, gr_o, scale)
 
 
+def _bwd_path(inp, use_pre):
+    """(segments, CTAs per SM) of swx_scan_bwd for these inputs: segments 0 = row kernel."""
+    from swiftx_b200 import _lib
+    from swiftx_b200.selective_scan import _fill_inputs, _prep
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+    a = _lib.ScanArgs()
+    u, dl, A, Bm, Cm, Dv, z, bias, h0, in_dt = _prep(*args[:8], None)
+    _fill_inputs(a, u, dl, A, Bm, Cm, Dv, z, bias, h0, True, in_dt)
+    a.out_pre = 16 if (use_pre and z is not None) else None          # only its presence matters here
+    lib = _lib.load()
+    return lib.swx_scan_bwd_segments(a), lib.swx_scan_bwd_ctas_per_sm(a)
+
+
+def _run_bwd(inp, use_pre):
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+    pre = torch.empty(inp["u"].shape, device=DEV, dtype=torch.float32) if use_pre else None
+    _, ck, _ = scan_forward(*args, checkpoints=True, pre_out=pre)
+    return scan_backward(*args, None, ck, inp["dout"], y_pre=pre)
+
+
 @pytest.mark.parametrize("shape,gate,use_pre", [((5, 100, 1024, 16), True, True),
                                                 ((5, 100, 1024, 16), True, False),
                                                 ((10, 37, 520, 5), False, False)])
 def test_bwd_batch_split_bit_identical(shape, gate, use_pre):
-    """bf16 inputs, with and without the saved pre-gate output, N < 16 and a partial last
-    channel block: the segmented backward's plan depends on (L, D) only, so each row's
-    per-row gradients are bit-identical whether the rows are passed together or in two
-    smaller batches; the batch sums agree to fp32 re-association, and everything matches
-    the oracle at the bf16 tolerance."""
-    from swiftx_b200 import _lib
-    from swiftx_b200.selective_scan import _fill_inputs, _prep
+    """fp32 inputs (the time-segmented backward), with and without the saved pre-gate
+    output, N < 16 and a partial last channel block: its segment plan depends on (L, D)
+    only, so each row's per-row gradients are bit-identical whether the rows are passed
+    together or in two smaller batches; the batch sums agree to fp32 re-association, and
+    everything matches the oracle."""
     b, L, D, N = shape
-    inp = config_inputs(b, L, D, N, seed=41, gate=gate, device=DEV, dtype=torch.bfloat16)
+    inp = config_inputs(b, L, D, N, seed=41, gate=gate, device=DEV)
     rowwise = ("u", "delta", "z", "B", "C", "dout")
     cut = 2 if b == 5 else 4
-
-    def run(rows):
-        sub = {k: (v[rows] if k in rowwise and v is not None else v) for k, v in inp.items()}
-        args = (sub["u"], sub["delta"], sub["A"], sub["B"], sub["C"], sub["D"], sub["z"], sub["delta_bias"], True)
-        pre = torch.empty(sub["u"].shape, device=DEV, dtype=torch.float32) if use_pre else None
-        _, ck, _ = scan_forward(*args, checkpoints=True, pre_out=pre)
-        a = _lib.ScanArgs()
-        u, dl, A, Bm, Cm, Dv, z, bias, h0, in_dt = _prep(*args[:8], None)
-        _fill_inputs(a, u, dl, A, Bm, Cm, Dv, z, bias, h0, True, in_dt)
-        a.out_pre = pre.data_ptr() if pre is not None else None
-        ctas = _lib.load().swx_scan_bwd_ctas_per_sm(a)
-        return scan_backward(*args, None, ck, sub["dout"], y_pre=pre), ctas
-
-    g_all, ctas_all = run(slice(0, b))
-    g_a, ctas_a = run(slice(0, cut))
-    g_b, ctas_b = run(slice(cut, b))
-    assert ctas_all == ctas_a == ctas_b >= 1
+    sub = lambda rows: {k: (v[rows] if k in rowwise and v is not None else v) for k, v in inp.items()}  # noqa: E731
+    paths = {_bwd_path(sub(r), use_pre) for r in (slice(0, b), slice(0, cut), slice(cut, b))}
+    assert len(paths) == 1 and next(iter(paths))[0] >= 1          # one segmented plan for all three
+    g_all, g_a, g_b = _run_bwd(sub(slice(0, b)), use_pre), _run_bwd(sub(slice(0, cut)), use_pre), \
+        _run_bwd(sub(slice(cut, b)), use_pre)
     for k in ("du", "ddelta", "dz", "dB", "dC"):
         if g_all[k] is not None:
             assert torch.equal(g_all[k], torch.cat([g_a[k], g_b[k]])), k
     for k in ("dA", "dD", "ddelta_bias"):
         want = (g_a[k] + g_b[k]).double().cpu().numpy()
         np.testing.assert_allclose(np64(g_all[k]), want, rtol=1e-5, atol=1e-5 * np.abs(want).max(), err_msg=k)
-    out_o, _, gr_o, scale = oracle_case(inp, gate=gate)
+    _, _, gr_o, scale = oracle_case(inp, gate=gate)
+    check_grads({k: v for k, v in g_all.items() if v is not None}, gr_o, scale)
+
+
+@pytest.mark.parametrize("shape,gate,use_pre", [((5, 100, 1024, 16), True, True),
+                                                ((5, 100, 1024, 16), True, False),
+                                                ((10, 37, 520, 5), False, False),
+                                                ((16, 64, 512, 16), True, True)])
+def test_bwd_row_kernel_bf16_vs_oracle(shape, gate, use_pre):
+    """bf16 problems whose 32-channel x row grid fills every SM (two CTAs each) run the
+    whole-row backward kernel (the Sift LM block's shape among them): against the oracle at
+    the bf16 tolerance, rtol 2e-2 with atol 2e-2 of each gradient's magnitude."""
+    inp = config_inputs(*shape, seed=41, gate=gate, device=DEV, dtype=torch.bfloat16)
+    assert _bwd_path(inp, use_pre) == (0, 2)
+    g = _run_bwd(inp, use_pre)
+    _, _, gr_o, scale = oracle_case(inp, gate=gate)
     for k in ("du", "ddelta", "dz", "dB", "dC", "dA", "dD", "ddelta_bias"):
         if k not in gr_o:
             continue
         want = gr_o[k]
-        # bf16 inputs with fp32 state: rtol 2e-2, atol 2e-2 of the gradient's magnitude
-        assert_close(np64(g_all[k]), want, 2e-2, 2e-2 * np.abs(want).max() + 1e-5 * np.abs(scale[k]).max(), k)
+        assert_close(np64(g[k]), want, 2e-2, 2e-2 * np.abs(want).max() + 1e-5 * np.abs(scale[k]).max(), k)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["fp32", "bf16"])
@@ -309,10 +329,9 @@ def test_bwd_many_segments_vs_oracle(dtype):
     """A long sequence over few channels: the backward walks it as several time segments
     (carries from 16-step sub-segment summaries), with a tail chunk, an initial state and
     its gradient; against the oracle (fp32 1e-4 / bf16 2e-2)."""
-    from swiftx_b200 import _lib
     b, L, D, N = 2, 1000, 64, 16
-    assert _lib.load().swx_scan_bwd_segments(L, D) >= 4
     inp = config_inputs(b, L, D, N, seed=17, device=DEV, dtype=dtype)
+    assert _bwd_path(inp, True)[0] >= 4
     h0 = (torch.randn(b, D, N, generator=torch.Generator().manual_seed(5)) * 0.3).to(DEV)
     out_o, hl_o, gr_o, scale = oracle_case(inp, h0=h0)
     pre = torch.empty(inp["u"].shape, device=DEV, dtype=torch.float32)

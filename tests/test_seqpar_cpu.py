@@ -1,9 +1,11 @@
 """Host logic of the sequence-parallel scan on CPU ranks (gloo, world sizes 2 and 3).
 
-Each rank runs sequence_parallel_scan on its chunk; the per-chunk kernel is replaced by
-the CPU oracle (through the `local_scan` hook), so what is tested here is the boundary
-exchange (all_gather) and the prefix combine.  The concatenated outputs must equal the
-oracle's scan of the whole sequence."""
+Each rank runs sequence_parallel_scan on its chunk; the two kernel calls are replaced
+through the hooks: the chunk's scan from a zero state by the CPU oracle, and the
+initial-state correction by a float64 NumPy restatement of its formula
+(out_t += silu(z_t) sum_n C_t[n] exp(A[:, n] S_t) h_in[n]).  What is tested is the
+peer-to-peer boundary exchange, the prefix combine and the correction's mathematics:
+the concatenated outputs must equal the oracle's scan of the whole sequence."""
 import os
 import socket
 
@@ -20,16 +22,27 @@ from swiftx_b200.workloads import config_inputs
 B_, L_, D_, N_ = 2, 90, 12, 16
 
 
-def oracle_local_scan(u, delta, A, B, C, D, z, delta_bias, softplus, h0, write_out, out_dtype):
+def oracle_local_scan(u, delta, A, B, C, D, z, delta_bias, softplus, out_dtype):
     n = lambda t: None if t is None else t.double().numpy()  # noqa: E731
     out, h_end = oracle.scan_fwd(n(u), n(delta), n(A), n(B), n(C), n(D), z=n(z), delta_bias=n(delta_bias),
-                                 delta_softplus=softplus, h0=n(h0), return_last_state=True)
-    bias = delta_bias if delta_bias is not None else 0.0
-    dte = torch.nn.functional.softplus(delta.double() + bias) if softplus else delta.double() + bias
-    dsum = dte.sum(1)
-    if not write_out:
-        return None, torch.from_numpy(h_end), dsum
-    return torch.from_numpy(out), None, None
+                                 delta_softplus=softplus, return_last_state=True)
+    return torch.from_numpy(out), torch.from_numpy(h_end), _delta_eff(delta, delta_bias, softplus).sum(1)
+
+
+def _delta_eff(delta, delta_bias, softplus):
+    bias = delta_bias.double() if delta_bias is not None else 0.0
+    return torch.nn.functional.softplus(delta.double() + bias) if softplus else delta.double() + bias
+
+
+def numpy_correct(out, h_in, u, delta, A, B, C, z, delta_bias, softplus):
+    """out_t += silu(z_t) * sum_n C_t[n] * exp(A[d, n] * S_t) * h_in[d, n], S_t = sum_{s<=t} delta_eff."""
+    S = torch.cumsum(_delta_eff(delta, delta_bias, softplus), 1).numpy()           # (b, L, D)
+    P = np.exp(A.double().numpy()[None, None] * S[..., None])                       # (b, L, D, N)
+    corr = np.einsum("bln,bldn,bdn->bld", C.double().numpy(), P, h_in.double().numpy())
+    if z is not None:
+        zz = z.double().numpy()
+        corr = corr * zz / (1.0 + np.exp(-zz))
+    return out + torch.from_numpy(corr)
 
 
 def _worker(rank, world, port, bounds, q):
@@ -41,7 +54,8 @@ def _worker(rank, world, port, bounds, q):
         s, e = bounds[rank], bounds[rank + 1]
         ch = {k: inp[k][:, s:e] for k in ("u", "delta", "z", "B", "C")}
         out = sequence_parallel_scan(ch["u"], ch["delta"], inp["A"], ch["B"], ch["C"], inp["D"], ch["z"],
-                                     inp["delta_bias"], True, local_scan=oracle_local_scan)
+                                     inp["delta_bias"], True, local_scan=oracle_local_scan,
+                                     correct=numpy_correct)
         q.put((rank, out.numpy()))
     finally:
         dist.destroy_process_group()

@@ -1,12 +1,13 @@
-"""Sequence-parallel scan on one GPU: chunks scanned as separate 'ranks' (pass 1 without
-output -> boundary values -> prefix combine -> pass 2 from the true initial state) must
-reproduce the one-pass scan of the whole sequence and the oracle."""
+"""Sequence-parallel scan on one GPU: chunks scanned as separate 'ranks' (each chunk's
+forward from a zero state -> boundary values -> prefix combine -> the initial-state
+correction swx_scan_correct) must reproduce the one-pass scan of the whole sequence and
+the oracle."""
 import numpy as np
 import pytest
 import torch
 
 import oracle
-from swiftx_b200.selective_scan import scan_forward
+from swiftx_b200.selective_scan import scan_correct, scan_forward
 from swiftx_b200.seqpar import combine_prefix
 from swiftx_b200.workloads import config_inputs
 
@@ -16,23 +17,49 @@ DEV = "cuda"
 
 def chunked_scan(inp, bounds, out_dtype=torch.float32):
     keys = ("u", "delta", "z", "B", "C")
-    ends, sums = [], []
+    outs, ends, sums = [], [], []
     for s, e in zip(bounds[:-1], bounds[1:]):
         ch = {k: inp[k][:, s:e] for k in keys}
         out, _, h_end, dsum = scan_forward(ch["u"], ch["delta"], inp["A"], ch["B"], ch["C"], inp["D"], ch["z"],
-                                           inp["delta_bias"], True, return_last_state=True,
-                                           return_delta_sum=True, write_out=False)
-        assert out is None
+                                           inp["delta_bias"], True, out_dtype=out_dtype, return_last_state=True,
+                                           return_delta_sum=True)
+        outs.append(out)
         ends.append(h_end)
         sums.append(dsum)
-    outs = []
     for g, (s, e) in enumerate(zip(bounds[:-1], bounds[1:])):
+        if g == 0:
+            continue
         ch = {k: inp[k][:, s:e] for k in keys}
-        h0 = combine_prefix(ends, sums, inp["A"].float(), g) if g > 0 else None
-        out, _, _ = scan_forward(ch["u"], ch["delta"], inp["A"], ch["B"], ch["C"], inp["D"], ch["z"],
-                                 inp["delta_bias"], True, h0=h0, out_dtype=out_dtype)
-        outs.append(out)
+        h_in = combine_prefix(ends, sums, inp["A"].float(), g)
+        scan_correct(outs[g], h_in, ch["u"], ch["delta"], inp["A"], ch["B"], ch["C"], z=ch["z"],
+                     delta_bias=inp["delta_bias"], delta_softplus=True)
     return torch.cat(outs, 1)
+
+
+@pytest.mark.parametrize("dtype,out_dtype,gate,N", [(torch.float32, torch.float32, True, 16),
+                                                    (torch.float32, torch.float32, False, 5),
+                                                    (torch.bfloat16, torch.float32, True, 16),
+                                                    (torch.bfloat16, torch.bfloat16, True, 12)])
+def test_correct_equals_scan_from_initial_state(dtype, out_dtype, gate, N):
+    """swx_scan_correct turns the forward from a zero state into the forward from h_in:
+    against the kernel's own forward with h0 = h_in and against the oracle (D not a
+    multiple of the 128-channel block, L not a multiple of the 256-step block)."""
+    b, L, D = 2, 700, 200
+    inp = config_inputs(b, L, D, N, seed=13, gate=gate, device=DEV, dtype=dtype)
+    h_in = (torch.randn(b, D, N, generator=torch.Generator().manual_seed(1)) * 0.5).to(DEV)
+    z = inp["z"] if gate else None
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], z, inp["delta_bias"], True)
+    out0, _, _ = scan_forward(*args, out_dtype=out_dtype)
+    want_k, _, _ = scan_forward(*args, h0=h_in, out_dtype=out_dtype)
+    got = scan_correct(out0, h_in, inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], z=z,
+                       delta_bias=inp["delta_bias"], delta_softplus=True)
+    n = lambda t: None if t is None else t.double().cpu().numpy()  # noqa: E731
+    want = oracle.scan_fwd(*(n(inp[k]) for k in ("u", "delta", "A", "B", "C")), D=n(inp["D"]), z=n(z),
+                           delta_bias=n(inp["delta_bias"]), delta_softplus=True, h0=n(h_in))
+    tol = dict(rtol=1e-4, atol=1e-5) if (dtype, out_dtype) == (torch.float32, torch.float32) else \
+        dict(rtol=2e-2, atol=2e-2 * np.abs(want).max())
+    np.testing.assert_allclose(n(got), want, **tol)
+    np.testing.assert_allclose(n(got), n(want_k), **tol)
 
 
 def test_delta_sum_output():
