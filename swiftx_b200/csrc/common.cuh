@@ -150,6 +150,52 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" :: "n"(N)); }
 
+// ---------------------------------------------------------------- bulk copies (TMA engine)
+// One-thread bulk global -> shared copies that complete on an mbarrier: the issuing thread
+// announces the bytes it expects (arrive.expect_tx), the copies count them down, and the
+// phase completes when all have landed.  Waits are bounded: a phase that does not complete
+// within `limit` polls (a byte count that does not match the copies) is reported instead
+// of spinning forever.
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    uint64_t state;
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 %0, [%1], %2;"
+                 : "=l"(state) : "r"(smem_u32(bar)), "r"(bytes) : "memory");
+    (void)state;
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred P;\n\t"
+                 "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, P;\n\t}"
+                 : "=r"(done) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t limit) {
+    for (uint32_t i = 0; i < limit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+// Order this thread's view of shared memory (after a barrier that followed other threads'
+// ordinary loads) before the bulk copies it issues next into the same memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// A 3-D tile of the tensor described by `map` (a __grid_constant__ kernel parameter),
+// starting at element coordinates (x, y, z), into this CTA's shared memory; completes on
+// `bar`.  x times the element size must be a multiple of 16 bytes; coordinates past the
+// tensor's extent read zeros.  No multicast: the tile lands in this CTA only.
+__device__ __forceinline__ void tma_load_3d(void* sdst, const void* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile("cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+                 "[%0], [%1, {%2, %3, %4}], [%5];"
+                 :: "r"(smem_u32(sdst)), "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)) : "memory");
+}
+
 // Copy a [rows x W] tile (row r at g + r*row_stride, columns [0, w_valid)) into
 // dense shared memory s[rows][W], zero-filling invalid rows and columns.
 // vec: every row start is 16-byte aligned, so 16-byte cp.async is used;

@@ -29,6 +29,8 @@
 //      stores and sums the four warps' dB / dC values into the CTA's partial row.
 // Every sum is taken in a fixed order: the gradients are bit-reproducible (no atomics,
 // unlike models/triton_scan.py:101-102,108-109).
+#include <cuda.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -36,6 +38,15 @@
 #include "scan_params.cuh"
 
 namespace swx {
+
+// TMA descriptors of the main kernel's inputs: (channel, step, row) tiles of 64 x 16 x 1
+// for u, delta, z, dout and the saved pre-gate output, 16 x 16 x 1 for B and C.  `ok`:
+// every descriptor was encoded (16-byte-aligned bases and strides); otherwise the kernel
+// stages with per-thread cp.async.
+struct SegMaps {
+    CUtensorMap u, dl, z, dout, yp, B, C;
+    int ok;
+};
 
 constexpr int SG_WARPS = 4;
 constexpr int SG_CH = 16 * SG_WARPS;      // channels per CTA
@@ -197,6 +208,7 @@ struct SegSmem {
     float ypv[YV ? TCK : 1][2][2][SG_CH / 2 + 2];   // the same for the readout (without YPRE)
     float bcw[SG_WARPS][TCK][32];          // per-warp dB | dC sums over its 16 channels
     float red[4][SG_THREADS];
+    uint64_t mbar[SG_RING];                // completion of each staging slot's TMA copies
 };
 
 // The states of one 8-step half: the chunk's states after each step and each step's
@@ -348,9 +360,9 @@ __device__ __forceinline__ void chunk_pass(SegSmem<Tin, YV>& S, int r, int nt, i
 }
 
 template <typename Tin, bool HAS_Z, bool YPRE>
-__global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanDev p) {
+__global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanDev p, const __grid_constant__ SegMaps tm) {
     constexpr bool YV = HAS_Z && !YPRE;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+    extern __shared__ __align__(128) unsigned char smem_raw[];   // TMA destinations: 128-byte aligned
     SegSmem<Tin, YV>& S = *reinterpret_cast<SegSmem<Tin, YV>*>(smem_raw);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -368,37 +380,35 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
     const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
     const float* gyp = YPRE ? p.ypre + (int64_t)bi * p.L * p.D + d0 : nullptr;
 
-    // staging: full 16 x 64 tiles of aligned rows (the common case) take a fast path with
-    // per-thread offsets computed once; anything else goes through stage_tile
-    constexpr int EPS = 16 / sizeof(Tin);                 // elements per 16-byte segment
-    constexpr int SEGS = SG_CH / EPS;                      // segments per row
-    const bool fast = nd == SG_CH && p.vec_u && p.vec_dl && p.vec_dout && (!HAS_Z || p.vec_z) &&
-                      (!YPRE || p.vec_yp) && p.N == NS && p.vec_B && p.vec_C;
+    // staging.  When the inputs' bases and strides are 16-byte aligned (the common case),
+    // one thread loads each input's whole 16-step tile with one TMA copy per tensor, all
+    // completing on the slot's mbarrier (steps past L and channels past D read zeros);
+    // otherwise every thread stages with 16-byte cp.async (stage_tile).
+    const bool fast = tm.ok != 0;
+    constexpr uint32_t TILE = TCK * SG_CH * sizeof(Tin), TILE_Y = TCK * SG_CH * 4, TILE_BC = TCK * NS * sizeof(Tin);
+    if (fast) {
+        if (tid == 0) {
+            mbar_init(&S.mbar[0], 1);
+            mbar_init(&S.mbar[1], 1);
+            mbar_fence_init();
+        }
+        __syncthreads();
+    }
     auto issue = [&](int k) {
         if (k < nk) {
             const int c = ck0 + nk - 1 - k, t0 = c * TCK, rv = min(TCK, p.L - t0), r = k & 1;
-            if (fast && rv == TCK) {
-#pragma unroll
-                for (int i = tid; i < TCK * SEGS; i += SG_THREADS) {
-                    const int row = i / SEGS, col = (i % SEGS) * EPS;
-                    const int64_t t = t0 + row;
-                    cp_async16(&S.u[r][row][col], gu + t * p.u_sl + col, 16);
-                    cp_async16(&S.dl[r][row][col], gdl + t * p.dl_sl + col, 16);
-                    if (HAS_Z) cp_async16(&S.z[r][row][col], gz + t * p.z_sl + col, 16);
-                    cp_async16(&S.dout[r][row][col], gdo + t * p.dout_sl + col, 16);
-                }
-                if (YPRE) {
-#pragma unroll
-                    for (int i = tid; i < TCK * SG_CH / 4; i += SG_THREADS) {
-                        const int row = i / (SG_CH / 4), col = (i % (SG_CH / 4)) * 4;
-                        cp_async16(&S.yp[r][row][col], gyp + (int64_t)(t0 + row) * p.D + col, 16);
-                    }
-                }
-                if (tid < 2 * TCK * NS / EPS) {                // B and C rows: NS / EPS segments each
-                    const int which = tid / (TCK * NS / EPS), i = tid % (TCK * NS / EPS);
-                    const int row = i / (NS / EPS), col = (i % (NS / EPS)) * EPS;
-                    const Tin* src = which ? gC + (int64_t)(t0 + row) * p.C_sl : gB + (int64_t)(t0 + row) * p.B_sl;
-                    cp_async16(which ? &S.C[r][row][col] : &S.B[r][row][col], src + col, 16);
+            if (fast) {
+                if (tid == 0) {
+                    fence_proxy_async_smem();            // the slot's last readers are past a barrier
+                    const uint32_t bytes = (HAS_Z ? 4 : 3) * TILE + (YPRE ? TILE_Y : 0) + 2 * TILE_BC;
+                    mbar_arrive_expect_tx(&S.mbar[r], bytes);
+                    tma_load_3d(&S.u[r][0][0], &tm.u, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.dl[r][0][0], &tm.dl, d0, t0, bi, &S.mbar[r]);
+                    if (HAS_Z) tma_load_3d(&S.z[r][0][0], &tm.z, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.dout[r][0][0], &tm.dout, d0, t0, bi, &S.mbar[r]);
+                    if (YPRE) tma_load_3d(&S.yp[r][0][0], &tm.yp, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.B[r][0][0], &tm.B, 0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.C[r][0][0], &tm.C, 0, t0, bi, &S.mbar[r]);
                 }
             } else {
                 stage_tile<Tin, SG_CH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, TCK, rv, nd, p.vec_u, tid, SG_THREADS);
@@ -416,7 +426,16 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
                 stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, TCK, rv, p.N, p.vec_C, tid, SG_THREADS);
             }
         }
-        cp_async_commit();
+        if (!fast) cp_async_commit();
+    };
+    // Wait for chunk k's inputs; false (every thread alike) if a bounded wait gave up.
+    auto arrived = [&](int k) -> bool {
+        bool ok = true;
+        if (fast) ok = mbar_wait_bounded(&S.mbar[k & 1], (k >> 1) & 1, 1u << 24);
+        else cp_async_wait<1>();
+        const bool bad = __syncthreads_or(!ok);
+        if (bad && tid == 0 && p.err) *p.err = SWX_ERR_TIMEOUT;
+        return !bad;
     };
 
     // ---- per-thread roles
@@ -477,8 +496,7 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
     for (int k = 0; k < nk; ++k) {
         const int c = ck0 + nk - 1 - k, t0 = c * TCK, nt = min(TCK, p.L - t0), r = k & 1;
         issue(k + 1);
-        cp_async_wait<1>();
-        __syncthreads();
+        if (!arrived(k)) return;                         // inputs never arrived: leave, flagged
 
         // ---------------------------------------------------------------- A: derive
 #pragma unroll
@@ -673,6 +691,55 @@ __global__ void scan_bwd_seg_finalize_kernel(const ScanDev p) {
 }
 
 // ===================================================================== launchers
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled, resolved through the runtime (no link to the driver library).
+static EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) !=
+                cudaSuccess || q != cudaDriverEntryPointSuccess)
+            return static_cast<EncodeTiledFn>(nullptr);
+        return reinterpret_cast<EncodeTiledFn>(f);
+    }();
+    return fn;
+}
+
+// A (inner, L, b) tensor with element strides (1, row, batch) and a box of (box_inner, 16, 1).
+static bool encode_3d(CUtensorMap* m, const void* base, int es, int64_t inner, int64_t L, int64_t b, int64_t row,
+                      int64_t batch, uint32_t box_inner) {
+    const EncodeTiledFn f = encode_tiled();
+    if (!f || !base || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+    const int64_t rs = row * es, bs = (b > 1 ? batch : row * L) * es;
+    if (rs % 16 || bs % 16 || rs <= 0 || bs <= 0 || rs >= (int64_t(1) << 40) || bs >= (int64_t(1) << 40)) return false;
+    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)L, (cuuint64_t)b};
+    cuuint64_t strides[2] = {(cuuint64_t)rs, (cuuint64_t)bs};
+    cuuint32_t box[3] = {box_inner, (cuuint32_t)TCK, 1};
+    cuuint32_t unit[3] = {1, 1, 1};
+    return f(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
+             const_cast<void*>(base), dims, strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+           CUDA_SUCCESS;
+}
+
+template <typename Tin, bool HAS_Z>
+static SegMaps seg_maps(const ScanDev& p) {
+    SegMaps m{};
+    const int es = sizeof(Tin);
+    bool ok = encode_3d(&m.u, p.u, es, p.D, p.L, p.b, p.u_sl, p.u_sb, SG_CH) &&
+              encode_3d(&m.dl, p.dl, es, p.D, p.L, p.b, p.dl_sl, p.dl_sb, SG_CH) &&
+              encode_3d(&m.dout, p.dout, es, p.D, p.L, p.b, p.dout_sl, p.dout_sb, SG_CH) &&
+              encode_3d(&m.B, p.B, es, p.N, p.L, p.b, p.B_sl, p.B_sb, NS) &&
+              encode_3d(&m.C, p.C, es, p.N, p.L, p.b, p.C_sl, p.C_sb, NS);
+    if (ok && HAS_Z) ok = encode_3d(&m.z, p.z, es, p.D, p.L, p.b, p.z_sl, p.z_sb, SG_CH);
+    if (ok && HAS_Z && p.ypre) ok = encode_3d(&m.yp, p.ypre, 4, p.D, p.L, p.b, p.D, (int64_t)p.L * p.D, SG_CH);
+    m.ok = ok ? 1 : 0;
+    return m;
+}
+
 template <typename Tin, bool HAS_Z>
 static cudaError_t launch_seg_t(const ScanDev& p, cudaStream_t st) {
     cudaError_t e;
@@ -691,7 +758,7 @@ static cudaError_t launch_seg_t(const ScanDev& p, cudaStream_t st) {
     const int smem = ypre ? sizeof(SegSmem<Tin, false>) : sizeof(SegSmem<Tin, HAS_Z>);
     if ((e = allow_smem(k, smem)) != cudaSuccess) return e;
     dim3 grid(p.nblk64, p.b, p.nseg);
-    k<<<grid, SG_THREADS, smem, st>>>(p);
+    k<<<grid, SG_THREADS, smem, st>>>(p, seg_maps<Tin, HAS_Z>(p));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const int64_t total = 2LL * NS * p.b * p.L + (int64_t)p.D * p.N + p.D;
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);

@@ -45,6 +45,7 @@ struct ScanDev {
     int nblk64;              // 64-channel blocks along D
     float* ws_q;             // (nsub, b, D, 16) local carry a_t0 * g_t0 of each sub-segment
     float* ws_s;             // (nsub, b, D) sum of delta_eff over each sub-segment
+    int* err;                // optional: set to SWX_ERR_TIMEOUT when a bounded wait gave up
 };
 
 }  // namespace swx
