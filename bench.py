@@ -56,9 +56,13 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+BWD_PROFILE = "scan_bwd_seg_kernel_8x2048x512.md"
+
+
 def profiled_traffic():
-    """dram bytes per launch of the backward kernel from the committed ncu summary."""
-    p = os.path.join(ROOT, "profiles", "scan_bwd_kernel_8x2048x512.md")
+    """dram bytes of one backward call (its summary, main and finalize launches) from the
+    committed ncu summary of the current backward kernels (BWD_PROFILE)."""
+    p = os.path.join(ROOT, "profiles", BWD_PROFILE)
     try:
         with open(p) as f:
             for line in f:
@@ -231,7 +235,11 @@ def run_ours(args, world, rank, local):
     e2e = run_e2e(args, inp, dev, world)
 
     peak, peak_kind = measured_peak()
-    dom_ms, dom_bytes, dom_name = (bwd_ms, bwd_b, "scan_bwd_kernel") if bwd_ms >= fwd_ms else \
+    # the dominant kernel is the backward's main kernel; it is timed with the two short
+    # launches of the same scan_backward call (its segment summaries before it, the dB/dC
+    # finalize after it), which the traffic figure also covers
+    dom_ms, dom_bytes, dom_name = (bwd_ms, bwd_b, "scan_bwd_seg_kernel (+ scan_bwd_summary_kernel, "
+                                   "scan_bwd_seg_finalize_kernel: one scan_backward call)") if bwd_ms >= fwd_ms else \
         (fwd_ms, fwd_b, "scan_fwd_kernel")
     achieved = dom_bytes / (dom_ms * 1e-3) / 1e9
     res = {
@@ -250,8 +258,9 @@ def run_ours(args, world, rank, local):
         "frac_of_hbm_step": round(value / world / peak, 4),
         "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                     "traffic": profiled_traffic(), "alg_bytes_per_launch": dom_bytes},
-        "gpu_launches": 3 * args.steps,
+                     "traffic": profiled_traffic() if bwd_ms >= fwd_ms else None,
+                     "traffic_source": "profiles/" + BWD_PROFILE, "alg_bytes_per_launch": dom_bytes},
+        "gpu_launches": 4 * args.steps,
         "e2e": e2e,
     }
     if sampler:
@@ -520,14 +529,17 @@ def run_long_scan(args, world, rank, local):
     """Long-sequence forward scan, bf16 u/delta/B/C/z, fp32 state and output, gated:
     b=4, L=65536, D=2048, N=16, split along the sequence over the ranks (sequence
     parallel: each rank's full forward from a zero state, the boundary values sent peer to
-    peer to the later ranks, prefix combine, initial-state correction on ranks > 0)."""
+    peer to the later ranks, prefix combine, initial-state correction on ranks > 0).  The
+    split is seqpar.chunk_bounds: rank 0, which has no correction to run, takes the
+    longer chunk."""
     import math
 
     from swiftx_b200.selective_scan import scan_correct, scan_forward
-    from swiftx_b200.seqpar import combine_prefix, exchange_boundaries, sequence_parallel_scan
+    from swiftx_b200.seqpar import chunk_bounds, combine_prefix, exchange_boundaries, sequence_parallel_scan
     dev = torch.device("cuda", local)
     b, L, D, N = 4, 65536, 2048, 16
-    Lr = L // world
+    bounds = chunk_bounds(L, world)
+    Lr = bounds[rank + 1] - bounds[rank]
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     bf = torch.bfloat16
     u = torch.randn(b, Lr, D, generator=g, device=dev).to(bf)
@@ -551,7 +563,7 @@ def run_long_scan(args, world, rank, local):
     res = base_line(args, world, METRIC, round(alg / (ms * 1e-3) / 1e9, 1), "GB/s", ms, "bf16-in/f32-state",
                     {"workload": "long-sequence scan fwd, b=4 L=65536 D=2048 N=16, bf16 in / fp32 state", "batch": b, "seqlen": L, "d_inner": D,
                      "d_state": N, "parallelism": f"sequence-parallel x{world}" if world > 1 else "single GPU",
-                     "alg_bytes": alg}, scaling="strong")
+                     "chunk_bounds": bounds, "alg_bytes": alg}, scaling="strong")
     res["clocks"] = clocks
     # phase split of one step on this rank (CUDA events; max over ranks): the chunk's
     # forward, the peer-to-peer exchange of boundary values, the combine + correction
@@ -575,6 +587,51 @@ def run_long_scan(args, world, rank, local):
                         "combine_and_correct": round(split[2], 4)}
     # kernel launches per step on the slowest rank: forward; correction = block sums + correct
     res["gpu_launches"] = (1 + (2 if world > 1 else 0)) * args.steps
+    return res
+
+
+def run_correct(args, world, rank, local):
+    """The sequence-parallel initial-state correction alone, on one rank's chunk of the
+    long-sequence workload: b=4, L=32768 (half of 65536), D=2048, N=16, bf16 u/delta/C/z,
+    fp32 output read and written in place, gated, softplus.  Reads delta, z (bf16), C and
+    the output; writes the output.  One chunk per rank (weak scaling)."""
+    import math
+
+    from swiftx_b200.selective_scan import scan_correct
+    dev = torch.device("cuda", local)
+    b, L, D, N = 4, args.corr_len, 2048, 16
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    bf = torch.bfloat16
+    u = torch.randn(b, L, D, generator=g, device=dev).to(bf)
+    dr = (torch.randn(b, L, D, generator=g, device=dev) * 0.5).to(bf)
+    z = torch.randn(b, L, D, generator=g, device=dev).to(bf)
+    Bm = torch.randn(b, L, N, generator=g, device=dev).to(bf)
+    Cm = torch.randn(b, L, N, generator=g, device=dev).to(bf)
+    gc = torch.Generator().manual_seed(0)
+    dt = torch.exp(torch.rand(D, generator=gc) * (math.log(0.1) - math.log(1e-3)) + math.log(1e-3))
+    bias = (dt + torch.log(-torch.expm1(-dt))).to(dev)
+    A = -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1).to(dev)
+    out = torch.randn(b, L, D, generator=g, device=dev)
+    h_in = torch.randn(b, D, N, generator=g, device=dev) * 0.1
+
+    def step():
+        scan_correct(out, h_in, u, dr, A, Bm, Cm, z=z, delta_bias=bias, delta_softplus=True)
+
+    ms, clocks = timed_steps(step, args, world, local, dev)
+    alg = b * L * D * (2 + 2 + 4 + 4) + b * L * N * 2
+    peak, kind = measured_peak()
+    achieved = alg / (ms * 1e-3) / 1e9
+    res = base_line(args, world, METRIC, round(alg * world / (ms * 1e-3) / 1e9, 1), "GB/s", ms, "bf16-in/f32-out",
+                    {"workload": f"sequence-parallel initial-state correction, b=4 L={L} D=2048 N=16",
+                     "batch": b, "seqlen": L, "d_inner": D, "d_state": N,
+                     "parallelism": f"one chunk per rank x{world}" if world > 1 else "single GPU",
+                     "l2": "inputs larger than L2", "alg_bytes_per_step": alg})
+    res["roofline"] = {"bound": "mufu (16 decays + softplus + silu per channel-step); hbm fraction shown",
+                       "kernel": "scan_correct_kernel (+ scan_correct_sums_kernel)",
+                       "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind, "unit": "GB/s",
+                       "frac": round(achieved / peak, 4), "traffic": None, "alg_bytes_per_launch": alg}
+    res["clocks"] = clocks
+    res["gpu_launches"] = 2 * args.steps
     return res
 
 
@@ -696,10 +753,13 @@ def main():
     ap.add_argument("--ls-batch", type=int, default=8, help="linear_scan: batch rows (8 = the measured size)")
     ap.add_argument("--e2e-streams", type=int, default=1, help="scan e2e: compute streams of the pipeline")
     ap.add_argument("--e2e-bufs", type=int, default=2, help="scan e2e: device buffer sets of the pipeline")
-    ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode", "linear_scan"], default="scan",
+    ap.add_argument("--corr-len", type=int, default=32768, help="correct: chunk length")
+    ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode", "linear_scan", "correct"],
+                    default="scan",
                     help="scan: fused scan fwd+bwd at b=8 L=2048 D=512 N=16 (default); lm_train: Sift LM training step; "
                          "long_scan: b=4 L=65536 D=2048 forward; decode: batch-256 24-layer recurrent step; "
-                         "linear_scan: parallel_scan fwd+bwd at (8, 2048, 512, 16)")
+                         "linear_scan: parallel_scan fwd+bwd at (8, 2048, 512, 16); "
+                         "correct: the sequence-parallel correction kernel on a b=4 L=32768 D=2048 chunk")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
@@ -716,6 +776,8 @@ def main():
         res = run_decode(args, world, rank, local)
     elif args.workload == "linear_scan":
         res = run_linear_scan(args, world, rank, local)
+    elif args.workload == "correct":
+        res = run_correct(args, world, rank, local)
     else:
         res = run_ours(args, world, rank, local)
     if rank == 0 and res is not None:

@@ -14,7 +14,8 @@ state), and the true initial state of chunk g is the prefix
            sum of delta_eff (swx_scan_correct) -- no step waits for the previous one
            except through S_t, so it runs at the throughput of its exponentials, not as
            a second serial walk of the chunk.
-Rank 0 needs no correction.
+Rank 0 needs no correction, so an even split leaves it idle while the later ranks
+correct; chunk_bounds() gives rank 0 the longer chunk that evens out the ranks' times.
 """
 import torch
 import torch.distributed as dist
@@ -31,6 +32,26 @@ def _kernel_local_scan(u, delta, A, B, C, D, z, delta_bias, delta_softplus, out_
 def _kernel_correct(out, h_in, u, delta, A, B, C, z, delta_bias, delta_softplus):
     return scan_correct(out, h_in, u, delta, A, B, C, z=z, delta_bias=delta_bias,
                         delta_softplus=delta_softplus)
+
+
+def chunk_bounds(L, world, correction_cost=0.7, multiple=256):
+    """Chunk boundaries [0, e_0, ..., L] that balance the ranks' work: rank 0 runs only the
+    forward of its chunk, every later rank the forward and the correction, which costs
+    `correction_cost` times the forward per step (0.70 measured on one B200 at b=4,
+    D=2048, N=16, bf16 in / fp32 out: 1.80 ms against 2.56 ms for a 32768-step chunk).
+    With rank 0's length x and the others' y, x = (1 + c) y and x + (world - 1) y = L.
+    Lengths are rounded to `multiple` steps; the last rank takes the remainder."""
+    if world <= 1:
+        return [0, L]
+    y = L / (world + correction_cost)
+    lens = [(1.0 + correction_cost) * y] + [y] * (world - 1)
+    bounds, acc = [0], 0.0
+    for r in range(world - 1):
+        acc += lens[r]
+        e = int(round(acc / multiple)) * multiple
+        bounds.append(min(max(e, bounds[-1]), L))
+    bounds.append(L)
+    return bounds
 
 
 def combine_prefix(h_end_all, dsum_all, A, rank):

@@ -16,7 +16,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from swiftx_b200.seqpar import combine_prefix, sequence_parallel_scan
+from swiftx_b200.seqpar import chunk_bounds, combine_prefix, sequence_parallel_scan
 from swiftx_b200.workloads import config_inputs
 
 B_, L_, D_, N_ = 2, 90, 12, 16
@@ -67,7 +67,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("bounds", [[0, 41, 90], [0, 30, 31, 90]])
+@pytest.mark.parametrize("bounds", [[0, 41, 90], [0, 30, 31, 90], chunk_bounds(90, 3, multiple=1)])
 def test_sequence_parallel_matches_whole_sequence(bounds):
     world = len(bounds) - 1
     ctx = mp.get_context("spawn")
@@ -98,3 +98,16 @@ def test_combine_prefix_is_the_chained_recurrence():
         h = torch.exp(A * dsums[k][..., None]) * h + h_ends[k]
     assert torch.allclose(combine_prefix(h_ends, dsums, A, 3), h)
     assert torch.equal(combine_prefix(h_ends, dsums, A, 0), torch.zeros(b, D, N, dtype=torch.float64))
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_chunk_bounds_balance(world):
+    L, c = 65536, 0.7
+    b = chunk_bounds(L, world, correction_cost=c)
+    assert b[0] == 0 and b[-1] == L and len(b) == world + 1
+    lens = [b[r + 1] - b[r] for r in range(world)]
+    assert all(n > 0 and n % 256 == 0 for n in lens)
+    # every rank's modelled time (forward, plus the correction on ranks > 0) within one
+    # rounding unit of the others
+    cost = [lens[0]] + [(1 + c) * n for n in lens[1:]]
+    assert max(cost) - min(cost) <= 2 * 256 * (1 + c)
