@@ -273,7 +273,7 @@ def run_ours(args, world, rank, local):
         for name, fn in (("lm_train", run_lm_train), ("long_scan", run_long_scan)):
             sub = fn(args, world, rank, local)
             keep = ("value", "unit", "ms_per_step", "scaling", "dtype", "config", "clocks", "e2e", "allreduce_ms",
-                    "allreduce_bytes", "phases_ms", "gpu_launches")
+                    "allreduce_bytes", "phases_ms", "step_latency_ms", "gpu_launches")
             res[name] = {k: sub[k] for k in keep if k in sub}
         res["gpu_launches"] += res["lm_train"]["gpu_launches"] + res["long_scan"]["gpu_launches"]
     return res
@@ -563,7 +563,10 @@ def run_long_scan(args, world, rank, local):
     res = base_line(args, world, METRIC, round(alg / (ms * 1e-3) / 1e9, 1), "GB/s", ms, "bf16-in/f32-state",
                     {"workload": "long-sequence scan fwd, b=4 L=65536 D=2048 N=16, bf16 in / fp32 state", "batch": b, "seqlen": L, "d_inner": D,
                      "d_state": N, "parallelism": f"sequence-parallel x{world}" if world > 1 else "single GPU",
-                     "chunk_bounds": bounds, "alg_bytes": alg}, scaling="strong")
+                     "chunk_bounds": bounds, "alg_bytes": alg,
+                     "timing": "K independent batches issued back to back (a rank starts the next batch's "
+                               "forward while later ranks correct the previous one); step_latency_ms: one "
+                               "batch alone"}, scaling="strong")
     res["clocks"] = clocks
     # phase split of one step on this rank (CUDA events; max over ranks): the chunk's
     # forward, the peer-to-peer exchange of boundary values, the combine + correction
@@ -582,9 +585,31 @@ def run_long_scan(args, world, rank, local):
                      delta_softplus=True)
     ev[3].record()
     torch.cuda.synchronize()
-    split = [max_over_ranks(ev[i].elapsed_time(ev[i + 1]), world, dev) for i in range(3)]
-    res["phases_ms"] = {"chunk_forward": round(split[0], 4), "exchange": round(split[1], 4),
-                        "combine_and_correct": round(split[2], 4)}
+    mine = torch.tensor([ev[i].elapsed_time(ev[i + 1]) for i in range(3)], dtype=torch.float64, device=dev)
+    if world > 1:
+        import torch.distributed as dist
+        every = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(every, mine)
+    else:
+        every = [mine]
+    # per rank (rank order): the exchange phase of a later rank includes its wait for the
+    # earlier ranks' longer forwards
+    res["phases_ms"] = {name: [round(float(t[i]), 4) for t in every]
+                        for i, name in enumerate(("chunk_forward", "exchange", "combine_and_correct"))}
+    # one step alone (nothing queued behind it; median of 3, max over ranks): a later rank
+    # cannot start its correction before every earlier rank's forward is done, so this is
+    # longer than ms_per_step, where a rank starts the next batch while later ranks correct
+    lat = []
+    for _ in range(3):
+        barrier(world)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        step()
+        e1.record()
+        torch.cuda.synchronize()
+        lat.append(max_over_ranks(e0.elapsed_time(e1), world, dev))
+    res["step_latency_ms"] = round(statistics.median(lat), 4)
     # kernel launches per step on the slowest rank: forward; correction = block sums + correct
     res["gpu_launches"] = (1 + (2 if world > 1 else 0)) * args.steps
     return res

@@ -151,6 +151,10 @@ def load():
     lib.swx_scan_bwd_segments.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_exp2_fma_eval.restype = ctypes.c_int
     lib.swx_exp2_fma_eval.argtypes = [vp, vp, i64, vp]
+    lib.swx_device_wait_status.restype = ctypes.c_int
+    lib.swx_device_wait_status.argtypes = []
+    lib.swx_diag_wait_timeout.restype = ctypes.c_int
+    lib.swx_diag_wait_timeout.argtypes = [ctypes.c_uint32, vp]
     lib.swx_rmsnorm_bwd_workspace_bytes.restype = i64
     lib.swx_rmsnorm_bwd_workspace_bytes.argtypes = [i64]
     lib.swx_embedding_bwd_workspace_bytes.restype = i64

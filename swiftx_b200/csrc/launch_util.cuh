@@ -9,6 +9,12 @@
 
 namespace swx {
 
+// status.cu: device address of one of the library's __device__ variables in the current
+// context (cached per device, context and variable), and the address of the status word
+// that kernels with bounded waits set to SWX_ERR_TIMEOUT (nullptr if the lookup failed).
+int device_symbol_address(const void* sym, void** out);
+int* wait_status_address();
+
 // Opt a kernel into more than 48 KB of dynamic shared memory.  Done once per kernel
 // and device (cached), so later launches -- e.g. inside CUDA-graph capture -- make no
 // runtime configuration calls.

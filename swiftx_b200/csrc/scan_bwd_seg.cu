@@ -54,6 +54,7 @@ constexpr int SG_THREADS = 32 * SG_WARPS;
 constexpr int SG_HALF = TCK / 2;          // steps whose states / decays live in registers
 constexpr int SG_RING = 2;                // raw staging slots
 constexpr int SUM_THREADS = 128;          // summary kernel: one channel per thread
+constexpr uint32_t SG_WAIT_POLLS = 1u << 24;   // mbarrier polls before a tile wait gives up
 
 __device__ __forceinline__ float load_A_sg(const ScanDev& p, int64_t i) {
     const float a = p.A[i];
@@ -431,10 +432,16 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
     // Wait for chunk k's inputs; false (every thread alike) if a bounded wait gave up.
     auto arrived = [&](int k) -> bool {
         bool ok = true;
-        if (fast) ok = mbar_wait_bounded(&S.mbar[k & 1], (k >> 1) & 1, 1u << 24);
+        if (fast) ok = mbar_wait_bounded(&S.mbar[k & 1], (k >> 1) & 1, SG_WAIT_POLLS);
         else cp_async_wait<1>();
         const bool bad = __syncthreads_or(!ok);
-        if (bad && tid == 0 && p.err) *p.err = SWX_ERR_TIMEOUT;
+        if (bad && tid == 0) {
+            if (p.err) *p.err = SWX_ERR_TIMEOUT;
+            // the copies still in flight (chunk k's and, if issued, chunk k+1's) write into
+            // this CTA's shared memory: give each a second bounded wait before leaving
+            mbar_wait_bounded(&S.mbar[k & 1], (k >> 1) & 1, SG_WAIT_POLLS);
+            if (k + 1 < nk) mbar_wait_bounded(&S.mbar[(k + 1) & 1], ((k + 1) >> 1) & 1, SG_WAIT_POLLS);
+        }
         return !bad;
     };
 
@@ -741,8 +748,10 @@ static SegMaps seg_maps(const ScanDev& p) {
 }
 
 template <typename Tin, bool HAS_Z>
-static cudaError_t launch_seg_t(const ScanDev& p, cudaStream_t st) {
+static cudaError_t launch_seg_t(const ScanDev& p0, cudaStream_t st) {
     cudaError_t e;
+    ScanDev p = p0;
+    p.err = wait_status_address();               // where a timed-out tile wait is recorded
     if (p.nseg > 1) {
         const int64_t nsum = p.nsub - p.first_sub;
         const int64_t gs = (int64_t)((p.D + SUM_THREADS - 1) / SUM_THREADS) * p.b * nsum;
