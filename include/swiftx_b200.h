@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 11
+#define SWX_ABI_VERSION 12
 
 /* status codes */
 #define SWX_OK 0
@@ -91,7 +91,22 @@ typedef struct swx_scan_args {
        when non-NULL; the backward then reads it for the gate gradient instead of
        recomputing the readout (Mamba's save-vs-recompute trade for the gate). */
     float* out_pre;
+    /* optional, with z: the SiftX pathway mix (models/sift_block.py:137-142) fused into the
+       gate.  group_w: (b, L, ngroups) fp32 per-token group weights (group stride 1; the
+       block's softmax(pathway(x)) * ngroups); group_of: (D,) int32 group of each channel,
+       in [0, ngroups); 1 <= ngroups <= SWX_MAX_GROUPS.  The forward writes
+       out_t = y_t * group_w[t, group_of[d]] * silu(z_t) (out_pre stays y_t).  The
+       backward reads dout through the same factor and, when d_group_w is non-NULL
+       (requires out_pre), writes d_group_w[b, t, g] = sum over the channels of group g of
+       dout * silu(z) * y: (b, L, ngroups) dense fp32, fixed summation order.  Not for
+       float64 inputs. */
+    const float* group_w; int64_t group_w_sb, group_w_sl;
+    const int32_t* group_of;
+    int32_t ngroups;
+    float* d_group_w;
 } swx_scan_args;
+
+#define SWX_MAX_GROUPS 8
 
 int swx_abi_version(void);
 const char* swx_status_string(int status);
@@ -241,6 +256,13 @@ typedef struct swx_decode_args {
     float* out;                       /* (b, D) */
     int32_t flags;                    /* SWX_DECODE_A_LOG; other bits must be zero */
     int32_t reserved;
+    /* optional, with z: the SiftX pathway mix before the gate (models/sift_block.py:
+       137-142, 172-173), out = y * group_w[b, group_of[d]] * silu(z).  group_w (b, ngroups)
+       fp32 with group stride 1; group_of (D,) int32; 1 <= ngroups <= SWX_MAX_GROUPS. */
+    const float* group_w; int64_t group_w_sb;
+    const int32_t* group_of;
+    int32_t ngroups;
+    int32_t reserved2;
 } swx_decode_args;
 
 /* Replaces SiftBlock.step's conv-window roll, conv dot + bias + SiLU and in-place

@@ -16,6 +16,7 @@ SWX_ERR_INVALID_ARG = 1
 SWX_ERR_UNSUPPORTED = 2
 SWX_ERR_CUDA = 3
 SWX_ERR_TIMEOUT = 4
+SWX_MAX_GROUPS = 8
 # capacity of the static scratch of swx_scan_bwd_static_scratch (SWX_STATIC_SCRATCH_BYTES)
 SWX_STATIC_SCRATCH_BYTES = 8 << 20
 
@@ -48,6 +49,8 @@ class ScanArgs(ctypes.Structure):
         ("workspace", vp), ("workspace_bytes", i64),
         ("delta_sum", vp),
         ("out_pre", vp),
+        ("group_w", vp), ("group_w_sb", i64), ("group_w_sl", i64),
+        ("group_of", vp), ("ngroups", i32), ("d_group_w", vp),
     ]
 
 
@@ -79,6 +82,7 @@ class DecodeArgs(ctypes.Structure):
         ("conv_weight", vp), ("conv_bias", vp), ("A", vp), ("Dskip", vp), ("delta_bias", vp),
         ("conv_state", vp), ("ssm_state", vp), ("xc_out", vp), ("out", vp),
         ("flags", i32), ("reserved", i32),
+        ("group_w", vp), ("group_w_sb", i64), ("group_of", vp), ("ngroups", i32), ("reserved2", i32),
     ]
 
 

@@ -12,6 +12,7 @@ cudaError_t launch_scan_fwd_f64(const ScanDev& p, cudaStream_t st);
 cudaError_t launch_scan_bwd_f64(const ScanDev& p, cudaStream_t st);
 cudaError_t launch_scan_bwd_seg(const ScanDev& p, int in_dtype, bool has_z, cudaStream_t st);
 cudaError_t launch_scan_bwd_rows(const ScanDev& p, bool has_z, cudaStream_t st);
+cudaError_t launch_group_w_grad(const ScanDev& p, int in_dtype, cudaStream_t st);
 cudaError_t scan_bwd_rows_applicable(const ScanDev& p, int in_dtype, bool has_z, bool* yes);
 cudaError_t launch_scan_correct(const ScanDev& p, int in_dtype, int out_dtype, bool has_z, float* ws,
                                 cudaStream_t st);
@@ -113,6 +114,13 @@ int check_common(const swx_scan_args* a) {
     if (a->batch > 65535 || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
     if (elem_size(a->in_dtype) == 0) return SWX_ERR_UNSUPPORTED;
     if (a->flags & ~SWX_SCAN_A_LOG) return SWX_ERR_INVALID_ARG;
+    if (a->group_w || a->d_group_w) {
+        // the pathway mix: with the gate, fp32 / bf16 only, a bounded number of groups
+        if (a->in_dtype == SWX_DTYPE_F64 || !a->z) return SWX_ERR_UNSUPPORTED;
+        if (a->ngroups < 1 || a->ngroups > SWX_MAX_GROUPS) return SWX_ERR_UNSUPPORTED;
+        if (!a->group_w || !a->group_of) return SWX_ERR_INVALID_ARG;
+        if (a->group_w_sb < 0 || a->group_w_sl < 0) return SWX_ERR_INVALID_ARG;
+    }
     if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
     if (!a->u || !a->delta || !a->B || !a->C || !a->A) return SWX_ERR_INVALID_ARG;
     return SWX_OK;
@@ -144,6 +152,10 @@ swx::ScanDev pack(const swx_scan_args* a) {
     p.du = a->du; p.ddl = a->ddelta; p.dz = a->dz; p.dB = a->dB; p.dC = a->dC;
     p.dA = a->dA; p.dD = a->dD; p.ddbias = a->ddelta_bias; p.dh0 = a->dh0;
     p.nblk = (int)((a->dim + 31) / 32);
+    if (a->group_w) {
+        p.gw = a->group_w; p.gw_sb = a->group_w_sb; p.gw_sl = a->group_w_sl;
+        p.gof = a->group_of; p.ngroups = a->ngroups; p.dgw = a->d_group_w;
+    }
     return p;
 }
 
@@ -214,6 +226,7 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     if (!a->dout || !a->du || !a->ddelta || !a->dB || !a->dC || !a->dA || !a->checkpoints)
         return SWX_ERR_INVALID_ARG;
     if (a->z && !a->dz) return SWX_ERR_INVALID_ARG;
+    if (a->d_group_w && !a->out_pre) return SWX_ERR_INVALID_ARG;     // the weights' gradient reads y
     if (!aligned16(a->checkpoints) || !a->workspace || !aligned16(a->workspace)) return SWX_ERR_INVALID_ARG;
     const bool f64 = a->in_dtype == SWX_DTYPE_F64;
     const WsLayout w = ws_layout(a->batch, a->seqlen, a->dim, f64 ? 8 : 4);
@@ -225,16 +238,22 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     p.ws_d = reinterpret_cast<float*>(ws + w.d);
     p.ws_bias = reinterpret_cast<float*>(ws + w.bias);
     if (f64) return from_cuda(swx::launch_scan_bwd_f64(p, static_cast<cudaStream_t>(stream)));
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
     bool rows = false;
     if (swx::scan_bwd_rows_applicable(p, a->in_dtype, a->z != nullptr, &rows) != cudaSuccess) return SWX_ERR_CUDA;
-    if (rows)
-        return from_cuda(swx::launch_scan_bwd_rows(p, a->z != nullptr, static_cast<cudaStream_t>(stream)));
-    const SegPlan sp = seg_plan(a->seqlen, a->dim);
-    p.seg_len = (int)sp.seg_len; p.nseg = (int)sp.nseg; p.sub_len = (int)sp.sub_len;
-    p.nsub = (int)sp.nsub; p.first_sub = (int)sp.first_sub; p.nblk64 = (int)sp.nblk64;
-    p.ws_q = reinterpret_cast<float*>(ws + w.q);
-    p.ws_s = reinterpret_cast<float*>(ws + w.s);
-    return from_cuda(swx::launch_scan_bwd_seg(p, a->in_dtype, a->z != nullptr, static_cast<cudaStream_t>(stream)));
+    cudaError_t e;
+    if (rows) {
+        e = swx::launch_scan_bwd_rows(p, a->z != nullptr, st);
+    } else {
+        const SegPlan sp = seg_plan(a->seqlen, a->dim);
+        p.seg_len = (int)sp.seg_len; p.nseg = (int)sp.nseg; p.sub_len = (int)sp.sub_len;
+        p.nsub = (int)sp.nsub; p.first_sub = (int)sp.first_sub; p.nblk64 = (int)sp.nblk64;
+        p.ws_q = reinterpret_cast<float*>(ws + w.q);
+        p.ws_s = reinterpret_cast<float*>(ws + w.s);
+        e = swx::launch_scan_bwd_seg(p, a->in_dtype, a->z != nullptr, st);
+    }
+    if (e == cudaSuccess && p.dgw) e = swx::launch_group_w_grad(p, a->in_dtype, st);
+    return from_cuda(e);
 }
 
 int64_t swx_scan_correct_workspace_bytes(int64_t batch, int64_t seqlen, int64_t dim) {

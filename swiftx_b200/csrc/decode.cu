@@ -29,7 +29,14 @@ struct DecDev {
     const float* cw; const float* cb;
     const float* A; const float* Dskip; const float* dbias;
     float* conv_state; float* ssm_state; float* xc_out; float* out;
+    const float* gw; int64_t gw_sb;    // SiftX pathway mix: (b, ngroups) weights, or nullptr
+    const int* gof;                    // (D,) group of each channel
 };
+
+// Pathway weight of channel d's group for batch row r (1 without the mix).
+__device__ __forceinline__ float dec_group_weight(const DecDev& p, int64_t r, int d) {
+    return p.gw ? p.gw[r * p.gw_sb + p.gof[d]] : 1.f;
+}
 
 // Four consecutive entries of A from offset i (16-byte aligned), formed as -expf(A_log)
 // when the caller passed log(-A) -- expf is the function torch.exp evaluates for fp32.
@@ -72,7 +79,7 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
     }
 
     // ---- loads for all rows
-    float xin[DEC_RB], zv[DEC_RB], raw[DEC_RB], win[DEC_RB][K];
+    float xin[DEC_RB], zv[DEC_RB], gwv[DEC_RB], raw[DEC_RB], win[DEC_RB][K];
     float4 h4[DEC_RB], b4[DEC_RB], c4[DEC_RB];
     bool valid[DEC_RB];
 #pragma unroll
@@ -82,6 +89,7 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
         const int bc = valid[r] ? bi : 0;
         const int64_t bd = (int64_t)bc * p.D + dc;
         xin[r] = p.x[bc * p.x_sb + dc];
+        gwv[r] = 1.f;
         if (conv) {
             const float* cs = p.conv_state + bd * K;
             if (K == 4) {
@@ -95,6 +103,7 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
         if (ssm) {
             raw[r] = p.dl[bc * p.dl_sb + dc] + dbi;
             zv[r] = HAS_Z ? p.z[bc * p.z_sb + dc] : 0.f;
+            gwv[r] = HAS_Z ? dec_group_weight(p, bc, dc) : 1.f;
             if (full) {
                 h4[r] = *reinterpret_cast<const float4*>(p.ssm_state + bd * NS + 4 * j);
                 b4[r] = *reinterpret_cast<const float4*>(p.B + bc * p.B_sb + 4 * j);
@@ -159,7 +168,7 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
         y += __shfl_xor_sync(0xffffffffu, y, 2);
         if (valid[r] && j == 0) {
             y = fmaf(dsk, xc, y);
-            if (HAS_Z) y *= silu_f(zv[r]);
+            if (HAS_Z) y *= silu_f(zv[r]) * gwv[r];
             p.out[bd] = y;
         }
     }
@@ -278,7 +287,7 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
                 if (p.xc_out) p.xc_out[bd] = xc;
             }
             y = fmaf(dsk, xc, y);
-            if (HAS_Z) y *= silu_f(T.z[ch]);
+            if (HAS_Z) y *= silu_f(T.z[ch]) * dec_group_weight(p, r, d);
             p.out[bd] = y;
         }
         __syncthreads();                  // slot k % DP_STAGES is refilled at k+1
@@ -352,6 +361,12 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     p.dl = a->delta; p.dl_sb = a->delta_sb; p.B = a->B; p.B_sb = a->B_sb; p.C = a->C; p.C_sb = a->C_sb;
     p.cw = a->conv_weight; p.cb = a->conv_bias; p.A = a->A; p.Dskip = a->Dskip; p.dbias = a->delta_bias;
     p.conv_state = a->conv_state; p.ssm_state = a->ssm_state; p.xc_out = a->xc_out; p.out = a->out;
+    if (a->group_w) {
+        if (!a->z || !(a->mode & SWX_DECODE_SSM)) return SWX_ERR_UNSUPPORTED;
+        if (!a->group_of || a->group_w_sb < 0 || a->ngroups < 1 || a->ngroups > SWX_MAX_GROUPS)
+            return SWX_ERR_INVALID_ARG;
+        p.gw = a->group_w; p.gw_sb = a->group_w_sb; p.gof = a->group_of;
+    }
     cudaStream_t st = static_cast<cudaStream_t>(stream);
     if (swx::stream_ok(p)) return swx::launch_stream(p, st) == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
     switch ((a->mode & SWX_DECODE_CONV) ? p.K : 4) {

@@ -110,7 +110,8 @@ __device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], c
 // variant is built for two CTAs per SM (at most 128 registers a thread): the output-writing
 // kernels need ~100 anyway, and the sequence-parallel pass 1 (no output) then fits two CTAs
 // per SM at the cost of a few spilled bytes.
-template <typename Tin, typename Tout, bool HAS_Z, bool WR, int NA>
+// GW: the SiftX pathway mix is applied before the gate (only with HAS_Z and WR).
+template <typename Tin, typename Tout, bool HAS_Z, bool WR, int NA, bool GW = false>
 __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel(const ScanDev p) {
     constexpr int FNAUX = NA, FNTH = NSCAN + NA;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
         const bool evalid = ech < nd;
         const float eD = (p.Dskip && evalid) ? p.Dskip[d0 + ech] : 0.f;
         const float ebias = (p.dbias && evalid) ? p.dbias[d0 + ech] : 0.f;
+        const int egroup = (GW && evalid) ? p.gof[d0 + ech] : 0;       // pathway group of the channel
         const Tin* gu = static_cast<const Tin*>(p.u) + bi * p.u_sb + d0;
         const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + d0;
         const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + d0 : nullptr;
@@ -220,6 +222,9 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
                         if (t < nt) q[0] = y.x;
                         if (t + 1 < nt) q[p.D] = y.y;
                     }
+                    if (GW)                            // SiftX pathway mix, before the gate
+                        y = mul2(y, f2(t < nt ? group_weight(p, bi, t0 + t, egroup) : 0.f,
+                                       t + 1 < nt ? group_weight(p, bi, t0 + t + 1, egroup) : 0.f));
                     const float2 zz = f2(Elem<Tin>::to_f(S.z[r][t][ech]), Elem<Tin>::to_f(S.z[r][t + 1][ech]));
                     y = mul2(y, mul2(zz, sigmoid2(zz)));
                 }
@@ -278,6 +283,12 @@ template <typename Tin, typename Tout, bool HAS_Z>
 static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
     auto k2 = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true, 256> : scan_fwd_kernel<Tin, Tout, HAS_Z, false, 256>;
     auto k1 = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true, 128> : scan_fwd_kernel<Tin, Tout, HAS_Z, false, 128>;
+    if constexpr (HAS_Z) {
+        if (p.gw && p.out) {
+            k2 = scan_fwd_kernel<Tin, Tout, true, true, 256, true>;
+            k1 = scan_fwd_kernel<Tin, Tout, true, true, 128, true>;
+        }
+    }
     const int smem = sizeof(FwdSmem<Tin>);
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
     const long long nblocks = (long long)grid.x * grid.y;

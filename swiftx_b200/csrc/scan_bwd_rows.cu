@@ -179,7 +179,8 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
 // most 128 registers a thread, about 100 KB of shared memory with bf16 inputs): B is
 // reloaded from shared memory in the reverse pass instead of kept in registers, and the
 // per-step results are handed to the helper warps in 4-step tiles instead of 8.
-template <typename Tin, bool HAS_Z, bool YPRE, bool LOWREG>
+// GW (with HAS_Z): the forward applied the SiftX pathway mix before the gate.
+template <typename Tin, bool HAS_Z, bool YPRE, bool LOWREG, bool GW = false>
 __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const ScanDev p) {
     constexpr bool YV = HAS_Z && !YPRE;
     constexpr int HTQ = LOWREG ? 4 : HT;       // steps per hand-off tile
@@ -262,6 +263,7 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         const bool evalid = ech < nd;
         const float eD = (p.Dskip && evalid) ? p.Dskip[d0 + ech] : 0.f;
         const float ebias = (p.dbias && evalid) ? p.dbias[d0 + ech] : 0.f;
+        const int egroup = (GW && evalid) ? p.gof[d0 + ech] : 0;       // pathway group of the channel
         const Tin* gu = static_cast<const Tin*>(p.u) + bi * p.u_sb + d0;
         const Tin* gdl = static_cast<const Tin*>(p.dl) + bi * p.dl_sb + d0;
         const Tin* gz = HAS_Z ? static_cast<const Tin*>(p.z) + bi * p.z_sb + d0 : nullptr;
@@ -294,12 +296,16 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         const float2 bias2 = bc2(ebias);
         auto derive = [&](int k) {
             const int r = k % RING, s = k & 1;
+            const int t0 = (nck - 1 - k) * TCK, nt = min(TCK, p.L - t0);
 #pragma unroll
             for (int m = 0; m < TCK * SCH / (2 * NAUX); ++m) {
                 const int t = 2 * (at / SCH + m * (NAUX / SCH));
                 const float2 raw = add2(f2(Elem<Tin>::to_f(S.dl[r][t][ech]), Elem<Tin>::to_f(S.dl[r][t + 1][ech])), bias2);
                 const float2 uv = f2(Elem<Tin>::to_f(S.u[r][t][ech]), Elem<Tin>::to_f(S.u[r][t + 1][ech]));
-                const float2 dov = f2(Elem<Tin>::to_f(S.dout[r][t][ech]), Elem<Tin>::to_f(S.dout[r][t + 1][ech]));
+                float2 dov = f2(Elem<Tin>::to_f(S.dout[r][t][ech]), Elem<Tin>::to_f(S.dout[r][t + 1][ech]));
+                if (GW)                                // the pathway mix scales the gate's input
+                    dov = mul2(dov, f2(t < nt ? group_weight(p, bi, t0 + t, egroup) : 0.f,
+                                       t + 1 < nt ? group_weight(p, bi, t0 + t + 1, egroup) : 0.f));
                 float2 dte = raw, dsp = bc2(1.f);
                 if (p.softplus) softplus2(raw, dte, dsp);
                 float2 dy = dov, q = bc2(0.f);
@@ -494,6 +500,9 @@ template <typename Tin, bool HAS_Z>
 static cudaError_t launch_t(const ScanDev& p, cudaStream_t st) {
     const bool ypre = HAS_Z && p.ypre;
     auto k = ypre ? scan_bwd_kernel<Tin, HAS_Z, true, true> : scan_bwd_kernel<Tin, HAS_Z, false, true>;
+    if constexpr (HAS_Z) {
+        if (p.gw) k = ypre ? scan_bwd_kernel<Tin, true, true, true, true> : scan_bwd_kernel<Tin, true, false, true, true>;
+    }
     const int smem = sizeof(BwdSmem<Tin, 4>);
     cudaError_t e = allow_smem(k, smem);
     if (e != cudaSuccess) return e;

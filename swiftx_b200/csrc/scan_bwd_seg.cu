@@ -94,7 +94,9 @@ struct SumSmem {
     Tin z[2][SUM_BLK][SUM_THREADS];
 };
 
-template <typename Tin, bool HAS_Z>
+// GW (with HAS_Z): the forward applied the SiftX pathway mix before the gate, so the
+// gate's input gradient carries the channel's group weight.
+template <typename Tin, bool HAS_Z, bool GW = false>
 __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const ScanDev p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SumSmem<Tin>& S = *reinterpret_cast<SumSmem<Tin>*>(smem_raw);
@@ -135,6 +137,7 @@ __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const Sca
         S.C[row][n] = n < p.N ? Elem<Tin>::to_f(gC[(int64_t)(t0 + row) * p.C_sl + n]) : 0.f;
     }
     const float bias = p.dbias ? p.dbias[dc] : 0.f;
+    const int grp = GW ? p.gof[dc] : 0;                  // pathway group of the channel
     float2 A2[NS / 2], g[NS / 2], an[NS / 2];
 #pragma unroll
     for (int i = 0; i < NS / 2; ++i) {
@@ -159,7 +162,8 @@ __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const Sca
             const float dov = Elem<Tin>::to_f(S.dout[r][row][tid]);
             const float dte = p.softplus ? softplus_f(raw) : raw;
             ssum += dte;
-            const float dy = HAS_Z ? dov * silu_f(Elem<Tin>::to_f(S.z[r][row][tid])) : dov;
+            float dy = HAS_Z ? dov * silu_f(Elem<Tin>::to_f(S.z[r][row][tid])) : dov;
+            if (GW) dy *= p.gw[(int64_t)bi * p.gw_sb + (int64_t)t * p.gw_sl + grp];
             const float4* cr = reinterpret_cast<const float4*>(&S.C[t - t0][0]);
             const float2 dt2 = bc2(dte), dy2 = bc2(dy);
 #pragma unroll
@@ -360,7 +364,7 @@ __device__ __forceinline__ void chunk_pass(SegSmem<Tin, YV>& S, int r, int nt, i
     }
 }
 
-template <typename Tin, bool HAS_Z, bool YPRE>
+template <typename Tin, bool HAS_Z, bool YPRE, bool GW = false>
 __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanDev p, const __grid_constant__ SegMaps tm) {
     constexpr bool YV = HAS_Z && !YPRE;
     extern __shared__ __align__(128) unsigned char smem_raw[];   // TMA destinations: 128-byte aligned
@@ -450,6 +454,7 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
     const int ech = tid & (SG_CH - 1), eh = tid >> 6;
     const bool evalid = ech < nd;
     const float ebias = (p.dbias && evalid) ? p.dbias[d0 + ech] : 0.f;
+    const int egroup = (GW && evalid) ? p.gof[d0 + ech] : 0;       // pathway group of the channel
     // phase C: channel pair cp (channels 2cp, 2cp + 1), steps ch4, ch4 + 4, ch4 + 8, ch4 + 12
     const int cpair = tid & 31, ch4 = tid >> 5;
     const bool cv0 = 2 * cpair < nd, cv1 = 2 * cpair + 1 < nd;
@@ -512,7 +517,10 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
             const float2 uv = f2(Elem<Tin>::to_f(S.u[r][ta][ech]), Elem<Tin>::to_f(S.u[r][tb][ech]));
             const float2 raw = add2(f2(Elem<Tin>::to_f(S.dl[r][ta][ech]), Elem<Tin>::to_f(S.dl[r][tb][ech])),
                                     bc2(ebias));
-            const float2 dov = f2(Elem<Tin>::to_f(S.dout[r][ta][ech]), Elem<Tin>::to_f(S.dout[r][tb][ech]));
+            float2 dov = f2(Elem<Tin>::to_f(S.dout[r][ta][ech]), Elem<Tin>::to_f(S.dout[r][tb][ech]));
+            if (GW)                                      // the pathway mix scales the gate's input
+                dov = mul2(dov, f2(ta < nt ? group_weight(p, bi, t0 + ta, egroup) : 0.f,
+                                   tb < nt ? group_weight(p, bi, t0 + tb, egroup) : 0.f));
             float2 dte = raw, dsp = bc2(1.f);
             if (p.softplus) softplus2(raw, dte, dsp);
             float2 dy = dov, qz = bc2(0.f);
@@ -757,6 +765,9 @@ static cudaError_t launch_seg_t(const ScanDev& p0, cudaStream_t st) {
         const int64_t gs = (int64_t)((p.D + SUM_THREADS - 1) / SUM_THREADS) * p.b * nsum;
         if (gs > INT32_MAX) return cudaErrorInvalidConfiguration;
         auto ks = scan_bwd_summary_kernel<Tin, HAS_Z>;
+        if constexpr (HAS_Z) {
+            if (p.gw) ks = scan_bwd_summary_kernel<Tin, true, true>;
+        }
         const int ssm = sizeof(SumSmem<Tin>);
         if ((e = allow_smem(ks, ssm)) != cudaSuccess) return e;
         ks<<<(unsigned)gs, SUM_THREADS, ssm, st>>>(p);
@@ -764,6 +775,9 @@ static cudaError_t launch_seg_t(const ScanDev& p0, cudaStream_t st) {
     }
     const bool ypre = HAS_Z && p.ypre;
     auto k = ypre ? scan_bwd_seg_kernel<Tin, HAS_Z, true> : scan_bwd_seg_kernel<Tin, HAS_Z, false>;
+    if constexpr (HAS_Z) {
+        if (p.gw) k = ypre ? scan_bwd_seg_kernel<Tin, true, true, true> : scan_bwd_seg_kernel<Tin, true, false, true>;
+    }
     const int smem = ypre ? sizeof(SegSmem<Tin, false>) : sizeof(SegSmem<Tin, HAS_Z>);
     if ((e = allow_smem(k, smem)) != cudaSuccess) return e;
     dim3 grid(p.nblk64, p.b, p.nseg);

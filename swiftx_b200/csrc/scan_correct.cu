@@ -4,7 +4,8 @@
 // gains  P_t h_in  with P_t = prod_{s<=t} exp(delta_s A) = exp(A S_t),  S_t = sum_{s<=t}
 // delta_s  (per channel; one decay per state), so the output gains
 //     corr_t = sum_n C_t[n] exp(A[n] S_t) h_in[n],   out_t += gate_t * corr_t
-// (gate_t = silu(z_t), the gate being a factor of the pre-gate output).  Unlike a
+// (gate_t = silu(z_t), times the pathway group weight when the mix is fused, the gate
+// being a factor of the pre-gate output).  Unlike a
 // rescan, no step depends on the previous one except through the running sum S_t, so the
 // work is split over (channel, 256-step block) threads:
 //   1. scan_correct_sums_kernel: sum of delta_eff over each block;
@@ -47,7 +48,7 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_sums_kernel(const Sca
     bsum[((int64_t)bi * nblk + k) * p.D + d] = s;
 }
 
-template <typename Tin, typename Tout, bool HAS_Z>
+template <typename Tin, typename Tout, bool HAS_Z, bool GW = false>
 __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev p, const float* bsum, int nblk) {
     __shared__ __align__(16) float Cs[CR_CROWS][NS];
     const int tid = threadIdx.x;
@@ -77,6 +78,7 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev 
     const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
     Tout* out = static_cast<Tout*>(p.out) + (int64_t)bi * p.L * p.D + dc;
     const float bias = p.dbias ? p.dbias[dc] : 0.f;
+    const int grp = GW ? p.gof[dc] : 0;        // pathway group of the channel (mix fused into the gate)
     for (int tb = t0; tb < t1; tb += CR_CROWS) {
         const int nr = min(CR_CROWS, t1 - tb);
         __syncthreads();
@@ -116,6 +118,7 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev 
                 const float2 acc = add2(acc0, acc1);
                 float corr = acc.x + acc.y;
                 if (HAS_Z) corr *= silu_f(zz[i]);
+                if (GW) corr *= p.gw[(int64_t)bi * p.gw_sb + (int64_t)(tb + r0 + i) * p.gw_sl + grp];
                 oo[i] += corr;
             }
 #pragma unroll
@@ -132,7 +135,8 @@ static cudaError_t launch_correct_t(const ScanDev& p, float* ws, bool has_z, cud
     scan_correct_sums_kernel<Tin><<<grid, CR_THREADS, 0, st>>>(p, ws, nblk);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
-    if (has_z) scan_correct_kernel<Tin, Tout, true><<<grid, CR_THREADS, 0, st>>>(p, ws, nblk);
+    if (has_z && p.gw) scan_correct_kernel<Tin, Tout, true, true><<<grid, CR_THREADS, 0, st>>>(p, ws, nblk);
+    else if (has_z) scan_correct_kernel<Tin, Tout, true><<<grid, CR_THREADS, 0, st>>>(p, ws, nblk);
     else scan_correct_kernel<Tin, Tout, false><<<grid, CR_THREADS, 0, st>>>(p, ws, nblk);
     return cudaGetLastError();
 }

@@ -46,6 +46,17 @@ struct ScanDev {
     float* ws_q;             // (nsub, b, D, 16) local carry a_t0 * g_t0 of each sub-segment
     float* ws_s;             // (nsub, b, D) sum of delta_eff over each sub-segment
     int* err;                // optional: set to SWX_ERR_TIMEOUT when a bounded wait gave up
+    // SiftX pathway mix fused into the gate: out = y * gw[b, t, gof[d]] * silu(z)
+    const float* gw; int64_t gw_sb, gw_sl;   // (b, L, ngroups) fp32, or nullptr
+    const int* gof;                            // (D,) group of each channel
+    int ngroups;
+    float* dgw;                                // (b, L, ngroups) backward output, optional
 };
+
+// Weight of channel d's group at step t of row bi (the row's base and the channel's group
+// resolved by the caller): 1 without the mix.
+__device__ __forceinline__ float group_weight(const ScanDev& p, int bi, int64_t t, int g) {
+    return p.gw ? p.gw[(int64_t)bi * p.gw_sb + t * p.gw_sl + g] : 1.f;
+}
 
 }  // namespace swx

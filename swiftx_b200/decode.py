@@ -23,7 +23,7 @@ def _row(t):
 
 def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, delta=None, B=None,
           C=None, A=None, Dskip=None, delta_bias=None, ssm_state=None, delta_softplus=True,
-          want_xc=False, A_is_log=False):
+          want_xc=False, A_is_log=False, group_w=None, group_of=None):
     lib = _lib.load()
     x, z, delta, B, C = map(_row, (x, z, delta, B, C))
     b, D = x.shape
@@ -61,6 +61,11 @@ def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, de
         a.A, a.ssm_state, a.out = Af.data_ptr(), ssm_state.data_ptr(), out.data_ptr()
         if z is not None:
             a.z, a.z_sb = z.data_ptr(), z.stride(0)
+        if group_w is not None:                   # the SiftX pathway mix, before the gate
+            gw = group_w.detach().float().contiguous()
+            gof = group_of.to(torch.int32).contiguous()
+            keep += [gw, gof]
+            a.group_w, a.group_w_sb, a.group_of, a.ngroups = gw.data_ptr(), gw.stride(0), gof.data_ptr(), gw.shape[1]
         for name, t in (("Dskip", Dskip), ("delta_bias", delta_bias)):
             if t is not None:
                 tf = t.detach().float().contiguous()
@@ -76,12 +81,14 @@ def decode_conv_step(x, conv_state, conv_weight, conv_bias=None):
 
 
 def decode_ssm_step(xc, delta, B, C, A, ssm_state, Dskip=None, z=None, delta_bias=None,
-                    delta_softplus=True, A_is_log=False):
+                    delta_softplus=True, A_is_log=False, group_w=None, group_of=None):
     """Returns out (b, D); ssm_state (b, D, N) is updated in place.  A_is_log: A holds
-    log(-A) (the block's A_log parameter) and the kernel forms A = -exp(A_log) itself."""
+    log(-A) (the block's A_log parameter) and the kernel forms A = -exp(A_log) itself.
+    group_w (b, G), group_of (D,): the SiftX pathway mix applied before the gate (with z),
+    out = y * group_w[:, group_of] * silu(z)."""
     return _call(_lib.SWX_DECODE_SSM, xc, z=z, delta=delta, B=B, C=C, A=A, Dskip=Dskip,
                  delta_bias=delta_bias, ssm_state=ssm_state, delta_softplus=delta_softplus,
-                 A_is_log=A_is_log)[0]
+                 A_is_log=A_is_log, group_w=group_w, group_of=group_of)[0]
 
 
 def decode_step(x, conv_state, conv_weight, conv_bias, delta, B, C, A, ssm_state, Dskip=None,

@@ -68,6 +68,29 @@ def _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, softplus, in_dt, A_
     a.h0 = h0.data_ptr() if h0 is not None else None
 
 
+def _prep_groups(group_w, group_of, u, z):
+    """The SiftX pathway mix fused into the gate: group_w (b, L, G) per-token group weights
+    (fp32, made contiguous) and group_of (D,) channel -> group (int32).  Returns the pair
+    as the kernels take it, or (None, None)."""
+    if group_w is None:
+        return None, None
+    if z is None:
+        raise ValueError("group_w (the pathway mix) needs the gate z")
+    b, L, Dm = u.shape
+    if group_of is None or group_w.dim() != 3 or group_w.shape[:2] != (b, L) or group_of.shape != (Dm,):
+        raise ValueError("expected group_w (b, L, G) and group_of (D,)")
+    if not 1 <= group_w.shape[2] <= _lib.SWX_MAX_GROUPS:
+        raise ValueError(f"at most {_lib.SWX_MAX_GROUPS} pathway groups are supported")
+    _require_cuda(group_w, group_of)
+    return group_w.detach().float().contiguous(), group_of.to(torch.int32).contiguous()
+
+
+def _fill_groups(a, gw, gof):
+    if gw is not None:
+        a.group_w, a.group_w_sb, a.group_w_sl = gw.data_ptr(), gw.stride(0), gw.stride(1)
+        a.group_of, a.ngroups = gof.data_ptr(), gw.shape[2]
+
+
 def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
     _require_cuda(u, delta, A, B, C, D, z, delta_bias, h0)
     in_dt = _in_dtype(u)
@@ -89,7 +112,8 @@ def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
 
 def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
                  h0=None, out_dtype=None, checkpoints=False, return_last_state=False,
-                 return_delta_sum=False, write_out=True, pre_out=None, A_is_log=False):
+                 return_delta_sum=False, write_out=True, pre_out=None, A_is_log=False,
+                 group_w=None, group_of=None):
     """One kernel launch of the forward scan (no autograd).
 
     Returns (out, checkpoints or None, last_state or None), plus delta_sum (b, D) -- the
@@ -97,9 +121,11 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     (out is None), for callers that only need the final state / delta_sum.  pre_out, a
     dense fp32 (b, L, D) tensor, receives the pre-gate output when z is given (the
     backward can then skip recomputing it).  A_is_log: A holds log(-A) (see
-    selective_scan_fn)."""
+    selective_scan_fn).  group_w, group_of: the SiftX pathway mix fused into the gate
+    (see selective_scan_fn)."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
+    gw, gof = _prep_groups(group_w, group_of, u, z)
     b, L, Dm = u.shape
     N = A.shape[1]
     pdt = _param_dtype(in_dt)
@@ -120,6 +146,7 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
         if pre_out.dtype != pdt or not pre_out.is_contiguous() or pre_out.shape != (b, L, Dm):
             raise ValueError(f"pre_out must be a dense {pdt} (b, L, D) tensor")
         a.out_pre = pre_out.data_ptr()
+    _fill_groups(a, gw, gof)
     _lib.check(lib.swx_scan_fwd(a, _lib.stream_ptr(u.device)), "swx_scan_fwd")
     if return_delta_sum:
         return out, ck, hl, ds
@@ -127,12 +154,15 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
 
 
 def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, dout, y_pre=None,
-                  A_is_log=False):
+                  A_is_log=False, group_w=None, group_of=None, group_w_grad=False):
     """One call of the backward kernels (no autograd).  Returns a dict of gradients.
     y_pre: the pre-gate output the forward wrote to pre_out (optional, with z).
-    A_is_log: A holds log(-A), and "dA" is the gradient with respect to it."""
+    A_is_log: A holds log(-A), and "dA" is the gradient with respect to it.
+    group_w, group_of: the pathway mix of the forward; with group_w_grad (needs y_pre)
+    "d_group_w" (b, L, G) is the gradient with respect to group_w."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
+    gw, gof = _prep_groups(group_w, group_of, u, z)
     b, L, Dm = u.shape
     N = A.shape[1]
     dout = _rows(dout.to(in_dt))
@@ -158,6 +188,13 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
     if y_pre is not None and z is not None:
         a.out_pre = y_pre.data_ptr()
+    _fill_groups(a, gw, gof)
+    g["d_group_w"] = None
+    if gw is not None and group_w_grad:
+        if y_pre is None:
+            raise ValueError("the gradient of group_w needs the pre-gate output y_pre")
+        g["d_group_w"] = torch.empty(gw.shape, device=dev, dtype=torch.float32)
+        a.d_group_w = g["d_group_w"].data_ptr()
     _lib.check(lib.swx_scan_bwd(a, _lib.stream_ptr(dev)), "swx_scan_bwd")
     return g
 
@@ -192,18 +229,20 @@ class SelectiveScanFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, out_dtype,
-                return_last_state, A_is_log):
-        need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9))
+                return_last_state, A_is_log, group_w=None, group_of=None):
+        need_grad = any(ctx.needs_input_grad[i] for i in (0, 1, 2, 3, 4, 5, 6, 7, 9, 13))
         pre = (torch.empty(u.shape, device=u.device, dtype=_param_dtype(_in_dtype(u)))
                if need_grad and z is not None else None)
         out, ck, hl = scan_forward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0,
                                    out_dtype, checkpoints=need_grad,
-                                   return_last_state=return_last_state, pre_out=pre, A_is_log=A_is_log)
+                                   return_last_state=return_last_state, pre_out=pre, A_is_log=A_is_log,
+                                   group_w=group_w, group_of=group_of)
         ctx.delta_softplus = delta_softplus
         ctx.A_is_log = A_is_log
-        ctx.dtypes = [t.dtype if t is not None else None for t in (u, delta, A, B, C, D, z, delta_bias, h0)]
+        ctx.dtypes = [t.dtype if t is not None else None
+                      for t in (u, delta, A, B, C, D, z, delta_bias, h0, group_w)]
         if need_grad:
-            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, h0, ck, pre)
+            ctx.save_for_backward(u, delta, A, B, C, D, z, delta_bias, h0, ck, pre, group_w, group_of)
         if return_last_state:
             ctx.mark_non_differentiable(hl)
             return out, hl
@@ -211,19 +250,21 @@ class SelectiveScanFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dout, *unused):
-        u, delta, A, B, C, D, z, delta_bias, h0, ck, pre = ctx.saved_tensors
+        u, delta, A, B, C, D, z, delta_bias, h0, ck, pre, group_w, group_of = ctx.saved_tensors
         g = scan_backward(u, delta, A, B, C, D, z, delta_bias, ctx.delta_softplus, h0, ck, dout, y_pre=pre,
-                          A_is_log=ctx.A_is_log)
+                          A_is_log=ctx.A_is_log, group_w=group_w, group_of=group_of,
+                          group_w_grad=group_w is not None and ctx.needs_input_grad[13])
         dts = ctx.dtypes
         cast = lambda t, dt: None if t is None or dt is None else t.to(dt)  # noqa: E731
         return (cast(g["du"], dts[0]), cast(g["ddelta"], dts[1]), cast(g["dA"], dts[2]),
                 cast(g["dB"], dts[3]), cast(g["dC"], dts[4]), cast(g["dD"], dts[5]),
                 cast(g["dz"], dts[6]), cast(g["ddelta_bias"], dts[7]), None,
-                cast(g["dh0"], dts[8]), None, None, None)
+                cast(g["dh0"], dts[8]), None, None, None, cast(g["d_group_w"], dts[9]), None)
 
 
 def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
-                      h0=None, out_dtype=None, return_last_state=False, A_is_log=False):
+                      h0=None, out_dtype=None, return_last_state=False, A_is_log=False,
+                      group_w=None, group_of=None):
     """Fused selective scan with optional SiLU(z) gate and softplus(delta + delta_bias).
 
     out = (scan(u, delta_eff, A, B, C) + D*u) * silu(z),  delta_eff = softplus(delta + delta_bias).
@@ -232,9 +273,13 @@ def selective_scan_fn(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_
     A_is_log=True: the tensor passed as A holds log(-A) -- the block's A_log parameter --
     and the kernels form A = -exp(A_log) themselves (models/sift_block.py:121 does it in
     two elementwise ops before each call, plus two more in the backward); its gradient
-    is returned with respect to A_log."""
+    is returned with respect to A_log.
+
+    group_w (b, L, G), group_of (D,): the SiftX pathway mix (models/sift_block.py:137-142)
+    fused into the gate, out = y * group_w[..., group_of] * silu(z) with y the D-skipped
+    scan output; group_w receives its gradient (fp32 or bf16 inputs, G <= 8, with z)."""
     return SelectiveScanFn.apply(u, delta, A, B, C, D, z, delta_bias, bool(delta_softplus), h0,
-                                 out_dtype, bool(return_last_state), bool(A_is_log))
+                                 out_dtype, bool(return_last_state), bool(A_is_log), group_w, group_of)
 
 
 _MODES = ("auto", "parallel", "sequential", "fused", "triton")

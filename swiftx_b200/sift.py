@@ -16,9 +16,10 @@ RMSNorm runs on its fused kernels, each residual add folded into the next norm, 
 in training, the token embedding's weight gradient on the sort-free swx_embedding_bwd.
 Fusing the gate is exactly the reference's y * silu(z) when no SiftX pathway mixing is
 configured (models/sift_block.py:132-142).  With pathway_gate (SiftX), the per-token
-group weights sit between the scan and the gate, so the scan kernel runs without z
-(D skip and softplus still fused) and the mix and gate follow in torch, as in the
-reference.
+group weights softmax(pathway(x)) x G are computed in torch (a (b, L, G) tensor) and the
+scan kernels apply them between the scan and the gate, out = y * w[group] * silu(z),
+returning their gradient from the backward (the decode kernel applies them too); float64
+blocks keep the mix and gate in torch.
 """
 import math
 from dataclasses import dataclass
@@ -172,6 +173,8 @@ class SiftBlock(nn.Module):
         for i in range(G):
             group_of[edges[i]:edges[i + 1]] = i
         self.register_buffer("group_of", group_of, persistent=False)
+        # the same map as the kernels take it (int32), so no conversion runs per call
+        self.register_buffer("group_of_i32", group_of.to(torch.int32), persistent=False)
         present = {"bias": bias, "conv_bias": conv_bias, "pathway": bool(pathway_gate and G > 1)}
         for key, shape, rule, no_decay, when in _BLOCK_TABLE:
             if when is not None and not present[when]:
@@ -235,21 +238,34 @@ class SiftBlock(nn.Module):
         x, z = xz.chunk(2, dim=-1)                        # strided views, row stride 2D
         x = causal_conv1d_fn(x, self.conv1d.weight, self.conv1d.bias, "silu")
         delta, B, C = self._split(x)
-        gate = z if self.pathway is None else None
+        fuse_mix = self.pathway is not None and self._mix_fusable(x)
+        gate = z if self.pathway is None or fuse_mix else None
+        # SiftX: the per-token group weights (models/sift_block.py:140), computed under the
+        # caller's autocast like the reference; the kernels apply them before the gate
+        gw = self._pathway_weights(x) if fuse_mix else None
         with torch.autocast(device_type=x.device.type, enabled=False):
             # A = -exp(A_log) is formed inside the scan kernels (A_is_log)
             y = selective_scan_fn(x, delta, self.A_log.float(), B, C, self.D.float(), z=gate,
-                                  delta_bias=self.dt_proj.bias.float(), delta_softplus=True, A_is_log=True)
+                                  delta_bias=self.dt_proj.bias.float(), delta_softplus=True, A_is_log=True,
+                                  group_w=gw, group_of=self.group_of_i32 if fuse_mix else None)
         y = y.to(xz.dtype)
-        if self.pathway is not None:
+        if self.pathway is not None and not fuse_mix:
             y = self._mix_pathways(y, x) * F.silu(z)
         return _linear(y, self.out_proj.weight, self.out_proj.bias)
 
+    def _pathway_weights(self, x):
+        """softmax(pathway(x)) x G: (b, L, G) per-token group weights (models/sift_block.py:140)."""
+        return torch.softmax(F.linear(x, self.pathway.weight, self.pathway.bias), dim=-1) * self.n_groups
+
+    def _mix_fusable(self, x):
+        """The scan kernels apply the group mix themselves for fp32 / bf16 inputs and at
+        most SWX_MAX_GROUPS groups; float64 blocks keep the mix in torch."""
+        return x.dtype in (torch.float32, torch.bfloat16) and self.n_groups <= 8
+
     def _mix_pathways(self, y, x):
         """SiftX: reweight the channel groups per token, softmax x G (1 at init)
-        (models/sift_block.py:137-142)."""
-        w = torch.softmax(F.linear(x, self.pathway.weight, self.pathway.bias), dim=-1) * self.n_groups
-        return y * w[..., self.group_of]
+        (models/sift_block.py:137-142); the unfused form, for float64 and more than 8 groups."""
+        return y * self._pathway_weights(x)[..., self.group_of]
 
     def allocate_state(self, batch, device=None, dtype=torch.float32):
         """(conv window (b, D, d_conv), SSM state (b, D, d_state)), zeroed: the recurrent
@@ -264,11 +280,14 @@ class SiftBlock(nn.Module):
         x, z = xz.chunk(2, dim=-1)
         xc = decode_conv_step(x, conv_state, self.conv1d.weight, self.conv1d.bias)
         delta, B, C = self._split(xc)
-        gate = z if self.pathway is None else None
-        # A = -exp(A_log) is formed inside the kernel (A_is_log)
+        fuse_mix = self.pathway is not None and self.n_groups <= 8
+        gate = z if self.pathway is None or fuse_mix else None
+        gw = self._pathway_weights(xc).float() if fuse_mix else None
+        # A = -exp(A_log) is formed inside the kernel (A_is_log); the pathway mix too
         y = decode_ssm_step(xc, delta.float(), B.float(), C.float(), self.A_log, ssm_state, Dskip=self.D,
-                            z=gate, delta_bias=self.dt_proj.bias, A_is_log=True)
-        if self.pathway is not None:
+                            z=gate, delta_bias=self.dt_proj.bias, A_is_log=True,
+                            group_w=gw, group_of=self.group_of_i32 if fuse_mix else None)
+        if self.pathway is not None and not fuse_mix:
             y = self._mix_pathways(y, xc) * F.silu(z)
         return _linear(y.to(self.out_proj.weight.dtype), self.out_proj.weight, self.out_proj.bias)
 

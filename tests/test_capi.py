@@ -33,7 +33,7 @@ def test_struct_mirrors_match():
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
     assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
     assert lib.swx_embedding_args_size() == ctypes.sizeof(_lib.EmbeddingArgs)
-    assert lib.swx_abi_version() == 11
+    assert lib.swx_abi_version() == 12
 
 
 def test_status_strings():
