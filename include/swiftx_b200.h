@@ -263,7 +263,19 @@ typedef struct swx_decode_args {
     const int32_t* group_of;
     int32_t ngroups;
     int32_t reserved2;
+    /* optional (SSM mode): dt_proj folded into the step (models/sift_block.py:167,106-108).
+       With dt_in set, delta[b, d] = sum_r dt_weight[d, r] * dt_in[b, r] replaces the delta
+       row (then delta must be NULL; delta_bias and softplus apply as before).  dt_in
+       (b, dt_rank) fp32, unit element stride, row stride dt_in_sb (a multiple of 4);
+       dt_weight (D, dt_rank) dense fp32; both 16-byte aligned; dt_rank a multiple of 4,
+       at most SWX_DECODE_MAX_DT_RANK.  The sum runs in a fixed order. */
+    const float* dt_in; int64_t dt_in_sb;
+    const float* dt_weight;
+    int32_t dt_rank;
+    int32_t reserved3;
 } swx_decode_args;
+
+#define SWX_DECODE_MAX_DT_RANK 256
 
 /* Replaces SiftBlock.step's conv-window roll, conv dot + bias + SiLU and in-place
  * state update / readout / gate (models/sift_block.py:153-175). */

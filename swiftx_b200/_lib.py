@@ -17,6 +17,7 @@ SWX_ERR_UNSUPPORTED = 2
 SWX_ERR_CUDA = 3
 SWX_ERR_TIMEOUT = 4
 SWX_MAX_GROUPS = 8
+SWX_DECODE_MAX_DT_RANK = 256
 # capacity of the static scratch of swx_scan_bwd_static_scratch (SWX_STATIC_SCRATCH_BYTES)
 SWX_STATIC_SCRATCH_BYTES = 8 << 20
 
@@ -83,6 +84,7 @@ class DecodeArgs(ctypes.Structure):
         ("conv_state", vp), ("ssm_state", vp), ("xc_out", vp), ("out", vp),
         ("flags", i32), ("reserved", i32),
         ("group_w", vp), ("group_w_sb", i64), ("group_of", vp), ("ngroups", i32), ("reserved2", i32),
+        ("dt_in", vp), ("dt_in_sb", i64), ("dt_weight", vp), ("dt_rank", i32), ("reserved3", i32),
     ]
 
 

@@ -31,7 +31,27 @@ struct DecDev {
     float* conv_state; float* ssm_state; float* xc_out; float* out;
     const float* gw; int64_t gw_sb;    // SiftX pathway mix: (b, ngroups) weights, or nullptr
     const int* gof;                    // (D,) group of each channel
+    const float* dti; int64_t dti_sb;  // dt_proj folded in: (b, R) low-rank dt rows, or nullptr
+    const float* dtw;                  // (D, R) dt_proj weight
+    int R;
 };
+
+// Lane j's share of <dt_weight[d, :], v> (the float4 groups j, j+4, ...); the four lanes of
+// a channel add their shares with two xor shuffles, so all four hold the same sum.
+__device__ __forceinline__ float dt_dot_part(const float* __restrict__ w, const float* v, int R, int j) {
+    float acc = 0.f;
+    for (int r4 = j; 4 * r4 < R; r4 += 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(w) + r4);
+        const float4 b = *reinterpret_cast<const float4*>(v + 4 * r4);
+        acc = fmaf(a.x, b.x, acc);
+        acc = fmaf(a.y, b.y, acc);
+        acc = fmaf(a.z, b.z, acc);
+        acc = fmaf(a.w, b.w, acc);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    return acc;
+}
 
 // Pathway weight of channel d's group for batch row r (1 without the mix).
 __device__ __forceinline__ float dec_group_weight(const DecDev& p, int64_t r, int d) {
@@ -53,7 +73,8 @@ constexpr int DEC_RB = 4;            // batch rows per thread (independent chain
 // Thread (channel d, state group j) handles DEC_RB batch rows of that channel: all of
 // their loads are issued before any math, and the per-channel parameters (A, conv
 // weights, biases) are loaded once and reused across the rows.
-template <int K, bool HAS_Z>
+// DTP: delta from the folded dt_proj (DecDev::dti / dtw) instead of a delta row.
+template <int K, bool HAS_Z, bool DTP = false>
 __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
     const int j = threadIdx.x & 3;
     const int d = blockIdx.x * DEC_CH + (threadIdx.x >> 2);
@@ -101,7 +122,8 @@ __global__ void __launch_bounds__(DEC_NT) decode_kernel(const DecDev p) {
             }
         }
         if (ssm) {
-            raw[r] = p.dl[bc * p.dl_sb + dc] + dbi;
+            raw[r] = (DTP ? dt_dot_part(p.dtw + (int64_t)dc * p.R, p.dti + bc * p.dti_sb, p.R, j)
+                          : p.dl[bc * p.dl_sb + dc]) + dbi;
             zv[r] = HAS_Z ? p.z[bc * p.z_sb + dc] : 0.f;
             gwv[r] = HAS_Z ? dec_group_weight(p, bc, dc) : 1.f;
             if (full) {
@@ -193,9 +215,40 @@ struct __align__(16) DecTile {
     float4 B[4], C[4];
 };
 
-template <bool CONV, bool HAS_Z>
-__global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, int row_groups) {
+// Folded dt_proj: a CTA computes delta for all of its rows before its walk (so the dot
+// products stay off the walk's per-row path) into a (rows, 64) block of shared memory;
+// the launcher keeps a CTA's rows at or below this count.
+constexpr int DTP_MAX_ROWS = 32;
+
+// Row stride (floats) of the CTA's dt_proj weight block in shared memory: at least R and
+// 16 more than a multiple of 32, so that the float4 loads of one quarter-warp (two
+// channels x four lanes, lane j at float offset 4j + 16i of its channel's row) hit 32
+// different banks.
+__host__ __device__ constexpr int dtw_stride(int R) { return R + ((16 - R % 32) + 32) % 32; }
+
+// Lane j's share of <W row, v> from shared memory, then the sum over the channel's four
+// lanes (same order as dt_dot_part: float4 groups j, j+4, ...; two xor shuffles).
+__device__ __forceinline__ float dt_dot_smem(const float* w, const float* v, int R, int j) {
+    float acc = 0.f;
+#pragma unroll 4
+    for (int r4 = j; 4 * r4 < R; r4 += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(w + 4 * r4);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(v) + r4);
+        acc = fmaf(a.x, b.x, acc);
+        acc = fmaf(a.y, b.y, acc);
+        acc = fmaf(a.z, b.z, acc);
+        acc = fmaf(a.w, b.w, acc);
+    }
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    return acc;
+}
+
+template <bool CONV, bool HAS_Z, bool DTP>
+__device__ __forceinline__ void decode_stream_body(const DecDev& p, int row_groups) {
     __shared__ DecTile S[DP_STAGES];
+    // DTP: the CTA's (64, dtw_stride(R)) dt_proj block, then its rows' (DTP_MAX_ROWS, 64) delta
+    extern __shared__ __align__(16) float sW[];
     const int tid = threadIdx.x;
     const int j = tid & 3, ch = tid >> 2;
     const int nblk = p.D / DP_CH;
@@ -213,6 +266,16 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
     const float dsk = p.Dskip ? p.Dskip[d] : 0.f;
     const float dbi = p.dbias ? p.dbias[d] : 0.f;
     const float2 A01 = f2(A4.x, A4.y), A23 = f2(A4.z, A4.w);
+    const int ws = DTP ? dtw_stride(p.R) : 0;
+    if (DTP) {                            // the weight block, once per CTA
+        const int q4 = p.R / 4;
+        for (int i = tid; i < DP_CH * q4; i += DP_NT) {
+            const int c = i / q4, q = i - c * q4;
+            *reinterpret_cast<float4*>(sW + c * ws + 4 * q) =
+                __ldg(reinterpret_cast<const float4*>(p.dtw + (int64_t)(d0 + c) * p.R) + q);
+        }
+        __syncthreads();
+    }
 
     // tile copies: every thread one 16-byte piece of the state; threads 0..63 the conv
     // window, 64..111 x / z / delta, 112..119 B and C
@@ -226,7 +289,7 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
         } else if (tid < 96) {
             if (HAS_Z) cp_async16(&T.z[4 * (tid - 80)], p.z + r * p.z_sb + d0 + 4 * (tid - 80), 16);
         } else if (tid < 112) {
-            cp_async16(&T.dr[4 * (tid - 96)], p.dl + r * p.dl_sb + d0 + 4 * (tid - 96), 16);
+            if (!DTP) cp_async16(&T.dr[4 * (tid - 96)], p.dl + r * p.dl_sb + d0 + 4 * (tid - 96), 16);
         } else if (tid < 116) {
             cp_async16(&T.B[tid - 112], p.B + r * p.B_sb + 4 * (tid - 112), 16);
         } else if (tid < 120) {
@@ -239,6 +302,13 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
         const int r = rg + k * row_groups;
         if (r < p.b) issue(r, k);
         cp_async_commit();
+    }
+    float* sDr = sW + DP_CH * ws;
+    if (DTP) {                            // delta of every row of this CTA, while the ring fills
+        for (int k = 0; rg + k * row_groups < p.b; ++k) {
+            const float v = dt_dot_smem(sW + ch * ws, p.dti + (int64_t)(rg + k * row_groups) * p.dti_sb, p.R, j);
+            if (j == 0) sDr[k * DP_CH + ch] = v;
+        }
     }
     for (int k = 0;; ++k) {
         const int r = rg + k * row_groups;
@@ -263,7 +333,7 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
             acc = fmaf(win.w, cw.w, acc);
             xc = silu_f(acc);
         }
-        const float raw = T.dr[ch] + dbi;
+        const float raw = (DTP ? sDr[k * DP_CH + ch] : T.dr[ch]) + dbi;
         float dte = raw;
         if (p.softplus) {
             float2 sp, dsp;
@@ -295,6 +365,18 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
     cp_async_wait<0>();
 }
 
+template <bool CONV, bool HAS_Z>
+__global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, int row_groups) {
+    decode_stream_body<CONV, HAS_Z, false>(p, row_groups);
+}
+
+// The folded-dt_proj variant: at most 64 registers, so that four CTAs share an SM as the
+// plain kernel's do.
+template <bool HAS_Z>
+__global__ void __launch_bounds__(DP_NT, 4) decode_stream_dtp_kernel(const DecDev p, int row_groups) {
+    decode_stream_body<false, HAS_Z, true>(p, row_groups);
+}
+
 // The streaming variant applies when every tile is full and every row is 16-byte aligned.
 static bool stream_ok(const DecDev& p) {
     auto al = [](const void* q) { return q == nullptr || (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
@@ -306,21 +388,33 @@ static bool stream_ok(const DecDev& p) {
     return true;
 }
 
-template <bool CONV, bool HAS_Z>
+template <bool CONV, bool HAS_Z, bool DTP = false>
 static cudaError_t launch_stream_t(const DecDev& p, cudaStream_t st) {
-    auto k = decode_stream_kernel<CONV, HAS_Z>;
-    int sms = 0, per_sm = 0;
-    cudaError_t e = sm_fit(k, DP_NT, 0, &sms, &per_sm);
+    auto k = DTP ? decode_stream_dtp_kernel<HAS_Z> : decode_stream_kernel<CONV, HAS_Z>;
+    // dynamic shared memory: the weight block and the rows' delta (opted in up to the
+    // largest a call can pass)
+    const int used = DTP ? DP_CH * (dtw_stride(p.R) + DTP_MAX_ROWS) * 4 : 0;
+    cudaError_t e = DTP ? allow_smem(k, DP_CH * (dtw_stride(SWX_DECODE_MAX_DT_RANK) + DTP_MAX_ROWS) * 4)
+                        : cudaSuccess;
     if (e != cudaSuccess) return e;
+    int sms = 0, per_sm = 0;
+    e = sm_fit(k, DP_NT, 0, &sms, &per_sm);
+    if (e != cudaSuccess) return e;
+    if (DTP) {                           // CTAs per SM at this call's weight-block size
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, DP_NT, used);
+        if (e != cudaSuccess) return e;
+    }
     const int nblk = p.D / DP_CH;
     const int slots = std::max(1, sms * per_sm);
-    const int row_groups = std::max(1, std::min(p.b, slots / nblk));
-    k<<<nblk * row_groups, DP_NT, 0, st>>>(p, row_groups);
+    int row_groups = std::max(1, std::min(p.b, slots / nblk));
+    if (DTP) row_groups = std::max(row_groups, (p.b + DTP_MAX_ROWS - 1) / DTP_MAX_ROWS);   // rows per CTA <= 32
+    k<<<nblk * row_groups, DP_NT, used, st>>>(p, row_groups);
     return cudaGetLastError();
 }
 
 static cudaError_t launch_stream(const DecDev& p, cudaStream_t st) {
     const bool conv = p.mode & SWX_DECODE_CONV;
+    if (p.dti) return p.z ? launch_stream_t<false, true, true>(p, st) : launch_stream_t<false, false, true>(p, st);
     if (conv) return p.z ? launch_stream_t<true, true>(p, st) : launch_stream_t<true, false>(p, st);
     return p.z ? launch_stream_t<false, true>(p, st) : launch_stream_t<false, false>(p, st);
 }
@@ -328,8 +422,14 @@ static cudaError_t launch_stream(const DecDev& p, cudaStream_t st) {
 template <int K>
 static void launch_dec(const DecDev& p, cudaStream_t st) {
     dim3 grid((p.D + DEC_CH - 1) / DEC_CH, (p.b + DEC_RB - 1) / DEC_RB);
-    if (p.z) decode_kernel<K, true><<<grid, DEC_NT, 0, st>>>(p);
-    else decode_kernel<K, false><<<grid, DEC_NT, 0, st>>>(p);
+    if (p.dti) {
+        if (p.z) decode_kernel<K, true, true><<<grid, DEC_NT, 0, st>>>(p);
+        else decode_kernel<K, false, true><<<grid, DEC_NT, 0, st>>>(p);
+    } else if (p.z) {
+        decode_kernel<K, true><<<grid, DEC_NT, 0, st>>>(p);
+    } else {
+        decode_kernel<K, false><<<grid, DEC_NT, 0, st>>>(p);
+    }
 }
 
 }  // namespace swx
@@ -345,7 +445,17 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     if (a->dim > (int64_t)INT32_MAX || (a->batch + 3) / 4 > 65535) return SWX_ERR_UNSUPPORTED;
     if (!a->x) return SWX_ERR_INVALID_ARG;
     if ((a->mode & SWX_DECODE_CONV) && (!a->conv_weight || !a->conv_state)) return SWX_ERR_INVALID_ARG;
-    if ((a->mode & SWX_DECODE_SSM) && (!a->delta || !a->B || !a->C || !a->A || !a->ssm_state || !a->out))
+    if (a->dt_in) {
+        // dt_proj folded in: SSM-only steps (the conv's output feeds x_proj first)
+        if (a->mode != SWX_DECODE_SSM) return SWX_ERR_UNSUPPORTED;
+        if (a->delta || !a->dt_weight || a->dt_rank < 4 || a->dt_rank % 4 || a->dt_rank > SWX_DECODE_MAX_DT_RANK)
+            return SWX_ERR_INVALID_ARG;
+        if ((((uintptr_t)a->dt_in | (uintptr_t)a->dt_weight) & 15u) || a->dt_in_sb < 0 || a->dt_in_sb % 4)
+            return SWX_ERR_INVALID_ARG;
+    } else if ((a->mode & SWX_DECODE_SSM) && !a->delta) {
+        return SWX_ERR_INVALID_ARG;
+    }
+    if ((a->mode & SWX_DECODE_SSM) && (!a->B || !a->C || !a->A || !a->ssm_state || !a->out))
         return SWX_ERR_INVALID_ARG;
     if ((a->mode & SWX_DECODE_SSM) && a->dstate == swx::NS &&
         (((uintptr_t)a->ssm_state | (uintptr_t)a->A | (uintptr_t)a->B | (uintptr_t)a->C) & 15u ||
@@ -361,6 +471,9 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
     p.dl = a->delta; p.dl_sb = a->delta_sb; p.B = a->B; p.B_sb = a->B_sb; p.C = a->C; p.C_sb = a->C_sb;
     p.cw = a->conv_weight; p.cb = a->conv_bias; p.A = a->A; p.Dskip = a->Dskip; p.dbias = a->delta_bias;
     p.conv_state = a->conv_state; p.ssm_state = a->ssm_state; p.xc_out = a->xc_out; p.out = a->out;
+    if (a->dt_in) {
+        p.dti = a->dt_in; p.dti_sb = a->dt_in_sb; p.dtw = a->dt_weight; p.R = a->dt_rank;
+    }
     if (a->group_w) {
         if (!a->z || !(a->mode & SWX_DECODE_SSM)) return SWX_ERR_UNSUPPORTED;
         if (!a->group_of || a->group_w_sb < 0 || a->ngroups < 1 || a->ngroups > SWX_MAX_GROUPS)

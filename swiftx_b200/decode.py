@@ -23,7 +23,7 @@ def _row(t):
 
 def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, delta=None, B=None,
           C=None, A=None, Dskip=None, delta_bias=None, ssm_state=None, delta_softplus=True,
-          want_xc=False, A_is_log=False, group_w=None, group_of=None):
+          want_xc=False, A_is_log=False, group_w=None, group_of=None, dt_in=None, dt_weight=None):
     lib = _lib.load()
     x, z, delta, B, C = map(_row, (x, z, delta, B, C))
     b, D = x.shape
@@ -56,7 +56,15 @@ def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, de
         keep.append(Af)
         a.dstate = Af.shape[1]
         out = torch.empty((b, D), device=x.device, dtype=torch.float32)
-        a.delta, a.delta_sb = delta.data_ptr(), delta.stride(0)
+        if dt_in is not None:                     # dt_proj folded into the kernel
+            dti = _row(dt_in)
+            if dti.stride(0) % 4 or dti.data_ptr() % 16:
+                dti = dti.contiguous()
+            dtw = dt_weight.detach().float().contiguous()
+            keep += [dti, dtw]
+            a.dt_in, a.dt_in_sb, a.dt_weight, a.dt_rank = dti.data_ptr(), dti.stride(0), dtw.data_ptr(), dtw.shape[1]
+        else:
+            a.delta, a.delta_sb = delta.data_ptr(), delta.stride(0)
         a.B, a.B_sb, a.C, a.C_sb = B.data_ptr(), B.stride(0), C.data_ptr(), C.stride(0)
         a.A, a.ssm_state, a.out = Af.data_ptr(), ssm_state.data_ptr(), out.data_ptr()
         if z is not None:
@@ -81,14 +89,19 @@ def decode_conv_step(x, conv_state, conv_weight, conv_bias=None):
 
 
 def decode_ssm_step(xc, delta, B, C, A, ssm_state, Dskip=None, z=None, delta_bias=None,
-                    delta_softplus=True, A_is_log=False, group_w=None, group_of=None):
+                    delta_softplus=True, A_is_log=False, group_w=None, group_of=None, dt_in=None,
+                    dt_weight=None):
     """Returns out (b, D); ssm_state (b, D, N) is updated in place.  A_is_log: A holds
     log(-A) (the block's A_log parameter) and the kernel forms A = -exp(A_log) itself.
     group_w (b, G), group_of (D,): the SiftX pathway mix applied before the gate (with z),
-    out = y * group_w[:, group_of] * silu(z)."""
+    out = y * group_w[:, group_of] * silu(z).  dt_in (b, R), dt_weight (D, R): dt_proj
+    folded into the kernel, delta = dt_in @ dt_weight.T (pass delta=None); R a multiple of
+    4, at most 256."""
+    if dt_in is not None and (delta is not None or dt_weight is None):
+        raise ValueError("dt_in replaces delta and needs dt_weight")
     return _call(_lib.SWX_DECODE_SSM, xc, z=z, delta=delta, B=B, C=C, A=A, Dskip=Dskip,
                  delta_bias=delta_bias, ssm_state=ssm_state, delta_softplus=delta_softplus,
-                 A_is_log=A_is_log, group_w=group_w, group_of=group_of)[0]
+                 A_is_log=A_is_log, group_w=group_w, group_of=group_of, dt_in=dt_in, dt_weight=dt_weight)[0]
 
 
 def decode_step(x, conv_state, conv_weight, conv_bias, delta, B, C, A, ssm_state, Dskip=None,

@@ -221,3 +221,34 @@ def test_decode_a_log_formed_in_kernel(b, D, N):
         close(outs[1], n64(outs[0]), rtol=1e-6, atol=1e-7)
         close(states[1][1], n64(states[0][1]), rtol=1e-6, atol=1e-7)
         assert torch.equal(states[1][0], states[0][0])
+
+
+@pytest.mark.parametrize("D,N,R", [(2048, 16, 64), (96, 12, 20), (512, 16, 128)])
+def test_decode_dt_proj_folded(D, N, R):
+    """decode_ssm_step with dt_proj folded in (dt_in, dt_weight) against the block's step
+    recurrence (models/sift_block.py:167-174) in float64, fed delta = dt_in @ dt_weight.T
+    (the streaming kernel for D a multiple of 64 with N=16, the general kernel otherwise);
+    dt_in, B and C are strided column slices of an x_proj-like output, as in the block."""
+    b = 7
+    g = torch.Generator().manual_seed(41)
+    r = lambda *s, sc=1.0: torch.randn(*s, generator=g) * sc  # noqa: E731
+    xc, z = r(b, D), r(b, D)
+    x_dbl = r(b, R + 2 * N, sc=0.3)
+    W = r(D, R, sc=R ** -0.5)
+    Bm, Cm = x_dbl[:, R:R + N], x_dbl[:, R + N:]
+    A = -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1)
+    Dsk, bias = r(D), r(D, sc=0.1)
+    h = r(b, D, N, sc=0.1)
+    dev = lambda t: t.to(DEV)  # noqa: E731
+    hd = dev(h)
+    xd = dev(x_dbl)
+    y = decode_ssm_step(dev(xc), None, xd[:, R:R + N], xd[:, R + N:], dev(A), hd, Dskip=dev(Dsk), z=dev(z),
+                        delta_bias=dev(bias), dt_in=xd[:, :R], dt_weight=dev(W))
+    delta = x_dbl[:, :R].double() @ W.double().T
+    dte = torch.nn.functional.softplus(delta + bias.double())
+    a = torch.exp(dte[..., None] * A.double())
+    hn = a * h.double() + (dte * xc.double())[..., None] * Bm.double()[:, None, :]
+    yo = (hn * Cm.double()[:, None, :]).sum(-1) + Dsk.double() * xc.double()
+    yo = yo * z.double() * torch.sigmoid(z.double())
+    np.testing.assert_allclose(y.double().cpu().numpy(), yo.numpy(), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(hd.double().cpu().numpy(), hn.numpy(), rtol=1e-4, atol=1e-5)

@@ -1,6 +1,8 @@
 """Sequence-parallel scan over NCCL on 2+ GPUs (skipped with fewer): every rank scans
-its chunk, boundary values go through all_gather, and rank outputs concatenated along
-the sequence must match a one-pass scan of the whole sequence on one GPU."""
+its chunk (the balanced split of seqpar.chunk_bounds) from a zero state, the boundary
+values go peer to peer to the later ranks, each later rank corrects its output for its
+initial state, and the rank outputs concatenated along the sequence must match a
+one-pass scan of the whole sequence on one GPU."""
 import os
 import socket
 
@@ -16,7 +18,7 @@ def _worker(rank, world, port, q):
 
     import torch.distributed as dist
 
-    from swiftx_b200.seqpar import sequence_parallel_scan
+    from swiftx_b200.seqpar import chunk_bounds, sequence_parallel_scan
     from swiftx_b200.workloads import config_inputs
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -26,7 +28,8 @@ def _worker(rank, world, port, q):
     try:
         b, L, D = 2, 600, 64
         inp = config_inputs(b, L, D, 16, seed=5, device=f"cuda:{rank}")
-        s, e = rank * L // world, (rank + 1) * L // world
+        bounds = chunk_bounds(L, world, multiple=8)
+        s, e = bounds[rank], bounds[rank + 1]
         ch = {k: inp[k][:, s:e] for k in ("u", "delta", "z", "B", "C")}
         out = sequence_parallel_scan(ch["u"], ch["delta"], inp["A"], ch["B"], ch["C"], inp["D"], ch["z"],
                                      inp["delta_bias"], True)
