@@ -94,3 +94,29 @@ def test_long_sequence_bf16_eight_chunks():
     want = oracle.scan_fwd(*(n(inp[k]) for k in ("u", "delta", "A", "B", "C")), D=n(inp["D"]), z=n(inp["z"]),
                            delta_bias=n(inp["delta_bias"]), delta_softplus=True)
     np.testing.assert_allclose(n(got), want, rtol=2e-2, atol=1e-3 * np.abs(want).max())
+
+
+def test_correct_after_the_decays_underflow():
+    """A long chunk whose decays exp(A S_t) underflow for whole warps part way (large dt,
+    so S_t grows fast): the kernel stops evaluating those state pairs once every lane's
+    decay is 0 in fp32, which must leave the result equal to the float64 formula
+    out_t += silu(z_t) sum_n C_t[n] exp(A[:, n] S_t) h_in[n] (the skipped terms are
+    exactly zero in fp32).  Half the channels decay slowly (dt 1e-3), so some pairs stay
+    live to the end."""
+    b, L, D, N = 2, 4096, 256, 16
+    g = torch.Generator().manual_seed(21)
+    dt = torch.where(torch.arange(D) % 64 < 32, torch.full((D,), 0.2), torch.full((D,), 1e-3))
+    bias = (dt + torch.log(-torch.expm1(-dt))).to(DEV)
+    delta = (torch.randn(b, L, D, generator=g) * 0.3).to(DEV)
+    C = torch.randn(b, L, N, generator=g).to(DEV)
+    z = torch.randn(b, L, D, generator=g).to(DEV)
+    A = -torch.arange(1, N + 1, dtype=torch.float32).repeat(D, 1).to(DEV)
+    h_in = (torch.randn(b, D, N, generator=g) * 0.5).to(DEV)
+    u, Bm = torch.zeros(b, L, D, device=DEV), torch.zeros(b, L, N, device=DEV)
+    out0 = torch.randn(b, L, D, generator=g).to(DEV)
+    got = scan_correct(out0.clone(), h_in, u, delta, A, Bm, C, z=z, delta_bias=bias, delta_softplus=True)
+    S = torch.cumsum(torch.nn.functional.softplus(delta.double() + bias.double()), 1)       # (b, L, D)
+    P = torch.exp(A.double()[None, None] * S[..., None])                                     # (b, L, D, N)
+    corr = torch.einsum("bln,bldn,bdn->bld", C.double(), P, h_in.double()) * torch.nn.functional.silu(z.double())
+    want = out0.double() + corr
+    np.testing.assert_allclose(got.double().cpu().numpy(), want.cpu().numpy(), rtol=1e-5, atol=1e-5)
