@@ -273,6 +273,12 @@ typedef struct swx_decode_args {
     const float* dt_weight;
     int32_t dt_rank;
     int32_t reserved3;
+    /* swx_decode_layer_step only: x_proj (xproj_rows = dt_rank + 2 * dstate, D) dense fp32,
+       16-byte aligned, and a scratch workspace of swx_decode_layer_workspace_bytes(). */
+    const float* xproj_weight;
+    int32_t xproj_rows;
+    int32_t reserved4;
+    void* workspace; int64_t workspace_bytes;
 } swx_decode_args;
 
 #define SWX_DECODE_MAX_DT_RANK 256
@@ -280,6 +286,22 @@ typedef struct swx_decode_args {
 /* Replaces SiftBlock.step's conv-window roll, conv dot + bias + SiLU and in-place
  * state update / readout / gate (models/sift_block.py:153-175). */
 int swx_decode_step(const swx_decode_args* args, void* stream);
+
+/* The whole recurrent step of one block between in_proj and out_proj, with both of its
+ * projections folded in (models/sift_block.py:160-175): conv window roll + conv + SiLU,
+ * x_proj (xproj_weight) split into dt | B | C, delta = softplus(dt_weight @ dt +
+ * delta_bias), the state update, readout, D skip and SiLU(z) gate.  Two launches: the conv
+ * with each 64-channel block's partial x_proj products, then the state update, which
+ * sums the partials in block order.  Arguments as swx_decode_step with mode =
+ * SWX_DECODE_CONV | SWX_DECODE_SSM, delta / B / C / dt_in NULL, dt_weight and dt_rank
+ * set, xproj_weight, xproj_rows = dt_rank + 2 * dstate, workspace; dstate 16, width 4,
+ * dim a multiple of 64, 16-byte aligned rows (x_sb, z_sb multiples of 4); no pathway
+ * mix (its weights need the conv output first).  Returns SWX_ERR_UNSUPPORTED for other
+ * shapes, which the caller then runs as swx_decode_step around its own projections. */
+int swx_decode_layer_step(const swx_decode_args* args, void* stream);
+/* Scratch bytes of swx_decode_layer_step: the partial x_proj products and the conv
+ * output; -1 for negative sizes. */
+int64_t swx_decode_layer_workspace_bytes(int64_t batch, int64_t dim, int64_t xproj_rows);
 
 /* Linear recurrence along the sequence, for every (batch row, element) chain:
  *   h_t = a_t * h_{t-1} + x_t,  h_{-1} = 0

@@ -85,6 +85,7 @@ class DecodeArgs(ctypes.Structure):
         ("flags", i32), ("reserved", i32),
         ("group_w", vp), ("group_w_sb", i64), ("group_of", vp), ("ngroups", i32), ("reserved2", i32),
         ("dt_in", vp), ("dt_in_sb", i64), ("dt_weight", vp), ("dt_rank", i32), ("reserved3", i32),
+        ("xproj_weight", vp), ("xproj_rows", i32), ("reserved4", i32), ("workspace", vp), ("workspace_bytes", i64),
     ]
 
 
@@ -157,6 +158,10 @@ def load():
     lib.swx_scan_bwd_segments.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_exp2_fma_eval.restype = ctypes.c_int
     lib.swx_exp2_fma_eval.argtypes = [vp, vp, i64, vp]
+    lib.swx_decode_layer_step.restype = ctypes.c_int
+    lib.swx_decode_layer_step.argtypes = [ctypes.POINTER(DecodeArgs), vp]
+    lib.swx_decode_layer_workspace_bytes.restype = i64
+    lib.swx_decode_layer_workspace_bytes.argtypes = [i64, i64, i64]
     lib.swx_device_wait_status.restype = ctypes.c_int
     lib.swx_device_wait_status.argtypes = []
     lib.swx_diag_wait_timeout.restype = ctypes.c_int

@@ -34,6 +34,11 @@ struct DecDev {
     const float* dti; int64_t dti_sb;  // dt_proj folded in: (b, R) low-rank dt rows, or nullptr
     const float* dtw;                  // (D, R) dt_proj weight
     int R;
+    // x_proj folded in too (the layer path): (J, D) weight, J = R + 2N; the conv kernel
+    // writes each 64-channel block's partial products (nblk, b, J) and the conv output
+    // (b, D) to the workspace, the state-update kernel sums the partials in block order
+    const float* xw; int J;
+    float* xpart; float* xcbuf;
 };
 
 // Lane j's share of <dt_weight[d, :], v> (the float4 groups j, j+4, ...); the four lanes of
@@ -233,7 +238,7 @@ __device__ __forceinline__ float dt_dot_smem(const float* w, const float* v, int
 #pragma unroll 4
     for (int r4 = j; 4 * r4 < R; r4 += 4) {
         const float4 a = *reinterpret_cast<const float4*>(w + 4 * r4);
-        const float4 b = __ldg(reinterpret_cast<const float4*>(v) + r4);
+        const float4 b = *reinterpret_cast<const float4*>(v + 4 * r4);   // global or shared
         acc = fmaf(a.x, b.x, acc);
         acc = fmaf(a.y, b.y, acc);
         acc = fmaf(a.z, b.z, acc);
@@ -244,7 +249,10 @@ __device__ __forceinline__ float dt_dot_smem(const float* w, const float* v, int
     return acc;
 }
 
-template <bool CONV, bool HAS_Z, bool DTP>
+// XP (with DTP): x_proj folded in as well; the CTA's rows' (DTP_MAX_ROWS, J) x_proj
+// outputs follow the delta block in shared memory, summed from the conv kernel's
+// per-block partials, and B, C come from there.
+template <bool CONV, bool HAS_Z, bool DTP, bool XP = false>
 __device__ __forceinline__ void decode_stream_body(const DecDev& p, int row_groups) {
     __shared__ DecTile S[DP_STAGES];
     // DTP: the CTA's (64, dtw_stride(R)) dt_proj block, then its rows' (DTP_MAX_ROWS, 64) delta
@@ -291,9 +299,9 @@ __device__ __forceinline__ void decode_stream_body(const DecDev& p, int row_grou
         } else if (tid < 112) {
             if (!DTP) cp_async16(&T.dr[4 * (tid - 96)], p.dl + r * p.dl_sb + d0 + 4 * (tid - 96), 16);
         } else if (tid < 116) {
-            cp_async16(&T.B[tid - 112], p.B + r * p.B_sb + 4 * (tid - 112), 16);
+            if (!XP) cp_async16(&T.B[tid - 112], p.B + r * p.B_sb + 4 * (tid - 112), 16);
         } else if (tid < 120) {
-            cp_async16(&T.C[tid - 116], p.C + r * p.C_sb + 4 * (tid - 116), 16);
+            if (!XP) cp_async16(&T.C[tid - 116], p.C + r * p.C_sb + 4 * (tid - 116), 16);
         }
     };
 
@@ -304,10 +312,23 @@ __device__ __forceinline__ void decode_stream_body(const DecDev& p, int row_grou
         cp_async_commit();
     }
     float* sDr = sW + DP_CH * ws;
+    float* sX = sDr + DTP_MAX_ROWS * DP_CH;
+    if (XP) {                             // x_proj outputs of this CTA's rows: partials in block order
+        for (int k = 0; rg + k * row_groups < p.b; ++k) {
+            const int r = rg + k * row_groups;
+            for (int o = tid; o < p.J; o += DP_NT) {
+                float acc = 0.f;
+                for (int q = 0; q < nblk; ++q) acc += p.xpart[((int64_t)q * p.b + r) * p.J + o];
+                sX[k * p.J + o] = acc;
+            }
+        }
+        __syncthreads();
+    }
     if (DTP) {                            // delta of every row of this CTA, while the ring fills
         for (int k = 0; rg + k * row_groups < p.b; ++k) {
-            const float v = dt_dot_smem(sW + ch * ws, p.dti + (int64_t)(rg + k * row_groups) * p.dti_sb, p.R, j);
-            if (j == 0) sDr[k * DP_CH + ch] = v;
+            const float* v = XP ? sX + k * p.J : p.dti + (int64_t)(rg + k * row_groups) * p.dti_sb;
+            const float dv = dt_dot_smem(sW + ch * ws, v, p.R, j);
+            if (j == 0) sDr[k * DP_CH + ch] = dv;
         }
     }
     for (int k = 0;; ++k) {
@@ -340,7 +361,9 @@ __device__ __forceinline__ void decode_stream_body(const DecDev& p, int row_grou
             softplus2(bc2(raw), sp, dsp);
             dte = sp.x;
         }
-        const float4 h4 = T.ss[ch][j], b4 = T.B[j], c4 = T.C[j];
+        const float4 h4 = T.ss[ch][j];
+        const float4 b4 = XP ? *reinterpret_cast<const float4*>(sX + k * p.J + p.R + 4 * j) : T.B[j];
+        const float4 c4 = XP ? *reinterpret_cast<const float4*>(sX + k * p.J + p.R + NS + 4 * j) : T.C[j];
         // same operation order as decode_kernel, so both give identical bits
         const float2 dt = bc2(dte * LOG2E), dx = bc2(dte * xc);
         const float2 h01 = fma2(ex2x2(mul2(dt, A01)), f2(h4.x, h4.y), mul2(dx, f2(b4.x, b4.y)));
@@ -375,6 +398,53 @@ __global__ void __launch_bounds__(DP_NT) decode_stream_kernel(const DecDev p, in
 template <bool HAS_Z>
 __global__ void __launch_bounds__(DP_NT, 4) decode_stream_dtp_kernel(const DecDev p, int row_groups) {
     decode_stream_body<false, HAS_Z, true>(p, row_groups);
+}
+
+// x_proj and dt_proj folded in: the state-update half of the layer path.
+template <bool HAS_Z>
+__global__ void __launch_bounds__(DP_NT, 3) decode_stream_xp_kernel(const DecDev p, int row_groups) {
+    decode_stream_body<false, HAS_Z, true, true>(p, row_groups);
+}
+
+// The conv half of the layer path (width 4, D a multiple of 64): CTA = 64 channels of
+// one row.  It rolls the conv window, writes xc = silu(conv + bias) to the workspace and
+// the block's partial x_proj products  sum_{d in block} W[o, d] xc[d]  for every output
+// o < J (the state-update kernel adds the blocks in order).
+__global__ void __launch_bounds__(DP_NT) decode_conv_xproj_kernel(const DecDev p) {
+    __shared__ __align__(16) float xs[DP_CH];
+    const int tid = threadIdx.x;
+    const int cb = blockIdx.x, r = blockIdx.y;
+    const int d0 = cb * DP_CH;
+    if (tid < DP_CH) {
+        const int d = d0 + tid;
+        const int64_t bd = (int64_t)r * p.D + d;
+        const float4 w = *reinterpret_cast<const float4*>(p.conv_state + bd * 4);
+        const float4 cw = *reinterpret_cast<const float4*>(p.cw + (int64_t)d * 4);
+        const float4 win = make_float4(w.y, w.z, w.w, p.x[r * p.x_sb + d]);
+        float acc = p.cb ? p.cb[d] : 0.f;          // same order as the streaming kernel's conv
+        acc = fmaf(win.x, cw.x, acc);
+        acc = fmaf(win.y, cw.y, acc);
+        acc = fmaf(win.z, cw.z, acc);
+        acc = fmaf(win.w, cw.w, acc);
+        const float xc = silu_f(acc);
+        *reinterpret_cast<float4*>(p.conv_state + bd * 4) = win;
+        p.xcbuf[bd] = xc;
+        xs[tid] = xc;
+    }
+    __syncthreads();
+    for (int o = tid; o < p.J; o += DP_NT) {
+        const float4* wr = reinterpret_cast<const float4*>(p.xw + (int64_t)o * p.D + d0);
+        float acc = 0.f;
+#pragma unroll 4
+        for (int c4 = 0; c4 < DP_CH / 4; ++c4) {
+            const float4 a = __ldg(wr + c4);
+            acc = fmaf(a.x, xs[4 * c4], acc);
+            acc = fmaf(a.y, xs[4 * c4 + 1], acc);
+            acc = fmaf(a.z, xs[4 * c4 + 2], acc);
+            acc = fmaf(a.w, xs[4 * c4 + 3], acc);
+        }
+        p.xpart[((int64_t)cb * p.b + r) * p.J + o] = acc;
+    }
 }
 
 // The streaming variant applies when every tile is full and every row is 16-byte aligned.
@@ -417,6 +487,34 @@ static cudaError_t launch_stream(const DecDev& p, cudaStream_t st) {
     if (p.dti) return p.z ? launch_stream_t<false, true, true>(p, st) : launch_stream_t<false, false, true>(p, st);
     if (conv) return p.z ? launch_stream_t<true, true>(p, st) : launch_stream_t<true, false>(p, st);
     return p.z ? launch_stream_t<false, true>(p, st) : launch_stream_t<false, false>(p, st);
+}
+
+// The layer path: the conv + partial x_proj kernel, then the state update with x_proj
+// and dt_proj folded in, reading the conv output from the workspace.
+static cudaError_t launch_layer(const DecDev& p0, cudaStream_t st) {
+    const int nblk = p0.D / DP_CH;
+    decode_conv_xproj_kernel<<<dim3(nblk, p0.b), DP_NT, 0, st>>>(p0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    DecDev p = p0;
+    p.x = p0.xcbuf; p.x_sb = p0.D; p.mode = SWX_DECODE_SSM;
+    auto k = p.z ? decode_stream_xp_kernel<true> : decode_stream_xp_kernel<false>;
+    const int used = (DP_CH * (dtw_stride(p.R) + DTP_MAX_ROWS) + DTP_MAX_ROWS * p.J) * 4;
+    const int most = (DP_CH * (dtw_stride(SWX_DECODE_MAX_DT_RANK) + DTP_MAX_ROWS) +
+                      DTP_MAX_ROWS * (SWX_DECODE_MAX_DT_RANK + 2 * NS)) * 4;
+    if ((e = allow_smem(k, most)) != cudaSuccess) return e;
+    int sms = 0, per_sm = 0;
+    if ((e = sm_fit(k, DP_NT, 0, &sms, &per_sm)) != cudaSuccess) return e;
+    if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, DP_NT, used)) != cudaSuccess) return e;
+    const int slots = std::max(1, sms * per_sm);
+    int row_groups = std::max(1, std::min(p.b, slots / nblk));
+    row_groups = std::max(row_groups, (p.b + DTP_MAX_ROWS - 1) / DTP_MAX_ROWS);   // rows per CTA <= 32
+    k<<<nblk * row_groups, DP_NT, used, st>>>(p, row_groups);
+    return cudaGetLastError();
+}
+
+int64_t layer_workspace_floats(int64_t b, int64_t D, int64_t J) {
+    return (D / DP_CH) * b * J + b * D;
 }
 
 template <int K>
@@ -491,4 +589,47 @@ extern "C" int swx_decode_step(const swx_decode_args* a, void* stream) {
         default: swx::launch_dec<6>(p, st); break;
     }
     return cudaGetLastError() == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
+}
+
+extern "C" int64_t swx_decode_layer_workspace_bytes(int64_t batch, int64_t dim, int64_t xproj_rows) {
+    if (batch < 0 || dim < 0 || xproj_rows < 0 || dim > (int64_t)INT32_MAX || xproj_rows > 4096) return -1;
+    return swx::layer_workspace_floats(batch, dim, xproj_rows) * 4;
+}
+
+extern "C" int swx_decode_layer_step(const swx_decode_args* a, void* stream) {
+    if (!a) return SWX_ERR_INVALID_ARG;
+    if (a->batch < 0 || a->dim < 0 || a->flags & ~SWX_DECODE_A_LOG) return SWX_ERR_INVALID_ARG;
+    if (a->mode != (SWX_DECODE_CONV | SWX_DECODE_SSM) || a->dstate != swx::NS || a->width != 4 ||
+        a->dim % swx::DP_CH != 0 || a->group_w)
+        return SWX_ERR_UNSUPPORTED;
+    if (a->batch * a->dim == 0) return SWX_OK;
+    if (a->dim > (int64_t)INT32_MAX || a->batch > 65535) return SWX_ERR_UNSUPPORTED;
+    if (a->delta || a->B || a->C || a->dt_in) return SWX_ERR_INVALID_ARG;
+    if (!a->x || !a->conv_weight || !a->conv_state || !a->A || !a->ssm_state || !a->out || !a->dt_weight ||
+        !a->xproj_weight || !a->workspace)
+        return SWX_ERR_INVALID_ARG;
+    if (a->dt_rank < 4 || a->dt_rank % 4 || a->dt_rank > SWX_DECODE_MAX_DT_RANK ||
+        a->xproj_rows != a->dt_rank + 2 * a->dstate)
+        return SWX_ERR_INVALID_ARG;
+    auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    if (!al(a->x) || (a->z && !al(a->z)) || !al(a->conv_state) || !al(a->conv_weight) || !al(a->A) ||
+        !al(a->ssm_state) || !al(a->dt_weight) || !al(a->xproj_weight) || !al(a->workspace) ||
+        a->x_sb % 4 || (a->z && a->z_sb % 4) || a->x_sb < 0 || a->z_sb < 0)
+        return SWX_ERR_INVALID_ARG;
+    const int64_t need = swx_decode_layer_workspace_bytes(a->batch, a->dim, a->xproj_rows);
+    if (need < 0 || a->workspace_bytes < need) return SWX_ERR_INVALID_ARG;
+    swx::DecDev p{};
+    p.b = (int)a->batch; p.D = (int)a->dim; p.N = (int)a->dstate; p.K = 4;
+    p.softplus = a->delta_softplus ? 1 : 0; p.mode = a->mode;
+    p.a_log = (a->flags & SWX_DECODE_A_LOG) ? 1 : 0;
+    p.x = a->x; p.x_sb = a->x_sb; p.z = a->z; p.z_sb = a->z_sb;
+    p.cw = a->conv_weight; p.cb = a->conv_bias; p.A = a->A; p.Dskip = a->Dskip; p.dbias = a->delta_bias;
+    p.conv_state = a->conv_state; p.ssm_state = a->ssm_state; p.out = a->out;
+    p.dtw = a->dt_weight; p.R = a->dt_rank;
+    p.xw = a->xproj_weight; p.J = a->xproj_rows;
+    p.xpart = static_cast<float*>(a->workspace);
+    p.xcbuf = p.xpart + (int64_t)(a->dim / swx::DP_CH) * a->batch * a->xproj_rows;
+    // the conv output's rows must stay 16-byte aligned for the state update's tile copies
+    if (reinterpret_cast<uintptr_t>(p.xcbuf) & 15u) return SWX_ERR_INVALID_ARG;
+    return swx::launch_layer(p, static_cast<cudaStream_t>(stream)) == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
 }

@@ -113,3 +113,51 @@ def decode_step(x, conv_state, conv_weight, conv_bias, delta, B, C, A, ssm_state
                     z, delta, B, C, A, Dskip, delta_bias, ssm_state, delta_softplus, want_xc=return_xc,
                     A_is_log=A_is_log)
     return (out, xc) if return_xc else out
+
+
+def decode_layer_step(x, conv_state, conv_weight, conv_bias, xproj_weight, dt_weight, A, ssm_state, Dskip=None,
+                      z=None, delta_bias=None, delta_softplus=True, A_is_log=False):
+    """One block's recurrent step between in_proj and out_proj with x_proj and dt_proj
+    folded into the kernels (models/sift_block.py:160-175): two launches, no GEMM.
+    x, z (b, D) fp32 rows (unit element stride); conv_state (b, D, 4), ssm_state (b, D, 16)
+    updated in place; xproj_weight (R + 32, D), dt_weight (D, R).  Returns out (b, D), or
+    None when the shape is not one the fused path takes (d_state 16, width 4, D a
+    multiple of 64, R a multiple of 4 up to 256, 16-byte aligned rows)."""
+    lib = _lib.load()
+    x, z = _row(x), _row(z)
+    b, D = x.shape
+    Af = A.detach().float().contiguous()
+    N = Af.shape[1]
+    w = conv_weight.detach().reshape(D, -1).float().contiguous()
+    xw = xproj_weight.detach().float().contiguous()
+    dtw = dt_weight.detach().float().contiguous()
+    R = dtw.shape[1]
+    if (N != 16 or w.shape[1] != 4 or D % 64 or R % 4 or R > _lib.SWX_DECODE_MAX_DT_RANK
+            or xw.shape != (R + 2 * N, D) or not conv_state.is_contiguous() or not ssm_state.is_contiguous()):
+        return None
+    if x.stride(0) % 4 or x.data_ptr() % 16 or (z is not None and (z.stride(0) % 4 or z.data_ptr() % 16)):
+        return None
+    keep = [w, Af, xw, dtw]
+    a = _lib.DecodeArgs()
+    a.batch, a.dim, a.dstate, a.width = b, D, N, 4
+    a.mode = _lib.SWX_DECODE_CONV | _lib.SWX_DECODE_SSM
+    a.delta_softplus = 1 if delta_softplus else 0
+    a.flags = _lib.SWX_DECODE_A_LOG if A_is_log else 0
+    a.x, a.x_sb = x.data_ptr(), x.stride(0)
+    if z is not None:
+        a.z, a.z_sb = z.data_ptr(), z.stride(0)
+    a.conv_weight, a.conv_state = w.data_ptr(), conv_state.data_ptr()
+    for name, t in (("conv_bias", conv_bias), ("Dskip", Dskip), ("delta_bias", delta_bias)):
+        if t is not None:
+            tf = t.detach().float().contiguous()
+            keep.append(tf)
+            setattr(a, name, tf.data_ptr())
+    out = torch.empty((b, D), device=x.device, dtype=torch.float32)
+    a.A, a.ssm_state, a.out = Af.data_ptr(), ssm_state.data_ptr(), out.data_ptr()
+    a.dt_weight, a.dt_rank = dtw.data_ptr(), R
+    a.xproj_weight, a.xproj_rows = xw.data_ptr(), R + 2 * N
+    wsb = lib.swx_decode_layer_workspace_bytes(b, D, R + 2 * N)
+    ws = torch.empty(max(wsb, 16), device=x.device, dtype=torch.uint8)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
+    _lib.check(lib.swx_decode_layer_step(a, _lib.stream_ptr(x.device)), "swx_decode_layer_step")
+    return out

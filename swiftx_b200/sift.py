@@ -33,7 +33,7 @@ import torch.nn.functional as F
 from . import embedding as embedding_kernels
 from . import norm as norm_kernels
 from .conv import causal_conv1d_fn
-from .decode import decode_conv_step, decode_ssm_step
+from .decode import decode_conv_step, decode_layer_step, decode_ssm_step
 from .selective_scan import selective_scan_fn
 
 
@@ -97,7 +97,7 @@ def _bf16_copies(weights, flat=None):
     return out
 
 
-# Largest batch whose decode step folds dt_proj into the state-update kernel (see
+# Largest batch whose decode step folds the projections into the kernels (see
 # SiftBlock.step).
 _FOLD_DT_MAX_BATCH = 32
 
@@ -284,6 +284,18 @@ class SiftBlock(nn.Module):
         conv_state, ssm_state = state
         xz = _linear(hidden, self.in_proj.weight, self.in_proj.bias).float()
         x, z = xz.chunk(2, dim=-1)
+        if self.pathway is None and hidden.shape[0] <= _FOLD_DT_MAX_BATCH:
+            # small batches: conv, x_proj, dt_proj, state update and gate in two launches
+            # with both projections inside the kernels (None: a shape the path does not
+            # take).  Measured on the graphed 24-layer d_model 1024 step, ms per token
+            # fp32 / bf16 projections: batch 1, 0.97 / 1.19 against 1.12 / 1.45 with the
+            # GEMMs; batch 16, 1.98 / 1.29 against 2.21 / 1.50; batch 64, 3.19 / 1.69
+            # against 3.23 / 1.58; batch 256, 5.44 / 3.64 against 3.97 / 2.03
+            y = decode_layer_step(x, conv_state, self.conv1d.weight, self.conv1d.bias, self.x_proj.weight,
+                                  self.dt_proj.weight, self.A_log, ssm_state, Dskip=self.D, z=z,
+                                  delta_bias=self.dt_proj.bias, A_is_log=True)
+            if y is not None:
+                return _linear(y.to(self.out_proj.weight.dtype), self.out_proj.weight, self.out_proj.bias)
         xc = decode_conv_step(x, conv_state, self.conv1d.weight, self.conv1d.bias)
         fuse_mix = self.pathway is not None and self.n_groups <= 8
         gate = z if self.pathway is None or fuse_mix else None
@@ -292,8 +304,8 @@ class SiftBlock(nn.Module):
         # there.  For small batches dt_proj is folded in too (the kernel forms
         # delta = dt_proj.weight @ dt itself, models/sift_block.py:167,106-108), which saves
         # the GEMM's launch; from a few dozen rows on, the GEMM plus the plain kernel is
-        # faster (measured on the 24-layer d_model 1024 step: 2.14 against 2.21 ms per
-        # token at batch 16, 4.08 against 3.97 at batch 256, fp32)
+        # faster (2.14 against 2.21 ms per token at batch 16, 4.08 against 3.97 at batch
+        # 256, fp32, on the step above)
         x_dbl = _linear(xc, self.x_proj.weight)
         dt, B, C = torch.split(x_dbl, [self.dt_rank, self.d_state, self.d_state], dim=-1)
         fold = self.dt_rank % 4 == 0 and self.dt_rank <= 256 and hidden.shape[0] <= _FOLD_DT_MAX_BATCH

@@ -252,3 +252,52 @@ def test_decode_dt_proj_folded(D, N, R):
     yo = yo * z.double() * torch.sigmoid(z.double())
     np.testing.assert_allclose(y.double().cpu().numpy(), yo.numpy(), rtol=1e-4, atol=1e-5)
     np.testing.assert_allclose(hd.double().cpu().numpy(), hn.numpy(), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("b,D,R", [(1, 128, 8), (7, 2048, 64), (40, 512, 128)])
+def test_decode_layer_step_folds_both_projections(b, D, R):
+    """swx_decode_layer_step (conv + x_proj + dt_proj + state update + gate, both
+    projections inside the kernels) against the block's step in float64
+    (models/sift_block.py:160-175): conv window roll, xc = silu(conv + bias),
+    dt | B | C = x_proj(xc), delta = softplus(dt_proj(dt) + bias), the recurrence, readout,
+    D skip and gate.  Batch 40 gives the state-update CTAs more than one row each."""
+    from swiftx_b200.decode import decode_layer_step
+    N, K = 16, 4
+    g = torch.Generator().manual_seed(43)
+    r = lambda *s, sc=1.0: torch.randn(*s, generator=g) * sc  # noqa: E731
+    xz = r(b, 2 * D)
+    cw, cb = r(D, 1, K, sc=0.5), r(D, sc=0.1)
+    Wx, Wdt = r(R + 2 * N, D, sc=D ** -0.5), r(D, R, sc=R ** -0.5)
+    A_log = torch.log(torch.arange(1, N + 1, dtype=torch.float32)).repeat(D, 1)
+    Dsk, bias = r(D), r(D, sc=0.1) - 4.0
+    cs, h = r(b, D, K), r(b, D, N, sc=0.1)
+    dev = lambda t: t.to(DEV)  # noqa: E731
+    xzd, csd, hd = dev(xz), dev(cs), dev(h)
+    y = decode_layer_step(xzd[:, :D], csd, dev(cw), dev(cb), dev(Wx), dev(Wdt), dev(A_log), hd, Dskip=dev(Dsk),
+                          z=xzd[:, D:], delta_bias=dev(bias), A_is_log=True)
+    assert y is not None
+    d = lambda t: t.double()  # noqa: E731
+    x, z = d(xz[:, :D]), d(xz[:, D:])
+    win = torch.cat([d(cs)[..., 1:], x[..., None]], -1)
+    xc = torch.nn.functional.silu((win * d(cw)[:, 0, :]).sum(-1) + d(cb))
+    x_dbl = xc @ d(Wx).T
+    dt, Bm, Cm = x_dbl[:, :R], x_dbl[:, R:R + N], x_dbl[:, R + N:]
+    dte = torch.nn.functional.softplus(dt @ d(Wdt).T + d(bias))
+    hn = torch.exp(dte[..., None] * -torch.exp(d(A_log))) * d(h) + (dte * xc)[..., None] * Bm[:, None, :]
+    yo = ((hn * Cm[:, None, :]).sum(-1) + d(Dsk) * xc) * torch.nn.functional.silu(z)
+    np.testing.assert_allclose(y.double().cpu().numpy(), yo.numpy(), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(hd.double().cpu().numpy(), hn.numpy(), rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(csd.double().cpu().numpy(), win.numpy(), rtol=0, atol=0)
+
+
+def test_decode_layer_step_declines_other_shapes():
+    """D not a multiple of 64 (or d_state != 16): None, and the states are untouched."""
+    from swiftx_b200.decode import decode_layer_step
+    b, D, N, R = 3, 96, 16, 8
+    xz = torch.randn(b, 2 * D, device=DEV)
+    cs, h = torch.randn(b, D, 4, device=DEV), torch.randn(b, D, N, device=DEV)
+    cs0, h0 = cs.clone(), h.clone()
+    y = decode_layer_step(xz[:, :D], cs, torch.randn(D, 1, 4, device=DEV), None,
+                          torch.randn(R + 2 * N, D, device=DEV), torch.randn(D, R, device=DEV),
+                          -torch.ones(D, N, device=DEV), h, z=xz[:, D:])
+    assert y is None and torch.equal(cs, cs0) and torch.equal(h, h0)
