@@ -67,7 +67,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("bounds", [[0, 41, 90], [0, 30, 31, 90], chunk_bounds(90, 3, multiple=1)])
+@pytest.mark.parametrize("bounds", [[0, 41, 90], [0, 30, 31, 90], chunk_bounds(90, 3, correction_offset=0, multiple=1)])
 def test_sequence_parallel_matches_whole_sequence(bounds):
     world = len(bounds) - 1
     ctx = mp.get_context("spawn")
@@ -102,12 +102,17 @@ def test_combine_prefix_is_the_chained_recurrence():
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_chunk_bounds_balance(world):
-    L, c = 65536, 0.7
-    b = chunk_bounds(L, world, correction_cost=c)
+    L, c, c0 = 65536, 0.58, 4136
+    b = chunk_bounds(L, world, correction_cost=c, correction_offset=c0)
     assert b[0] == 0 and b[-1] == L and len(b) == world + 1
     lens = [b[r + 1] - b[r] for r in range(world)]
     assert all(n > 0 and n % 256 == 0 for n in lens)
     # every rank's modelled time (forward, plus the correction on ranks > 0) within one
     # rounding unit of the others
-    cost = [lens[0]] + [(1 + c) * n for n in lens[1:]]
+    cost = [lens[0]] + [(1 + c) * n + c0 for n in lens[1:]]
     assert max(cost) - min(cost) <= 2 * 256 * (1 + c)
+
+
+def test_chunk_bounds_short_sequence():
+    """A sequence too short for the correction's fixed cost: rank 0 takes it whole."""
+    assert chunk_bounds(2048, 4) == [0, 2048, 2048, 2048, 2048]

@@ -28,7 +28,7 @@ def _worker(rank, world, port, q):
     try:
         b, L, D = 2, 600, 64
         inp = config_inputs(b, L, D, 16, seed=5, device=f"cuda:{rank}")
-        bounds = chunk_bounds(L, world, multiple=8)
+        bounds = chunk_bounds(L, world, correction_offset=0, multiple=8)
         s, e = bounds[rank], bounds[rank + 1]
         ch = {k: inp[k][:, s:e] for k in ("u", "delta", "z", "B", "C")}
         out = sequence_parallel_scan(ch["u"], ch["delta"], inp["A"], ch["B"], ch["C"], inp["D"], ch["z"],
