@@ -13,15 +13,13 @@
 //      prologue), then per step S += delta_eff and the 16 decays exp2(A log2e S) against
 //      C_t h_in.  The kernel is bound by instruction issue, so the decays stay on the MUFU
 //      unit (moving a share to the FMA-pipe exp2 was measured slower: 1.78 ms with none,
-//      2.07 with half, 2.70 with all at b=4, L=32768, D=2048, bf16).
-// With softplus, S only grows, so a state's decay, once below 2^-127 (flushed to 0 by
-// ex2.approx.ftz), stays 0: every 8 steps a warp vote drops the trailing state groups
-// whose decays are 0 in every lane, and the 8 steps run with the live groups unrolled (a
-// dropped group would add exact zeros, so the result is the same bit for bit for finite
-// inputs).  1.79 -> 1.71 ms at b=4, L=32768, D=2048 with log-uniform dt in [1e-3, 0.1]:
-// per-step branches instead of one dispatch per 8 steps were slower (2.1 - 2.8 ms).
+//      2.07 with half, 2.70 with all at b=4, L=32768, D=2048, bf16).  Skipping the state
+//      groups whose decays have underflowed in every lane (S only grows under softplus)
+//      was measured too: with one warp-uniform dispatch per 8 steps over copies of the
+//      step body for 4..0 live groups, 1.75 against 1.79 ms at L=32768 but 0.71 against
+//      0.59 ms at L=8192, where few decays underflow and the copies miss the instruction
+//      cache; not kept.
 #include <algorithm>
-#include <type_traits>
 
 #include "common.cuh"
 #include "launch_util.cuh"
@@ -55,20 +53,6 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_sums_kernel(const Sca
     bsum[((int64_t)bi * nblk + k) * p.D + d] = s;
 }
 
-// The terms of state groups 0..M-1 (four states each: pairs 2v, 2v+1) of one step's
-// correction sum, accumulated in group order into two accumulators.
-template <int M>
-__device__ __forceinline__ void corr_terms(float2 s2, const float4* cr, const float2 (&A2)[NS / 2],
-                                           const float2 (&H)[NS / 2], float2& acc0, float2& acc1) {
-#pragma unroll
-    for (int v = 0; v < M; ++v) {
-        const float4 c4 = cr[v];
-        const float2 p0 = ex2x2(mul2(s2, A2[2 * v])), p1 = ex2x2(mul2(s2, A2[2 * v + 1]));
-        acc0 = fma2(mul2(p0, H[2 * v]), f2(c4.x, c4.y), acc0);
-        acc1 = fma2(mul2(p1, H[2 * v + 1]), f2(c4.z, c4.w), acc1);
-    }
-}
-
 template <typename Tin, typename Tout, bool HAS_Z, bool GW = false>
 __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev p, const float* bsum, int nblk) {
     __shared__ __align__(16) float Cs[CR_CROWS][NS];
@@ -100,14 +84,6 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev 
     Tout* out = static_cast<Tout*>(p.out) + (int64_t)bi * p.L * p.D + dc;
     const float bias = p.dbias ? p.dbias[dc] : 0.f;
     const int grp = GW ? p.gof[dc] : 0;        // pathway group of the channel (mix fused into the gate)
-    // state groups 0..m-1 (four states each) are evaluated; the groups from m on have
-    // decays that are 0 in fp32 in every lane of the warp (warp-uniform), or lie wholly
-    // past N (h_in = 0 there)
-    int m = (min(p.N, NS) + 3) / 4;
-    float gmax[NS / 4];                        // the least negative A log2e of each group
-#pragma unroll
-    for (int g = 0; g < NS / 4; ++g)
-        gmax[g] = fmaxf(fmaxf(A2[2 * g].x, A2[2 * g].y), fmaxf(A2[2 * g + 1].x, A2[2 * g + 1].y));
     for (int tb = t0; tb < t1; tb += CR_CROWS) {
         const int nr = min(CR_CROWS, t1 - tb);
         __syncthreads();
@@ -120,16 +96,6 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev 
         // eight steps at a time: their delta, z and output loads are issued before the
         // arithmetic (the running sum S is the only dependence between steps)
         for (int r0 = 0; r0 < nr; r0 += 8) {
-            if (p.softplus) {
-                // delta_eff = softplus(...) >= 0, so S never decreases: once S * A log2e
-                // is below -127 for all four states of the last evaluated group in every
-                // lane, their decays flush to 0 (ex2.approx.ftz) for the rest of the block
-                // and the group's terms would add exactly nothing
-                const unsigned am = __activemask();
-#pragma unroll
-                for (int g = NS / 4 - 1; g >= 0; --g)            // static indices: A2 stays in registers
-                    if (g == m - 1 && __all_sync(am, S * gmax[g] < -127.f)) m = g;
-            }
             float raw[8], zz[8], oo[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
@@ -139,32 +105,26 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev 
                 zz[i] = HAS_Z ? Elem<Tin>::to_f(zp[t * p.z_sl]) : 0.f;
                 oo[i] = Elem<Tout>::to_f(out[t * p.D]);
             }
-            // the group's 8 steps with the live state groups 0..M-1 fully unrolled: one
-            // warp-uniform dispatch per 8 steps keeps the steps' exponentials interleaved
-            auto steps = [&](auto mc) {
-                constexpr int M = decltype(mc)::value;
 #pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    if (r0 + i >= nr) break;
-                    if (M > 0) S += p.softplus ? softplus_f(raw[i]) : raw[i];   // S matters only while a group lives
-                    const float2 s2 = bc2(S);
-                    const float4* cr = reinterpret_cast<const float4*>(&Cs[r0 + i][0]);
-                    // two accumulators halve the dependent chain of the 16-term sum
-                    float2 acc0 = bc2(0.f), acc1 = bc2(0.f);
-                    corr_terms<M>(s2, cr, A2, H, acc0, acc1);
-                    const float2 acc = add2(acc0, acc1);
-                    float corr = acc.x + acc.y;
-                    if (HAS_Z) corr *= silu_f(zz[i]);
-                    if (GW) corr *= p.gw[(int64_t)bi * p.gw_sb + (int64_t)(tb + r0 + i) * p.gw_sl + grp];
-                    oo[i] += corr;
+            for (int i = 0; i < 8; ++i) {
+                if (r0 + i >= nr) break;
+                S += p.softplus ? softplus_f(raw[i]) : raw[i];
+                const float2 s2 = bc2(S);
+                const float4* cr = reinterpret_cast<const float4*>(&Cs[r0 + i][0]);
+                // two accumulators halve the dependent chain of the 16-term sum
+                float2 acc0 = bc2(0.f), acc1 = bc2(0.f);
+#pragma unroll
+                for (int v = 0; v < NS / 4; ++v) {
+                    const float4 c4 = cr[v];
+                    const float2 p0 = ex2x2(mul2(s2, A2[2 * v])), p1 = ex2x2(mul2(s2, A2[2 * v + 1]));
+                    acc0 = fma2(mul2(p0, H[2 * v]), f2(c4.x, c4.y), acc0);
+                    acc1 = fma2(mul2(p1, H[2 * v + 1]), f2(c4.z, c4.w), acc1);
                 }
-            };
-            switch (m) {
-                case 4: steps(std::integral_constant<int, 4>{}); break;
-                case 3: steps(std::integral_constant<int, 3>{}); break;
-                case 2: steps(std::integral_constant<int, 2>{}); break;
-                case 1: steps(std::integral_constant<int, 1>{}); break;
-                default: steps(std::integral_constant<int, 0>{}); break;
+                const float2 acc = add2(acc0, acc1);
+                float corr = acc.x + acc.y;
+                if (HAS_Z) corr *= silu_f(zz[i]);
+                if (GW) corr *= p.gw[(int64_t)bi * p.gw_sb + (int64_t)(tb + r0 + i) * p.gw_sl + grp];
+                oo[i] += corr;
             }
 #pragma unroll
             for (int i = 0; i < 8; ++i)
