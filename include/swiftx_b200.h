@@ -132,7 +132,9 @@ int64_t swx_scan_bwd_workspace_bytes_f64(int64_t batch, int64_t seqlen, int64_t 
  * Replaces selective_scan_fast / selective_scan_ref forward
  * (models/selective_scan.py:34-60, :112-125, :246-265) and TritonScanFn.forward
  * (models/triton_scan.py:118-135); the gate and softplus fold in the block glue of
- * models/sift_block.py:108,134. */
+ * models/sift_block.py:108,134.  An empty problem (batch * seqlen * dim = 0) launches no
+ * kernel; with seqlen = 0 the forward sets h_last to h0 (or zeros) and delta_sum to zeros,
+ * and the backward sets dA, dD, ddelta_bias and dh0 to zeros (async on the stream). */
 int swx_scan_fwd(const swx_scan_args* args, void* stream);
 
 /* Backward of swx_scan_fwd; needs the checkpoints the forward wrote with the same

@@ -161,6 +161,32 @@ swx::ScanDev pack(const swx_scan_args* a) {
 
 int from_cuda(cudaError_t e) { return e == cudaSuccess ? SWX_OK : SWX_ERR_CUDA; }
 
+// An empty sequence (L = 0) still has per-row and per-channel results: the final state is
+// the initial one (or zero), the sum of delta_eff is zero, and the gradients of the
+// parameters and of h0 are zero (nothing depends on them).  Written with async copies /
+// fills on the stream; nothing else is touched.
+int empty_scan_fwd(const swx_scan_args* a, cudaStream_t st) {
+    const int64_t es = a->in_dtype == SWX_DTYPE_F64 ? 8 : 4;
+    const int64_t bdn = a->batch * a->dim * a->dstate, bd = a->batch * a->dim;
+    cudaError_t e = cudaSuccess;
+    if (a->h_last && bdn > 0)
+        e = a->h0 ? cudaMemcpyAsync(a->h_last, a->h0, bdn * es, cudaMemcpyDeviceToDevice, st)
+                  : cudaMemsetAsync(a->h_last, 0, bdn * es, st);
+    if (e == cudaSuccess && a->delta_sum && bd > 0) e = cudaMemsetAsync(a->delta_sum, 0, bd * es, st);
+    return from_cuda(e);
+}
+
+int empty_scan_bwd(const swx_scan_args* a, cudaStream_t st) {
+    const int64_t es = a->in_dtype == SWX_DTYPE_F64 ? 8 : 4;
+    const int64_t D = a->dim, N = a->dstate;
+    cudaError_t e = cudaSuccess;
+    if (a->dA && D * N > 0) e = cudaMemsetAsync(a->dA, 0, D * N * es, st);
+    if (e == cudaSuccess && a->dD && D > 0) e = cudaMemsetAsync(a->dD, 0, D * es, st);
+    if (e == cudaSuccess && a->ddelta_bias && D > 0) e = cudaMemsetAsync(a->ddelta_bias, 0, D * es, st);
+    if (e == cudaSuccess && a->dh0 && a->batch * D * N > 0) e = cudaMemsetAsync(a->dh0, 0, a->batch * D * N * es, st);
+    return from_cuda(e);
+}
+
 }  // namespace
 
 namespace swx {
@@ -205,7 +231,7 @@ int64_t swx_scan_bwd_workspace_bytes_f64(int64_t batch, int64_t seqlen, int64_t 
 int swx_scan_fwd(const swx_scan_args* a, void* stream) {
     int s = check_common(a);
     if (s != SWX_OK) return s;
-    if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
+    if (a->batch * a->seqlen * a->dim == 0) return empty_scan_fwd(a, static_cast<cudaStream_t>(stream));
     if (elem_size(a->out_dtype) == 0) return SWX_ERR_UNSUPPORTED;
     if (!a->out && !a->h_last && !a->delta_sum && !a->checkpoints) return SWX_OK;   // nothing requested
     if (a->checkpoints && !aligned16(a->checkpoints)) return SWX_ERR_INVALID_ARG;
@@ -222,7 +248,7 @@ int swx_scan_fwd(const swx_scan_args* a, void* stream) {
 int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     int s = check_common(a);
     if (s != SWX_OK) return s;
-    if (a->batch * a->seqlen * a->dim == 0) return SWX_OK;
+    if (a->batch * a->seqlen * a->dim == 0) return empty_scan_bwd(a, static_cast<cudaStream_t>(stream));
     if (!a->dout || !a->du || !a->ddelta || !a->dB || !a->dC || !a->dA || !a->checkpoints)
         return SWX_ERR_INVALID_ARG;
     if (a->z && !a->dz) return SWX_ERR_INVALID_ARG;

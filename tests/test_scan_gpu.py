@@ -410,3 +410,26 @@ def test_float64_long_sequence_vs_oracle():
     for k, v in gr_o.items():
         np.testing.assert_allclose(g[k].detach().cpu().numpy(), v, rtol=1e-9, atol=1e-9 * np.abs(v).max(),
                                    err_msg=k)
+
+
+@pytest.mark.parametrize("shape", [(2, 0, 64), (0, 50, 64)], ids=["L=0", "b=0"])
+def test_empty_problems(shape):
+    """An empty sequence or batch: empty outputs, the final state equal to h0 (nothing
+    decays it), and zero gradients for the parameters and h0 (nothing depends on them),
+    as the reference's expressions give."""
+    b, L, D = shape
+    N = 16
+    g = torch.Generator(device=DEV).manual_seed(3)
+    t = lambda *s: torch.randn(*s, device=DEV, generator=g).requires_grad_()  # noqa: E731
+    u, dl, z = t(b, L, D), t(b, L, D), t(b, L, D)
+    Bm, Cm = t(b, L, N), t(b, L, N)
+    A = (-torch.rand(D, N, device=DEV, generator=g) - 0.1).requires_grad_()
+    Dv, bias, h0 = t(D), t(D), t(b, D, N)
+    out, hl = selective_scan_fn(u, dl, A, Bm, Cm, Dv, z=z, delta_bias=bias, delta_softplus=True, h0=h0,
+                                return_last_state=True)
+    assert out.shape == (b, L, D)
+    if L == 0:
+        assert torch.equal(hl, h0.detach())
+    out.sum().backward()
+    for name, p in (("A", A), ("D", Dv), ("delta_bias", bias), ("h0", h0)):
+        assert p.grad is not None and torch.equal(p.grad, torch.zeros_like(p)), name
