@@ -354,7 +354,15 @@ int swx_conv1d_fwd(const swx_conv_args* a, void* stream) {
 
 int swx_conv1d_bwd(const swx_conv_args* a, void* stream) {
     int s = conv_check(a);
-    if (s != SWX_OK || a->batch * a->seqlen * a->dim == 0) return s;
+    if (s != SWX_OK) return s;
+    if (a->batch * a->seqlen * a->dim == 0) {
+        // no step contributes: the weight and bias gradients are zero
+        cudaStream_t st = static_cast<cudaStream_t>(stream);
+        cudaError_t e = cudaSuccess;
+        if (a->dweight && a->dim * a->width > 0) e = cudaMemsetAsync(a->dweight, 0, a->dim * a->width * 4, st);
+        if (e == cudaSuccess && a->dbias && a->dim > 0) e = cudaMemsetAsync(a->dbias, 0, a->dim * 4, st);
+        return e == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
+    }
     if (!a->dout || !a->dx || !a->dweight || !a->workspace) return SWX_ERR_INVALID_ARG;
     if (a->workspace_bytes < swx_conv1d_bwd_workspace_bytes(a->batch, a->seqlen, a->dim, a->width))
         return SWX_ERR_INVALID_ARG;

@@ -248,7 +248,13 @@ int swx_rmsnorm_fwd(const swx_rmsnorm_args* a, void* stream) {
 
 int swx_rmsnorm_bwd(const swx_rmsnorm_args* a, void* stream) {
     const int s = norm_check(a, true);
-    if (s != SWX_OK || a->rows * a->dim == 0) return s;
+    if (s != SWX_OK) return s;
+    if (a->rows * a->dim == 0) {          // no row contributes: the weight gradient is zero
+        if (a->dweight && a->dim > 0)
+            return cudaMemsetAsync(a->dweight, 0, a->dim * 4, static_cast<cudaStream_t>(stream)) == cudaSuccess
+                       ? SWX_OK : SWX_ERR_CUDA;
+        return SWX_OK;
+    }
     if (a->workspace_bytes < swx_rmsnorm_bwd_workspace_bytes(a->dim)) return SWX_ERR_INVALID_ARG;
     const swx::NormDev p = norm_pack(a);
     cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -301,3 +301,15 @@ def test_decode_layer_step_declines_other_shapes():
                           torch.randn(R + 2 * N, D, device=DEV), torch.randn(D, R, device=DEV),
                           -torch.ones(D, N, device=DEV), h, z=xz[:, D:])
     assert y is None and torch.equal(cs, cs0) and torch.equal(h, h0)
+
+
+def test_conv_empty_sequence_zero_weight_grads():
+    """An empty sequence: empty output, and zero weight / bias gradients (no step
+    contributes), as torch's conv1d gives."""
+    x = torch.randn(2, 0, 64, device=DEV, requires_grad=True)
+    w = torch.randn(64, 1, 4, device=DEV, requires_grad=True)
+    bias = torch.randn(64, device=DEV, requires_grad=True)
+    y = causal_conv1d_fn(x, w, bias, "silu")
+    assert y.shape == (2, 0, 64)
+    y.sum().backward()
+    assert torch.equal(w.grad, torch.zeros_like(w)) and torch.equal(bias.grad, torch.zeros_like(bias))

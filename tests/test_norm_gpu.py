@@ -132,3 +132,13 @@ def test_backbone_fused_residual_norm_matches_per_layer_form():
     assert torch.equal(l1, l0)
     for a, b in zip(g1, g0):
         assert torch.equal(a, b)
+
+
+def test_no_rows_zero_weight_grad():
+    """No rows: an empty output and a zero weight gradient (no row contributes)."""
+    x = torch.randn(0, 256, device="cuda", requires_grad=True)
+    w = torch.randn(256, device="cuda", requires_grad=True)
+    y = rms_norm(x, w)
+    assert y.shape == (0, 256)
+    y.sum().backward()
+    assert torch.equal(w.grad, torch.zeros_like(w))
