@@ -45,6 +45,12 @@ extern "C" {
    (models/sift_block.py:121 forms A that way before every scan call).  The kernels form A
    themselves and the backward's dA receives the gradient with respect to A_log. */
 #define SWX_SCAN_A_LOG 1
+/* swx_scan_args.flags, forward only: the forward may cut each row's sequence into
+   segments scanned in parallel when the batch is too small to fill the GPU (the chunk
+   scans from a zero state, a prefix combine of their end states, then the initial-state
+   correction of every later segment's output, checkpoints and pre-gate output).  It then
+   uses args->workspace, which must hold swx_scan_fwd_workspace_bytes(args) bytes. */
+#define SWX_SCAN_SPLIT_FWD 2
 
 /* Arguments of the scan entry points (forward and backward share one struct). */
 typedef struct swx_scan_args {
@@ -136,6 +142,11 @@ int64_t swx_scan_bwd_workspace_bytes_f64(int64_t batch, int64_t seqlen, int64_t 
  * kernel; with seqlen = 0 the forward sets h_last to h0 (or zeros) and delta_sum to zeros,
  * and the backward sets dA, dD, ddelta_bias and dh0 to zeros (async on the stream). */
 int swx_scan_fwd(const swx_scan_args* args, void* stream);
+/* Workspace bytes the forward uses with SWX_SCAN_SPLIT_FWD for these arguments on the
+ * current device: 0 when it would not split (float64, no output, rows whose batch stride
+ * is not seqlen row strides, a grid that already fills the GPU, or sequences shorter than
+ * 4096 steps or not a multiple of 16 times the segment count); -1 for bad arguments. */
+int64_t swx_scan_fwd_workspace_bytes(const swx_scan_args* args);
 
 /* Backward of swx_scan_fwd; needs the checkpoints the forward wrote with the same
  * inputs.  Replaces _SelectiveScanFn.backward / _FusedScanFn.backward

@@ -17,6 +17,7 @@ SWX_ERR_UNSUPPORTED = 2
 SWX_ERR_CUDA = 3
 SWX_ERR_TIMEOUT = 4
 SWX_MAX_GROUPS = 8
+SWX_SCAN_SPLIT_FWD = 2
 SWX_DECODE_MAX_DT_RANK = 256
 # capacity of the static scratch of swx_scan_bwd_static_scratch (SWX_STATIC_SCRATCH_BYTES)
 SWX_STATIC_SCRATCH_BYTES = 8 << 20
@@ -158,6 +159,8 @@ def load():
     lib.swx_scan_bwd_segments.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_exp2_fma_eval.restype = ctypes.c_int
     lib.swx_exp2_fma_eval.argtypes = [vp, vp, i64, vp]
+    lib.swx_scan_fwd_workspace_bytes.restype = i64
+    lib.swx_scan_fwd_workspace_bytes.argtypes = [ctypes.POINTER(ScanArgs)]
     lib.swx_decode_layer_step.restype = ctypes.c_int
     lib.swx_decode_layer_step.argtypes = [ctypes.POINTER(DecodeArgs), vp]
     lib.swx_decode_layer_workspace_bytes.restype = i64

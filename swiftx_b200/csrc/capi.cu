@@ -15,7 +15,9 @@ cudaError_t launch_scan_bwd_rows(const ScanDev& p, bool has_z, cudaStream_t st);
 cudaError_t launch_group_w_grad(const ScanDev& p, int in_dtype, cudaStream_t st);
 cudaError_t scan_bwd_rows_applicable(const ScanDev& p, int in_dtype, bool has_z, bool* yes);
 cudaError_t launch_scan_correct(const ScanDev& p, int in_dtype, int out_dtype, bool has_z, float* ws,
-                                cudaStream_t st);
+                                cudaStream_t st, bool fix);
+cudaError_t launch_seg_combine(const ScanDev& p, int G, const float* h_end, const float* dsum, float* h_in,
+                               float* h_last, float* dsum_out, cudaStream_t st);
 int64_t scan_correct_workspace_floats(int64_t b, int64_t L, int64_t D);
 }  // namespace swx
 
@@ -35,20 +37,25 @@ bool vec_ok(const void* p, int64_t sb, int64_t sl, int es) {
 constexpr int64_t kAlign = 256;
 int64_t round_up(int64_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
 
-// Segments of the time-segmented backward, a function of (L, D) alone: results do not
-// depend on the device, and the rows of a batch get bit-identical gradients whether they
-// are passed together or in smaller batches.  Sized for about two 64-channel CTAs per SM
-// of a 148-SM B200 at a batch of 8 rows, with segments of at least 128 steps; the reverse
-// carries are summarised over sub-segments of up to 128 steps that divide a segment.
+// Segments of the time-segmented backward, a function of (L, D) and of the batch below
+// 8 rows: results do not depend on the device, and the rows of batches of 8 rows or more
+// get bit-identical gradients whether they are passed together or in smaller batches of
+// 8 or more.  Sized for about two 64-channel CTAs per SM of a 148-SM B200, with segments
+// of at least 128 steps; the reverse carries are summarised over sub-segments of up to
+// 128 steps that divide a segment.
 struct SegPlan {
     int64_t seg_len, nseg, sub_len, nsub, first_sub, nblk64;
 };
 
-SegPlan seg_plan(int64_t L, int64_t D) {
+SegPlan seg_plan(int64_t L, int64_t D, int64_t b) {
     SegPlan s{};
     const int64_t nck = (L + 15) / 16;
     s.nblk64 = (D + 63) / 64;
-    int64_t G = std::max<int64_t>(1, 37 / std::max<int64_t>(1, s.nblk64));   // 8 rows x blocks x G ~ 2 x 148
+    // rows x blocks x G ~ 2 x 148 CTAs, counting at most 8 rows: batches of 8 rows or more
+    // share one plan (and give bit-identical rows however they are split), smaller ones
+    // cut their rows into more segments to fill the GPU
+    const int64_t rows = std::min<int64_t>(8, std::max<int64_t>(1, b));
+    int64_t G = std::max<int64_t>(1, 296 / (rows * std::max<int64_t>(1, s.nblk64)));
     G = std::min<int64_t>(G, std::max<int64_t>(1, nck / 8));
     const int64_t per = std::max<int64_t>(1, (nck + G - 1) / G);   // checkpoint chunks per segment
     s.nseg = std::max<int64_t>(1, (nck + per - 1) / per);
@@ -84,7 +91,7 @@ WsLayout ws_layout(int64_t b, int64_t L, int64_t D, int64_t es = 4) {
         w.total = w.q;
         return w;
     }
-    const SegPlan sp = seg_plan(L, D);
+    const SegPlan sp = seg_plan(L, D, b);
     w.bc = 0;
     w.a = w.bc + round_up(nblk32 * b * L * 2 * swx::NS * 4);
     w.d = w.a + round_up(sp.nseg * b * D * swx::NS * 4);
@@ -113,7 +120,7 @@ int check_common(const swx_scan_args* a) {
     // batch rows index the grid's y dimension (at most 65535)
     if (a->batch > 65535 || a->seqlen > INT32_MAX || a->dim > INT32_MAX) return SWX_ERR_UNSUPPORTED;
     if (elem_size(a->in_dtype) == 0) return SWX_ERR_UNSUPPORTED;
-    if (a->flags & ~SWX_SCAN_A_LOG) return SWX_ERR_INVALID_ARG;
+    if (a->flags & ~(SWX_SCAN_A_LOG | SWX_SCAN_SPLIT_FWD)) return SWX_ERR_INVALID_ARG;
     if (a->group_w || a->d_group_w) {
         // the pathway mix: with the gate, fp32 / bf16 only, a bounded number of groups
         if (a->in_dtype == SWX_DTYPE_F64 || !a->z) return SWX_ERR_UNSUPPORTED;
@@ -187,6 +194,91 @@ int empty_scan_bwd(const swx_scan_args* a, cudaStream_t st) {
     return from_cuda(e);
 }
 
+// ---- split forward (SWX_SCAN_SPLIT_FWD): each row's sequence cut into G segments that
+// the forward scans as G independent rows of a (b * G, L / G, D) view of the same
+// buffers (the checkpoint, output and pre-gate layouts of the view are the full rows'),
+// then a prefix combine of the segments' end states and the correction of every later
+// segment.
+int sm_count() {
+    static int cached[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (!cached[dev]) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+        cached[dev] = n;
+    }
+    return cached[dev];
+}
+
+// Segments per row: the largest of 8, 4, 2 with (rows x 32-channel blocks x G) at most two
+// CTAs per SM, segments of at least 2048 steps and a multiple of 16; 1 (no split) when the
+// whole-row grid already holds an SM each or the rows are not laid out seqlen row
+// strides apart.
+int fwd_split_segments(const swx_scan_args* a) {
+    if (!(a->flags & SWX_SCAN_SPLIT_FWD) || a->in_dtype == SWX_DTYPE_F64 || !a->out) return 1;
+    const int64_t L = a->seqlen;
+    auto rows_ok = [&](const void* ptr, int64_t sb, int64_t sl) { return !ptr || sb == L * sl; };
+    if (!rows_ok(a->u, a->u_sb, a->u_sl) || !rows_ok(a->delta, a->delta_sb, a->delta_sl) ||
+        !rows_ok(a->z, a->z_sb, a->z_sl) || !rows_ok(a->B, a->B_sb, a->B_sl) || !rows_ok(a->C, a->C_sb, a->C_sl) ||
+        (a->group_w && a->group_w_sb != L * a->group_w_sl))
+        return 1;
+    const int sms = sm_count();
+    const int64_t base = a->batch * ((a->dim + 31) / 32);
+    if (sms <= 0 || base > sms) return 1;
+    for (int G = 8; G >= 2; G /= 2)
+        if (base * G <= 2LL * sms && L % (16LL * G) == 0 && L / G >= 2048 && a->batch * G <= 65535) return G;
+    return 1;
+}
+
+struct FwdWs {
+    int64_t h_end, dsum, h_in, corr, total;
+};
+
+FwdWs fwd_ws_layout(const swx_scan_args* a, int G) {
+    FwdWs w{};
+    const int64_t bg = a->batch * G, D = a->dim, N = a->dstate;
+    w.h_end = 0;
+    w.dsum = round_up(bg * D * N * 4);
+    w.h_in = w.dsum + round_up(bg * D * 4);
+    w.corr = w.h_in + round_up(bg * D * N * 4);
+    w.total = w.corr + round_up(swx::scan_correct_workspace_floats(bg, a->seqlen / G, D) * 4);
+    return w;
+}
+
+cudaError_t split_forward(const swx_scan_args* a, int G, const FwdWs& w, cudaStream_t st) {
+    char* ws = static_cast<char*>(a->workspace);
+    float* h_end = reinterpret_cast<float*>(ws + w.h_end);
+    float* dsum = reinterpret_cast<float*>(ws + w.dsum);
+    float* h_in = reinterpret_cast<float*>(ws + w.h_in);
+    float* corr = reinterpret_cast<float*>(ws + w.corr);
+    const int64_t Ls = a->seqlen / G;
+    // the (b * G, Ls, D) view: segment s of row r is view row r * G + s
+    swx_scan_args v = *a;
+    v.batch = a->batch * G;
+    v.seqlen = Ls;
+    v.u_sb = Ls * a->u_sl; v.delta_sb = Ls * a->delta_sl; v.z_sb = Ls * a->z_sl;
+    v.B_sb = Ls * a->B_sl; v.C_sb = Ls * a->C_sl; v.group_w_sb = Ls * a->group_w_sl;
+    v.h0 = nullptr;                      // every segment from a zero state
+    v.h_last = h_end;
+    v.delta_sum = dsum;
+    const bool has_z = a->z != nullptr;
+    cudaError_t e = swx::launch_scan_fwd(pack(&v), a->in_dtype, a->out_dtype, has_z, st);
+    if (e != cudaSuccess) return e;
+    // each segment's true initial state; the rows' final states and delta sums
+    e = swx::launch_seg_combine(pack(a), G, h_end, dsum, h_in, a->h_last, a->delta_sum, st);
+    if (e != cudaSuccess) return e;
+    // out, checkpoints and the pre-gate output of every segment gain its initial state's term
+    swx_scan_args c = v;
+    c.h0 = h_in;
+    c.h_last = nullptr;
+    c.delta_sum = nullptr;
+    swx::ScanDev pc = pack(&c);
+    pc.seg_g = G;
+    pc.skip_first_seg = a->h0 ? 0 : 1;
+    return swx::launch_scan_correct(pc, a->in_dtype, a->out_dtype, has_z, corr, st, true);
+}
+
 }  // namespace
 
 namespace swx {
@@ -241,8 +333,20 @@ int swx_scan_fwd(const swx_scan_args* a, void* stream) {
         return from_cuda(swx::launch_scan_fwd_f64(p, static_cast<cudaStream_t>(stream)));
     }
     if (a->out_dtype == SWX_DTYPE_F64) return SWX_ERR_UNSUPPORTED;
+    const int G = fwd_split_segments(a);
+    if (G > 1) {
+        const FwdWs w = fwd_ws_layout(a, G);
+        if (!a->workspace || !aligned16(a->workspace) || a->workspace_bytes < w.total) return SWX_ERR_INVALID_ARG;
+        return from_cuda(split_forward(a, G, w, static_cast<cudaStream_t>(stream)));
+    }
     return from_cuda(swx::launch_scan_fwd(p, a->in_dtype, a->out_dtype, a->z != nullptr,
                                           static_cast<cudaStream_t>(stream)));
+}
+
+int64_t swx_scan_fwd_workspace_bytes(const swx_scan_args* a) {
+    if (check_common(a) != SWX_OK) return -1;
+    const int G = fwd_split_segments(a);
+    return G > 1 ? fwd_ws_layout(a, G).total : 0;
 }
 
 int swx_scan_bwd(const swx_scan_args* a, void* stream) {
@@ -271,7 +375,7 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     if (rows) {
         e = swx::launch_scan_bwd_rows(p, a->z != nullptr, st);
     } else {
-        const SegPlan sp = seg_plan(a->seqlen, a->dim);
+        const SegPlan sp = seg_plan(a->seqlen, a->dim, a->batch);
         p.seg_len = (int)sp.seg_len; p.nseg = (int)sp.nseg; p.sub_len = (int)sp.sub_len;
         p.nsub = (int)sp.nsub; p.first_sub = (int)sp.first_sub; p.nblk64 = (int)sp.nblk64;
         p.ws_q = reinterpret_cast<float*>(ws + w.q);
@@ -298,7 +402,8 @@ int swx_scan_correct(const swx_scan_args* a, void* stream) {
     if (a->workspace_bytes < swx_scan_correct_workspace_bytes(a->batch, a->seqlen, a->dim)) return SWX_ERR_INVALID_ARG;
     swx::ScanDev p = pack(a);
     return from_cuda(swx::launch_scan_correct(p, a->in_dtype, a->out_dtype, a->z != nullptr,
-                                              static_cast<float*>(a->workspace), static_cast<cudaStream_t>(stream)));
+                                              static_cast<float*>(a->workspace), static_cast<cudaStream_t>(stream),
+                                              false));
 }
 
 int swx_scan_bwd_ctas_per_sm(const swx_scan_args* a) {
@@ -321,7 +426,7 @@ int swx_scan_bwd_segments(const swx_scan_args* a) {
     const swx::ScanDev p = pack(a);
     bool rows = false;
     if (swx::scan_bwd_rows_applicable(p, a->in_dtype, a->z != nullptr, &rows) != cudaSuccess) return -SWX_ERR_CUDA;
-    return rows ? 0 : (int)seg_plan(a->seqlen, a->dim).nseg;
+    return rows ? 0 : (int)seg_plan(a->seqlen, a->dim, a->batch).nseg;
 }
 
 }  // extern "C"

@@ -51,6 +51,9 @@ struct ScanDev {
     const int* gof;                            // (D,) group of each channel
     int ngroups;
     float* dgw;                                // (b, L, ngroups) backward output, optional
+    // the correction of a split forward (rows = segments of seg_g consecutive segments per
+    // batch row): the first segment of each row needs none when the row starts from zero
+    int seg_g, skip_first_seg;
 };
 
 // Weight of channel d's group at step t of row bi (the row's base and the channel's group

@@ -113,7 +113,7 @@ def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
 def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
                  h0=None, out_dtype=None, checkpoints=False, return_last_state=False,
                  return_delta_sum=False, write_out=True, pre_out=None, A_is_log=False,
-                 group_w=None, group_of=None):
+                 group_w=None, group_of=None, split=True):
     """One kernel launch of the forward scan (no autograd).
 
     Returns (out, checkpoints or None, last_state or None), plus delta_sum (b, D) -- the
@@ -122,7 +122,8 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     dense fp32 (b, L, D) tensor, receives the pre-gate output when z is given (the
     backward can then skip recomputing it).  A_is_log: A holds log(-A) (see
     selective_scan_fn).  group_w, group_of: the SiftX pathway mix fused into the gate
-    (see selective_scan_fn)."""
+    (see selective_scan_fn).  split: let the library cut long sequences of a small batch
+    into segments scanned in parallel (SWX_SCAN_SPLIT_FWD; same results to fp32 rounding)."""
     lib = _lib.load()
     u, delta, A, B, C, D, z, delta_bias, h0, in_dt = _prep(u, delta, A, B, C, D, z, delta_bias, h0)
     gw, gof = _prep_groups(group_w, group_of, u, z)
@@ -147,6 +148,13 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
             raise ValueError(f"pre_out must be a dense {pdt} (b, L, D) tensor")
         a.out_pre = pre_out.data_ptr()
     _fill_groups(a, gw, gof)
+    ws = None
+    if split:
+        a.flags |= _lib.SWX_SCAN_SPLIT_FWD
+        wsb = lib.swx_scan_fwd_workspace_bytes(a)
+        if wsb > 0:
+            ws = torch.empty(wsb, device=u.device, dtype=torch.uint8)
+            a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
     _lib.check(lib.swx_scan_fwd(a, _lib.stream_ptr(u.device)), "swx_scan_fwd")
     if return_delta_sum:
         return out, ck, hl, ds

@@ -57,8 +57,9 @@ def test_sizes_of_checkpoints_and_workspace():
         return lib.swx_scan_bwd_segments(ctypes.byref(a))
     nseg = segments(8, 2048, 512)
     assert nseg == 4 and segments(16, 512, 512) == 4 and segments(8, 64, 512) == 1
-    assert segments(4, 65536, 2048) == 1 and segments(1, -1, 8) < 0
-    assert segments(1, 2048, 512) == nseg                        # a function of (L, D) alone
+    assert segments(4, 65536, 2048) == 2 and segments(1, 65536, 2048) == 9 and segments(1, -1, 8) < 0
+    assert segments(16, 2048, 512) == nseg                       # rows beyond 8 do not change the plan
+    assert segments(1, 2048, 512) == 16                          # a single row: more segments
     ws = lib.swx_scan_bwd_workspace_bytes(8, 2048, 512)
     assert ws >= 8 * 8 * 2048 * 32 * 4 + nseg * 8 * 512 * (16 + 2) * 4 + (2048 // 128) * 8 * 512 * 17 * 4
     assert lib.swx_scan_bwd_workspace_bytes(65535, 1 << 30, 1 << 30) == -1

@@ -279,17 +279,19 @@ def _run_bwd(inp, use_pre):
 
 @pytest.mark.parametrize("shape,gate,use_pre", [((5, 100, 1024, 16), True, True),
                                                 ((5, 100, 1024, 16), True, False),
-                                                ((10, 37, 520, 5), False, False)])
+                                                ((10, 37, 520, 5), False, False),
+                                                ((16, 1024, 128, 16), True, True)])
 def test_bwd_batch_split_bit_identical(shape, gate, use_pre):
     """fp32 inputs (the time-segmented backward), with and without the saved pre-gate
     output, N < 16 and a partial last channel block: its segment plan depends on (L, D)
-    only, so each row's per-row gradients are bit-identical whether the rows are passed
-    together or in two smaller batches; the batch sums agree to fp32 re-association, and
-    everything matches the oracle."""
+    and counts at most 8 rows (short sequences get one segment whatever the batch), so
+    each row's per-row gradients are bit-identical whether the rows are passed together
+    or in two smaller batches -- at 16 rows split 8 + 8, 8 segments each; the batch sums
+    agree to fp32 re-association, and everything matches the oracle."""
     b, L, D, N = shape
     inp = config_inputs(b, L, D, N, seed=41, gate=gate, device=DEV)
     rowwise = ("u", "delta", "z", "B", "C", "dout")
-    cut = 2 if b == 5 else 4
+    cut = {5: 2, 10: 4, 16: 8}[b]
     sub = lambda rows: {k: (v[rows] if k in rowwise and v is not None else v) for k, v in inp.items()}  # noqa: E731
     paths = {_bwd_path(sub(r), use_pre) for r in (slice(0, b), slice(0, cut), slice(cut, b))}
     assert len(paths) == 1 and next(iter(paths))[0] >= 1          # one segmented plan for all three
