@@ -615,6 +615,36 @@ def run_long_scan(args, world, rank, local):
     return res
 
 
+def run_small_batch(args, world, rank, local):
+    """Long rows at a small batch, fwd + bwd through the public calls: b=1, L=65536, D=2048,
+    N=16, bf16 inputs, fp32 state, gated, softplus (a long-context training step of one
+    block at batch 1).  Whole-row kernels would leave most SMs idle: the forward cuts
+    each row into segments (SWX_SCAN_SPLIT_FWD; --no-split turns it off) and the
+    backward's segment plan counts the single row.  One row per rank (weak scaling)."""
+    from swiftx_b200.selective_scan import scan_backward, scan_forward
+    from swiftx_b200.workloads import config_inputs
+    dev = torch.device("cuda", local)
+    b, L, D, N = 1, 65536, 2048, 16
+    inp = config_inputs(b, L, D, N, seed=rank, device=dev, dtype=torch.bfloat16)
+    fargs = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+    pre = torch.empty((b, L, D), device=dev, dtype=torch.float32)
+
+    def step():
+        _, ck, _ = scan_forward(*fargs, checkpoints=True, pre_out=pre, split=not args.no_split)
+        scan_backward(*fargs, None, ck, inp["dout"], y_pre=pre)
+
+    ms, clocks = timed_steps(step, args, world, local, dev)
+    fwd_b, bwd_b = alg_bytes(b, L, D, N, es=2)
+    alg = fwd_b + bwd_b
+    res = base_line(args, world, METRIC, round(alg * world / (ms * 1e-3) / 1e9, 1), "GB/s", ms, "bf16-in/f32-state",
+                    {"workload": f"selective_scan fwd+bwd at batch 1, L={L} D={D} N={N}, bf16 in",
+                     "batch": b, "seqlen": L, "d_inner": D, "d_state": N, "split_forward": not args.no_split,
+                     "parallelism": f"one row per rank x{world}" if world > 1 else "single GPU",
+                     "alg_bytes_per_step": alg, "l2": "inputs larger than L2"})
+    res["clocks"] = clocks
+    return res
+
+
 def run_correct(args, world, rank, local):
     """The sequence-parallel initial-state correction alone, on one rank's chunk of the
     long-sequence workload: b=4, L=32768 (half of 65536), D=2048, N=16, bf16 u/delta/C/z,
@@ -779,12 +809,15 @@ def main():
     ap.add_argument("--e2e-streams", type=int, default=1, help="scan e2e: compute streams of the pipeline")
     ap.add_argument("--e2e-bufs", type=int, default=2, help="scan e2e: device buffer sets of the pipeline")
     ap.add_argument("--corr-len", type=int, default=32768, help="correct: chunk length")
-    ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode", "linear_scan", "correct"],
+    ap.add_argument("--no-split", action="store_true", help="small_batch: whole-row forward")
+    ap.add_argument("--workload", choices=["scan", "lm_train", "long_scan", "decode", "linear_scan", "correct",
+                                           "small_batch"],
                     default="scan",
                     help="scan: fused scan fwd+bwd at b=8 L=2048 D=512 N=16 (default); lm_train: Sift LM training step; "
                          "long_scan: b=4 L=65536 D=2048 forward; decode: batch-256 24-layer recurrent step; "
                          "linear_scan: parallel_scan fwd+bwd at (8, 2048, 512, 16); "
-                         "correct: the sequence-parallel correction kernel on a b=4 L=32768 D=2048 chunk")
+                         "correct: the sequence-parallel correction kernel on a b=4 L=32768 D=2048 chunk; "
+                         "small_batch: fwd+bwd at b=1 L=65536 D=2048 bf16")
     args = ap.parse_args()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
@@ -803,6 +836,8 @@ def main():
         res = run_linear_scan(args, world, rank, local)
     elif args.workload == "correct":
         res = run_correct(args, world, rank, local)
+    elif args.workload == "small_batch":
+        res = run_small_batch(args, world, rank, local)
     else:
         res = run_ours(args, world, rank, local)
     if rank == 0 and res is not None:
