@@ -3,9 +3,12 @@
 //   conv_state <- roll left, append x ;  xc = silu(<conv_state, w> + conv_bias)
 //   delta = softplus(delta_raw + delta_bias) ;  h <- exp(delta*A) * h + delta * B * xc
 //   y = <h, C> + Dskip * xc ;  out = y * silu(z)
-// The state is updated in place.  In the model, x_proj / dt_proj (small GEMVs on cuBLAS)
-// sit between the conv and the state update, so the step can run as two launches
-// (SWX_DECODE_CONV, then SWX_DECODE_SSM); with delta/B/C given it is one fused launch.
+// The state is updated in place.  In the model, x_proj / dt_proj sit between the conv and
+// the state update, so the step can run as two launches (SWX_DECODE_CONV, then
+// SWX_DECODE_SSM) around the caller's GEMMs; with delta/B/C given it is one fused launch.
+// dt_proj can be folded into the state update (dt_in / dt_weight), and
+// swx_decode_layer_step folds both projections: the conv kernel writes each 64-channel
+// block's partial x_proj products, the state update sums them in block order.
 //
 // HBM-bound: per (row, channel) the state (N floats) is read and written once, the conv
 // window once, and the per-token vectors once.  Four adjacent lanes own the 16 states of
