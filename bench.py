@@ -610,8 +610,9 @@ def run_long_scan(args, world, rank, local):
         torch.cuda.synchronize()
         lat.append(max_over_ranks(e0.elapsed_time(e1), world, dev))
     res["step_latency_ms"] = round(statistics.median(lat), 4)
-    # kernel launches per step on the slowest rank: forward; correction = block sums + correct
-    res["gpu_launches"] = (1 + (2 if world > 1 else 0)) * args.steps
+    # kernel launches per step on the slowest rank: forward; correction = block sums,
+    # their prefix, correct
+    res["gpu_launches"] = (1 + (3 if world > 1 else 0)) * args.steps
     return res
 
 
@@ -682,11 +683,11 @@ def run_correct(args, world, rank, local):
                      "parallelism": f"one chunk per rank x{world}" if world > 1 else "single GPU",
                      "l2": "inputs larger than L2", "alg_bytes_per_step": alg})
     res["roofline"] = {"bound": "mufu (16 decays + softplus + silu per channel-step); hbm fraction shown",
-                       "kernel": "scan_correct_kernel (+ scan_correct_sums_kernel)",
+                       "kernel": "scan_correct_kernel (+ scan_correct_sums_kernel, scan_correct_prefix_kernel)",
                        "achieved": round(achieved, 1), "peak": peak, "peak_kind": kind, "unit": "GB/s",
                        "frac": round(achieved / peak, 4), "traffic": None, "alg_bytes_per_launch": alg}
     res["clocks"] = clocks
-    res["gpu_launches"] = 2 * args.steps
+    res["gpu_launches"] = 3 * args.steps
     return res
 
 

@@ -8,9 +8,10 @@
 // being a factor of the pre-gate output).  Unlike a
 // rescan, no step depends on the previous one except through the running sum S_t, so the
 // work is split over (channel, 256-step block) threads:
-//   1. scan_correct_sums_kernel: sum of delta_eff over each block;
-//   2. scan_correct_kernel: the block's starting S from the earlier blocks' sums (its
-//      prologue), then per step S += delta_eff and the 16 decays exp2(A log2e S) against
+//   1. scan_correct_sums_kernel: sum of delta_eff over each block, then
+//      scan_correct_prefix_kernel: each block's starting S, the earlier blocks' sums;
+//   2. scan_correct_kernel: from its block's starting S, per step S += delta_eff and the
+//      16 decays exp2(A log2e S) against
 //      C_t h_in.  The kernel is bound by instruction issue, so the decays stay on the MUFU
 //      unit (moving a share to the FMA-pipe exp2 was measured slower: 1.78 ms with none,
 //      2.07 with half, 2.70 with all at b=4, L=32768, D=2048, bf16).  Skipping the state
@@ -53,6 +54,20 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_sums_kernel(const Sca
     bsum[((int64_t)bi * nblk + k) * p.D + d] = s;
 }
 
+// In place, per (row, channel): each block's sum of delta_eff becomes the sum over the
+// blocks before it (an exclusive prefix in block order).
+__global__ void scan_correct_prefix_kernel(float* bsum, int64_t rows_d, int D, int nblk) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;       // row * D + channel
+    if (i >= rows_d) return;
+    float* bs = bsum + (i / D) * (int64_t)nblk * D + i % D;
+    float s = 0.f;
+    for (int q = 0; q < nblk; ++q) {
+        const float v = bs[(int64_t)q * D];
+        bs[(int64_t)q * D] = s;
+        s += v;
+    }
+}
+
 // FIX: the correction of a split forward -- besides the output, the 16-step state
 // checkpoints (each gains exp(A S) h_in at its step) and the pre-gate output (gains the
 // un-gated term) are corrected too, when the forward wrote them.
@@ -66,13 +81,9 @@ __global__ void __launch_bounds__(CR_THREADS) scan_correct_kernel(const ScanDev 
     const bool ok = d < p.D;
     const int dc = ok ? d : p.D - 1;
     const int t0 = k * CR_BLK, t1 = min(p.L, t0 + CR_BLK);
-    // S at the block's start: the earlier blocks' sums, in block order
-    float S = 0.f;
-    {
-        const float* bs = bsum + (int64_t)bi * nblk * p.D + dc;
-#pragma unroll 8
-        for (int q = 0; q < k; ++q) S += bs[(int64_t)q * p.D];
-    }
+    // S at the block's start: the earlier blocks' sums, added in block order by
+    // scan_correct_prefix_kernel
+    float S = bsum[((int64_t)bi * nblk + k) * p.D + dc];
     float2 A2[NS / 2], H[NS / 2];
     const float* h_in = p.h0 + ((int64_t)bi * p.D + dc) * p.N;
 #pragma unroll
@@ -172,6 +183,9 @@ static cudaError_t launch_correct_t(const ScanDev& p, float* ws, bool has_z, boo
     scan_correct_sums_kernel<Tin><<<grid, CR_THREADS, 0, st>>>(p, ws, nblk);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return e;
+    const int64_t rows_d = (int64_t)p.b * p.D;
+    scan_correct_prefix_kernel<<<(unsigned)((rows_d + 255) / 256), 256, 0, st>>>(ws, rows_d, p.D, nblk);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
     if (fix) launch_correct_k<Tin, Tout, true>(p, ws, nblk, has_z, grid, st);
     else launch_correct_k<Tin, Tout, false>(p, ws, nblk, has_z, grid, st);
     return cudaGetLastError();
