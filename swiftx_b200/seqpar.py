@@ -34,13 +34,13 @@ def _kernel_correct(out, h_in, u, delta, A, B, C, z, delta_bias, delta_softplus)
                         delta_softplus=delta_softplus)
 
 
-def chunk_bounds(L, world, correction_cost=0.66, correction_offset=2585, multiple=256):
+def chunk_bounds(L, world, correction_cost=0.73, correction_offset=950, multiple=256):
     """Chunk boundaries [0, e_0, ..., L] that balance the ranks' work: rank 0 runs only the
     forward of its chunk, every later rank the forward and the correction.  In units of
     one forward step, a chunk of n steps costs n to scan and correction_offset +
     correction_cost * n to correct.  The defaults are fitted to one B200 at b=4, D=2048,
-    N=16, bf16 in / fp32 out: the forward at 73.5 ns a step, the correction 1.79 ms at
-    32768 steps and 0.59 ms at 8192.  With rank 0's length x and the others' y:
+    N=16, bf16 in / fp32 out: the forward at 73.5 ns a step, the correction 1.83 ms at
+    32768 steps and 0.51 ms at 8192.  With rank 0's length x and the others' y:
     x = (1 + cost) y + offset and x + (world - 1) y = L.  Lengths are rounded to
     `multiple` steps; the last rank takes the remainder."""
     if world <= 1:

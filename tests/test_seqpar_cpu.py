@@ -102,7 +102,7 @@ def test_combine_prefix_is_the_chained_recurrence():
 
 @pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
 def test_chunk_bounds_balance(world):
-    L, c, c0 = 65536, 0.66, 2585
+    L, c, c0 = 65536, 0.73, 950
     b = chunk_bounds(L, world, correction_cost=c, correction_offset=c0)
     assert b[0] == 0 and b[-1] == L and len(b) == world + 1
     lens = [b[r + 1] - b[r] for r in range(world)]
@@ -115,4 +115,4 @@ def test_chunk_bounds_balance(world):
 
 def test_chunk_bounds_short_sequence():
     """A sequence too short for the correction's fixed cost: rank 0 takes it whole."""
-    assert chunk_bounds(2048, 4) == [0, 2048, 2048, 2048, 2048]
+    assert chunk_bounds(512, 4) == [0, 512, 512, 512, 512]
