@@ -2,7 +2,8 @@
 in row chunks over several streams.
 
 Rows of the scan are independent, so every per-row result (out, du, ddelta, dz, dB, dC)
-must equal, bit for bit, the whole-batch kernel call on device tensors.  dA, dD and
+must equal, bit for bit, the whole-batch kernel call on device tensors (the sequences
+here are short enough that every chunk gets the whole batch's backward segment plan).  dA, dD and
 d(delta_bias) are sums over the batch that the pipeline adds per chunk and then across
 chunks; they match the whole-batch sums to fp32 re-association (rtol 1e-5, atol 1e-6 of
 the largest entry).  One case is also checked against the float64 oracle.
