@@ -106,3 +106,23 @@ def test_split_forward_bf16_and_pathway_mix():
     res = [scan_forward(*args, out_dtype=torch.float32, group_w=w, group_of=gof, split=s)[0] for s in (True, False)]
     want = n64(res[1])
     np.testing.assert_allclose(n64(res[0]), want, rtol=2e-2, atol=2e-2 * np.abs(want).max())
+
+
+def test_split_forward_partial_block_small_state_a_log():
+    """N < 16, a partial 32-channel block and A given as log(-A): split against whole rows
+    and the oracle, final state included."""
+    b, L, D, N = 1, 8192, 200, 12
+    inp = config_inputs(b, L, D, N, seed=54, device=DEV)
+    assert _split_bytes(inp) > 0
+    A_log = torch.log(-inp["A"])
+    h0 = (torch.randn(b, D, N, generator=torch.Generator().manual_seed(5)) * 0.3).to(DEV)
+    args = (inp["u"], inp["delta"], A_log, inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+    res = [scan_forward(*args, h0=h0, return_last_state=True, A_is_log=True, split=s) for s in (True, False)]
+    for g, w, name in zip(res[0], res[1], ("out", "checkpoints", "h_last")):
+        if g is not None:
+            np.testing.assert_allclose(n64(g), n64(w), rtol=1e-4, atol=1e-5, err_msg=name)
+    want, hl = oracle.scan_fwd(*(n64(inp[k]) for k in ("u", "delta", "A", "B", "C")), D=n64(inp["D"]),
+                               z=n64(inp["z"]), delta_bias=n64(inp["delta_bias"]), delta_softplus=True,
+                               h0=n64(h0), return_last_state=True)
+    np.testing.assert_allclose(n64(res[0][0]), want, rtol=1e-4, atol=1e-5)
+    np.testing.assert_allclose(n64(res[0][2]), hl, rtol=1e-4, atol=1e-5)
