@@ -14,7 +14,8 @@
 //      16 decays exp2(A log2e S) against
 //      C_t h_in.  The kernel is bound by instruction issue, so the decays stay on the MUFU
 //      unit (moving a share to the FMA-pipe exp2 was measured slower: 1.78 ms with none,
-//      2.07 with half, 2.70 with all at b=4, L=32768, D=2048, bf16).  Skipping the state
+//      2.07 with half, 2.70 with all at b=4, L=32768, D=2048, bf16; with 2, 4 or 6 of the
+//      16 decays 1.78, 1.83 and 1.93 against 1.80 ms in a later run).  Skipping the state
 //      groups whose decays have underflowed in every lane (S only grows under softplus)
 //      was measured too: with one warp-uniform dispatch per 8 steps over copies of the
 //      step body for 4..0 live groups, 1.75 against 1.79 ms at L=32768 but 0.71 against
