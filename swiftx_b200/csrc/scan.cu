@@ -9,8 +9,10 @@
 //     8 channels).  Per step: a = 2^(delta_eff * A*log2e) on the MUFU unit, then
 //     h = a*h + delta_eff*u*B with packed f32x2 FMAs.  They read only pre-computed
 //     per-(t, channel) scalars and the channel-shared B_t / C_t from shared memory.
-//   * 4 or 8 helper warps: stage raw tiles of u, delta, z, B, C with 16-byte cp.async
-//     into a 4-slot ring (three tiles ahead), compute the per-(t, channel) scalars once
+//   * 4 or 8 helper warps: stage raw tiles of u, delta, z, B, C into a 4-slot ring (three
+//     tiles ahead) -- one thread issues a TMA tile copy per tensor (cp.async.bulk.tensor,
+//     completion on the slot's mbarrier; per-thread 16-byte cp.async when a tensor's base
+//     or strides are not 16-byte aligned) --, compute the per-(t, channel) scalars once
 //     per channel (softplus(delta + bias), delta*u), and run the epilogue (readout sum,
 //     D skip, SiLU(z) gate, coalesced stores).
 //
@@ -24,6 +26,7 @@
 #include "common.cuh"
 #include "scan_params.cuh"
 #include "launch_util.cuh"
+#include "tma_util.cuh"
 
 namespace swx {
 
@@ -36,6 +39,15 @@ constexpr int FT = 32;                // forward tile (steps)
 constexpr int RING = 4;               // raw staging slots
 
 enum : int { BAR_AUX = 1, BAR_D0 = 2, BAR_X0 = 4 };
+constexpr uint32_t FWD_WAIT_POLLS = 1u << 24;   // mbarrier polls before a tile wait gives up
+
+// TMA descriptors of the forward's inputs: (channel, step, row) tiles of 32 x 32 x 1 for u,
+// delta, z and 16 x 32 x 1 for B and C.  ok = 0: some tensor is not 16-byte aligned; the
+// helpers stage with per-thread cp.async.
+struct FwdMaps {
+    CUtensorMap u, dl, z, B, C;
+    int ok;
+};
 
 // Four consecutive staged elements as fp32 (one 16-byte load for fp32, 8-byte for bf16).
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
@@ -63,6 +75,8 @@ struct FwdSmem {
     float2 dd[2][FT][SCH];        // (delta_eff, delta_eff * u)
     float yp[2][FT][SCH][4];      // partial readouts of the 4 state groups
     float red[FNAUX_MAX];          // per-thread sums of delta_eff
+    uint64_t mbar[RING];           // completion of each ring slot's TMA copies
+    int stop;                      // a tile wait gave up: no further copies, no further waits
 };
 
 template <bool FULL, bool WR, typename Tin>
@@ -124,9 +138,10 @@ __device__ __forceinline__ void fwd_tile(const float2 (*__restrict__ dd)[SCH], c
 // per SM at the cost of a few spilled bytes.
 // GW: the SiftX pathway mix is applied before the gate (only with HAS_Z and WR).
 template <typename Tin, typename Tout, bool HAS_Z, bool WR, int NA, bool GW = false>
-__global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel(const ScanDev p) {
+__global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1)
+    scan_fwd_kernel(const ScanDev p, const __grid_constant__ FwdMaps tm) {
     constexpr int FNAUX = NA, FNTH = NSCAN + NA;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+    extern __shared__ __align__(128) unsigned char smem_raw[];   // TMA destinations: 128-byte aligned
     FwdSmem<Tin>& S = *reinterpret_cast<FwdSmem<Tin>*>(smem_raw);
 
     const int tid = threadIdx.x;
@@ -134,6 +149,16 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
     const int d0 = blockIdx.x * SCH;
     const int nd = min(SCH, p.D - d0);
     const int nchunk = (p.L + FT - 1) / FT;
+    const bool fast = tm.ok != 0;
+    if (fast) {
+        if (tid == 0) {
+#pragma unroll
+            for (int r = 0; r < RING; ++r) mbar_init(&S.mbar[r], 1);
+            mbar_fence_init();
+            S.stop = 0;
+        }
+        __syncthreads();
+    }
 
     if (tid < NSCAN) {
         // ------------------------------------------------ recurrence warps
@@ -158,6 +183,10 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
                              ? p.ck + (((int64_t)bi * p.nck + t0 / TCK) * p.D + d) * NS + 4 * j
                              : nullptr;
             const int r = c % RING;
+            // the helpers waited for this tile before deriving it; the wait here orders the
+            // bulk copies' writes of B / C before this thread's reads (it returns at once)
+            if (fast && !*reinterpret_cast<volatile int*>(&S.stop))
+                mbar_wait_bounded(&S.mbar[r], (c / RING) & 1, FWD_WAIT_POLLS);
             if (nt == FT)
                 fwd_tile<true, WR>(S.dd[s], S.B[r], S.C[r], S.yp[s], nt, ch, j, A01, A23, h01, h23, ckp, ck_stride);
             else
@@ -187,7 +216,28 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
         const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
         Tout* gout = static_cast<Tout*>(p.out) + (int64_t)bi * p.L * p.D + d0;
 
+        // staging.  TMA: helper thread 0 issues one tile copy per tensor for tile c into
+        // ring slot c % RING, all completing on the slot's mbarrier; after a wait that gave
+        // up it issues nothing more (the copies still in flight are waited for at the end)
+        int issued = 0;
+        volatile int* stop = &S.stop;
+        constexpr uint32_t TILE = FT * SCH * sizeof(Tin), TILE_BC = FT * NS * sizeof(Tin);
         auto issue = [&](int c) {
+            if (fast) {
+                if (c < nchunk && at == 0 && !*stop) {
+                    const int t0 = c * FT, r = c % RING;
+                    fence_proxy_async_smem();            // the slot's last readers are past a barrier
+                    const uint32_t bytes = (HAS_Z && WR ? 3 : 2) * TILE + (WR ? 2 : 1) * TILE_BC;
+                    mbar_arrive_expect_tx(&S.mbar[r], bytes);
+                    tma_load_3d(&S.u[r][0][0], &tm.u, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.dl[r][0][0], &tm.dl, d0, t0, bi, &S.mbar[r]);
+                    if (HAS_Z && WR) tma_load_3d(&S.z[r][0][0], &tm.z, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.B[r][0][0], &tm.B, 0, t0, bi, &S.mbar[r]);
+                    if (WR) tma_load_3d(&S.C[r][0][0], &tm.C, 0, t0, bi, &S.mbar[r]);
+                    issued = c + 1;
+                }
+                return;
+            }
             if (c < nchunk) {
                 const int t0 = c * FT, rv = min(FT, p.L - t0), r = c % RING;
                 stage_tile<Tin, SCH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, FT, rv, nd, p.vec_u, at, FNAUX);
@@ -199,6 +249,17 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
                     stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, FT, rv, p.N, p.vec_C, at, FNAUX);
             }
             cp_async_commit();
+        };
+        // Wait for tile k's copies.  A wait that gives up is recorded in the status word and
+        // stops further copies and waits; the kernel then runs to its end on what is in
+        // shared memory (its results are incomplete, the barrier protocol and the context
+        // stay intact).
+        auto tile_wait = [&](int k) {
+            if (*stop) return;
+            if (!mbar_wait_bounded(&S.mbar[k % RING], (k / RING) & 1, FWD_WAIT_POLLS)) {
+                *stop = 1;
+                if (p.err) *p.err = SWX_ERR_TIMEOUT;
+            }
         };
         // per-(t, channel) work: each thread takes pairs of steps (t, t+1) of channel `ech`
         const float2 bias2 = bc2(ebias), D2 = bc2(eD);
@@ -251,7 +312,8 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
         issue(0);
         issue(1);
         issue(2);
-        cp_async_wait<2>();
+        if (fast) tile_wait(0);
+        else cp_async_wait<2>();
         bar_sync(BAR_AUX, FNAUX);
         derive(0);
         bar_arrive(BAR_D0, FNTH);
@@ -261,7 +323,8 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
                 epilogue(c - 1);
             }
             if (c + 1 < nchunk) {
-                cp_async_wait<1>();
+                if (fast) tile_wait(c + 1);
+                else cp_async_wait<1>();
                 bar_sync(BAR_AUX, FNAUX);
                 derive(c + 1);
                 bar_arrive(BAR_D0 + ((c + 1) & 1), FNTH);
@@ -271,7 +334,14 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
         }
         bar_sync(BAR_X0 + ((nchunk - 1) & 1), FNTH);
         epilogue(nchunk - 1);
-        cp_async_wait<0>();
+        if (!fast) {
+            cp_async_wait<0>();
+        } else if (at == 0 && *stop) {
+            // copies that may still be landing in this CTA's shared memory: the last tile
+            // issued into each slot, each given a second bounded wait before the CTA exits
+            for (int k = max(0, issued - RING); k < issued; ++k)
+                mbar_wait_bounded(&S.mbar[k % RING], (k / RING) & 1, FWD_WAIT_POLLS);
+        }
         if (p.dsum) {                      // sum over the 4 thread groups of a channel
             S.red[at] = dsum;
             bar_sync(BAR_AUX, FNAUX);
@@ -291,8 +361,24 @@ __global__ void __launch_bounds__(NSCAN + NA, NA == 128 ? 2 : 1) scan_fwd_kernel
 // has more CTAs than SMs and the 128-helper CTA fits twice on an SM (bf16 inputs: 95
 // registers, 81 KB of shared memory), two co-resident CTAs -- two recurrence warps per
 // sub-partition, one wave instead of two -- are faster.
+template <typename Tin, bool HAS_Z>
+static FwdMaps fwd_maps(const ScanDev& p) {
+    FwdMaps m{};
+    const int es = sizeof(Tin);
+    bool ok = encode_3d(&m.u, p.u, es, p.D, p.L, p.b, p.u_sl, p.u_sb, SCH, FT) &&
+              encode_3d(&m.dl, p.dl, es, p.D, p.L, p.b, p.dl_sl, p.dl_sb, SCH, FT) &&
+              encode_3d(&m.B, p.B, es, p.N, p.L, p.b, p.B_sl, p.B_sb, NS, FT);
+    if (ok && p.out) ok = encode_3d(&m.C, p.C, es, p.N, p.L, p.b, p.C_sl, p.C_sb, NS, FT);
+    if (ok && HAS_Z && p.out) ok = encode_3d(&m.z, p.z, es, p.D, p.L, p.b, p.z_sl, p.z_sb, SCH, FT);
+    m.ok = ok ? 1 : 0;
+    return m;
+}
+
 template <typename Tin, typename Tout, bool HAS_Z>
-static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
+static cudaError_t launch_fwd_t(const ScanDev& p0, cudaStream_t st) {
+    ScanDev p = p0;
+    p.err = wait_status_address();               // where a timed-out tile wait is recorded
+    const FwdMaps maps = fwd_maps<Tin, HAS_Z>(p);
     auto k2 = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true, 256> : scan_fwd_kernel<Tin, Tout, HAS_Z, false, 256>;
     auto k1 = p.out ? scan_fwd_kernel<Tin, Tout, HAS_Z, true, 128> : scan_fwd_kernel<Tin, Tout, HAS_Z, false, 128>;
     if constexpr (HAS_Z) {
@@ -310,11 +396,11 @@ static cudaError_t launch_fwd_t(const ScanDev& p, cudaStream_t st) {
     e = sm_fit(k1, NSCAN + 128, smem, &sms, &per_sm);
     if (e != cudaSuccess) return e;
     if (nblocks > sms && per_sm >= 2) {
-        k1<<<grid, NSCAN + 128, smem, st>>>(p);
+        k1<<<grid, NSCAN + 128, smem, st>>>(p, maps);
     } else {
         e = allow_smem(k2, smem);
         if (e != cudaSuccess) return e;
-        k2<<<grid, NSCAN + 256, smem, st>>>(p);
+        k2<<<grid, NSCAN + 256, smem, st>>>(p, maps);
     }
     return cudaGetLastError();
 }

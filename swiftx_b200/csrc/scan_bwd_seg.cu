@@ -36,6 +36,7 @@
 #include "common.cuh"
 #include "launch_util.cuh"
 #include "scan_params.cuh"
+#include "tma_util.cuh"
 
 namespace swx {
 
@@ -706,51 +707,17 @@ __global__ void scan_bwd_seg_finalize_kernel(const ScanDev p) {
 }
 
 // ===================================================================== launchers
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-// cuTensorMapEncodeTiled, resolved through the runtime (no link to the driver library).
-static EncodeTiledFn encode_tiled() {
-    static EncodeTiledFn fn = [] {
-        void* f = nullptr;
-        cudaDriverEntryPointQueryResult q{};
-        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) !=
-                cudaSuccess || q != cudaDriverEntryPointSuccess)
-            return static_cast<EncodeTiledFn>(nullptr);
-        return reinterpret_cast<EncodeTiledFn>(f);
-    }();
-    return fn;
-}
-
-// A (inner, L, b) tensor with element strides (1, row, batch) and a box of (box_inner, 16, 1).
-static bool encode_3d(CUtensorMap* m, const void* base, int es, int64_t inner, int64_t L, int64_t b, int64_t row,
-                      int64_t batch, uint32_t box_inner) {
-    const EncodeTiledFn f = encode_tiled();
-    if (!f || !base || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
-    const int64_t rs = row * es, bs = (b > 1 ? batch : row * L) * es;
-    if (rs % 16 || bs % 16 || rs <= 0 || bs <= 0 || rs >= (int64_t(1) << 40) || bs >= (int64_t(1) << 40)) return false;
-    cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)L, (cuuint64_t)b};
-    cuuint64_t strides[2] = {(cuuint64_t)rs, (cuuint64_t)bs};
-    cuuint32_t box[3] = {box_inner, (cuuint32_t)TCK, 1};
-    cuuint32_t unit[3] = {1, 1, 1};
-    return f(m, es == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
-             const_cast<void*>(base), dims, strides, box, unit, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-           CUDA_SUCCESS;
-}
-
 template <typename Tin, bool HAS_Z>
 static SegMaps seg_maps(const ScanDev& p) {
     SegMaps m{};
     const int es = sizeof(Tin);
-    bool ok = encode_3d(&m.u, p.u, es, p.D, p.L, p.b, p.u_sl, p.u_sb, SG_CH) &&
-              encode_3d(&m.dl, p.dl, es, p.D, p.L, p.b, p.dl_sl, p.dl_sb, SG_CH) &&
-              encode_3d(&m.dout, p.dout, es, p.D, p.L, p.b, p.dout_sl, p.dout_sb, SG_CH) &&
-              encode_3d(&m.B, p.B, es, p.N, p.L, p.b, p.B_sl, p.B_sb, NS) &&
-              encode_3d(&m.C, p.C, es, p.N, p.L, p.b, p.C_sl, p.C_sb, NS);
-    if (ok && HAS_Z) ok = encode_3d(&m.z, p.z, es, p.D, p.L, p.b, p.z_sl, p.z_sb, SG_CH);
-    if (ok && HAS_Z && p.ypre) ok = encode_3d(&m.yp, p.ypre, 4, p.D, p.L, p.b, p.D, (int64_t)p.L * p.D, SG_CH);
+    bool ok = encode_3d(&m.u, p.u, es, p.D, p.L, p.b, p.u_sl, p.u_sb, SG_CH, TCK) &&
+              encode_3d(&m.dl, p.dl, es, p.D, p.L, p.b, p.dl_sl, p.dl_sb, SG_CH, TCK) &&
+              encode_3d(&m.dout, p.dout, es, p.D, p.L, p.b, p.dout_sl, p.dout_sb, SG_CH, TCK) &&
+              encode_3d(&m.B, p.B, es, p.N, p.L, p.b, p.B_sl, p.B_sb, NS, TCK) &&
+              encode_3d(&m.C, p.C, es, p.N, p.L, p.b, p.C_sl, p.C_sb, NS, TCK);
+    if (ok && HAS_Z) ok = encode_3d(&m.z, p.z, es, p.D, p.L, p.b, p.z_sl, p.z_sb, SG_CH, TCK);
+    if (ok && HAS_Z && p.ypre) ok = encode_3d(&m.yp, p.ypre, 4, p.D, p.L, p.b, p.D, (int64_t)p.L * p.D, SG_CH, TCK);
     m.ok = ok ? 1 : 0;
     return m;
 }
