@@ -10,12 +10,15 @@
 // channels x 512 steps, ~130 us against ~167 us); the segmented kernel covers everything
 // else.  Per 16-step chunk the recurrence warps reload the checkpoint, recompute the
 // states into registers and run g_t = a_{t+1} g_{t+1} + dy_t C_t (models/selective_scan.py
-// :146-148); every reduction is a fixed-order sum (no float atomics).
+// :146-148); every reduction is a fixed-order sum (no float atomics).  Tiles arrive by TMA
+// (one helper thread, completion on the ring slot's mbarrier, bounded waits), or by
+// per-thread cp.async when a tensor is not 16-byte aligned.
 #include <algorithm>
 
 #include "common.cuh"
 #include "launch_util.cuh"
 #include "scan_params.cuh"
+#include "tma_util.cuh"
 
 namespace swx {
 namespace rowk {
@@ -28,6 +31,14 @@ constexpr int HT = TCK / 2;
 constexpr int RING = 4;               // raw staging slots
 
 enum : int { BAR_AUX = 1, BAR_D0 = 2, BAR_X0 = 4, BAR_E0 = 6 };
+constexpr uint32_t ROW_WAIT_POLLS = 1u << 24;   // mbarrier polls before a tile wait gives up
+
+// TMA descriptors: (channel, step, row) tiles of 32 x 16 x 1 for u, delta, z, dout and the
+// saved pre-gate output, 16 x 16 x 1 for B and C.  ok = 0: per-thread cp.async staging.
+struct RowMaps {
+    CUtensorMap u, dl, z, dout, yp, B, C;
+    int ok;
+};
 
 __device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
 __device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
@@ -59,6 +70,8 @@ struct BwdSmem {
     float2 nsd[2][HTQ][SCH][4];        // per state group: (sum g*B, sum g*a*h_prev*A)
     float nyp[2][HTQ][SCH][4];         // per state group: sum h*C (gate without YPRE)
     float red[2][NAUX];
+    uint64_t mbar[RING];               // completion of each ring slot's TMA copies
+    int stop;                          // a tile wait gave up: no further copies, no further waits
 };
 
 // Recompute the 16 states of a chunk from its checkpoint (and, without a saved pre-gate
@@ -181,12 +194,12 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
 // per-step results are handed to the helper warps in 4-step tiles instead of 8.
 // GW (with HAS_Z): the forward applied the SiftX pathway mix before the gate.
 template <typename Tin, bool HAS_Z, bool YPRE, bool LOWREG, bool GW = false>
-__global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const ScanDev p) {
+__global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const ScanDev p, const __grid_constant__ RowMaps tm) {
     constexpr bool YV = HAS_Z && !YPRE;
     constexpr int HTQ = LOWREG ? 4 : HT;       // steps per hand-off tile
     constexpr int NQ = TCK / HTQ;              // hand-off tiles per chunk
     constexpr bool AREG = !LOWREG;             // decays kept in registers (see bwd_half)
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+    extern __shared__ __align__(128) unsigned char smem_raw[];   // TMA destinations: 128-byte aligned
     BwdSmem<Tin, HTQ>& S = *reinterpret_cast<BwdSmem<Tin, HTQ>*>(smem_raw);
 
     const int tid = threadIdx.x;
@@ -194,6 +207,16 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
     const int d0 = blockIdx.x * SCH;
     const int nd = min(SCH, p.D - d0);
     const int nck = p.nck;
+    const bool fast = tm.ok != 0;
+    if (fast) {
+        if (tid == 0) {
+#pragma unroll
+            for (int r = 0; r < RING; ++r) mbar_init(&S.mbar[r], 1);
+            mbar_fence_init();
+            S.stop = 0;
+        }
+        __syncthreads();
+    }
 
     if (tid < NSCAN) {
         // ------------------------------------------------ recurrence warps
@@ -213,6 +236,10 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         for (int k = 0; k < nck; ++k) {
             const int c = nck - 1 - k, s = k & 1, r = k % RING, t0 = c * TCK, nt = min(TCK, p.L - t0);
             bar_sync(BAR_D0 + s, NTH);
+            // the helpers waited for this chunk before deriving it; the wait here orders the
+            // bulk copies' writes of B / C before this thread's reads (it returns at once)
+            if (fast && !*reinterpret_cast<volatile int*>(&S.stop))
+                mbar_wait_bounded(&S.mbar[r], (k / RING) & 1, ROW_WAIT_POLLS);
             float2 hck01 = f2(0.f, 0.f), hck23 = hck01;
             if (dvalid) {
                 const float4 v = *reinterpret_cast<const float4*>(
@@ -278,7 +305,30 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         const float* gyp = YPRE ? p.ypre + (int64_t)bi * p.L * p.D + d0 : nullptr;
         float accD = 0.f, accB = 0.f;
 
+        // staging.  TMA: helper thread 0 issues one tile copy per tensor for chunk k into ring
+        // slot k % RING, all completing on the slot's mbarrier; after a wait that gave up it
+        // issues nothing more (copies still in flight are waited for at the end)
+        int issued = 0;
+        volatile int* stop = &S.stop;
+        constexpr uint32_t TILE = TCK * SCH * sizeof(Tin), TILE_Y = TCK * SCH * 4, TILE_BC = TCK * NS * sizeof(Tin);
         auto issue = [&](int k) {
+            if (fast) {
+                if (k < nck && at == 0 && !*stop) {
+                    const int t0 = (nck - 1 - k) * TCK, r = k % RING;
+                    fence_proxy_async_smem();            // the slot's last readers are past a barrier
+                    const uint32_t bytes = (HAS_Z ? 4 : 3) * TILE + (YPRE ? TILE_Y : 0) + 2 * TILE_BC;
+                    mbar_arrive_expect_tx(&S.mbar[r], bytes);
+                    tma_load_3d(&S.u[r][0][0], &tm.u, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.dl[r][0][0], &tm.dl, d0, t0, bi, &S.mbar[r]);
+                    if (HAS_Z) tma_load_3d(&S.z[r][0][0], &tm.z, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.dout[r][0][0], &tm.dout, d0, t0, bi, &S.mbar[r]);
+                    if (YPRE) tma_load_3d(&S.yp[r][0][0], &tm.yp, d0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.B[r][0][0], &tm.B, 0, t0, bi, &S.mbar[r]);
+                    tma_load_3d(&S.C[r][0][0], &tm.C, 0, t0, bi, &S.mbar[r]);
+                    issued = k + 1;
+                }
+                return;
+            }
             if (k < nck) {
                 const int c = nck - 1 - k, t0 = c * TCK, rv = min(TCK, p.L - t0), r = k % RING;
                 stage_tile<Tin, SCH>(&S.u[r][0][0], gu + t0 * p.u_sl, p.u_sl, TCK, rv, nd, p.vec_u, at, NAUX);
@@ -292,6 +342,16 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
                 stage_tile<Tin, NS>(&S.C[r][0][0], gC + t0 * p.C_sl, p.C_sl, TCK, rv, p.N, p.vec_C, at, NAUX);
             }
             cp_async_commit();
+        };
+        // Wait for chunk k's copies; a wait that gives up is recorded in the status word and
+        // stops further copies and waits (the kernel runs to its end on what is in shared
+        // memory: incomplete results, intact barrier protocol and context).
+        auto tile_wait = [&](int k) {
+            if (*stop) return;
+            if (!mbar_wait_bounded(&S.mbar[k % RING], (k / RING) & 1, ROW_WAIT_POLLS)) {
+                *stop = 1;
+                if (p.err) *p.err = SWX_ERR_TIMEOUT;
+            }
         };
         const float2 bias2 = bc2(ebias);
         auto derive = [&](int k) {
@@ -407,7 +467,8 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         issue(0);
         issue(1);
         issue(2);
-        cp_async_wait<2>();
+        if (fast) tile_wait(0);
+        else cp_async_wait<2>();
         bar_sync(BAR_AUX, NAUX);
         derive(0);
         bar_arrive(BAR_D0, NTH);
@@ -415,7 +476,8 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         bar_arrive(BAR_E0 + 1, NTH);
         for (int k = 0; k < nck; ++k) {
             if (k + 1 < nck) {
-                cp_async_wait<1>();
+                if (fast) tile_wait(k + 1);
+                else cp_async_wait<1>();
                 bar_sync(BAR_AUX, NAUX);
                 derive(k + 1);
                 bar_arrive(BAR_D0 + ((k + 1) & 1), NTH);
@@ -430,7 +492,14 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
             bar_sync(BAR_AUX, NAUX);      // raw slot (k-1) % RING no longer read
             issue(k + 3);
         }
-        cp_async_wait<0>();
+        if (!fast) {
+            cp_async_wait<0>();
+        } else if (at == 0 && *stop) {
+            // copies that may still be landing in this CTA's shared memory: the last chunk
+            // issued into each slot, each given a second bounded wait before the CTA exits
+            for (int k = max(0, issued - RING); k < issued; ++k)
+                mbar_wait_bounded(&S.mbar[k % RING], (k / RING) & 1, ROW_WAIT_POLLS);
+        }
         S.red[0][at] = accD;
         S.red[1][at] = accB;
         bar_sync(BAR_AUX, NAUX);
@@ -497,7 +566,24 @@ static cudaError_t fits_t(const ScanDev& p, int* per_sm, int* sms) {
 }
 
 template <typename Tin, bool HAS_Z>
-static cudaError_t launch_t(const ScanDev& p, cudaStream_t st) {
+static RowMaps row_maps(const ScanDev& p) {
+    RowMaps m{};
+    const int es = sizeof(Tin);
+    bool ok = encode_3d(&m.u, p.u, es, p.D, p.L, p.b, p.u_sl, p.u_sb, SCH, TCK) &&
+              encode_3d(&m.dl, p.dl, es, p.D, p.L, p.b, p.dl_sl, p.dl_sb, SCH, TCK) &&
+              encode_3d(&m.dout, p.dout, es, p.D, p.L, p.b, p.dout_sl, p.dout_sb, SCH, TCK) &&
+              encode_3d(&m.B, p.B, es, p.N, p.L, p.b, p.B_sl, p.B_sb, NS, TCK) &&
+              encode_3d(&m.C, p.C, es, p.N, p.L, p.b, p.C_sl, p.C_sb, NS, TCK);
+    if (ok && HAS_Z) ok = encode_3d(&m.z, p.z, es, p.D, p.L, p.b, p.z_sl, p.z_sb, SCH, TCK);
+    if (ok && HAS_Z && p.ypre) ok = encode_3d(&m.yp, p.ypre, 4, p.D, p.L, p.b, p.D, (int64_t)p.L * p.D, SCH, TCK);
+    m.ok = ok ? 1 : 0;
+    return m;
+}
+
+template <typename Tin, bool HAS_Z>
+static cudaError_t launch_t(const ScanDev& p0, cudaStream_t st) {
+    ScanDev p = p0;
+    p.err = wait_status_address();               // where a timed-out tile wait is recorded
     const bool ypre = HAS_Z && p.ypre;
     auto k = ypre ? scan_bwd_kernel<Tin, HAS_Z, true, true> : scan_bwd_kernel<Tin, HAS_Z, false, true>;
     if constexpr (HAS_Z) {
@@ -507,7 +593,7 @@ static cudaError_t launch_t(const ScanDev& p, cudaStream_t st) {
     cudaError_t e = allow_smem(k, smem);
     if (e != cudaSuccess) return e;
     dim3 grid((p.D + SCH - 1) / SCH, p.b);
-    k<<<grid, NTH, smem, st>>>(p);
+    k<<<grid, NTH, smem, st>>>(p, row_maps<Tin, HAS_Z>(p));
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     const int64_t total = 2LL * NS * p.b * p.L + (int64_t)p.D * p.N + p.D;
     const int blocks = (int)std::min<int64_t>((total + 255) / 256, 148 * 8);
