@@ -80,7 +80,8 @@ __device__ __forceinline__ void store2(__nv_bfloat16* q, float2 v) {
 // Thread = one channel of one row, all 16 states; walks its sub-segment backwards from a
 // zero carry.  The sub-segment's C rows (the same for every thread of the CTA) are staged
 // in shared memory once; the CTA's delta / dout / z rows arrive in 16-step blocks through
-// a two-slot cp.async pipeline, one block ahead of the arithmetic.  The decays of the
+// a two-slot pipeline, one block ahead of the arithmetic: TMA tile copies issued by one
+// thread (per-thread cp.async when a tensor is not 16-byte aligned).  The decays of the
 // first SUM_FMA_PAIRS state pairs are computed on the FMA pipe (ex2x2_fma), the others on
 // the MUFU unit, which this kernel otherwise saturates.
 constexpr int SUM_MAXLEN = 128;           // longest sub-segment (sub_len <= 128)
@@ -93,15 +94,33 @@ struct SumSmem {
     Tin dl[2][SUM_BLK][SUM_THREADS];
     Tin dout[2][SUM_BLK][SUM_THREADS];
     Tin z[2][SUM_BLK][SUM_THREADS];
+    uint64_t mbar[2];                     // completion of each slot's TMA copies
+};
+
+// TMA descriptors of the summary kernel: (channel, step, row) tiles of 128 x 16 x 1 for
+// delta, dout and z.  ok = 0: per-thread cp.async staging.
+struct SumMaps {
+    CUtensorMap dl, dout, z;
+    int ok;
 };
 
 // GW (with HAS_Z): the forward applied the SiftX pathway mix before the gate, so the
 // gate's input gradient carries the channel's group weight.
 template <typename Tin, bool HAS_Z, bool GW = false>
-__global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const ScanDev p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
+__global__ void __launch_bounds__(SUM_THREADS)
+    scan_bwd_summary_kernel(const ScanDev p, const __grid_constant__ SumMaps tm) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];   // TMA destinations: 128-byte aligned
     SumSmem<Tin>& S = *reinterpret_cast<SumSmem<Tin>*>(smem_raw);
     const int tid = threadIdx.x;
+    const bool fast = tm.ok != 0;
+    if (fast) {
+        if (tid == 0) {
+            mbar_init(&S.mbar[0], 1);
+            mbar_init(&S.mbar[1], 1);
+            mbar_fence_init();
+        }
+        __syncthreads();
+    }
     const int nxb = (p.D + SUM_THREADS - 1) / SUM_THREADS;
     const int64_t blk = blockIdx.x;                      // (sub-segment, row, channel block)
     const int d0 = (int)(blk % nxb) * SUM_THREADS;
@@ -119,7 +138,22 @@ __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const Sca
     const Tin* gC = static_cast<const Tin*>(p.C) + bi * p.C_sb;
 
     // block k of the walk covers steps [hi - SUM_BLK, hi), hi = t1 - k * SUM_BLK, clipped at t0
+    // (the TMA tile always starts at hi - SUM_BLK >= 0: the rows before t0 are loaded, not used)
+    bool stop = false;                                   // a tile wait gave up (all threads alike)
+    constexpr uint32_t TILE_S = SUM_BLK * SUM_THREADS * sizeof(Tin);
     auto issue = [&](int k) {
+        if (fast) {
+            if (k < nblk && tid == 0 && !stop) {
+                const int r = k & 1;
+                fence_proxy_async_smem();                // the slot's last readers are past a barrier
+                mbar_arrive_expect_tx(&S.mbar[r], (HAS_Z ? 3 : 2) * TILE_S);
+                const int y = t1 - k * SUM_BLK - SUM_BLK;
+                tma_load_3d(&S.dl[r][0][0], &tm.dl, d0, y, bi, &S.mbar[r]);
+                tma_load_3d(&S.dout[r][0][0], &tm.dout, d0, y, bi, &S.mbar[r]);
+                if (HAS_Z) tma_load_3d(&S.z[r][0][0], &tm.z, d0, y, bi, &S.mbar[r]);
+            }
+            return;
+        }
         if (k < nblk) {
             const int hi = t1 - k * SUM_BLK, lo = max(t0, hi - SUM_BLK), rv = hi - lo, r = k & 1;
             stage_tile<Tin, SUM_THREADS>(&S.dl[r][0][0], gdl + (int64_t)lo * p.dl_sl, p.dl_sl, SUM_BLK, rv, nd,
@@ -150,10 +184,20 @@ __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const Sca
     float ssum = 0.f;
     for (int k = 0; k < nblk; ++k) {
         issue(k + 1);
-        cp_async_wait<1>();
-        __syncthreads();
+        if (fast) {
+            // bounded wait; one that gives up is recorded and stops further copies (the pass
+            // then runs on what is in shared memory: incomplete results, intact context)
+            bool ok = stop || mbar_wait_bounded(&S.mbar[k & 1], (k >> 1) & 1, SG_WAIT_POLLS);
+            if (__syncthreads_or(!ok)) {
+                if (!stop && tid == 0 && p.err) *p.err = SWX_ERR_TIMEOUT;
+                stop = true;
+            }
+        } else {
+            cp_async_wait<1>();
+            __syncthreads();
+        }
         const int hi = t1 - k * SUM_BLK, r = k & 1;
-        const int base = max(t0, hi - SUM_BLK);          // step of staged row 0
+        const int base = fast ? hi - SUM_BLK : max(t0, hi - SUM_BLK);   // step of staged row 0
 #pragma unroll 4
         for (int i = SUM_BLK - 1; i >= 0; --i) {
             const int t = hi - SUM_BLK + i;
@@ -179,7 +223,12 @@ __global__ void __launch_bounds__(SUM_THREADS) scan_bwd_summary_kernel(const Sca
         }
         __syncthreads();                                  // slot r is refilled two blocks on
     }
-    cp_async_wait<0>();
+    if (!fast) {
+        cp_async_wait<0>();
+    } else if (stop && tid == 0) {
+        // the copies that may still be landing: the last block issued into each slot
+        for (int k = max(0, nblk - 2); k < nblk; ++k) mbar_wait_bounded(&S.mbar[k & 1], (k >> 1) & 1, SG_WAIT_POLLS);
+    }
     if (ok) {
         float* q = p.ws_q + (((int64_t)ss * p.b + bi) * p.D + d) * NS;
 #pragma unroll
@@ -737,7 +786,13 @@ static cudaError_t launch_seg_t(const ScanDev& p0, cudaStream_t st) {
         }
         const int ssm = sizeof(SumSmem<Tin>);
         if ((e = allow_smem(ks, ssm)) != cudaSuccess) return e;
-        ks<<<(unsigned)gs, SUM_THREADS, ssm, st>>>(p);
+        SumMaps sm{};
+        const int es = sizeof(Tin);
+        bool ok = encode_3d(&sm.dl, p.dl, es, p.D, p.L, p.b, p.dl_sl, p.dl_sb, SUM_THREADS, SUM_BLK) &&
+                  encode_3d(&sm.dout, p.dout, es, p.D, p.L, p.b, p.dout_sl, p.dout_sb, SUM_THREADS, SUM_BLK);
+        if (ok && HAS_Z) ok = encode_3d(&sm.z, p.z, es, p.D, p.L, p.b, p.z_sl, p.z_sb, SUM_THREADS, SUM_BLK);
+        sm.ok = ok ? 1 : 0;
+        ks<<<(unsigned)gs, SUM_THREADS, ssm, st>>>(p, sm);
         if ((e = cudaGetLastError()) != cudaSuccess) return e;
     }
     const bool ypre = HAS_Z && p.ypre;
