@@ -257,10 +257,12 @@ struct SegSmem {
     float2 ee[TCK][2][SG_CH / 2 + 4];
     // per (state-group half jh, pair): (sum gB, sum g a h_prev A) of one channel of the pair
     // over that half's 8 states (channel jh after phase B's exchange), summed over the two
-    // halves in phase C; rows padded to 34 so that phase B's stores and phase C's loads
-    // (consecutive pairs) are both conflict-free
-    float2 nsp[TCK][2][2][SG_CH / 2 + 2];
-    float ypv[YV ? TCK : 1][2][2][SG_CH / 2 + 2];   // the same for the readout (without YPRE)
+    // halves in phase C.  Rows padded to 36 float2: in phase B each half-warp stores 4 pairs
+    // into each of the 4 rows of a step, and rows 36 float2 apart start 8 banks apart, so
+    // the 16 stores cover 32 distinct banks; phase C reads consecutive pairs of one row
+    float2 nsp[TCK][2][2][SG_CH / 2 + 4];
+    // the same for the readout (without YPRE), one float each: rows 40 floats (8 banks) apart
+    float ypv[YV ? TCK : 1][2][2][SG_CH / 2 + 8];
     float bcw[SG_WARPS][TCK][32];          // per-warp dB | dC sums over its 16 channels
     float red[4][SG_THREADS];
     uint64_t mbar[SG_RING];                // completion of each staging slot's TMA copies
