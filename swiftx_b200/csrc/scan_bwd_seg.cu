@@ -252,9 +252,10 @@ struct SegSmem {
     Tin C[SG_RING][TCK][NS];
     float4 dd2[TCK][SG_CH / 2];            // (delta_eff, delta_eff * u) of a channel pair
     float2 dy2[TCK][SG_CH / 2];            // dy of a channel pair
-    // (softplus', dz factor) of the even / odd channel of each pair; rows padded to 36 so
-    // that phase A's stores (lanes alternate even / odd) are conflict-free
-    float2 ee[TCK][2][SG_CH / 2 + 4];
+    // (softplus', dz factor) of the even / odd channel of each pair.  In phase A the lanes
+    // alternate even / odd channels: rows 40 float2 (16 banks) apart put a half-warp's even
+    // and odd stores on disjoint banks; phase C reads consecutive pairs of one row
+    float2 ee[TCK][2][SG_CH / 2 + 8];
     // per (state-group half jh, pair): (sum gB, sum g a h_prev A) of one channel of the pair
     // over that half's 8 states (channel jh after phase B's exchange), summed over the two
     // halves in phase C.  Rows padded to 36 float2: in phase B each half-warp stores 4 pairs
