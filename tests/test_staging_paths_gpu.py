@@ -1,0 +1,55 @@
+"""The two staging paths of the scan kernels give the same bits.
+
+Tiles reach shared memory by TMA (one thread, bulk tensor copies, mbarrier completion)
+when every input's base and strides are 16-byte aligned, and by per-thread loads
+otherwise.  The arithmetic after staging is the same, so a problem run once on aligned
+tensors and once on copies offset by one element (never 16-byte aligned) must give
+identical outputs, checkpoints, final states and gradients: the forward, the
+time-segmented backward (fp32) and the whole-row backward (a bf16 grid that fills the
+GPU), each with partial tiles at the sequence end and a partial channel block.
+"""
+import pytest
+import torch
+
+from swiftx_b200.selective_scan import scan_backward, scan_forward
+from swiftx_b200.workloads import config_inputs
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+KEYS = ("u", "delta", "B", "C", "z", "dout")
+
+
+def _offset_copy(t):
+    """A copy of t whose storage starts one element past a fresh allocation."""
+    buf = torch.empty(t.numel() + 8, dtype=t.dtype, device=t.device)
+    v = buf[1:1 + t.numel()].view(t.shape)
+    v.copy_(t)
+    assert v.data_ptr() % 16 != 0
+    return v
+
+
+def _run(inp, h0):
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+    pre = torch.empty(inp["u"].shape, device=DEV, dtype=torch.float32)
+    out, ck, hl = scan_forward(*args, h0=h0, out_dtype=torch.float32, checkpoints=True, return_last_state=True,
+                               pre_out=pre)
+    g = scan_backward(*args, h0, ck, inp["dout"], y_pre=pre)
+    return {"out": out, "ck": ck, "h_last": hl, "pre": pre, **{k: v for k, v in g.items() if v is not None}}
+
+
+@pytest.mark.parametrize("shape,dtype", [((2, 301, 96, 16), torch.float32),      # segmented backward
+                                         ((1, 2000, 200, 16), torch.float32),    # several segments
+                                         ((16, 77, 520, 16), torch.bfloat16)],   # whole-row backward
+                         ids=["fp32-short", "fp32-long", "bf16-rows"])
+def test_tma_and_per_thread_staging_agree(shape, dtype):
+    b, L, D, N = shape
+    inp = config_inputs(b, L, D, N, seed=61, device=DEV, dtype=dtype)
+    h0 = (torch.randn(b, D, N, generator=torch.Generator().manual_seed(6)) * 0.2).to(DEV)
+    aligned = _run(inp, h0)
+    shifted = dict(inp)
+    for k in KEYS:
+        shifted[k] = _offset_copy(inp[k])
+    unaligned = _run(shifted, h0)
+    assert set(aligned) == set(unaligned)
+    for k in aligned:
+        assert torch.equal(aligned[k], unaligned[k]), k
