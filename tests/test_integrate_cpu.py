@@ -1,7 +1,7 @@
 """The reference's own CPU test suite through the device-dispatching patch.
 
 swiftx_b200.integrate.patch_reference_module is what a maintainer appends to the
-reference's models/selective_scan.py to switch it over (INTEGRATION.md).  This test
+reference's models/selective_scan.py to switch it over.  This test
 copies the reference's models/ and tests/ to a temporary folder, appends those two
 lines, and runs the reference's tests for the scan, the block and the model
 (tests/test_selective_scan.py, test_sift_block.py, test_model.py) on CPU tensors: they
