@@ -438,21 +438,26 @@ def run_lm_train(args, world, rank, local):
     backward and the clip + AdamW update are each replayed as a CUDA graph (the step is
     otherwise bound by kernel-launch overhead); --no-graph runs them eagerly.  The backward
     assigns each parameter's gradient (FlatGradients(accumulate=False)): no zero fill and
-    no per-parameter accumulation add; with more than one rank one multi-tensor copy packs
-    them into the all-reduced buffer."""
-    from swiftx_b200.data_parallel import FlatGradients, broadcast_parameters
+    no per-parameter accumulation add; one multi-tensor copy packs them into the flat
+    buffer (the all-reduced one).  The parameters live in two flat buffers (with and
+    without weight decay, FlatParameters) laid out like the gradient buffer, so the clip
+    is one norm and one scale of the flat gradient and AdamW runs over two tensors."""
+    from swiftx_b200.data_parallel import FlatGradients, FlatParameters, broadcast_parameters
     from swiftx_b200.sift import SiftConfig, SiftLM
     dev = torch.device("cuda", local)
     torch.manual_seed(0)
     model = SiftLM(SiftConfig(vocab_size=256, d_model=256, n_layers=8, d_state=16, d_conv=4, expand=2)).to(dev)
     params = list(model.parameters())
     broadcast_parameters(params)                    # identical start on every rank
-    grads = FlatGradients(params, accumulate=False)     # the backward assigns gradients (no adds)
     decay = [p for p in params if p.dim() >= 2 and not getattr(p, "_no_weight_decay", False)]
     ids = {id(p) for p in decay}
     no_decay = [p for p in params if id(p) not in ids]
+    flat_params = FlatParameters([decay, no_decay])
+    grads = FlatGradients(decay + no_decay, accumulate=False)     # the backward assigns gradients (no adds)
+    flat_params.bind_gradients(grads)
     graphed = not args.no_graph
-    opt = torch.optim.AdamW([{"params": decay, "weight_decay": 0.1}, {"params": no_decay, "weight_decay": 0.0}],
+    opt = torch.optim.AdamW([{"params": [flat_params.flats[0]], "weight_decay": 0.1},
+                             {"params": [flat_params.flats[1]], "weight_decay": 0.0}],
                             lr=3e-4, betas=(0.9, 0.95), fused=True, capturable=graphed)
     B, L = 16, 512
     g = torch.Generator().manual_seed(1234 + rank)
@@ -464,11 +469,13 @@ def run_lm_train(args, world, rank, local):
         with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
             _, loss = model(tok[:, :-1], tok[:, 1:])
         loss.backward()
-        grads.pack_()                                   # into the flat buffer when ranks > 1
+        grads.pack_(always=True)                        # into the flat buffer the optimizer reads
         return loss.detach()
 
     def update():
-        torch.nn.utils.clip_grad_norm_(params, 1.0)
+        # clip_grad_norm_(params, 1.0) over the flat buffer: the global 2-norm, then one scale
+        norm = torch.linalg.vector_norm(grads.flat)
+        grads.flat.mul_(torch.clamp(1.0 / (norm + 1e-6), max=1.0))
         opt.step()
 
     def allreduce():

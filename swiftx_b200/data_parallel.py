@@ -65,12 +65,13 @@ class FlatGradients:
             for p in self.params:
                 p.grad = None
 
-    def pack_(self, group=None):
+    def pack_(self, group=None, always=False):
         """After a backward (accumulate=False): when the process group has more than one
-        rank, copy every p.grad into the buffer (a parameter without a gradient gets
-        zeros) and point p.grad at the buffer's views.  Otherwise, and in accumulate mode,
-        the gradients are already where the optimizer reads them: nothing to do."""
-        if self.accumulate or _world(group) == 1:
+        rank, or ``always`` (an optimizer that reads the flat buffer itself, see
+        FlatParameters), copy every p.grad into the buffer (a parameter without a gradient
+        gets zeros) and point p.grad at the buffer's views.  Otherwise, and in accumulate
+        mode, the gradients are already where the optimizer reads them: nothing to do."""
+        if self.accumulate or (_world(group) == 1 and not always):
             return
         have = [(v, p.grad) for v, p in zip(self.views, self.params) if p.grad is not None]
         for v, p in zip(self.views, self.params):
@@ -98,3 +99,45 @@ def _world(group=None):
     if not (dist.is_available() and dist.is_initialized()):
         return 1
     return dist.get_world_size(group)
+
+
+class FlatParameters:
+    """The parameters re-homed into one contiguous buffer per group.
+
+    groups: lists of parameters (e.g. those with and without weight decay).  Each
+    parameter's ``.data`` becomes a view of its group's buffer, in the given order, with
+    its values kept; ``flats[i]`` is a Parameter over the whole buffer of group i.  With a
+    FlatGradients built over the same parameters in the same order, ``bind_gradients``
+    points each flat Parameter's ``.grad`` at the matching slice of the gradient buffer,
+    so an optimizer given ``flats`` updates every parameter in one pass per group instead
+    of one per tensor.  The optimizer's arithmetic is element-wise, so the update is the
+    one it would make over the separate tensors."""
+
+    def __init__(self, groups, dtype=torch.float32):
+        self.groups = [list(g) for g in groups]
+        self.flats = []
+        for ps in self.groups:
+            if not ps:
+                raise ValueError("FlatParameters needs a non-empty group")
+            n = sum(p.numel() for p in ps)
+            buf = torch.empty(n, device=ps[0].device, dtype=dtype)
+            off = 0
+            for p in ps:
+                if p.dtype != dtype:
+                    raise ValueError(f"parameter dtype {p.dtype} differs from the buffer's {dtype}")
+                v = buf[off:off + p.numel()].view_as(p)
+                v.copy_(p.data)
+                p.data = v
+                off += p.numel()
+            self.flats.append(torch.nn.Parameter(buf))
+
+    def bind_gradients(self, grads):
+        """Point each flat Parameter's .grad at its slice of ``grads.flat`` (FlatGradients
+        over the concatenated groups, same order).  Call once; the slices stay valid."""
+        order = [p for g in self.groups for p in g]
+        if len(order) != len(grads.params) or any(a is not b for a, b in zip(order, grads.params)):
+            raise ValueError("the gradient buffer must hold the groups' parameters in the same order")
+        off = 0
+        for flat in self.flats:
+            flat.grad = grads.flat[off:off + flat.numel()]
+            off += flat.numel()

@@ -16,7 +16,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from swiftx_b200.data_parallel import FlatGradients, broadcast_parameters
+from swiftx_b200.data_parallel import FlatGradients, FlatParameters, broadcast_parameters
 
 STEPS, ROWS_PER_RANK, WORLD = 3, 6, 2
 
@@ -108,3 +108,39 @@ def test_assign_mode_leaves_gradients_to_autograd_on_one_rank():
         np.testing.assert_allclose(a.grad.numpy(), k + 1.0)
         np.testing.assert_allclose(b.grad.numpy(), (2 * b).detach().numpy())
         assert a.grad._base is not fg.flat
+
+
+def test_flat_parameters_keep_values_and_update_like_separate_tensors():
+    """FlatParameters re-homes the parameters into one buffer per group without changing
+    their values, and AdamW over the two flat Parameters (gradients bound to the packed
+    gradient buffer) makes bit for bit the update of AdamW over the separate tensors."""
+    g = torch.Generator().manual_seed(3)
+    shapes = [(4, 3), (5,), (2, 2, 2), (7,)]
+    ps_a = [torch.nn.Parameter(torch.randn(s, generator=g)) for s in shapes]
+    ps_b = [torch.nn.Parameter(p.detach().clone()) for p in ps_a]
+    decay_b, nodecay_b = [ps_b[0], ps_b[2]], [ps_b[1], ps_b[3]]
+    flat = FlatParameters([decay_b, nodecay_b])
+    for a, b in zip(ps_a, ps_b):
+        assert torch.equal(a.detach(), b.detach())
+    assert ps_b[2].data.data_ptr() == flat.flats[0].data_ptr() + 12 * 4       # a view of the buffer
+    grads = FlatGradients(decay_b + nodecay_b, accumulate=False)
+    flat.bind_gradients(grads)
+    kw = dict(lr=1e-2, betas=(0.9, 0.95), foreach=False)
+    opt_a = torch.optim.AdamW([{"params": [ps_a[0], ps_a[2]], "weight_decay": 0.1},
+                               {"params": [ps_a[1], ps_a[3]], "weight_decay": 0.0}], **kw)
+    opt_b = torch.optim.AdamW([{"params": [flat.flats[0]], "weight_decay": 0.1},
+                               {"params": [flat.flats[1]], "weight_decay": 0.0}], **kw)
+    for _ in range(3):
+        gs = [torch.randn(s, generator=g) for s in shapes]
+        for p, gr in zip(ps_a, gs):
+            p.grad = gr.clone()
+        grads.zero_()
+        for p, gr in zip(ps_b, gs):
+            p.grad = gr.clone()
+        grads.pack_(always=True)
+        opt_a.step()
+        opt_b.step()
+        for a, b in zip(ps_a, ps_b):
+            assert torch.equal(a.detach(), b.detach())
+    with pytest.raises(ValueError):
+        flat.bind_gradients(FlatGradients(list(reversed(decay_b + nodecay_b)), accumulate=False))
