@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define SWX_ABI_VERSION 12
+#define SWX_ABI_VERSION 13
 
 /* status codes */
 #define SWX_OK 0
@@ -110,6 +110,10 @@ typedef struct swx_scan_args {
     const int32_t* group_of;
     int32_t ngroups;
     float* d_group_w;
+    /* optional element strides (batch, row) of dz; 0, 0 = dense (L*D, D).  Lets the
+       backward write the gate gradient straight into the z half of the in_proj output's
+       gradient (row stride 2D).  dz_sl >= dim, dz_sb >= seqlen * dz_sl; fp32 / bf16 only. */
+    int64_t dz_sb, dz_sl;
 } swx_scan_args;
 
 #define SWX_MAX_GROUPS 8
@@ -229,6 +233,10 @@ typedef struct swx_conv_args {
     float* dweight;          /* (D, width) */
     float* dbias;            /* (D,) optional */
     void* workspace; int64_t workspace_bytes;  /* >= swx_conv1d_bwd_workspace_bytes() */
+    /* optional element strides (batch, row) of dx; 0, 0 = dense (L*D, D): the backward can
+       write into the x half of the in_proj output's gradient (row stride 2D).
+       dx_sl >= dim, dx_sb >= seqlen * dx_sl. */
+    int64_t dx_sb, dx_sl;
 } swx_conv_args;
 
 /* out = silu(conv(x) + bias), the conv segment of SiftBlock.forward

@@ -53,6 +53,7 @@ class ScanArgs(ctypes.Structure):
         ("out_pre", vp),
         ("group_w", vp), ("group_w_sb", i64), ("group_w_sl", i64),
         ("group_of", vp), ("ngroups", i32), ("d_group_w", vp),
+        ("dz_sb", i64), ("dz_sl", i64),
     ]
 
 
@@ -66,6 +67,7 @@ class ConvArgs(ctypes.Structure):
         ("dout", vp), ("dout_sb", i64), ("dout_sl", i64),
         ("dx", vp), ("dweight", vp), ("dbias", vp),
         ("workspace", vp), ("workspace_bytes", i64),
+        ("dx_sb", i64), ("dx_sl", i64),
     ]
 
 

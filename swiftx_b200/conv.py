@@ -54,7 +54,10 @@ def conv1d_forward(x, weight, bias=None, silu=True):
     return out
 
 
-def conv1d_backward(x, weight, bias, dout, silu=True):
+def conv1d_backward(x, weight, bias, dout, silu=True, dx_out=None):
+    """dx, dweight, dbias of conv1d_forward.  dx_out: optional (b, L, D) tensor of x's
+    dtype with unit channel stride (e.g. the x half of a (b, L, 2D) gradient) that receives
+    dx in place of a new tensor."""
     lib = _lib.load()
     x, w, bb = _prep(x, weight, bias)
     dout = dout.to(x.dtype)
@@ -62,7 +65,12 @@ def conv1d_backward(x, weight, bias, dout, silu=True):
         dout = dout.contiguous()
     b, L, D = x.shape
     K = w.shape[1]
-    dx = torch.empty(x.shape, device=x.device, dtype=x.dtype)
+    if dx_out is not None:
+        if dx_out.shape != x.shape or dx_out.dtype != x.dtype or dx_out.stride(-1) != 1 or dx_out.device != x.device:
+            raise ValueError("dx_out must be a (b, L, D) tensor of x's dtype with unit channel stride")
+        dx = dx_out
+    else:
+        dx = torch.empty(x.shape, device=x.device, dtype=x.dtype)
     dw = torch.empty((D, K), device=x.device, dtype=torch.float32)
     db = torch.empty(D, device=x.device, dtype=torch.float32) if bias is not None else None
     wsb = lib.swx_conv1d_bwd_workspace_bytes(b, L, D, K)
@@ -73,6 +81,8 @@ def conv1d_backward(x, weight, bias, dout, silu=True):
     a.dx, a.dweight = dx.data_ptr(), dw.data_ptr()
     a.dbias = db.data_ptr() if db is not None else None
     a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
+    if dx_out is not None:
+        a.dx_sb, a.dx_sl = dx.stride(0), dx.stride(1)
     _lib.check(lib.swx_conv1d_bwd(a, _lib.stream_ptr(x.device)), "swx_conv1d_bwd")
     return dx, dw, db
 

@@ -157,6 +157,8 @@ swx::ScanDev pack(const swx_scan_args* a) {
     p.vec_yp = vec_ok(a->out_pre, a->seqlen * a->dim, a->dim, 4);
     p.dout = a->dout; p.dout_sb = a->dout_sb; p.dout_sl = a->dout_sl;
     p.du = a->du; p.ddl = a->ddelta; p.dz = a->dz; p.dB = a->dB; p.dC = a->dC;
+    p.dz_sl = a->dz_sl ? a->dz_sl : a->dim;
+    p.dz_sb = a->dz_sb ? a->dz_sb : a->seqlen * p.dz_sl;
     p.dA = a->dA; p.dD = a->dD; p.ddbias = a->ddelta_bias; p.dh0 = a->dh0;
     p.nblk = (int)((a->dim + 31) / 32);
     if (a->group_w) {
@@ -356,6 +358,11 @@ int swx_scan_bwd(const swx_scan_args* a, void* stream) {
     if (!a->dout || !a->du || !a->ddelta || !a->dB || !a->dC || !a->dA || !a->checkpoints)
         return SWX_ERR_INVALID_ARG;
     if (a->z && !a->dz) return SWX_ERR_INVALID_ARG;
+    if ((a->dz_sb != 0) != (a->dz_sl != 0)) return SWX_ERR_INVALID_ARG;
+    if (a->dz_sl) {                                  // strided dz (e.g. the z half of d(xz))
+        if (a->in_dtype == SWX_DTYPE_F64) return SWX_ERR_UNSUPPORTED;
+        if (a->dz_sl < a->dim || a->dz_sb < a->seqlen * a->dz_sl) return SWX_ERR_INVALID_ARG;
+    }
     if (a->d_group_w && !a->out_pre) return SWX_ERR_INVALID_ARG;     // the weights' gradient reads y
     if (!aligned16(a->checkpoints) || !a->workspace || !aligned16(a->workspace)) return SWX_ERR_INVALID_ARG;
     const bool f64 = a->in_dtype == SWX_DTYPE_F64;

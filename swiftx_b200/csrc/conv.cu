@@ -28,6 +28,7 @@ struct ConvDev {
     void* out;
     const void* dout; int64_t do_sb, do_sl;
     void* dx; float* dw; float* dbias;
+    int64_t dx_sb, dx_sl;   // element strides of dx (dense: L*D, D)
     float* ws;        // (b, ntiles, D, K+1) partials of dw | dbias
     int ntiles;
 };
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(CONV_NT) conv_bwd_kernel(const ConvDev p) {
     if (d >= p.D) return;
     const T* x = static_cast<const T*>(p.x) + bi * p.x_sb + d;
     const T* dout = static_cast<const T*>(p.dout) + bi * p.do_sb + d;
-    T* dx = static_cast<T*>(p.dx) + (int64_t)bi * p.L * p.D + d;
+    T* dx = static_cast<T*>(p.dx) + (int64_t)bi * p.dx_sb + d;
     float w[K];
 #pragma unroll
     for (int k = 0; k < K; ++k) w[k] = p.w[(int64_t)d * K + k];
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(CONV_NT) conv_bwd_kernel(const ConvDev p) {
             float a = 0.f;
 #pragma unroll
             for (int k = 0; k < K; ++k) a = fmaf(w[k], gq[K - 1 - k], a);
-            dx[(int64_t)t * p.D] = Elem<T>::from_f(a);
+            dx[(int64_t)t * p.dx_sl] = Elem<T>::from_f(a);
         }
 #pragma unroll
         for (int k = 0; k < K - 1; ++k) xw[k] = xw[k + 1];
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(CONV_NT) conv_bwd_kernel(const ConvDev p) {
             float a = 0.f;
 #pragma unroll
             for (int k = 0; k < K; ++k) a = fmaf(w[k], gq[K - 1 - k], a);
-            dx[(int64_t)t * p.D] = Elem<T>::from_f(a);
+            dx[(int64_t)t * p.dx_sl] = Elem<T>::from_f(a);
         }
     }
     float* ws = p.ws + (((int64_t)bi * p.ntiles + tile) * p.D + d) * (K + 1);
@@ -328,6 +329,8 @@ swx::ConvDev conv_pack(const swx_conv_args* a) {
     p.out = a->out;
     p.dout = a->dout; p.do_sb = a->dout_sb; p.do_sl = a->dout_sl;
     p.dx = a->dx; p.dw = a->dweight; p.dbias = a->dbias;
+    p.dx_sl = a->dx_sl ? a->dx_sl : a->dim;
+    p.dx_sb = a->dx_sb ? a->dx_sb : a->seqlen * p.dx_sl;
     p.ntiles = (int)((a->seqlen + swx::CONV_TT - 1) / swx::CONV_TT);
     return p;
 }
@@ -364,6 +367,8 @@ int swx_conv1d_bwd(const swx_conv_args* a, void* stream) {
         return e == cudaSuccess ? SWX_OK : SWX_ERR_CUDA;
     }
     if (!a->dout || !a->dx || !a->dweight || !a->workspace) return SWX_ERR_INVALID_ARG;
+    if ((a->dx_sb != 0) != (a->dx_sl != 0)) return SWX_ERR_INVALID_ARG;
+    if (a->dx_sl && (a->dx_sl < a->dim || a->dx_sb < a->seqlen * a->dx_sl)) return SWX_ERR_INVALID_ARG;
     if (a->workspace_bytes < swx_conv1d_bwd_workspace_bytes(a->batch, a->seqlen, a->dim, a->width))
         return SWX_ERR_INVALID_ARG;
     swx::ConvDev p = conv_pack(a);

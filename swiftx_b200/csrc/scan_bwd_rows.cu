@@ -300,7 +300,7 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         const int64_t orow = (int64_t)bi * p.L * p.D + d0;
         Tin* gdu = static_cast<Tin*>(p.du) + orow;
         Tin* gddl = static_cast<Tin*>(p.ddl) + orow;
-        Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + orow : nullptr;
+        Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + (int64_t)bi * p.dz_sb + d0 : nullptr;   // may be strided
         float* wbc = p.ws_bc + ((int64_t)blockIdx.x * p.b + bi) * p.L * 2 * NS;
         const float* gyp = YPRE ? p.ypre + (int64_t)bi * p.L * p.D + d0 : nullptr;
         float accD = 0.f, accB = 0.f;
@@ -417,7 +417,7 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
                                 const float4 q4 = *reinterpret_cast<const float4*>(&S.nyp[slot][tt][ech][0]);
                                 y = fmaf(eD, e.x, (q4.x + q4.y) + (q4.z + q4.w));
                             }
-                            gdz[o] = Elem<Tin>::from_f(e.z * y);
+                            gdz[(int64_t)(t0 + t) * p.dz_sl + ech] = Elem<Tin>::from_f(e.z * y);
                         }
                         accD = fmaf(e.w, e.x, accD);
                         accB += draw;

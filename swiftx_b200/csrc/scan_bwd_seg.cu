@@ -620,8 +620,12 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
             const int64_t orow = (int64_t)bi * p.L * p.D + d0 + 2 * cpair;
             Tin* gdu = static_cast<Tin*>(p.du) + orow;
             Tin* gddl = static_cast<Tin*>(p.ddl) + orow;
-            Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + orow : nullptr;
+            Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + (int64_t)bi * p.dz_sb + d0 + 2 * cpair : nullptr;
             const bool pair_out = cv1 && (p.D % 2 == 0);   // both channels, 2-element aligned rows
+            // dz may be strided (the z half of a (b, L, 2D) gradient): paired stores only
+            // where its strides and base keep every pair aligned
+            const bool pair_dz = pair_out && ((p.dz_sb | p.dz_sl) & 1) == 0 &&
+                                 (reinterpret_cast<uintptr_t>(p.dz) % (2 * sizeof(Tin))) == 0;
 #pragma unroll
             for (int m = 0; m < TCK / 4; ++m) {
                 const int t = ch4 + 4 * m;
@@ -648,19 +652,24 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
                         }
                         dz = mul2(qq, y);
                     }
-                    const int64_t o = (int64_t)(t0 + t) * p.D;
+                    const int64_t o = (int64_t)(t0 + t) * p.D, oz = (int64_t)(t0 + t) * p.dz_sl;
                     if (pair_out) {
                         store2(gdu + o, du);
                         store2(gddl + o, draw);
-                        if (HAS_Z) store2(gdz + o, dz);
                     } else {
                         gdu[o] = Elem<Tin>::from_f(du.x);
                         gddl[o] = Elem<Tin>::from_f(draw.x);
-                        if (HAS_Z) gdz[o] = Elem<Tin>::from_f(dz.x);
                         if (cv1) {
                             gdu[o + 1] = Elem<Tin>::from_f(du.y);
                             gddl[o + 1] = Elem<Tin>::from_f(draw.y);
-                            if (HAS_Z) gdz[o + 1] = Elem<Tin>::from_f(dz.y);
+                        }
+                    }
+                    if (HAS_Z) {
+                        if (pair_dz) {
+                            store2(gdz + oz, dz);
+                        } else {
+                            gdz[oz] = Elem<Tin>::from_f(dz.x);
+                            if (cv1) gdz[oz + 1] = Elem<Tin>::from_f(dz.y);
                         }
                     }
                     accD = fma2(dyy, uu, accD);

@@ -31,6 +31,7 @@ struct ScanDev {
     // backward
     const void* dout; int64_t dout_sb, dout_sl;
     void* du; void* ddl; void* dz; void* dB; void* dC;
+    int64_t dz_sb, dz_sl;    // element strides of dz (dense: L*D, D)
     float* dA; float* dD; float* ddbias; float* dh0;
     float* ws_bc;            // (nblk, b, L, 2, 16) per-CTA dB/dC partials
     float* ws_a;             // (b, D, 16)

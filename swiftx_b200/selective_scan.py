@@ -162,9 +162,11 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
 
 
 def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, dout, y_pre=None,
-                  A_is_log=False, group_w=None, group_of=None, group_w_grad=False):
+                  A_is_log=False, group_w=None, group_of=None, group_w_grad=False, dz_out=None):
     """One call of the backward kernels (no autograd).  Returns a dict of gradients.
     y_pre: the pre-gate output the forward wrote to pre_out (optional, with z).
+    dz_out: optional (b, L, D) tensor of the input dtype with unit channel stride (e.g. the
+    z half of a (b, L, 2D) gradient) that receives dz in place of a new tensor.
     A_is_log: A holds log(-A), and "dA" is the gradient with respect to it.
     group_w, group_of: the pathway mix of the forward; with group_w_grad (needs y_pre)
     "d_group_w" (b, L, G) is the gradient with respect to group_w."""
@@ -179,7 +181,13 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     e = lambda *s, dt=in_dt: torch.empty(s, device=dev, dtype=dt)  # noqa: E731
     g = {"du": e(b, L, Dm), "ddelta": e(b, L, Dm), "dB": e(b, L, N), "dC": e(b, L, N),
          "dA": e(Dm, N, dt=pdt)}
-    g["dz"] = e(b, L, Dm) if z is not None else None
+    if dz_out is not None:
+        if z is None or dz_out.shape != (b, L, Dm) or dz_out.dtype != in_dt or dz_out.stride(-1) != 1 \
+                or dz_out.device != dev:
+            raise ValueError("dz_out must be a (b, L, D) tensor of the input dtype with unit channel stride")
+        g["dz"] = dz_out
+    else:
+        g["dz"] = e(b, L, Dm) if z is not None else None
     g["dD"] = e(Dm, dt=pdt) if D is not None else None
     g["ddelta_bias"] = e(Dm, dt=pdt) if delta_bias is not None else None
     g["dh0"] = e(b, Dm, N, dt=pdt) if h0 is not None else None
@@ -194,6 +202,8 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     for k in ("du", "ddelta", "dz", "dB", "dC", "dA", "dD", "ddelta_bias", "dh0"):
         setattr(a, k, g[k].data_ptr() if g[k] is not None else None)
     a.workspace, a.workspace_bytes = ws.data_ptr(), wsb
+    if dz_out is not None:
+        a.dz_sb, a.dz_sl = dz_out.stride(0), dz_out.stride(1)
     if y_pre is not None and z is not None:
         a.out_pre = y_pre.data_ptr()
     _fill_groups(a, gw, gof)

@@ -32,9 +32,9 @@ import torch.nn.functional as F
 
 from . import embedding as embedding_kernels
 from . import norm as norm_kernels
-from .conv import causal_conv1d_fn
+from .conv import causal_conv1d_fn, conv1d_backward, conv1d_forward
 from .decode import decode_conv_step, decode_layer_step, decode_ssm_step
-from .selective_scan import selective_scan_fn
+from .selective_scan import scan_backward, scan_forward, selective_scan_fn
 
 
 # bf16 copies of the projection weights for the current SiftLM forward under bf16 autocast
@@ -100,6 +100,61 @@ def _bf16_copies(weights, flat=None):
 # Largest batch whose decode step folds the projections into the kernels (see
 # SiftBlock.step).
 _FOLD_DT_MAX_BATCH = 32
+
+# Training forwards of pathway-free blocks under bf16 autocast (with the bf16 weight
+# copies) run the mixer between in_proj and out_proj as one autograd Function
+# (_MixerCore); False keeps the per-op autograd graph.
+_FUSED_CORE = True
+
+
+class _MixerCore(torch.autograd.Function):
+    """The mixer between in_proj and out_proj as one autograd node: conv1d + SiLU on the x
+    half of xz, x_proj, dt_proj, and the gated selective scan with softplus(delta + bias),
+    A = -exp(A_log) and the D skip (models/sift_block.py:111-135).  The forward runs the
+    same kernels and GEMMs as the per-op graph, so its output has the same bits.  The
+    backward writes the scan's dz and the conv's dx straight into the two halves of one
+    d(xz) buffer (no concatenation), and adds the scan's du to x_proj's input gradient
+    inside that GEMM (addmm; no separate add of the conv output's two gradients).
+    Weights: the fp32 parameters receive the gradients (fp32 straight from the GEMMs, as
+    _Bf16Linear); the GEMMs use the forward's bf16 copies."""
+
+    @staticmethod
+    def forward(ctx, xz, conv_w, conv_b, xw, xw16, dtw, dtw16, A_log, Dp, dt_bias):
+        Dm = xz.shape[-1] // 2
+        R = dtw.shape[1]
+        with torch.autocast(device_type="cuda", enabled=False):
+            x, z = xz[..., :Dm], xz[..., Dm:]
+            xc = conv1d_forward(x, conv_w, conv_b, True)
+            x_dbl = F.linear(xc, xw16)
+            N = (x_dbl.shape[-1] - R) // 2
+            delta = F.linear(x_dbl[..., :R], dtw16)
+            pre = torch.empty(xc.shape, device=xc.device, dtype=torch.float32)
+            y, ck, _ = scan_forward(xc, delta, A_log, x_dbl[..., R:R + N], x_dbl[..., R + N:], Dp, z, dt_bias, True,
+                                    checkpoints=True, pre_out=pre, A_is_log=True)
+        ctx.save_for_backward(xz, conv_w, conv_b, xc, x_dbl, delta, ck, pre, xw16, dtw16, A_log, Dp, dt_bias)
+        ctx.dims = (Dm, R, N)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        xz, conv_w, conv_b, xc, x_dbl, delta, ck, pre, xw16, dtw16, A_log, Dp, dt_bias = ctx.saved_tensors
+        Dm, R, N = ctx.dims
+        b, L = xz.shape[0], xz.shape[1]
+        with torch.autocast(device_type="cuda", enabled=False):
+            dxz = torch.empty_like(xz)
+            x, z = xz[..., :Dm], xz[..., Dm:]
+            g = scan_backward(xc, delta, A_log, x_dbl[..., R:R + N], x_dbl[..., R + N:], Dp, z, dt_bias, True, None,
+                              ck, dy.to(xz.dtype), y_pre=pre, A_is_log=True, dz_out=dxz[..., Dm:])
+            dd = g["ddelta"].reshape(-1, Dm)
+            x_dbl2 = x_dbl.reshape(-1, R + 2 * N)
+            dwdt = torch.mm(dd.t(), x_dbl2[:, :R], out_dtype=torch.float32)                    # dt_proj
+            dx_dbl = torch.cat([torch.mm(dd, dtw16), g["dB"].reshape(-1, N), g["dC"].reshape(-1, N)], dim=1)
+            dwx = torch.mm(dx_dbl.t(), xc.reshape(-1, Dm), out_dtype=torch.float32)            # x_proj
+            dxc = torch.addmm(g["du"].reshape(-1, Dm), dx_dbl, xw16)      # du + d(x_proj input)
+            _, dcw, dcb = conv1d_backward(x, conv_w, conv_b, dxc.view(b, L, Dm), True, dx_out=dxz[..., :Dm])
+        dcb = dcb.to(conv_b.dtype) if dcb is not None else None
+        return (dxz, dcw.reshape(conv_w.shape).to(conv_w.dtype), dcb, dwx, None, dwdt, None,
+                g["dA"], g["dD"], g["ddelta_bias"])
 
 
 # ----------------------------------------------------------------- parameter table
@@ -238,9 +293,24 @@ class SiftBlock(nn.Module):
         return [m.weight for m in (self.in_proj, self.x_proj, self.dt_proj, self.out_proj)
                 if m is self.dt_proj or m.bias is None]
 
+    def _core_weights(self, xz):
+        """The bf16 copies of x_proj's and dt_proj's weights when this forward can run the
+        mixer as one _MixerCore node (training, bf16, no pathway mix), else None."""
+        if not (_FUSED_CORE and _W16 is not None and self.pathway is None and torch.is_grad_enabled()
+                and xz.is_cuda and xz.dtype == torch.bfloat16 and self.x_proj.bias is None
+                and self.conv1d.bias is not None and self.d_inner % 2 == 0):
+            return None
+        w = (_W16.get(id(self.x_proj.weight)), _W16.get(id(self.dt_proj.weight)))
+        return w if w[0] is not None and w[1] is not None else None
+
     def forward(self, hidden):
         """hidden: (b, L, d_model) -> (b, L, d_model)"""
         xz = _linear(hidden, self.in_proj.weight, self.in_proj.bias)
+        w16 = self._core_weights(xz)
+        if w16 is not None:
+            y = _MixerCore.apply(xz, self.conv1d.weight, self.conv1d.bias, self.x_proj.weight, w16[0],
+                                 self.dt_proj.weight, w16[1], self.A_log, self.D, self.dt_proj.bias)
+            return _linear(y, self.out_proj.weight, self.out_proj.bias)
         x, z = xz.chunk(2, dim=-1)                        # strided views, row stride 2D
         x = causal_conv1d_fn(x, self.conv1d.weight, self.conv1d.bias, "silu")
         delta, B, C = self._split(x)

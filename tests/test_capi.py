@@ -33,7 +33,7 @@ def test_struct_mirrors_match():
     assert lib.swx_linear_scan_args_size() == ctypes.sizeof(_lib.LinearScanArgs)
     assert lib.swx_rmsnorm_args_size() == ctypes.sizeof(_lib.RMSNormArgs)
     assert lib.swx_embedding_args_size() == ctypes.sizeof(_lib.EmbeddingArgs)
-    assert lib.swx_abi_version() == 12
+    assert lib.swx_abi_version() == 13
 
 
 def test_status_strings():
@@ -143,3 +143,32 @@ def test_cpu_tensors_are_rejected_not_computed():
     from swiftx_b200 import parallel_scan
     with pytest.raises(RuntimeError):
         parallel_scan(torch.rand(2, 5, 3), torch.randn(2, 5, 3))
+
+
+def test_strided_gradient_output_arguments_are_checked():
+    """dz / dx strides come in pairs and may not overlap rows; float64 takes dense dz only.
+    The checks run before any device work."""
+    lib = _lib.load()
+    a = _lib.ScanArgs()
+    a.batch, a.seqlen, a.dim, a.dstate = 2, 32, 64, 16
+    a.in_dtype = a.out_dtype = 0                             # fp32
+    for k in ("u", "delta", "B", "C", "A", "dout", "du", "ddelta", "dB", "dC", "dA", "checkpoints", "workspace", "z", "dz"):
+        setattr(a, k, 4096)
+    a.u_sb = a.delta_sb = a.dout_sb = a.z_sb = 32 * 64
+    a.u_sl = a.delta_sl = a.dout_sl = a.z_sl = 64
+    a.B_sb = a.C_sb = 32 * 16
+    a.B_sl = a.C_sl = 16
+    a.workspace_bytes = 1 << 40
+    a.dz_sb, a.dz_sl = 32 * 128, 0                      # one stride without the other
+    assert lib.swx_scan_bwd(a, None) == _lib.SWX_ERR_INVALID_ARG
+    a.dz_sb, a.dz_sl = 32 * 128, 32                     # rows overlap
+    assert lib.swx_scan_bwd(a, None) == _lib.SWX_ERR_INVALID_ARG
+    c = _lib.ConvArgs()
+    c.batch, c.seqlen, c.dim, c.width = 2, 32, 64, 4
+    c.dtype = 0                                               # fp32
+    for k in ("x", "weight", "dout", "dx", "dweight", "workspace"):
+        setattr(c, k, 4096)
+    c.x_sb, c.x_sl, c.dout_sb, c.dout_sl = 32 * 64, 64, 32 * 64, 64
+    c.workspace_bytes = 1 << 40
+    c.dx_sb, c.dx_sl = 0, 128
+    assert lib.swx_conv1d_bwd(c, None) == _lib.SWX_ERR_INVALID_ARG

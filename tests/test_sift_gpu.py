@@ -243,6 +243,39 @@ def test_bf16_weight_copies_match_autocast():
         np.testing.assert_allclose(g1[n].cpu().numpy(), g0[n].cpu().numpy(), rtol=2e-2, atol=tol, err_msg=n)
 
 
+def test_fused_mixer_core_matches_per_op_graph():
+    """The mixer between in_proj and out_proj as one autograd node (_MixerCore: dz and the
+    conv's dx written into the two halves of one d(xz) buffer, the scan's du added inside
+    x_proj's input-gradient GEMM) against the per-op graph of the same kernels: identical
+    logits (the forward runs the same kernels and GEMMs), gradients equal to bf16 rounding
+    (the fused add rounds once instead of twice)."""
+    from swiftx_b200 import sift as sift_mod
+    torch.manual_seed(0)
+    m = SiftLM(SiftConfig(vocab_size=64, d_model=128, n_layers=2, d_state=16)).to(DEV)
+    tok = torch.randint(0, 64, (3, 130), device=DEV)
+
+    def run(fused):
+        prev = sift_mod._FUSED_CORE
+        sift_mod._FUSED_CORE = fused
+        try:
+            m.zero_grad(set_to_none=True)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                logits, loss = m(tok[:, :-1], tok[:, 1:])
+            loss.backward()
+        finally:
+            sift_mod._FUSED_CORE = prev
+        return logits.detach().float(), {n: p.grad.clone() for n, p in m.named_parameters()}
+
+    l1, g1 = run(True)
+    l0, g0 = run(False)
+    assert torch.equal(l1, l0)
+    assert set(g1) == set(g0)
+    for n in g0:
+        assert g1[n].dtype == g0[n].dtype and g1[n].shape == g0[n].shape, n
+        tol = 2e-2 * float(g0[n].abs().max())
+        np.testing.assert_allclose(g1[n].cpu().numpy(), g0[n].cpu().numpy(), rtol=2e-2, atol=tol, err_msg=n)
+
+
 def make_pathway_block():
     """SiftX block: three timescale groups over 32 channels (sizes 11/10/11) and the
     per-token pathway gate, with non-zero pathway weights so the mix is not the identity."""

@@ -53,3 +53,31 @@ def test_tma_and_per_thread_staging_agree(shape, dtype):
     assert set(aligned) == set(unaligned)
     for k in aligned:
         assert torch.equal(aligned[k], unaligned[k]), k
+
+
+@pytest.mark.parametrize("shape,dtype", [((2, 301, 96, 16), torch.float32), ((16, 77, 520, 16), torch.bfloat16)],
+                         ids=["fp32-segmented", "bf16-rows"])
+def test_strided_gradient_outputs_equal_dense(shape, dtype):
+    """dz written into the z half and the conv's dx into the x half of one (b, L, 2D)
+    buffer (row stride 2D, as the in_proj output's gradient) equal the dense outputs bit
+    for bit: the segmented and the whole-row backward, and the conv backward."""
+    from swiftx_b200.conv import conv1d_backward
+    b, L, D, N = shape
+    inp = config_inputs(b, L, D, N, seed=62, device=DEV, dtype=dtype)
+    args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
+    pre = torch.empty(inp["u"].shape, device=DEV, dtype=torch.float32)
+    _, ck, _ = scan_forward(*args, checkpoints=True, pre_out=pre)
+    dense = scan_backward(*args, None, ck, inp["dout"], y_pre=pre)
+    dxz = torch.full((b, L, 2 * D), float("nan"), device=DEV, dtype=dtype)
+    strided = scan_backward(*args, None, ck, inp["dout"], y_pre=pre, dz_out=dxz[..., D:])
+    assert strided["dz"].data_ptr() == dxz[..., D:].data_ptr()
+    for k in dense:
+        if dense[k] is not None:
+            assert torch.equal(dense[k], strided[k]), k
+    w = (torch.randn(D, 4, generator=torch.Generator().manual_seed(7)) * 0.3).to(DEV)
+    bias = torch.zeros(D, device=DEV)
+    dx0, dw0, db0 = conv1d_backward(inp["u"], w, bias, inp["dout"], True)
+    dx1, dw1, db1 = conv1d_backward(inp["u"], w, bias, inp["dout"], True, dx_out=dxz[..., :D])
+    assert dx1.data_ptr() == dxz.data_ptr()
+    assert torch.equal(dx0, dx1) and torch.equal(dw0, dw1) and torch.equal(db0, db1)
+    assert torch.equal(dxz[..., D:], dense["dz"])
