@@ -193,7 +193,8 @@ __device__ __forceinline__ void bwd_half(const float2 (*__restrict__ dd)[SCH], c
 // reloaded from shared memory in the reverse pass instead of kept in registers, and the
 // per-step results are handed to the helper warps in 4-step tiles instead of 8.
 // GW (with HAS_Z): the forward applied the SiftX pathway mix before the gate.
-template <typename Tin, bool HAS_Z, bool YPRE, bool LOWREG, bool GW = false>
+// DZS (with HAS_Z): dz has its own strides (the z half of a (b, L, 2D) gradient).
+template <typename Tin, bool HAS_Z, bool YPRE, bool LOWREG, bool GW = false, bool DZS = false>
 __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const ScanDev p, const __grid_constant__ RowMaps tm) {
     constexpr bool YV = HAS_Z && !YPRE;
     constexpr int HTQ = LOWREG ? 4 : HT;       // steps per hand-off tile
@@ -300,7 +301,7 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
         const int64_t orow = (int64_t)bi * p.L * p.D + d0;
         Tin* gdu = static_cast<Tin*>(p.du) + orow;
         Tin* gddl = static_cast<Tin*>(p.ddl) + orow;
-        Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + (int64_t)bi * p.dz_sb + d0 : nullptr;   // may be strided
+        Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + (DZS ? (int64_t)bi * p.dz_sb + d0 : orow) : nullptr;
         float* wbc = p.ws_bc + ((int64_t)blockIdx.x * p.b + bi) * p.L * 2 * NS;
         const float* gyp = YPRE ? p.ypre + (int64_t)bi * p.L * p.D + d0 : nullptr;
         float accD = 0.f, accB = 0.f;
@@ -417,7 +418,7 @@ __global__ void __launch_bounds__(NTH, LOWREG ? 2 : 1) scan_bwd_kernel(const Sca
                                 const float4 q4 = *reinterpret_cast<const float4*>(&S.nyp[slot][tt][ech][0]);
                                 y = fmaf(eD, e.x, (q4.x + q4.y) + (q4.z + q4.w));
                             }
-                            gdz[(int64_t)(t0 + t) * p.dz_sl + ech] = Elem<Tin>::from_f(e.z * y);
+                            gdz[DZS ? (int64_t)(t0 + t) * p.dz_sl + ech : o] = Elem<Tin>::from_f(e.z * y);
                         }
                         accD = fmaf(e.w, e.x, accD);
                         accB += draw;
@@ -587,7 +588,13 @@ static cudaError_t launch_t(const ScanDev& p0, cudaStream_t st) {
     const bool ypre = HAS_Z && p.ypre;
     auto k = ypre ? scan_bwd_kernel<Tin, HAS_Z, true, true> : scan_bwd_kernel<Tin, HAS_Z, false, true>;
     if constexpr (HAS_Z) {
-        if (p.gw) k = ypre ? scan_bwd_kernel<Tin, true, true, true, true> : scan_bwd_kernel<Tin, true, false, true, true>;
+        const bool dzs = p.dz_sl != p.D || p.dz_sb != (int64_t)p.L * p.D;    // strided dz
+        if (p.gw && dzs)
+            k = ypre ? scan_bwd_kernel<Tin, true, true, true, true, true> : scan_bwd_kernel<Tin, true, false, true, true, true>;
+        else if (p.gw)
+            k = ypre ? scan_bwd_kernel<Tin, true, true, true, true> : scan_bwd_kernel<Tin, true, false, true, true>;
+        else if (dzs)
+            k = ypre ? scan_bwd_kernel<Tin, true, true, true, false, true> : scan_bwd_kernel<Tin, true, false, true, false, true>;
     }
     const int smem = sizeof(BwdSmem<Tin, 4>);
     cudaError_t e = allow_smem(k, smem);

@@ -417,7 +417,9 @@ __device__ __forceinline__ void chunk_pass(SegSmem<Tin, YV>& S, int r, int nt, i
     }
 }
 
-template <typename Tin, bool HAS_Z, bool YPRE, bool GW = false>
+// DZS (with HAS_Z): dz has its own strides (the z half of a (b, L, 2D) gradient); without
+// it dz is dense like du and dd and shares their offsets.
+template <typename Tin, bool HAS_Z, bool YPRE, bool GW = false, bool DZS = false>
 __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanDev p, const __grid_constant__ SegMaps tm) {
     constexpr bool YV = HAS_Z && !YPRE;
     extern __shared__ __align__(128) unsigned char smem_raw[];   // TMA destinations: 128-byte aligned
@@ -620,12 +622,12 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
             const int64_t orow = (int64_t)bi * p.L * p.D + d0 + 2 * cpair;
             Tin* gdu = static_cast<Tin*>(p.du) + orow;
             Tin* gddl = static_cast<Tin*>(p.ddl) + orow;
-            Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + (int64_t)bi * p.dz_sb + d0 + 2 * cpair : nullptr;
+            Tin* gdz = HAS_Z ? static_cast<Tin*>(p.dz) + (DZS ? (int64_t)bi * p.dz_sb + d0 + 2 * cpair : orow)
+                             : nullptr;
             const bool pair_out = cv1 && (p.D % 2 == 0);   // both channels, 2-element aligned rows
-            // dz may be strided (the z half of a (b, L, 2D) gradient): paired stores only
-            // where its strides and base keep every pair aligned
-            const bool pair_dz = pair_out && ((p.dz_sb | p.dz_sl) & 1) == 0 &&
-                                 (reinterpret_cast<uintptr_t>(p.dz) % (2 * sizeof(Tin))) == 0;
+            // strided dz: paired stores only where its strides and base keep every pair aligned
+            const bool pair_dz = pair_out && (!DZS || (((p.dz_sb | p.dz_sl) & 1) == 0 &&
+                                 (reinterpret_cast<uintptr_t>(p.dz) % (2 * sizeof(Tin))) == 0));
 #pragma unroll
             for (int m = 0; m < TCK / 4; ++m) {
                 const int t = ch4 + 4 * m;
@@ -652,19 +654,23 @@ __global__ void __launch_bounds__(SG_THREADS, 2) scan_bwd_seg_kernel(const ScanD
                         }
                         dz = mul2(qq, y);
                     }
-                    const int64_t o = (int64_t)(t0 + t) * p.D, oz = (int64_t)(t0 + t) * p.dz_sl;
+                    const int64_t o = (int64_t)(t0 + t) * p.D;
                     if (pair_out) {
                         store2(gdu + o, du);
                         store2(gddl + o, draw);
+                        if (HAS_Z && !DZS) store2(gdz + o, dz);
                     } else {
                         gdu[o] = Elem<Tin>::from_f(du.x);
                         gddl[o] = Elem<Tin>::from_f(draw.x);
+                        if (HAS_Z && !DZS) gdz[o] = Elem<Tin>::from_f(dz.x);
                         if (cv1) {
                             gdu[o + 1] = Elem<Tin>::from_f(du.y);
                             gddl[o + 1] = Elem<Tin>::from_f(draw.y);
+                            if (HAS_Z && !DZS) gdz[o + 1] = Elem<Tin>::from_f(dz.y);
                         }
                     }
-                    if (HAS_Z) {
+                    if (HAS_Z && DZS) {
+                        const int64_t oz = (int64_t)(t0 + t) * p.dz_sl;
                         if (pair_dz) {
                             store2(gdz + oz, dz);
                         } else {
@@ -810,7 +816,13 @@ static cudaError_t launch_seg_t(const ScanDev& p0, cudaStream_t st) {
     const bool ypre = HAS_Z && p.ypre;
     auto k = ypre ? scan_bwd_seg_kernel<Tin, HAS_Z, true> : scan_bwd_seg_kernel<Tin, HAS_Z, false>;
     if constexpr (HAS_Z) {
-        if (p.gw) k = ypre ? scan_bwd_seg_kernel<Tin, true, true, true> : scan_bwd_seg_kernel<Tin, true, false, true>;
+        const bool dzs = p.dz_sl != p.D || p.dz_sb != (int64_t)p.L * p.D;    // strided dz
+        if (p.gw && dzs)
+            k = ypre ? scan_bwd_seg_kernel<Tin, true, true, true, true> : scan_bwd_seg_kernel<Tin, true, false, true, true>;
+        else if (p.gw)
+            k = ypre ? scan_bwd_seg_kernel<Tin, true, true, true> : scan_bwd_seg_kernel<Tin, true, false, true>;
+        else if (dzs)
+            k = ypre ? scan_bwd_seg_kernel<Tin, true, true, false, true> : scan_bwd_seg_kernel<Tin, true, false, false, true>;
     }
     const int smem = ypre ? sizeof(SegSmem<Tin, false>) : sizeof(SegSmem<Tin, HAS_Z>);
     if ((e = allow_smem(k, smem)) != cudaSuccess) return e;
