@@ -144,3 +144,10 @@ def test_flat_parameters_keep_values_and_update_like_separate_tensors():
             assert torch.equal(a.detach(), b.detach())
     with pytest.raises(ValueError):
         flat.bind_gradients(FlatGradients(list(reversed(decay_b + nodecay_b)), accumulate=False))
+
+
+def test_flat_parameters_reject_empty_groups_and_mixed_dtypes():
+    with pytest.raises(ValueError):
+        FlatParameters([[torch.nn.Parameter(torch.zeros(3))], []])
+    with pytest.raises(ValueError):
+        FlatParameters([[torch.nn.Parameter(torch.zeros(3)), torch.nn.Parameter(torch.zeros(2, dtype=torch.float64))]])
