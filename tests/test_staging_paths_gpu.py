@@ -55,15 +55,33 @@ def test_tma_and_per_thread_staging_agree(shape, dtype):
         assert torch.equal(aligned[k], unaligned[k]), k
 
 
-@pytest.mark.parametrize("shape,dtype", [((2, 301, 96, 16), torch.float32), ((16, 77, 520, 16), torch.bfloat16)],
-                         ids=["fp32-segmented", "bf16-rows"])
-def test_strided_gradient_outputs_equal_dense(shape, dtype):
+def _segments(inp):
+    """swx_scan_bwd_segments for these inputs: 0 = the whole-row kernel, else the segment count."""
+    from swiftx_b200 import _lib
+    from swiftx_b200.selective_scan import _fill_inputs, _prep
+    a = _lib.ScanArgs()
+    u, dl, A, Bm, Cm, Dv, z, bias, h0, in_dt = _prep(inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"],
+                                                     inp["D"], inp["z"], inp["delta_bias"], None)
+    _fill_inputs(a, u, dl, A, Bm, Cm, Dv, z, bias, h0, True, in_dt)
+    a.out_pre = 16                                    # only its presence matters here
+    return _lib.load().swx_scan_bwd_segments(a)
+
+
+@pytest.mark.parametrize("shape,dtype,rows", [((2, 301, 96, 16), torch.float32, False),
+                                              ((3, 67, 37, 16), torch.float32, False),
+                                              ((16, 77, 520, 16), torch.bfloat16, True),
+                                              ((16, 77, 519, 16), torch.bfloat16, True)],
+                         ids=["fp32-segmented", "fp32-segmented-odd", "bf16-rows", "bf16-rows-odd"])
+def test_strided_gradient_outputs_equal_dense(shape, dtype, rows):
     """dz written into the z half and the conv's dx into the x half of one (b, L, 2D)
     buffer (row stride 2D, as the in_proj output's gradient) equal the dense outputs bit
-    for bit: the segmented and the whole-row backward, and the conv backward."""
+    for bit: the segmented and the whole-row backward, and the conv backward.  With an odd
+    D the z half starts 4 (fp32) or 2 (bf16) bytes past an aligned address and every other
+    row is misaligned, so the segmented kernel's paired dz stores give way to single ones."""
     from swiftx_b200.conv import conv1d_backward
     b, L, D, N = shape
     inp = config_inputs(b, L, D, N, seed=62, device=DEV, dtype=dtype)
+    assert (_segments(inp) == 0) == rows
     args = (inp["u"], inp["delta"], inp["A"], inp["B"], inp["C"], inp["D"], inp["z"], inp["delta_bias"], True)
     pre = torch.empty(inp["u"].shape, device=DEV, dtype=torch.float32)
     _, ck, _ = scan_forward(*args, checkpoints=True, pre_out=pre)
