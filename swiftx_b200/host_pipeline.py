@@ -29,7 +29,9 @@ pageable memory works but serialises the copies.
 import torch
 
 from . import _lib
-from .selective_scan import _FLOAT_IN
+# fp32 or bf16 rows; parameters, partial sums, checkpoints and the pre-gate output are
+# fp32 buffers sized for these two (the float64 kernels take float64 throughout)
+_ROW_DTYPES = (torch.float32, torch.bfloat16)
 
 _INPUTS = ("u", "delta", "z", "B", "C", "dout")
 _ROW_GRADS = ("du", "ddelta", "dz", "dB", "dC")
@@ -53,10 +55,10 @@ class HostScanPipeline:
     def __init__(self, batch, seqlen, dim, dstate, *, dtype=torch.float32, has_z=True, has_D=True,
                  has_bias=True, delta_softplus=True, rows_per_chunk=None, nbuf=3, n_compute=2,
                  device=None, chain_calls=False):
-        if dtype not in _FLOAT_IN:
+        if dtype not in _ROW_DTYPES:
             raise ValueError(f"dtype must be float32 or bfloat16, got {dtype}")
         if not 1 <= dstate <= 16:
-            raise ValueError(f"d_state {dstate} > 16 is not supported")
+            raise ValueError(f"d_state must be in 1..16, got {dstate}")
         self.lib = _lib.load()
         dev = torch.device(device if device is not None else "cuda")
         if dev.type == "cuda" and dev.index is None:

@@ -143,6 +143,19 @@ def test_cpu_tensors_are_rejected_not_computed():
     from swiftx_b200 import parallel_scan
     with pytest.raises(RuntimeError):
         parallel_scan(torch.rand(2, 5, 3), torch.randn(2, 5, 3))
+    from swiftx_b200.decode import decode_conv_step
+    with pytest.raises(RuntimeError):
+        decode_conv_step(torch.randn(2, 3), torch.zeros(2, 3, 4), torch.randn(3, 4))
+    from swiftx_b200.norm import rms_norm
+    with pytest.raises(ValueError):
+        rms_norm(u, torch.ones(3))
+    from swiftx_b200.host_pipeline import HostScanPipeline
+    with pytest.raises(RuntimeError):
+        HostScanPipeline(2, 8, 3, 2, device="cpu")
+    for bad in (dict(dtype=torch.float64), dict(dstate=0), dict(dstate=17)):    # checked before any device use
+        kw = dict(dtype=torch.float32, dstate=2) | bad
+        with pytest.raises(ValueError):
+            HostScanPipeline(2, 8, 3, kw.pop("dstate"), **kw)
 
 
 def test_strided_gradient_output_arguments_are_checked():
