@@ -32,6 +32,8 @@ def _prep(x, weight, bias):
         raise RuntimeError("swiftx_b200 conv1d runs on CUDA tensors only (no CPU path)")
     if x.dim() != 3:
         raise ValueError("expected x of shape (b, L, D)")
+    if x.dtype == torch.float64:
+        raise ValueError("conv1d: the kernels take float32 or bfloat16 x (no float64 form)")
     if x.dtype not in _lib.DTYPE_CODES:
         x = x.float()
     if x.stride(-1) != 1:

@@ -19,8 +19,10 @@ Fusing the gate is exactly the reference's y * silu(z) when no SiftX pathway mix
 configured (models/sift_block.py:132-142).  With pathway_gate (SiftX), the per-token
 group weights softmax(pathway(x)) x G are computed in torch (a (b, L, G) tensor) and the
 scan kernels apply them between the scan and the gate, out = y * w[group] * silu(z),
-returning their gradient from the backward (the decode kernel applies them too); float64
-blocks keep the mix and gate in torch.
+returning their gradient from the backward (the decode kernel applies them too); with
+more than 8 groups the mix and gate stay in torch.  The block runs fp32 or bf16
+activations: the conv kernels have no float64 form (the scan's float64 kernels serve the
+reference's own float64 callers).
 """
 import math
 from dataclasses import dataclass
@@ -335,12 +337,12 @@ class SiftBlock(nn.Module):
 
     def _mix_fusable(self, x):
         """The scan kernels apply the group mix themselves for fp32 / bf16 inputs and at
-        most SWX_MAX_GROUPS groups; float64 blocks keep the mix in torch."""
+        most SWX_MAX_GROUPS groups; more groups keep the mix in torch."""
         return x.dtype in (torch.float32, torch.bfloat16) and self.n_groups <= 8
 
     def _mix_pathways(self, y, x):
         """SiftX: reweight the channel groups per token, softmax x G (1 at init)
-        (models/sift_block.py:137-142); the unfused form, for float64 and more than 8 groups."""
+        (models/sift_block.py:137-142); the unfused form, for more than 8 groups."""
         return y * self._pathway_weights(x)[..., self.group_of]
 
     def allocate_state(self, batch, device=None, dtype=torch.float32):
