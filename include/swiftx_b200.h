@@ -100,7 +100,8 @@ typedef struct swx_scan_args {
     /* optional, with z: the SiftX pathway mix (models/sift_block.py:137-142) fused into the
        gate.  group_w: (b, L, ngroups) fp32 per-token group weights (group stride 1; the
        block's softmax(pathway(x)) * ngroups); group_of: (D,) int32 group of each channel,
-       in [0, ngroups); 1 <= ngroups <= SWX_MAX_GROUPS.  The forward writes
+       in [0, ngroups) (device memory, not checked: the caller guarantees the range);
+       1 <= ngroups <= SWX_MAX_GROUPS.  The forward writes
        out_t = y_t * group_w[t, group_of[d]] * silu(z_t) (out_pre stays y_t).  The
        backward reads dout through the same factor and, when d_group_w is non-NULL
        (requires out_pre), writes d_group_w[b, t, g] = sum over the channels of group g of
@@ -279,7 +280,8 @@ typedef struct swx_decode_args {
     int32_t reserved;
     /* optional, with z: the SiftX pathway mix before the gate (models/sift_block.py:
        137-142, 172-173), out = y * group_w[b, group_of[d]] * silu(z).  group_w (b, ngroups)
-       fp32 with group stride 1; group_of (D,) int32; 1 <= ngroups <= SWX_MAX_GROUPS. */
+       fp32 with group stride 1; group_of (D,) int32 in [0, ngroups) (not checked: the
+       caller guarantees the range); 1 <= ngroups <= SWX_MAX_GROUPS. */
     const float* group_w; int64_t group_w_sb;
     const int32_t* group_of;
     int32_t ngroups;

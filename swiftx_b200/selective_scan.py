@@ -70,8 +70,10 @@ def _fill_inputs(a, u, delta, A, B, C, D, z, delta_bias, h0, softplus, in_dt, A_
 
 def _prep_groups(group_w, group_of, u, z):
     """The SiftX pathway mix fused into the gate: group_w (b, L, G) per-token group weights
-    (fp32, made contiguous) and group_of (D,) channel -> group (int32).  Returns the pair
-    as the kernels take it, or (None, None)."""
+    (fp32, made contiguous) and group_of (D,) channel -> group (int32, values in [0, G):
+    the kernels index group_w with them unchecked, and checking device values here would
+    cost a synchronisation per call).  Returns the pair as the kernels take it, or
+    (None, None)."""
     if group_w is None:
         return None, None
     if z is None:
