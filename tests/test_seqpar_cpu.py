@@ -5,7 +5,9 @@ through the hooks: the chunk's scan from a zero state by the CPU oracle, and the
 initial-state correction by a float64 NumPy restatement of its formula
 (out_t += silu(z_t) sum_n C_t[n] exp(A[:, n] S_t) h_in[n]).  What is tested is the
 peer-to-peer boundary exchange, the prefix combine and the correction's mathematics:
-the concatenated outputs must equal the oracle's scan of the whole sequence."""
+the concatenated outputs must equal the oracle's scan of the whole sequence, also when
+a rank's chunk is empty (chunk_bounds gives short sequences to rank 0 alone): its
+boundary passes the earlier ranks' state through unchanged."""
 import os
 import socket
 
@@ -67,7 +69,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("bounds", [[0, 41, 90], [0, 30, 31, 90], chunk_bounds(90, 3, correction_offset=0, multiple=1)])
+@pytest.mark.parametrize("bounds", [[0, 41, 90], [0, 30, 31, 90], chunk_bounds(90, 3, correction_offset=0, multiple=1),
+                                    [0, 90, 90], [0, 60, 60, 90]])
 def test_sequence_parallel_matches_whole_sequence(bounds):
     world = len(bounds) - 1
     ctx = mp.get_context("spawn")
