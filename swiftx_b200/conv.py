@@ -57,9 +57,10 @@ def conv1d_forward(x, weight, bias=None, silu=True):
 
 
 def conv1d_backward(x, weight, bias, dout, silu=True, dx_out=None):
-    """dx, dweight, dbias of conv1d_forward.  dx_out: optional (b, L, D) tensor of x's
-    dtype with unit channel stride (e.g. the x half of a (b, L, 2D) gradient) that receives
-    dx in place of a new tensor."""
+    """dx, dweight, dbias of conv1d_forward.  dx_out: optional (b, L, D) tensor with unit
+    channel stride (e.g. the x half of a (b, L, 2D) gradient) that receives dx in place of
+    a new tensor; its dtype is x's for fp32 / bf16 x, fp32 for x of another dtype (which
+    the kernels compute in fp32)."""
     lib = _lib.load()
     x, w, bb = _prep(x, weight, bias)
     dout = dout.to(x.dtype)
