@@ -146,8 +146,9 @@ def scan_forward(u, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softp
     a.checkpoints = ck.data_ptr() if ck is not None else None
     a.delta_sum = ds.data_ptr() if ds is not None else None
     if pre_out is not None and z is not None:
-        if pre_out.dtype != pdt or not pre_out.is_contiguous() or pre_out.shape != (b, L, Dm):
-            raise ValueError(f"pre_out must be a dense {pdt} (b, L, D) tensor")
+        if pre_out.dtype != pdt or not pre_out.is_contiguous() or pre_out.shape != (b, L, Dm) \
+                or pre_out.device != u.device:
+            raise ValueError(f"pre_out must be a dense {pdt} (b, L, D) tensor on {u.device}")
         a.out_pre = pre_out.data_ptr()
     _fill_groups(a, gw, gof)
     ws = None
@@ -180,6 +181,14 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     dout = _rows(dout.to(in_dt))
     dev = u.device
     pdt = _param_dtype(in_dt)
+    # the kernels read these two through bare pointers: check what they will index
+    need = lib.swx_scan_checkpoint_floats(b, L, Dm)
+    if ck is None or ck.dtype != pdt or ck.device != dev or not ck.is_contiguous() or ck.numel() < need:
+        raise ValueError(f"ck must be the forward's checkpoints: a contiguous {pdt} tensor of at least "
+                         f"{need} values on {dev}")
+    if y_pre is not None and z is not None and (y_pre.dtype != pdt or not y_pre.is_contiguous()
+                                                or y_pre.shape != (b, L, Dm) or y_pre.device != dev):
+        raise ValueError(f"y_pre must be the forward's pre_out: a dense {pdt} (b, L, D) tensor on {dev}")
     e = lambda *s, dt=in_dt: torch.empty(s, device=dev, dtype=dt)  # noqa: E731
     g = {"du": e(b, L, Dm), "ddelta": e(b, L, Dm), "dB": e(b, L, N), "dC": e(b, L, N),
          "dA": e(Dm, N, dt=pdt)}
