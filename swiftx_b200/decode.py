@@ -21,12 +21,28 @@ def _row(t):
     return t if t.stride(-1) == 1 else t.contiguous()
 
 
+def _expect(name, t, shape):
+    """Raise unless t (when given) has exactly this shape: the kernels index it through a
+    bare pointer with the sizes of x, the weights and the states."""
+    if t is not None and tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name}: expected shape {tuple(shape)}, got {tuple(t.shape)}")
+
+
+def _expect_vec(name, t, n):
+    """Raise unless t (when given) holds exactly n values (a per-channel vector)."""
+    if t is not None and t.numel() != n:
+        raise ValueError(f"{name}: expected {n} values, got {t.numel()}")
+
+
 def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, delta=None, B=None,
           C=None, A=None, Dskip=None, delta_bias=None, ssm_state=None, delta_softplus=True,
           want_xc=False, A_is_log=False, group_w=None, group_of=None, dt_in=None, dt_weight=None):
     lib = _lib.load()
     x, z, delta, B, C = map(_row, (x, z, delta, B, C))
+    if x.dim() != 2:
+        raise ValueError(f"x: expected (b, D), got {tuple(x.shape)}")
     b, D = x.shape
+    _expect("z", z, (b, D))
     a = _lib.DecodeArgs()
     a.batch, a.dim, a.mode = b, D, mode
     a.delta_softplus = 1 if delta_softplus else 0
@@ -36,7 +52,11 @@ def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, de
     if mode & _lib.SWX_DECODE_CONV:
         if not conv_state.is_contiguous() or conv_state.dtype != torch.float32:
             raise ValueError("conv_state must be a dense fp32 (b, D, K) tensor")
+        if conv_weight.shape[0] != D or conv_weight.numel() % D:
+            raise ValueError(f"conv_weight: expected (D, K) or (D, 1, K) with D={D}, got {tuple(conv_weight.shape)}")
         w = conv_weight.detach().reshape(D, -1).float().contiguous()
+        _expect("conv_state", conv_state, (b, D, w.shape[1]))
+        _expect_vec("conv_bias", conv_bias, D)
         keep.append(w)
         a.width = w.shape[1]
         a.conv_weight, a.conv_state = w.data_ptr(), conv_state.data_ptr()
@@ -52,15 +72,26 @@ def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, de
     if mode & _lib.SWX_DECODE_SSM:
         if not ssm_state.is_contiguous() or ssm_state.dtype != torch.float32:
             raise ValueError("ssm_state must be a dense fp32 (b, D, N) tensor")
+        if A.dim() != 2 or A.shape[0] != D:
+            raise ValueError(f"A: expected (D, N) with D={D}, got {tuple(A.shape)}")
         Af = A.detach().float().contiguous()
+        N = Af.shape[1]
+        _expect("ssm_state", ssm_state, (b, D, N))
+        _expect("delta", delta, (b, D))
+        _expect("B", B, (b, N))
+        _expect("C", C, (b, N))
+        _expect_vec("Dskip", Dskip, D)
+        _expect_vec("delta_bias", delta_bias, D)
         keep.append(Af)
-        a.dstate = Af.shape[1]
+        a.dstate = N
         out = torch.empty((b, D), device=x.device, dtype=torch.float32)
         if dt_in is not None:                     # dt_proj folded into the kernel
             dti = _row(dt_in)
             if dti.stride(0) % 4 or dti.data_ptr() % 16:
                 dti = dti.contiguous()
             dtw = dt_weight.detach().float().contiguous()
+            _expect("dt_weight", dtw, (D, dtw.shape[1] if dtw.dim() == 2 else -1))
+            _expect("dt_in", dti, (b, dtw.shape[1]))
             keep += [dti, dtw]
             a.dt_in, a.dt_in_sb, a.dt_weight, a.dt_rank = dti.data_ptr(), dti.stride(0), dtw.data_ptr(), dtw.shape[1]
         else:
@@ -72,6 +103,8 @@ def _call(mode, x, conv_state=None, conv_weight=None, conv_bias=None, z=None, de
         if group_w is not None:                   # the SiftX pathway mix, before the gate
             gw = group_w.detach().float().contiguous()
             gof = group_of.to(torch.int32).contiguous()
+            _expect("group_w", gw, (b, gw.shape[1] if gw.dim() == 2 else -1))
+            _expect_vec("group_of", gof, D)
             keep += [gw, gof]
             a.group_w, a.group_w_sb, a.group_of, a.ngroups = gw.data_ptr(), gw.stride(0), gof.data_ptr(), gw.shape[1]
         for name, t in (("Dskip", Dskip), ("delta_bias", delta_bias)):
@@ -137,6 +170,14 @@ def decode_layer_step(x, conv_state, conv_weight, conv_bias, xproj_weight, dt_we
         return None
     if x.stride(0) % 4 or x.data_ptr() % 16 or (z is not None and (z.stride(0) % 4 or z.data_ptr() % 16)):
         return None
+    # a shape the path takes: the remaining operands must match it (bare pointers below)
+    _expect("z", z, (b, D))
+    _expect("A", Af, (D, N))
+    _expect("dt_weight", dtw, (D, R))
+    _expect("conv_state", conv_state, (b, D, 4))
+    _expect("ssm_state", ssm_state, (b, D, N))
+    for name, t in (("conv_bias", conv_bias), ("Dskip", Dskip), ("delta_bias", delta_bias)):
+        _expect_vec(name, t, D)
     keep = [w, Af, xw, dtw]
     a = _lib.DecodeArgs()
     a.batch, a.dim, a.dstate, a.width = b, D, N, 4
