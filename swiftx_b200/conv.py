@@ -27,9 +27,14 @@ def _fill(a, x, weight, bias, silu):
     a.bias = bias.data_ptr() if bias is not None else None
 
 
+def _require_cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("swiftx_b200 conv1d runs on CUDA tensors only (no CPU path)")
+
+
 def _prep(x, weight, bias):
-    if not (x.is_cuda and weight.is_cuda):
-        raise RuntimeError("swiftx_b200 conv1d runs on CUDA tensors only (no CPU path)")
+    _require_cuda(x, weight)
     if x.dim() != 3:
         raise ValueError("expected x of shape (b, L, D)")
     if x.dtype == torch.float64:
@@ -42,6 +47,8 @@ def _prep(x, weight, bias):
     bb = bias.detach().float().contiguous() if bias is not None else None
     if w.shape[0] != x.shape[-1]:
         raise ValueError(f"weight has {w.shape[0]} channels, x has {x.shape[-1]}")
+    if bb is not None and bb.numel() != x.shape[-1]:
+        raise ValueError(f"bias has {bb.numel()} values, x has {x.shape[-1]} channels")
     return x, w, bb
 
 
@@ -63,6 +70,8 @@ def conv1d_backward(x, weight, bias, dout, silu=True, dx_out=None):
     the kernels compute in fp32)."""
     lib = _lib.load()
     x, w, bb = _prep(x, weight, bias)
+    if dout.shape != x.shape:
+        raise ValueError(f"dout: expected shape {tuple(x.shape)}, got {tuple(dout.shape)}")
     dout = dout.to(x.dtype)
     if dout.stride(-1) != 1:
         dout = dout.contiguous()

@@ -30,6 +30,8 @@ class RMSNormFn(torch.autograd.Function):
         d = x.shape[-1]
         xf = x.contiguous().view(-1, d)
         w = weight.detach().float().contiguous()
+        if w.numel() != d:
+            raise ValueError(f"rms_norm: weight has {w.numel()} values, x has {d} channels")
         out_dtype = out_dtype or x.dtype
         if out_dtype not in _DT:
             raise ValueError(f"rms_norm: output dtype {out_dtype} not supported")
@@ -85,6 +87,8 @@ class AddRMSNormFn(torch.autograd.Function):
         xf = x.contiguous().view(-1, d)
         rf = res.contiguous().view(-1, d)
         w = weight.detach().float().contiguous()
+        if w.numel() != d:
+            raise ValueError(f"rms_norm: weight has {w.numel()} values, x has {d} channels")
         out_dtype = out_dtype or x.dtype
         if out_dtype not in _DT:
             raise ValueError(f"add_rms_norm: output dtype {out_dtype} not supported")

@@ -109,6 +109,11 @@ def _prep(u, delta, A, B, C, D, z, delta_bias, h0):
         raise ValueError(f"shape mismatch: u {tuple(u.shape)}, A {tuple(A.shape)}, B {tuple(B.shape)}")
     if N > 16:
         raise ValueError(f"d_state {N} > 16 is not supported")
+    for name, t in (("D", D), ("delta_bias", delta_bias)):
+        if t is not None and t.numel() != Dm:
+            raise ValueError(f"{name}: expected {Dm} values, got {t.numel()}")
+    if h0 is not None and h0.shape != (b, Dm, N):
+        raise ValueError(f"h0: expected shape {(b, Dm, N)}, got {tuple(h0.shape)}")
     return u, delta, A, B, C, D, z, delta_bias, h0, in_dt
 
 
@@ -178,6 +183,8 @@ def scan_backward(u, delta, A, B, C, D, z, delta_bias, delta_softplus, h0, ck, d
     gw, gof = _prep_groups(group_w, group_of, u, z)
     b, L, Dm = u.shape
     N = A.shape[1]
+    if dout.shape != (b, L, Dm):
+        raise ValueError(f"dout: expected shape {(b, L, Dm)}, got {tuple(dout.shape)}")
     dout = _rows(dout.to(in_dt))
     dev = u.device
     pdt = _param_dtype(in_dt)

@@ -185,33 +185,3 @@ def test_strided_gradient_output_arguments_are_checked():
     c.workspace_bytes = 1 << 40
     c.dx_sb, c.dx_sl = 0, 128
     assert lib.swx_conv1d_bwd(c, None) == _lib.SWX_ERR_INVALID_ARG
-
-
-def test_backward_refuses_checkpoints_and_pre_output_it_cannot_index(monkeypatch):
-    """The backward kernels read the forward's checkpoints and pre-gate output through bare
-    pointers, so scan_backward checks them first: a missing, short, mistyped or strided
-    buffer raises before any kernel is launched (as does a mis-shaped pre_out given to
-    the forward).  CPU tensors stand in for device ones here (the CUDA check is switched
-    off), and every case is one the checks refuse, so nothing reaches the library's
-    launch functions."""
-    torch = pytest.importorskip("torch")
-    from swiftx_b200 import _lib, selective_scan
-    monkeypatch.setattr(selective_scan, "_require_cuda", lambda *ts: None)
-    g = torch.Generator().manual_seed(0)
-    b, L, D, N = 2, 40, 8, 4
-    u, dl, z, dout = (torch.randn(b, L, D, generator=g) for _ in range(4))
-    A, Bm, Cm = -torch.rand(D, N, generator=g) - 0.1, torch.randn(b, L, N, generator=g), torch.randn(b, L, N, generator=g)
-    args = (u, dl.abs(), A, Bm, Cm, torch.randn(D, generator=g), z, None, False)
-    need = _lib.load().swx_scan_checkpoint_floats(b, L, D)
-    assert need > 0
-    ck = torch.empty(need)
-    for bad_ck in (None, torch.empty(need - 1), torch.empty(need, dtype=torch.float64),
-                   torch.empty(2 * need)[::2]):
-        with pytest.raises(ValueError, match="ck must be"):
-            selective_scan.scan_backward(*args, None, bad_ck, dout)
-    for bad_pre in (torch.empty(b, L, D - 1), torch.empty(b, L, D, dtype=torch.bfloat16),
-                    torch.empty(b, D, L).transpose(1, 2)):
-        with pytest.raises(ValueError, match="y_pre must be"):
-            selective_scan.scan_backward(*args, None, ck, dout, y_pre=bad_pre)
-        with pytest.raises(ValueError, match="pre_out must be"):
-            selective_scan.scan_forward(*args, checkpoints=True, pre_out=bad_pre)
