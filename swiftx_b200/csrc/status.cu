@@ -1,10 +1,11 @@
 // The status word of the library's bounded device-side waits, and the lookup of device
 // addresses of the library's __device__ variables.
 //
-// A kernel that waits for its own asynchronous copies (the time-segmented backward's TMA
-// tiles) gives every wait an iteration limit.  When a wait runs out the kernel records
-// SWX_ERR_TIMEOUT in g_wait_status and returns, leaving its results incomplete but the
-// context usable; swx_device_wait_status() reads (and clears) the word on the host.
+// A kernel that waits for its own asynchronous copies (the TMA tiles of the scan forward,
+// the backward's summary and main kernels and the whole-row backward) gives every wait an
+// iteration limit.  When a wait runs out the kernel records SWX_ERR_TIMEOUT in
+// g_wait_status and returns, leaving its results incomplete but the context usable;
+// swx_device_wait_status() reads (and clears) the word on the host.
 #include <cuda.h>
 
 #include <mutex>
