@@ -418,9 +418,9 @@ int swx_embedding_bwd(const swx_embedding_args* args, void* stream);
  * device fp32 arrays of n values.  Not part of any reference interface. */
 int swx_exp2_fma_eval(const float* x, float* y, int64_t n, void* stream);
 
-/* Status of the library's bounded device-side waits on the current device.  The
- * time-segmented backward waits for its TMA tiles with an iteration limit (about a
- * second); if a wait runs out, the kernel records SWX_ERR_TIMEOUT, leaves its outputs
+/* Status of the library's bounded device-side waits on the current device.  The scan
+ * kernels (forward, both backward paths) wait for their TMA tiles with an iteration
+ * limit (about a second); if a wait runs out, the kernel records SWX_ERR_TIMEOUT, leaves its outputs
  * incomplete and returns, and the context stays usable.  This call synchronises the
  * device and returns SWX_OK, or SWX_ERR_TIMEOUT once for every run of timeouts (it
  * clears the status), or SWX_ERR_CUDA. */
