@@ -26,3 +26,20 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["config"]["batch"] == 8 and d["config"]["seqlen"] == 2048
+
+
+def test_reference_arm_under_torchrun_prints_on_rank_0_only():
+    """Launched as one of N ranks (torchrun sets WORLD_SIZE / RANK), the reference arm
+    runs on rank 0 alone: any other rank exits 0 at once, without output, and joins no
+    process group.  A workload other than the scan prints its "unavailable" line."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", WORLD_SIZE="2", RANK="1", LOCAL_RANK="1")
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--gpus", "2", "--steps", "1",
+                        "--warmup", "1"], cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    assert not [ln for ln in r.stdout.splitlines() if ln.startswith("{")], r.stdout
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", "lm_train"],
+                       cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [json.loads(ln) for ln in r.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1 and lines[0]["impl"] == "reference" and "unavailable" in lines[0]
