@@ -185,3 +185,29 @@ def test_strided_gradient_output_arguments_are_checked():
     c.workspace_bytes = 1 << 40
     c.dx_sb, c.dx_sl = 0, 128
     assert lib.swx_conv1d_bwd(c, None) == _lib.SWX_ERR_INVALID_ARG
+
+
+def test_header_is_plain_c_and_a_c_program_links_the_library(tmp_path):
+    """A C caller (a cgo or JNI binding's shim) compiles include/swiftx_b200.h as strict
+    C99, links the library, and sees the argument structs with the library's own sizes
+    (host-only calls: no GPU needed)."""
+    import shutil
+    import subprocess
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    lib = _lib.load()
+    src = tmp_path / "caller.c"
+    src.write_text(
+        '#include <stdio.h>\n#include "swiftx_b200.h"\n'
+        "int main(void) {\n"
+        "    printf(\"%d %lld %d %d %d %d\\n\", swx_abi_version(), (long long)swx_scan_checkpoint_floats(1, 17, 3),\n"
+        "           swx_scan_fwd(NULL, NULL), (int)(swx_scan_args_size() == sizeof(swx_scan_args)),\n"
+        "           (int)(swx_conv_args_size() == sizeof(swx_conv_args)),\n"
+        "           (int)(swx_decode_args_size() == sizeof(swx_decode_args)));\n"
+        "    return 0;\n}\n")
+    libdir = os.path.dirname(lib._name)
+    exe = tmp_path / "caller"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Wextra", "-pedantic", "-Werror", f"-I{ROOT}/include", str(src),
+                    f"-L{libdir}", "-lswiftx_b200", f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()
+    assert out == ["13", "96", str(_lib.SWX_ERR_INVALID_ARG), "1", "1", "1"]
