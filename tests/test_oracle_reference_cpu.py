@@ -6,7 +6,8 @@ in float64 under autograd: the block's expression around the scan,
 out = selective_scan_ref(u, softplus(delta + bias), A, B, C, D) * silu(z)
 (models/selective_scan.py:34-60, models/sift_block.py:108,134), with the softplus, the
 gate and the D skip each switched on or off (skipped where the reference checkout is not
-available; set SWIFTX_REFERENCE to point at one).  The block's causal conv + SiLU is
+available; set SWIFTX_REFERENCE to point at one), and the decode oracle against the
+reference's own SiftBlock.step over several tokens.  The block's causal conv + SiLU is
 torch's depthwise Conv1d in the reference, so its check needs no checkout.
 """
 import importlib
@@ -31,16 +32,20 @@ CASES = [((2, 33, 7, 5), dict(gate=True, softplus=True, skip=True)),
 
 
 @pytest.fixture(scope="module")
-def reference_scan():
-    """models.selective_scan imported from the reference checkout, removed afterwards."""
+def reference_models():
+    """Importer of the reference checkout's models.* modules, removed afterwards."""
     sys.path.insert(0, REF)
     try:
-        mod = importlib.import_module("models.selective_scan")
-        yield mod.selective_scan_ref
+        yield lambda name: importlib.import_module(f"models.{name}")
     finally:
         sys.path.remove(REF)
         for name in [m for m in sys.modules if m == "models" or m.startswith("models.")]:
             del sys.modules[name]
+
+
+@pytest.fixture(scope="module")
+def reference_scan(reference_models):
+    return reference_models("selective_scan").selective_scan_ref
 
 
 @needs_reference
@@ -102,3 +107,39 @@ def test_conv_oracle_matches_block_expression(b, L, D, K, bias):
         np.testing.assert_allclose(db, n(cb.grad), rtol=1e-11, atol=1e-12)
     else:
         assert db is None
+
+
+@needs_reference
+@pytest.mark.parametrize("b,d_model,d_state,d_conv", [(2, 12, 5, 3), (4, 16, 16, 4)])
+def test_decode_oracle_matches_block_step(reference_models, b, d_model, d_state, d_conv):
+    """oracle.decode_step against the reference's own SiftBlock.step (models/sift_block.py:
+    153-175) in float64 over four tokens: the step's inputs to the state update (x, z, the
+    dt projection, B, C) are captured from the block as it runs, and the oracle, fed them
+    and the previous states, must give the block's gated output and both new states."""
+    SiftBlock = reference_models("sift_block").SiftBlock
+    torch.manual_seed(b * d_model + d_state)
+    blk = SiftBlock(d_model=d_model, d_state=d_state, d_conv=d_conv, expand=2).double()
+    conv_state, ssm_state = blk.allocate_state(b, dtype=torch.float64)
+    g = torch.Generator().manual_seed(5)
+    conv_state.copy_(torch.randn(conv_state.shape, dtype=torch.float64, generator=g))
+    ssm_state.copy_(0.1 * torch.randn(ssm_state.shape, dtype=torch.float64, generator=g))
+    cap = {}
+    fwd = {k: getattr(blk, k).forward for k in ("in_proj", "x_proj", "dt_proj")}
+    blk.in_proj.forward = lambda h: cap.setdefault("xz", fwd["in_proj"](h))
+    blk.x_proj.forward = lambda t: cap.setdefault("xdbl", fwd["x_proj"](t))
+    blk.dt_proj.forward = lambda t: cap.setdefault("dr", fwd["dt_proj"](t))
+    blk.out_proj.forward = lambda y: cap.setdefault("y", y)
+    A = -torch.exp(blk.A_log.float()).double()                  # as the block forms it
+    n = lambda t: t.detach().numpy()  # noqa: E731
+    cs, ss = n(conv_state).copy(), n(ssm_state).copy()
+    for _ in range(4):
+        cap.clear()
+        with torch.no_grad():
+            blk.step(torch.randn(b, d_model, dtype=torch.float64, generator=g), (conv_state, ssm_state))
+        x, z = cap["xz"].chunk(2, dim=-1)
+        _, Bm, Cm = torch.split(cap["xdbl"], [blk.dt_rank, d_state, d_state], dim=-1)
+        out, cs, ss, _ = oracle.decode_step(n(x), n(z), n(cap["dr"]), n(Bm), n(Cm), n(blk.conv1d.weight.squeeze(1)),
+                                            n(blk.conv1d.bias), n(A), n(blk.D), None, cs, ss, delta_softplus=True)
+        np.testing.assert_allclose(out, n(cap["y"]), rtol=1e-11, atol=1e-12)
+        np.testing.assert_allclose(cs, n(conv_state), rtol=0, atol=0)
+        np.testing.assert_allclose(ss, n(ssm_state), rtol=1e-11, atol=1e-12)
